@@ -1,0 +1,176 @@
+/*
+ * stealcode_b200.h -- C ABI of libstealcode_cuda.so, the B200 (sm_100a)
+ * implementation of the streaming Nemotron/FastConformer encoder hot path of
+ * she-workss/stealcode: the Q8_0 weight x f32 activation GEMM and the
+ * cache-aware chunked streaming rel-pos self-attention.
+ *
+ * Conventions
+ *   - Every function returns SC_OK (0) or a negative SC_ERR_* code and never
+ *     aborts; sc_last_error() returns the calling thread's last message.
+ *   - `stream` arguments are cudaStream_t values passed as void* (NULL = the
+ *     legacy default stream).  Device-pointer entry points are asynchronous on
+ *     that stream; *_host entry points are synchronous.
+ *   - Reference citations are paths inside the reference's
+ *     crates/audio_engine/src/ directory.
+ *
+ * Dimension names: the reference's CPU operator q8_gemm(m, k, n, ...) uses
+ * m = output features (weight rows), k = input features, n = frames; the
+ * device API below calls the frame count `t` and the weight rows `rows`.
+ */
+#ifndef STEALCODE_B200_H
+#define STEALCODE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SC_ABI_VERSION 1
+
+#define SC_OK 0
+#define SC_ERR_INVALID (-1)     /* bad argument or shape */
+#define SC_ERR_ALLOC (-2)       /* device or host allocation failed */
+#define SC_ERR_CUDA (-3)        /* a CUDA runtime call failed */
+#define SC_ERR_TIMEOUT (-4)     /* a bounded device-side wait gave up */
+#define SC_ERR_UNSUPPORTED (-5) /* valid input outside what the kernels take */
+#define SC_ERR_STATE (-6)       /* call out of order (e.g. encoder out of sync) */
+
+/* Activation / output layouts.
+ * FEATURE_MAJOR: x is [k, t] (element (frame j, feature i) at x[i*ld + j]) and
+ *   y is [rows, t] -- the reference CPU layout of q8_gemm / Lin::forward_t
+ *   (sgemm_kernel.rs:92-97, nemotron/weights.rs:299-305).
+ * TIME_MAJOR: x is [t, k] (x[j*ld + i]) and y is [t, rows] -- the layout of
+ *   the reference wgpu kernel (gpu/shaders/q8_gemm.wgsl:1-8) and of the
+ *   device encoder. */
+#define SC_LAYOUT_FEATURE_MAJOR 0
+#define SC_LAYOUT_TIME_MAJOR 1
+
+/* Repacked Q8_0 weight matrix resident in device memory (opaque). */
+typedef struct sc_q8w sc_q8w;
+
+const char *sc_last_error(void);
+int sc_abi_version(void);
+
+/* ---- weights --------------------------------------------------------- */
+
+/* Repack a GGUF Q8_0 tensor once into the device layout: int8 quants in
+ * 128-row x 32-column tiles plus a separate f16 scale array.  `blocks` (host)
+ * holds `rows` rows of ceil(k/32) blocks of `block_bytes` bytes, scale at byte
+ * 0 and quants at byte `qoff` -- exactly Q8Mat's bytes
+ * (nemotron/weights.rs:91-111, as load_lin copies them from the GGUF,
+ * nemotron/weights.rs:640-697).  Replaces the reference GPU backend's
+ * load-time repack pack_q8 (gpu/kernels.rs:44-78).  Only the 34-byte
+ * f16-scale block (GGUF dtype 8, qoff 2) is accepted; the 36-byte f32-scale
+ * variant returns SC_ERR_UNSUPPORTED (pack_q8 has the same restriction: it
+ * reads quants at byte 2).  Synchronous. */
+int sc_q8_repack(const uint8_t *blocks, int64_t rows, int64_t k,
+                 int64_t block_bytes, int64_t qoff, sc_q8w **out);
+/* Same, from GGUF block bytes already in device memory; async on stream. */
+int sc_q8_repack_device(const uint8_t *blocks_dev, int64_t rows, int64_t k,
+                        int64_t block_bytes, int64_t qoff, void *stream,
+                        sc_q8w **out);
+int sc_q8w_free(sc_q8w *w);
+/* Q8Mat::rows / Q8Mat::row_len (nemotron/weights.rs:113-119). */
+int sc_q8w_shape(const sc_q8w *w, int64_t *rows, int64_t *k);
+/* Device pointers of the repacked layout (for tests and tooling). */
+int sc_q8w_device_layout(const sc_q8w *w, const int8_t **quants,
+                         const uint16_t **scales, int64_t *rows_pad,
+                         int64_t *nblocks);
+
+/* ---- Q8_0 GEMM ------------------------------------------------------- */
+
+/* Bytes of workspace sc_q8_gemm needs for t frames of k features. */
+int64_t sc_q8_gemm_workspace_bytes(int64_t t, int64_t k);
+
+/* y = W x (+ bias), device pointers: the device twin of q8_gemm
+ * (sgemm_kernel.rs:99-127) and Lin::forward_t (nemotron/weights.rs:305-337).
+ * Each activation frame is quantised per 32-block exactly as quantize_col
+ * (sgemm_kernel.rs:57-90) does, then multiplied with exact int8 block dots
+ * and an f32 per-block scale.  ldx/ldy <= 0 select the packed leading
+ * dimension of the layout.  `workspace` (256-byte aligned, at least
+ * sc_q8_gemm_workspace_bytes) may be NULL to use a per-device library
+ * workspace, which is then shared by all NULL-workspace calls on that device
+ * and must not be used from two streams at once.  t == 0 is a no-op, as in
+ * the reference. */
+int sc_q8_gemm(const sc_q8w *w, const float *x, int64_t t, int32_t x_layout,
+               int64_t ldx, const float *bias, float *y, int32_t y_layout,
+               int64_t ldy, void *workspace, int64_t workspace_bytes,
+               void *stream);
+
+/* Q8Mat::gemm_t (nemotron/weights.rs:186-202) with host activations and
+ * outputs: x_host is [k, t], y_host is [rows, t] (feature-major);
+ * synchronous. */
+int sc_q8mat_gemm_t(const sc_q8w *w, const float *x_host, int64_t t,
+                    float *y_host);
+
+/* Byte-for-byte twin of q8_gemm (sgemm_kernel.rs:99-109): host weight
+ * blocks, host x [k, n], host y [m, n]; repacks the weights on every call
+ * (use sc_q8_repack + sc_q8mat_gemm_t to keep them resident). */
+int sc_q8_gemm_host(size_t m, size_t k, size_t n, const uint8_t *w,
+                    size_t padded_row, size_t block_bytes, size_t qoff,
+                    const float *x, float *y);
+
+/* The activation quantiser alone (quantize_col, sgemm_kernel.rs:57-90), for
+ * bit-exact checks: xq is [m][32*ceil(k/32)] int8, dx is [ceil(k/32)][m]. */
+int sc_q8_quantize(const float *x, int64_t m, int64_t k, int32_t x_layout,
+                   int64_t ldx, int8_t *xq, float *dx, void *stream);
+
+/* The GEMM's integer path alone: dots[(row*t + frame)*nblocks + b] = the
+ * int32 dot of weight row `row` and quantised frame `frame` over block b --
+ * the exact integer the reference accumulates (sgemm_kernel.rs:171-174). */
+int sc_q8_block_dots(const sc_q8w *w, const float *x, int64_t t,
+                     int32_t x_layout, int64_t ldx, int32_t *dots,
+                     void *stream);
+
+/* ---- streaming attention --------------------------------------------- */
+
+/* AttnStreamKernel::forward (gpu/kernels.rs:1137-1156) on device pointers:
+ * q [c, d], kv/vv the band frames [k_lo, k_hi) as [band, d], pos_p [n_pos, d],
+ * q_bias/v_bias = pos_bias_u/pos_bias_v [d]; out [c, d].  Semantics of the CPU
+ * path: block_new's score/softmax loops (streaming.rs:492-589) with score_dot
+ * and softmax_v (simd_kernel.rs:919-1152).  band must equal k_hi - k_lo (1 ..
+ * 256), c is 1..16, head_dim = d / n_heads is 64 or 128.  n_pos is new (the
+ * reference passes pos_p as a slice) and is used to reject out-of-range pos
+ * rows. */
+int sc_attn_stream(const float *q, const float *kv, const float *vv,
+                   const float *pos_p, int64_t n_pos, const float *q_bias,
+                   const float *v_bias, int64_t c, int64_t d, int64_t n_heads,
+                   float scale, int64_t s, int64_t k_lo, int64_t band,
+                   int64_t chunk, int64_t left_chunks, int64_t k_hi,
+                   int64_t pos_off, float *out, void *stream);
+
+/* Host-buffer twin of AttnStreamKernel::forward (returns out in a host
+ * buffer, as forward returns Vec<f32>); synchronous. */
+int sc_attn_stream_host(const float *q, const float *kv, const float *vv,
+                        const float *pos_p, int64_t n_pos,
+                        const float *q_bias, const float *v_bias, int64_t c,
+                        int64_t d, int64_t n_heads, float scale, int64_t s,
+                        int64_t k_lo, int64_t band, int64_t chunk,
+                        int64_t left_chunks, int64_t k_hi, int64_t pos_off,
+                        float *out);
+
+/* Batched streaming attention over per-stream HBM ring caches: the
+ * device-resident replacement for block_new's band caches k_v/v_v and their
+ * drain/extend slide (streaming.rs:263-277, 307-312), over n_streams streams in
+ * lockstep.  Stream z's queries are rows z*c .. z*c+c-1 of q (row stride
+ * ldq), its new frames' K/V rows z*c.. of k_new/v_new (stride ld_new); frame
+ * fr of stream z lives in ring row z*cap + fr % cap (row stride d).  The
+ * call appends the new frames [s, s+c) to the rings and attends over
+ * [k_lo, k_hi = s + c); cap must be >= k_hi - k_lo.  out rows z*c + j (stride
+ * ldo).  Leading dimensions <= 0 mean d. */
+int sc_attn_stream_ring(const float *q, int64_t ldq, const float *k_new,
+                        const float *v_new, int64_t ld_new, float *k_ring,
+                        float *v_ring, int64_t cap, int64_t n_streams,
+                        const float *pos_p, int64_t n_pos,
+                        const float *q_bias, const float *v_bias, int64_t c,
+                        int64_t d, int64_t n_heads, float scale, int64_t s,
+                        int64_t k_lo, int64_t chunk, int64_t left_chunks,
+                        int64_t k_hi, int64_t pos_off, float *out,
+                        int64_t ldo, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

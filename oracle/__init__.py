@@ -1,0 +1,150 @@
+"""CPU oracle for the stealcode_b200 hot path -- TEST INFRASTRUCTURE ONLY.
+
+A ctypes binding of ``oracle/liboracle.so``, a plain-C restatement of the
+reference's CPU operators (see ``oracle/sc_oracle.h`` for the file:line each
+function restates).  Only the tests, ``__graft_entry__.smoke()`` and
+``bench.py``'s CPU-baseline leg use it, as the checker and the timed CPU
+baseline; the product never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import c_float, c_int, c_size_t, c_uint16, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+
+def build() -> None:
+    """Compile liboracle.so with gcc (make -C oracle)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+if not os.path.exists(LIB_PATH):
+    build()
+
+lib = ctypes.CDLL(LIB_PATH)
+_P = c_void_p
+_S = c_size_t
+for _name, _res, _args in [
+    ("orc_f16_to_f32", c_float, [c_uint16]),
+    ("orc_half_from_f32_trunc", c_uint16, [c_float]),
+    ("orc_quantize_col", None, [_P, _S, _S, _S, _S, _P, _P]),
+    ("orc_q8_gemm_scalar", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P]),
+    ("orc_q8_gemm_simd_order", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P]),
+    ("orc_q8_gemm", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P, c_int]),
+    ("orc_q8_block_dots", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P]),
+    ("orc_score_dot", c_float, [_P, _P, _P, _P, _P, _P, _S, c_float]),
+    ("orc_softmax_v", None, [_P, _S, _S, _S, _S, _P, _S, _P]),
+    ("orc_attn_stream", None, [_P, _P, _P, _P, _P, _P, _S, _S, _S, c_float, _S, _S, _S, _S, _S, _S,
+                               _S, _P]),
+    ("orc_attn_stream_testloop", None, [_P, _P, _P, _P, _P, _P, _S, _S, _S, c_float, _S, _S, _S, _S,
+                                        _S, _S, _P]),
+    ("orc_num_cpus", c_int, []),
+]:
+    _f = getattr(lib, _name)
+    _f.restype = _res
+    _f.argtypes = _args
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def f16_to_f32(h: int) -> float:
+    return lib.orc_f16_to_f32(h)
+
+
+def half_from_f32_trunc(v: float) -> int:
+    return lib.orc_half_from_f32_trunc(v)
+
+
+def quantize(x_km: np.ndarray):
+    """quantize_col over every column of feature-major x [k, n]:
+    returns (xq [n, k] int8, dx [n, nblocks] f32)."""
+    x = np.ascontiguousarray(x_km, dtype=np.float32)
+    k, n = x.shape
+    nb = (k + 31) // 32
+    xq = np.zeros((n, k), dtype=np.int8)
+    dx = np.zeros((n, nb), dtype=np.float32)
+    for nj in range(n):
+        lib.orc_quantize_col(_p(x), nj, k, n, nb, xq[nj:].ctypes.data, dx[nj:].ctypes.data)
+    return xq, dx
+
+
+def q8_gemm_scalar(m, k, n, w, padded_row, block_bytes, qoff, x_km):
+    """q8_gemm_scalar: y [m, n] from weight bytes and feature-major x [k, n]."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x_km, dtype=np.float32)
+    y = np.zeros((m, n), dtype=np.float32)
+    lib.orc_q8_gemm_scalar(m, k, n, _p(w), padded_row, block_bytes, qoff, _p(x), _p(y))
+    return y
+
+
+def q8_gemm_simd_order(m, k, n, w, padded_row, block_bytes, qoff, x_km):
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x_km, dtype=np.float32)
+    y = np.zeros((m, n), dtype=np.float32)
+    lib.orc_q8_gemm_simd_order(m, k, n, _p(w), padded_row, block_bytes, qoff, _p(x), _p(y))
+    return y
+
+
+def q8_gemm(m, k, n, w, padded_row, block_bytes, qoff, x_km, nthreads: int = 0, y=None):
+    """The threaded AVX2 dispatcher (timed CPU baseline); same bits as above."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x_km, dtype=np.float32)
+    if y is None:
+        y = np.zeros((m, n), dtype=np.float32)
+    lib.orc_q8_gemm(m, k, n, _p(w), padded_row, block_bytes, qoff, _p(x), _p(y), nthreads)
+    return y
+
+
+def q8_block_dots(m, k, n, w, padded_row, block_bytes, qoff, x_km):
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x_km, dtype=np.float32)
+    nb = (k + 31) // 32
+    dots = np.zeros((m, n, nb), dtype=np.int32)
+    lib.orc_q8_block_dots(m, k, n, _p(w), padded_row, block_bytes, qoff, _p(x), _p(dots))
+    return dots
+
+
+def score_dot(qu, uh, qv, vh, kk, p, scale):
+    arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (qu, uh, qv, vh, kk, p)]
+    return lib.orc_score_dot(*[_p(a) for a in arrs], arrs[0].size, scale)
+
+
+def softmax_v(srow, k0, k1, n_heads, h, v_rows, head_dim):
+    """v_rows: array [k1, head_dim] (row kk = v_at(kk))."""
+    srow = np.ascontiguousarray(srow, dtype=np.float32)
+    v = np.ascontiguousarray(v_rows, dtype=np.float32)
+    ptrs = (c_void_p * max(k1, 1))(*[v.ctypes.data + kk * head_dim * 4 for kk in range(k1)])
+    out = np.zeros(head_dim, dtype=np.float32)
+    lib.orc_softmax_v(_p(srow), k0, k1, n_heads, h, ctypes.cast(ptrs, c_void_p), head_dim, _p(out))
+    return out
+
+
+def attn_stream(q, kv, vv, pos_p, q_bias, v_bias, c, d, n_heads, scale, s, k_lo, band, chunk,
+                left_chunks, k_hi, pos_off):
+    arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, kv, vv, pos_p, q_bias, v_bias)]
+    out = np.zeros((c, d), dtype=np.float32)
+    lib.orc_attn_stream(*[_p(a) for a in arrs], c, d, n_heads, scale, s, k_lo, band, chunk,
+                        left_chunks, k_hi, pos_off, _p(out))
+    return out
+
+
+def attn_stream_testloop(q, kv, vv, pos_p, q_bias, v_bias, c, d, n_heads, scale, s, k_lo, chunk,
+                         left_chunks, k_hi, pos_off):
+    arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, kv, vv, pos_p, q_bias, v_bias)]
+    out = np.zeros((c, d), dtype=np.float32)
+    lib.orc_attn_stream_testloop(*[_p(a) for a in arrs], c, d, n_heads, scale, s, k_lo, chunk,
+                                 left_chunks, k_hi, pos_off, _p(out))
+    return out
+
+
+def num_cpus() -> int:
+    return lib.orc_num_cpus()

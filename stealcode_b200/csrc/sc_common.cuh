@@ -1,0 +1,59 @@
+// sc_common.cuh -- shared definitions for the stealcode_b200 CUDA library.
+//
+// Repacked Q8_0 weight layout ("row-group tiles"), used by every GEMM kernel:
+//   * rows are padded to a multiple of SC_GROUP_ROWS (128), K to a multiple of
+//     32 (one Q8_0 block);
+//   * quants: int8 tiles of [128 rows x 32 k] (4 KiB), tile (g, b) at byte
+//     (g * nb + b) * 4096; inside a tile, byte i of row r sits at
+//     (i / 16) * 2048 + r * 16 + (i % 16).  A warp that maps lanes to rows
+//     reads 512 contiguous bytes per 16-byte load, and the tile is the
+//     no-swizzle K-major canonical layout of a tcgen05 shared-memory operand
+//     (core matrix = 8 rows x 16 bytes; 128 bytes between row octets, 2048
+//     bytes between the two 16-byte K halves);
+//   * scales: f16 [G][nb][128]: the scale of row g*128 + r, block b at
+//     (g * nb + b) * 128 + r (256 contiguous bytes per tile).
+// Padding rows and padding K positions hold zero quants and zero scales.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define SC_GROUP_ROWS 128
+#define SC_TILE_BYTES (SC_GROUP_ROWS * 32)
+
+namespace sc {
+
+struct Q8Weights {
+  int64_t rows;       // N (output features)
+  int64_t k;          // K (input features)
+  int64_t rows_pad;   // N rounded up to 128
+  int64_t nb;         // K blocks of 32
+  int8_t *qs;         // device, rows_pad * nb * 32 bytes
+  __half *sc;         // device, rows_pad * nb halves
+  int device;
+};
+
+// Error codes shared with include/stealcode_b200.h.
+enum : int {
+  kOk = 0,
+  kErrInvalid = -1,
+  kErrAlloc = -2,
+  kErrCuda = -3,
+  kErrTimeout = -4,
+  kErrUnsupported = -5,
+  kErrState = -6,
+};
+
+void set_error(const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what);
+
+#define SC_CUDA(call)                                       \
+  do {                                                      \
+    cudaError_t _e = (call);                                \
+    if (_e != cudaSuccess) return sc::cuda_fail(_e, #call); \
+  } while (0)
+
+static inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace sc

@@ -1,0 +1,53 @@
+// sc_kernels.cuh -- argument structs and launchers shared between the kernel
+// translation units and the C ABI (sc_api.cu).
+#pragma once
+
+#include "sc_common.cuh"
+
+namespace sc {
+
+// q8_pack.cu
+int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k, int64_t block_bytes,
+                     int64_t qoff, Q8Weights *w, cudaStream_t st);
+int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx, bool feature_major,
+                 int64_t m_pad, int8_t *xq, float *dx, cudaStream_t st);
+
+// q8_gemm_small.cu
+struct SmallGemmArgs {
+  const Q8Weights *w;
+  const int8_t *xq;   // [m_pad][k_pad] quantised activations
+  const float *dx;    // [nb][m_pad] activation block scales
+  int64_t k_pad, m_pad, m;
+  const float *bias;  // [rows] or nullptr
+  float *y;
+  int y_time_major;   // 1: y[col*ldy + n]; 0: y[n*ldy + col]
+  int64_t ldy;
+  int32_t *dots;      // non-null: write raw int32 block dots instead of y
+};
+int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st);
+
+// attn_stream.cu
+struct AttnParams {
+  const float *q;       // query rows; stream z, query j at (z*c + j)*ldq
+  int64_t ldq;
+  const float *k_new;   // frames >= new_lo of stream z at (z*rows_new + fr - new_lo)*ld_new
+  const float *v_new;
+  int64_t ld_new, rows_new, new_lo;
+  float *k_ring;        // nullptr in band mode; stream z, frame fr at (z*cap + fr % cap)*d
+  float *v_ring;
+  int64_t cap;
+  const float *pos_p;   // [n_pos, d]
+  const float *u;       // pos_bias_u [d]
+  const float *v;       // pos_bias_v [d]
+  float *out;           // (z*c + j)*ldo
+  int64_t ldo;
+  int c, d, n_heads;
+  float scale;
+  int64_t s, k_lo, k_hi, chunk, left_chunks, pos_off;
+  int64_t pr_lo;        // first pos row the chunk touches (attn_prepare)
+  int np;               // number of pos rows touched (attn_prepare)
+};
+int attn_prepare(AttnParams &p, int64_t n_pos);
+int launch_attn(const AttnParams &p, int64_t n_streams, cudaStream_t st);
+
+}  // namespace sc
