@@ -99,9 +99,19 @@ int sc_q8_gemm(const sc_q8w *w, const float *x, int64_t t, int32_t x_layout,
                int64_t ldy, void *workspace, int64_t workspace_bytes,
                void *stream);
 
+/* Kernel half over pre-quantised activations -- q8_gemm_simd_q
+ * (simd_kernel.rs:160-234), which lets callers that feed one input to several
+ * matrices (the attention's Q/K/V) quantise once.  xq [t_pad][32*nblocks] and
+ * dx [nblocks][t_pad] are what sc_q8_quantize writes with m = t_pad; frames
+ * t .. t_pad-1 are ignored.  xq must be 16-byte aligned. */
+int sc_q8_gemm_q(const sc_q8w *w, const int8_t *xq, const float *dx,
+                 int64_t t, int64_t t_pad, const float *bias, float *y,
+                 int32_t y_layout, int64_t ldy, void *stream);
+
 /* Q8Mat::gemm_t (nemotron/weights.rs:186-202) with host activations and
- * outputs: x_host is [k, t], y_host is [rows, t] (feature-major);
- * synchronous. */
+ * outputs: x_host is [k, t], y_host is [rows, t] (feature-major).  Copies
+ * through a per-device staging buffer on the legacy default stream and
+ * returns when y_host is written (pinned host buffers copy fastest). */
 int sc_q8mat_gemm_t(const sc_q8w *w, const float *x_host, int64_t t,
                     float *y_host);
 

@@ -259,8 +259,13 @@ static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st
   int band = (int)(p.k_hi - p.k_lo);
   size_t smem = (size_t)CQ * (band + p.np) * sizeof(float);
   auto kern = attn_stream_kernel<HD, CQ>;
-  if (smem > 48 * 1024)
+  static size_t smem_set[64] = {};
+  int dev = 0;
+  SC_CUDA(cudaGetDevice(&dev));
+  if (smem > 48 * 1024 && dev < 64 && smem_set[dev] < smem) {
     SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    smem_set[dev] = smem;
+  }
   kern<<<dim3((unsigned)p.n_heads, (unsigned)n_streams), HD, smem, st>>>(p);
   SC_CUDA(cudaGetLastError());
   return kOk;

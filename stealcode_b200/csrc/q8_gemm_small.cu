@@ -196,8 +196,14 @@ static int launch_small(const SmallGemmArgs &a, int ks, cudaStream_t st) {
   size_t smem = (size_t)MT * nbl_max * 32 + (size_t)nbl_max * MT * 4 +
                 (size_t)kSmallWarps * MT * 32 * 4;
   auto kern = q8_gemm_small_kernel<MT, kDump>;
-  if (smem > 48 * 1024) {
+  // Raise the dynamic shared-memory limit once per device (not inside every
+  // launch, so graph capture sees only the launch itself).
+  static size_t smem_set[64] = {};
+  int dev = 0;
+  SC_CUDA(cudaGetDevice(&dev));
+  if (smem > 48 * 1024 && dev < 64 && smem_set[dev] < smem) {
     SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    smem_set[dev] = smem;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)row_groups, (unsigned)ks, (unsigned)mtiles);

@@ -32,7 +32,10 @@ struct DeviceState {
   int sm_count = 0;
   void *ws = nullptr;
   size_t ws_bytes = 0;
+  void *stage = nullptr;  // host-twin staging for x and y (grow-only)
+  size_t stage_bytes = 0;
   std::mutex mu;
+  std::mutex stage_mu;
 };
 static DeviceState g_dev[64];
 
@@ -283,26 +286,59 @@ int sc_q8mat_gemm_t(const sc_q8w *w, const float *x_host, int64_t t, float *y_ho
   if (!w || !x_host || !y_host || t < 0) { set_error("q8mat_gemm_t: invalid argument"); return kErrInvalid; }
   if (t == 0) return kOk;
   const Q8Weights &W = w->w;
-  size_t xb = (size_t)W.k * t * 4, yb = (size_t)W.rows * t * 4;
-  float *xd = nullptr, *yd = nullptr;
-  if (cudaMalloc(&xd, xb) != cudaSuccess || cudaMalloc(&yd, yb) != cudaSuccess) {
-    cudaGetLastError();
-    if (xd) cudaFree(xd);
-    set_error("q8mat_gemm_t: cudaMalloc failed");
-    return kErrAlloc;
+  int dev;
+  int rc = current_device(&dev, nullptr);
+  if (rc) return rc;
+  DeviceState &ds = g_dev[dev];
+  std::lock_guard<std::mutex> lk(ds.stage_mu);
+  size_t xb = ((size_t)W.k * t * 4 + 255) / 256 * 256, yb = (size_t)W.rows * t * 4;
+  if (ds.stage_bytes < xb + yb) {
+    if (ds.stage) {
+      cudaError_t e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+      cudaFree(ds.stage);
+      ds.stage = nullptr;
+      ds.stage_bytes = 0;
+    }
+    if (cudaMalloc(&ds.stage, xb + yb) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("q8mat_gemm_t: staging cudaMalloc(%zu) failed", xb + yb);
+      return kErrAlloc;
+    }
+    ds.stage_bytes = xb + yb;
   }
-  int rc = kOk;
-  cudaError_t e = cudaMemcpy(xd, x_host, xb, cudaMemcpyHostToDevice);
-  if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpy(x)");
-  if (!rc) rc = gemm_impl(&W, xd, t, SC_LAYOUT_FEATURE_MAJOR, t, nullptr, yd, SC_LAYOUT_FEATURE_MAJOR, t,
-                          nullptr, 0, nullptr, 0);
-  if (!rc) {
-    e = cudaMemcpy(y_host, yd, yb, cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpy(y)");
+  float *xd = (float *)ds.stage, *yd = (float *)((char *)ds.stage + xb);
+  cudaError_t e = cudaMemcpyAsync(xd, x_host, (size_t)W.k * t * 4, cudaMemcpyHostToDevice, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(x)");
+  rc = gemm_impl(&W, xd, t, SC_LAYOUT_FEATURE_MAJOR, t, nullptr, yd, SC_LAYOUT_FEATURE_MAJOR, t, nullptr, 0,
+                 nullptr, 0);
+  if (rc) return rc;
+  e = cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(y)");
+  e = cudaStreamSynchronize(0);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  return kOk;
+}
+
+int sc_q8_gemm_q(const sc_q8w *w, const int8_t *xq, const float *dx, int64_t t, int64_t t_pad,
+                 const float *bias, float *y, int32_t y_layout, int64_t ldy, void *stream) {
+  if (!w || !xq || !dx || !y || t < 0 || t_pad < t || !layout_ok(y_layout) ||
+      ((uintptr_t)xq & 15)) {
+    set_error("q8_gemm_q: invalid argument (xq must be 16-byte aligned, t_pad >= t)");
+    return kErrInvalid;
   }
-  cudaFree(xd);
-  cudaFree(yd);
-  return rc;
+  if (t == 0) return kOk;
+  const Q8Weights &W = w->w;
+  if (ldy <= 0) ldy = y_layout == SC_LAYOUT_TIME_MAJOR ? W.rows : t;
+  if ((y_layout == SC_LAYOUT_TIME_MAJOR && ldy < W.rows) || (y_layout == SC_LAYOUT_FEATURE_MAJOR && ldy < t)) {
+    set_error("q8_gemm_q: leading dimension too small");
+    return kErrInvalid;
+  }
+  int dev, sms;
+  int rc = current_device(&dev, &sms);
+  if (rc) return rc;
+  SmallGemmArgs a{&W, xq, dx, W.nb * 32, t_pad, t, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy, nullptr};
+  return gemm_small(a, sms, (cudaStream_t)stream);
 }
 
 int sc_q8_gemm_host(size_t m, size_t k, size_t n, const uint8_t *w, size_t padded_row, size_t block_bytes,

@@ -1,0 +1,225 @@
+"""Host-side mirror of the reference's operator interface over the C ABI.
+
+Names, argument order and meaning follow the reference's Rust operators so
+that code written against them reads the same:
+
+* ``q8_gemm(m, k, n, w, padded_row, block_bytes, qoff, x, y)`` --
+  sgemm_kernel.rs:99-127 (host buffers, weights repacked per call);
+* ``Q8Mat`` -- nemotron/weights.rs:69-232 (``gemm_t`` keeps the repacked
+  weights resident on the device);
+* ``Lin.forward_t`` -- nemotron/weights.rs:305-337 (GEMM + bias);
+* ``AttnStreamKernel.forward`` -- gpu/kernels.rs:1137-1156.
+
+Device-side entry points take ``torch`` CUDA tensors (PyTorch is used only
+for device memory and streams) and launch the library's kernels on the
+current torch stream.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+from ._lib import SC_LAYOUT_FEATURE_MAJOR, SC_LAYOUT_TIME_MAJOR, check, lib
+
+
+def _hp(a: np.ndarray) -> int:
+    if not a.flags["C_CONTIGUOUS"]:
+        raise ValueError("host buffers must be C-contiguous")
+    return a.ctypes.data
+
+
+def _stream_ptr(stream=None) -> int:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _dp(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def q8_gemm(m: int, k: int, n: int, w: np.ndarray, padded_row: int, block_bytes: int, qoff: int,
+            x: np.ndarray, y: np.ndarray) -> None:
+    """Twin of the reference ``q8_gemm``: y [m, n] = W [m, k] @ x [k, n] (host)."""
+    if m == 0 or k == 0 or n == 0:
+        return
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    if x.dtype != np.float32 or y.dtype != np.float32 or x.size != k * n or y.size != m * n:
+        raise ValueError("x must be f32 [k, n] and y f32 [m, n]")
+    check(lib.sc_q8_gemm_host(m, k, n, _hp(w), padded_row, block_bytes, qoff, _hp(x), _hp(y)))
+
+
+class Q8Mat:
+    """A Q8_0 matrix repacked once into device memory (``Q8Mat``, weights.rs:69-232)."""
+
+    def __init__(self, blocks: np.ndarray, rows: int, row_len: int, block_bytes: int = 34,
+                 qoff: int = 2):
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        padded_row = (row_len + 31) // 32 * block_bytes
+        if blocks.size != rows * padded_row:
+            raise ValueError(f"Q8Mat: {blocks.size} bytes != {rows} rows x {padded_row}")
+        h = ctypes.c_void_p()
+        check(lib.sc_q8_repack(_hp(blocks), rows, row_len, block_bytes, qoff, ctypes.byref(h)))
+        self._h = h
+        self.rows = rows
+        self.row_len = row_len
+        self.padded_row = padded_row
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._h
+
+    def free(self) -> None:
+        if self._h:
+            lib.sc_q8w_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def gemm_t(self, x: np.ndarray, t: int) -> np.ndarray:
+        """y [rows, t] = W @ x [row_len, t] with host arrays (``Q8Mat::gemm_t``)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty((self.rows, t), dtype=np.float32)
+        check(lib.sc_q8mat_gemm_t(self._h, _hp(x), t, _hp(y)))
+        return y
+
+    def gemm(self, x, *, x_layout: int = SC_LAYOUT_TIME_MAJOR, bias=None, out=None,
+             y_layout: int = SC_LAYOUT_TIME_MAJOR, ldx: int = 0, ldy: int = 0, workspace=None,
+             stream=None):
+        """Device GEMM on torch CUDA tensors; returns ``out``.
+
+        TIME_MAJOR: x [t, row_len] -> y [t, rows]; FEATURE_MAJOR: x [row_len, t] ->
+        y [rows, t].  ``workspace`` is an optional uint8 CUDA tensor of at least
+        ``workspace_bytes(t)`` bytes."""
+        import torch
+
+        if x_layout == SC_LAYOUT_TIME_MAJOR:
+            t = x.shape[0]
+        else:
+            t = x.shape[1]
+        if out is None:
+            shape = (t, self.rows) if y_layout == SC_LAYOUT_TIME_MAJOR else (self.rows, t)
+            out = torch.empty(shape, dtype=torch.float32, device=x.device)
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        check(lib.sc_q8_gemm(self._h, x.data_ptr(), t, x_layout, ldx, _dp(bias), out.data_ptr(), y_layout,
+                             ldy, _dp(workspace), ws_bytes, _stream_ptr(stream)))
+        return out
+
+    def workspace_bytes(self, t: int) -> int:
+        return int(lib.sc_q8_gemm_workspace_bytes(t, self.row_len))
+
+    def block_dots(self, x, *, x_layout: int = SC_LAYOUT_TIME_MAJOR, stream=None):
+        """int32 per-block dots [rows, t, nblocks] of the quantised frames."""
+        import torch
+
+        t = x.shape[0] if x_layout == SC_LAYOUT_TIME_MAJOR else x.shape[1]
+        nb = (self.row_len + 31) // 32
+        dots = torch.zeros((self.rows, t, nb), dtype=torch.int32, device=x.device)
+        check(lib.sc_q8_block_dots(self._h, x.data_ptr(), t, x_layout, 0, dots.data_ptr(),
+                                   _stream_ptr(stream)))
+        return dots
+
+
+class Lin:
+    """A Q8_0 linear layer with optional bias (``Lin``, weights.rs:241-337)."""
+
+    def __init__(self, q: Q8Mat, bias: Optional[np.ndarray] = None):
+        self.q = q
+        self.out = q.rows
+        self.inp = q.row_len
+        self.bias_host = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self._bias_dev = {}
+
+    def forward_t(self, x_t: np.ndarray, t: int) -> np.ndarray:
+        """y_t [out, t] = W @ x_t [inp, t] + bias (host arrays)."""
+        y = self.q.gemm_t(x_t, t)
+        if self.bias_host is not None:
+            y += self.bias_host[:, None]
+        return y
+
+    def forward(self, x, **kw):
+        """Device forward (bias fused into the GEMM epilogue)."""
+        import torch
+
+        bias = None
+        if self.bias_host is not None:
+            dev = x.device
+            if dev not in self._bias_dev:
+                self._bias_dev[dev] = torch.from_numpy(self.bias_host).to(dev)
+            bias = self._bias_dev[dev]
+        return self.q.gemm(x, bias=bias, **kw)
+
+
+def quantize(x, *, x_layout: int = SC_LAYOUT_TIME_MAJOR, stream=None):
+    """Device activation quantiser: returns (xq [t, k_pad] int8, dx [nb, t] f32)."""
+    import torch
+
+    if x_layout == SC_LAYOUT_TIME_MAJOR:
+        t, k = x.shape
+    else:
+        k, t = x.shape
+    nb = (k + 31) // 32
+    xq = torch.zeros((t, nb * 32), dtype=torch.int8, device=x.device)
+    dx = torch.zeros((nb, t), dtype=torch.float32, device=x.device)
+    check(lib.sc_q8_quantize(x.data_ptr(), t, k, x_layout, 0, xq.data_ptr(), dx.data_ptr(),
+                             _stream_ptr(stream)))
+    return xq, dx
+
+
+class AttnStreamKernel:
+    """Streaming rel-pos attention operator (``AttnStreamKernel``, gpu/kernels.rs:1057-1326)."""
+
+    @staticmethod
+    def forward(q, kv, vv, pos_p, q_bias, v_bias, c, d, n_heads, scale, s, k_lo, band, chunk,
+                left_chunks, k_hi, pos_off) -> np.ndarray:
+        """Host-buffer twin of ``forward``: returns out [c, d]."""
+        arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, kv, vv, pos_p, q_bias, v_bias)]
+        n_pos = arrs[3].size // d
+        out = np.zeros((c, d), dtype=np.float32)
+        check(lib.sc_attn_stream_host(*[_hp(a) for a in arrs[:4]], n_pos, _hp(arrs[4]), _hp(arrs[5]), c, d,
+                                      n_heads, scale, s, k_lo, band, chunk, left_chunks, k_hi, pos_off,
+                                      _hp(out)))
+        return out
+
+    @staticmethod
+    def forward_device(q, kv, vv, pos_p, q_bias, v_bias, c, d, n_heads, scale, s, k_lo, band, chunk,
+                       left_chunks, k_hi, pos_off, out=None, stream=None):
+        import torch
+
+        if out is None:
+            out = torch.empty((c, d), dtype=torch.float32, device=q.device)
+        n_pos = pos_p.numel() // d
+        check(lib.sc_attn_stream(q.data_ptr(), kv.data_ptr(), vv.data_ptr(), pos_p.data_ptr(), n_pos,
+                                 q_bias.data_ptr(), v_bias.data_ptr(), c, d, n_heads, scale, s, k_lo, band,
+                                 chunk, left_chunks, k_hi, pos_off, out.data_ptr(), _stream_ptr(stream)))
+        return out
+
+
+def attn_stream_ring(q, k_new, v_new, k_ring, v_ring, pos_p, q_bias, v_bias, *, c, d, n_heads, scale, s,
+                     k_lo, chunk, left_chunks, pos_off, out=None, ldq=0, ld_new=0, ldo=0, stream=None):
+    """Batched ring-cache attention over ``k_ring.shape[0]`` streams (torch CUDA tensors).
+
+    k_ring/v_ring: [n_streams, cap, d]; q/k_new/v_new: [n_streams * c, ld] rows."""
+    import torch
+
+    n_streams, cap = k_ring.shape[0], k_ring.shape[1]
+    if out is None:
+        out = torch.empty((n_streams * c, d), dtype=torch.float32, device=q.device)
+    n_pos = pos_p.numel() // d
+    check(lib.sc_attn_stream_ring(q.data_ptr(), ldq, k_new.data_ptr(), v_new.data_ptr(), ld_new,
+                                  k_ring.data_ptr(), v_ring.data_ptr(), cap, n_streams, pos_p.data_ptr(), n_pos,
+                                  q_bias.data_ptr(), v_bias.data_ptr(), c, d, n_heads, scale, s, k_lo, chunk,
+                                  left_chunks, s + c, pos_off, out.data_ptr(), ldo, _stream_ptr(stream)))
+    return out
+
+
+__all__ = ["q8_gemm", "Q8Mat", "Lin", "quantize", "AttnStreamKernel", "attn_stream_ring",
+           "SC_LAYOUT_FEATURE_MAJOR", "SC_LAYOUT_TIME_MAJOR", "_lib"]
