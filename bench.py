@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--profile", default=None, choices=["gemm", "attn"],
+                    help="small eager case for ncu captures (no timing, no JSON line)")
     return ap.parse_args()
 
 
@@ -319,8 +321,44 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+def run_profile(args):
+    """A few eager launches of one kernel family on a small case, for ncu."""
+    import math
+
+    import torch
+
+    from stealcode_b200 import synth
+    from stealcode_b200.ops import SC_LAYOUT_TIME_MAJOR, Q8Mat, attn_stream_ring
+
+    dev = torch.device("cuda", 0)
+    if args.profile == "gemm":
+        wh = host_weights()
+        for name, k, n in SHAPES:
+            mat = Q8Mat(wh[name], n, k)
+            for m in (8, 128):
+                x = torch.from_numpy(synth.normal(synth.SEED_BASE + 100 + m + k, (m, k))).to(dev)
+                for _ in range(3):
+                    mat.gemm(x, x_layout=SC_LAYOUT_TIME_MAJOR, y_layout=SC_LAYOUT_TIME_MAJOR)
+    else:
+        ns, c, d, nh, chunk, lc, cap, s = 64, 8, 1024, 8, 7, 10, 84, 140
+        k_lo = (s // chunk - lc) * chunk
+        z = lambda *shape: torch.from_numpy(synth.normal(7 + len(shape), shape)).to(dev)
+        q, kn, vn = z(ns * c, d), z(ns * c, d), z(ns * c, d)
+        rk, rv = z(ns, cap, d), z(ns, cap, d)
+        pos = z((lc + 2) * chunk - 1, d)
+        u, v = z(d) * 0.02, z(d) * 0.02
+        for _ in range(3):
+            attn_stream_ring(q, kn, vn, rk, rv, pos, u, v, c=c, d=d, n_heads=nh, scale=1 / math.sqrt(128), s=s,
+                             k_lo=k_lo, chunk=chunk, left_chunks=lc, pos_off=chunk - 1)
+    torch.cuda.synchronize()
+    print("profile case done")
+
+
 def main():
     args = parse()
+    if args.profile:
+        run_profile(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
