@@ -108,6 +108,29 @@ int sc_q8_gemm_q(const sc_q8w *w, const int8_t *xq, const float *dx,
                  int64_t t, int64_t t_pad, const float *bias, float *y,
                  int32_t y_layout, int64_t ldy, void *stream);
 
+/* Size of the fixed device array behind sc_q8_gemm_noalloc (4 MiB). */
+#define SC_Q8_GEMM_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* sc_q8_gemm for callers that must not allocate device memory; this entry
+ * point has no counterpart in the reference.  Such callers are plugins that
+ * run inside another framework's CUDA-graph capture (a cudaMalloc there
+ * breaks the capture), real-time audio callbacks (cudaMalloc and cudaFree can
+ * synchronise the device and stall the callback), and hosts that own all
+ * device memory.  The quantised-activation scratch lives in a file-scope
+ * device array of SC_Q8_GEMM_NOALLOC_SCRATCH_BYTES, which every GPU that
+ * loads the library holds until the process exits.  Calls whose scratch need
+ * (sc_q8_gemm_workspace_bytes(t, k)) exceeds it return SC_ERR_INVALID; split
+ * the frames over several calls.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  All calls share the one
+ * array, so calls that overlap on the GPU (different streams, or different
+ * host threads) race and corrupt each other's results; serialise them.  The
+ * array keeps the previous call's contents, but every byte a call reads is
+ * written earlier in that same call.  Arguments as sc_q8_gemm. */
+int sc_q8_gemm_noalloc(const sc_q8w *w, const float *x, int64_t t,
+                       int32_t x_layout, int64_t ldx, const float *bias,
+                       float *y, int32_t y_layout, int64_t ldy, void *stream);
+
 /* Q8Mat::gemm_t (nemotron/weights.rs:186-202) with host activations and
  * outputs: x_host is [k, t], y_host is [rows, t] (feature-major).  Copies
  * through a per-device staging buffer on the legacy default stream and

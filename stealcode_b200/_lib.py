@@ -62,6 +62,7 @@ SIGNATURES = {
                                      POINTER(c_int64)]),
     "sc_q8_gemm_workspace_bytes": (c_int64, [_I, _I]),
     "sc_q8_gemm": (c_int, [_P, _P, _I, c_int32, _I, _P, _P, c_int32, _I, _P, _I, _P]),
+    "sc_q8_gemm_noalloc": (c_int, [_P, _P, _I, c_int32, _I, _P, _P, c_int32, _I, _P]),
     "sc_q8_gemm_q": (c_int, [_P, _P, _P, _I, _I, _P, _P, c_int32, _I, _P]),
     "sc_q8mat_gemm_t": (c_int, [_P, _P, _I, _P]),
     "sc_q8_gemm_host": (c_int, [c_size_t, c_size_t, c_size_t, _P, c_size_t, c_size_t, c_size_t, _P, _P]),

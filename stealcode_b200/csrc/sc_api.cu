@@ -142,6 +142,10 @@ struct sc_q8w {
   Q8Weights w;
 };
 
+namespace sc {
+const Q8Weights *q8w_weights(const sc_q8w *w) { return &w->w; }
+}  // namespace sc
+
 extern "C" {
 
 const char *sc_last_error(void) { return g_err; }

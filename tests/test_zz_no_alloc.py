@@ -1,0 +1,74 @@
+"""sc_q8_gemm_noalloc, the GEMM entry point for callers that cannot allocate
+device memory (a plugin inside someone else's CUDA-graph capture, a
+real-time audio callback that must not stall in cudaMalloc, a host that owns
+all device memory).  Its scratch is a fixed device array inside the library.
+
+Checked through the C ABI against sc_q8_gemm (the entry point that takes a
+workspace) on two calls in a row, so the second call runs over the first
+call's leftovers in the shared array.  This file is collected last, and it
+passes both on its own in a fresh process and after the other tests.
+"""
+import numpy as np
+import pytest
+
+from stealcode_b200 import _lib, synth
+from stealcode_b200.ops import SC_LAYOUT_FEATURE_MAJOR, SC_LAYOUT_TIME_MAJOR, Q8Mat
+
+pytestmark = pytest.mark.gpu
+TOL_RMS = 1e-4  # the GEMM parity bar used by every GPU test
+SCRATCH = 4 << 20
+
+
+def _rms_err(got, ref):
+    ref = ref.astype(np.float64)
+    return float(np.max(np.abs(got.astype(np.float64) - ref)) / np.sqrt(np.mean(ref ** 2)))
+
+
+def _with_workspace(torch, mat, x, t, layout):
+    y = torch.empty((t, mat.rows), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib.sc_q8_gemm(mat.handle, x.data_ptr(), t, layout, 0, None, y.data_ptr(),
+                                   SC_LAYOUT_TIME_MAJOR, 0, None, 0, None))
+    return y
+
+
+def _no_alloc(torch, mat, x, t, layout):
+    y = torch.full((t, mat.rows), float("nan"), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib.sc_q8_gemm_noalloc(mat.handle, x.data_ptr(), t, layout, 0, None, y.data_ptr(),
+                                           SC_LAYOUT_TIME_MAJOR, 0, None))
+    return y
+
+
+def test_noalloc_matches_workspace_gemm_on_two_calls():
+    import torch
+
+    # first call: a large frame batch that fills much of the scratch
+    mat = Q8Mat(synth.q8_weights(901, 1024, 4096), 1024, 4096)
+    x1 = torch.from_numpy(synth.normal(902, (256, 4096))).cuda()
+    a1 = _no_alloc(torch, mat, x1, 256, SC_LAYOUT_TIME_MAJOR)
+    r1 = _with_workspace(torch, mat, x1, 256, SC_LAYOUT_TIME_MAJOR)
+    # second call, right after: fewer frames, another matrix and layout, so
+    # the array still holds the first call's codes beyond this call's range
+    mat2 = Q8Mat(synth.q8_weights(903, 3072, 1024), 3072, 1024)
+    x2 = torch.from_numpy(synth.normal(904, (1024, 8))).cuda()  # feature-major [k, t]
+    a2 = _no_alloc(torch, mat2, x2, 8, SC_LAYOUT_FEATURE_MAJOR)
+    r2 = _with_workspace(torch, mat2, x2, 8, SC_LAYOUT_FEATURE_MAJOR)
+    torch.cuda.synchronize()
+    for got, ref in ((a1, r1), (a2, r2)):
+        got, ref = got.cpu().numpy(), ref.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert _rms_err(got, ref) <= TOL_RMS
+
+
+def test_noalloc_rejects_frames_beyond_the_scratch():
+    import torch
+
+    mat = Q8Mat(synth.q8_weights(905, 128, 4096), 128, 4096)
+    t = 1024  # 1024 x 4096 codes alone are 4 MiB: over the fixed array
+    assert _lib.lib.sc_q8_gemm_workspace_bytes(t, 4096) > SCRATCH
+    x = torch.zeros((t, 4096), device="cuda")
+    y = torch.zeros((t, 128), device="cuda")
+    rc = _lib.lib.sc_q8_gemm_noalloc(mat.handle, x.data_ptr(), t, SC_LAYOUT_TIME_MAJOR, 0, None, y.data_ptr(),
+                                     SC_LAYOUT_TIME_MAJOR, 0, None)
+    assert rc == _lib.SC_ERR_INVALID
+    assert "scratch" in _lib.last_error()
+    assert _lib.lib.sc_q8_gemm_noalloc(None, None, 1, 0, 0, None, None, 0, 0, None) == _lib.SC_ERR_INVALID
