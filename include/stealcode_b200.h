@@ -53,6 +53,12 @@ typedef struct sc_q8w sc_q8w;
 const char *sc_last_error(void);
 int sc_abi_version(void);
 
+/* Status bits that kernels set on the current device when a bounded
+ * device-side wait gave up (SC_STATUS_WAIT_TIMEOUT); reading clears them.
+ * Synchronous.  New in this library (the reference has no device waits). */
+#define SC_STATUS_WAIT_TIMEOUT 1u
+int sc_device_status(uint32_t *flags);
+
 /* ---- weights --------------------------------------------------------- */
 
 /* Repack a GGUF Q8_0 tensor once into the device layout: int8 quants in

@@ -54,6 +54,7 @@ _I = c_int64
 SIGNATURES = {
     "sc_last_error": (c_char_p, []),
     "sc_abi_version": (c_int, []),
+    "sc_device_status": (c_int, [POINTER(ctypes.c_uint32)]),
     "sc_q8_repack": (c_int, [_P, _I, _I, _I, _I, POINTER(c_void_p)]),
     "sc_q8_repack_device": (c_int, [_P, _I, _I, _I, _I, _P, POINTER(c_void_p)]),
     "sc_q8w_free": (c_int, [_P]),
@@ -81,6 +82,13 @@ for _name, (_res, _args) in SIGNATURES.items():
     _fn = getattr(lib, _name)
     _fn.restype = _res
     _fn.argtypes = _args
+
+
+def device_status() -> int:
+    """Read and clear the kernels' status bits on the current device."""
+    v = ctypes.c_uint32(0)
+    check(lib.sc_device_status(ctypes.byref(v)))
+    return v.value
 
 
 def last_error() -> str:

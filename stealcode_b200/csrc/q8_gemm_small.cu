@@ -6,28 +6,56 @@
 // simd_kernel.rs:333-393: exact int8 x int8 block dots (dp4a, int32), one f32
 // scale product per (row, column, block), f32 accumulation.
 //
-// Mapping: a CTA owns 32 weight rows (lane = row) and a slice of the K
-// blocks; its 4 warps take interleaved blocks of that slice and each lane
-// reads its row's 32-byte block as two 16-byte loads that are 512 contiguous
-// bytes per warp (row-group tile layout, sc_common.cuh).  The quantised
-// activations of the CTA's K slice sit in shared memory and every lane reads
-// the same 32 bytes per block (a broadcast).  Partial sums are reduced over
-// the 4 warps through shared memory and over the K-split CTAs of a thread
-// block cluster through distributed shared memory -- no atomics, no global
-// scratch, deterministic.
+// A CTA owns one 128-row tile group and a slice of the K blocks:
+//   1. one thread issues two 1-D bulk copies (TMA engine, no multicast) of the
+//      slice's weight tiles and scales -- contiguous in the row-group tile
+//      layout -- into shared memory, then the CTA lets the next kernel launch
+//      (programmatic dependent launch) and waits for the previous one, so
+//      the weight stream overlaps the previous kernel's tail;
+//   2. the CTA quantises its frames' K slice itself (bit-exact quantize_col,
+//      one warp per 32-block), so no separate quantiser launch or global
+//      scratch is needed;
+//   3. 8 warps (4 row subgroups x 2 block parities) run dp4a block dots from
+//      shared memory -- lane = weight row, 16-byte conflict-free reads, the
+//      activations a broadcast -- with one f32 FMA per (row, frame, block);
+//   4. partial sums are reduced over the warps in shared memory and over the
+//      K-split CTAs of the thread-block cluster through distributed shared
+//      memory: deterministic, no atomics.
 #include <cooperative_groups.h>
 
+#include "sc_device.cuh"
 #include "sc_kernels.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace sc {
 
-constexpr int kSmallWarps = 4;
-constexpr int kUnroll = 4;
+constexpr int kStreamThreads = 256;
+constexpr int kNblCap = 40;  // K blocks per CTA slice (shared-memory bound)
 
-__device__ __forceinline__ int dot32(const int4 w0, const int4 w1, const int4 x0,
-                                     const int4 x1) {
+static __device__ unsigned g_small_status;
+
+struct StreamParams {
+  const int8_t *qs;
+  const __half *sc;
+  int64_t nb, n_rows, k;
+  const float *x;       // f32 activations (quantised in-kernel), or nullptr
+  int64_t ldx;
+  int x_feature_major;
+  const int8_t *xq;     // pre-quantised [m_pad][k_pad] when x == nullptr
+  const float *dx;      // [nb][m_pad]
+  int64_t k_pad, m_pad;
+  int64_t m;
+  const float *bias;
+  float *y;
+  int y_time_major;
+  int64_t ldy;
+  int ks, nbl_max;
+  int32_t *dots;
+  unsigned *status;
+};
+
+__device__ __forceinline__ int dot32(const int4 w0, const int4 w1, const int4 x0, const int4 x1) {
   int d = __dp4a(w0.x, x0.x, 0);
   d = __dp4a(w0.y, x0.y, d);
   d = __dp4a(w0.z, x0.z, d);
@@ -39,215 +67,248 @@ __device__ __forceinline__ int dot32(const int4 w0, const int4 w1, const int4 x0
   return d;
 }
 
-__device__ __forceinline__ int4 ldg_stream(const int8_t *p) {
-  int4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-// kDumpDots: instead of the scaled sum, write the raw int32 block dots
-// (dots[(n * m + col) * nb + b]) -- the same integer path, exposed so tests
-// can check the block dots bit for bit.
-template <int MT, bool kDumpDots>
-__global__ void __launch_bounds__(kSmallWarps * 32)
-    q8_gemm_small_kernel(const int8_t *__restrict__ qs,
-                         const __half *__restrict__ scl, int64_t nb,
-                         const int8_t *__restrict__ xq,
-                         const float *__restrict__ dx, int64_t k_pad,
-                         int64_t m_pad, int64_t m,
-                         const float *__restrict__ bias, float *__restrict__ y,
-                         int64_t n_rows, int y_time_major, int64_t ldy,
-                         int ks, int32_t *__restrict__ dots) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t rg = blockIdx.x;               // 32-row group
-  const int split = blockIdx.y;                // K split = cluster rank
+// kDump: write the raw int32 block dots (dots[(n*m + col)*nb + b]) instead of
+// y -- the same integer path, exposed so tests can check it bit for bit.
+template <int MT, bool kDump>
+__global__ void __launch_bounds__(kStreamThreads)
+    q8_gemm_stream_kernel(const __grid_constant__ StreamParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t g = blockIdx.x;
+  const int split = blockIdx.y;
   const int64_t col0 = (int64_t)blockIdx.z * MT;
-  const int64_t g = rg >> 2;                   // 128-row tile group
-  const int sub = (int)(rg & 3);               // 32-row subgroup in the tile
-  const int r = sub * 32 + lane;               // row inside the tile
-  const int64_t b0 = nb * split / ks, b1 = nb * (split + 1) / ks;
+  const int64_t b0 = p.nb * split / p.ks, b1 = p.nb * (split + 1) / p.ks;
   const int nbl = (int)(b1 - b0);
 
-  // Shared: xq slice [MT][nbl*32] bytes, dx slice [nbl][MT], partials.
-  int8_t *xs = (int8_t *)smem;
-  float *dxs = (float *)(smem + (size_t)MT * nbl * 32);
-  float *part = dxs + (size_t)nbl * MT;        // [kSmallWarps][MT][32]
+  unsigned char *wbuf = smem;                                    // [nbl][4096]
+  __half *sbuf = (__half *)(smem + (size_t)p.nbl_max * SC_TILE_BYTES);  // [nbl][128]
+  int8_t *xs = (int8_t *)(sbuf + (size_t)p.nbl_max * SC_GROUP_ROWS);   // [MT][nbl*32]
+  float *dxs = (float *)(xs + (size_t)MT * p.nbl_max * 32);      // [nbl][MT]
+  float *part = dxs + (size_t)p.nbl_max * MT;                    // [8][MT][32]
+  uint64_t *bar = (uint64_t *)(part + 8 * MT * 32);
 
-  for (int i = threadIdx.x; i < MT * nbl * 2; i += blockDim.x) {
-    int mm = i / (nbl * 2), c16 = i % (nbl * 2);
-    int64_t col = col0 + mm;
-    int4 v = make_int4(0, 0, 0, 0);
-    if (col < m_pad) v = *(const int4 *)(xq + col * k_pad + b0 * 32 + c16 * 16);
-    *(int4 *)(xs + (size_t)mm * nbl * 32 + c16 * 16) = v;
-  }
-  for (int i = threadIdx.x; i < nbl * MT; i += blockDim.x) {
-    int bb = i / MT, mm = i % MT;
-    int64_t col = col0 + mm;
-    dxs[i] = col < m_pad ? dx[(b0 + bb) * m_pad + col] : 0.0f;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
   }
   __syncthreads();
+  if (tid == 0) {
+    const uint32_t wbytes = (uint32_t)nbl * SC_TILE_BYTES, sbytes = (uint32_t)nbl * SC_GROUP_ROWS * 2;
+    mbar_arrive_expect_tx(bar, wbytes + sbytes);
+    bulk_g2s(wbuf, p.qs + (g * p.nb + b0) * SC_TILE_BYTES, wbytes, bar);
+    bulk_g2s(sbuf, p.sc + (g * p.nb + b0) * SC_GROUP_ROWS, sbytes, bar);
+  }
+  // Weights and scales are never written by a kernel, so they may be fetched
+  // before the previous kernel (which may produce x) has finished.
+  pdl_launch_dependents();
+  pdl_wait();
 
+  // ---- activations of this CTA's frames and K slice -> shared memory ----
+  if (p.x) {
+    for (int pair = warp; pair < MT * nbl; pair += kStreamThreads / 32) {
+      const int j = pair / nbl, bb = pair % nbl;
+      const int64_t col = col0 + j, kk = (b0 + bb) * 32 + lane;
+      const bool valid = col < p.m && kk < p.k;
+      float v = 0.0f;
+      if (valid) v = p.x_feature_major ? p.x[kk * p.ldx + col] : p.x[col * p.ldx + kk];
+      float s;
+      const int8_t q = warp_quantize_block(v, valid, s);
+      xs[(size_t)j * nbl * 32 + bb * 32 + lane] = q;
+      if (lane == 0) dxs[bb * MT + j] = col < p.m ? s : 0.0f;
+    }
+  } else {
+    for (int i = tid; i < MT * nbl * 2; i += kStreamThreads) {
+      const int j = i / (nbl * 2), c16 = i % (nbl * 2);
+      const int64_t col = col0 + j;
+      int4 v = make_int4(0, 0, 0, 0);
+      if (col < p.m_pad) v = *(const int4 *)(p.xq + col * p.k_pad + b0 * 32 + c16 * 16);
+      *(int4 *)(xs + (size_t)j * nbl * 32 + c16 * 16) = v;
+    }
+    for (int i = tid; i < nbl * MT; i += kStreamThreads) {
+      const int bb = i / MT, j = i % MT;
+      const int64_t col = col0 + j;
+      dxs[i] = col < p.m_pad ? p.dx[(b0 + bb) * p.m_pad + col] : 0.0f;
+    }
+  }
+  __syncthreads();
+  if (!mbar_wait(bar, 0) && lane == 0) atomicOr(p.status, kStatusWaitTimeout);
+
+  // ---- dp4a block dots ----
+  const int rs = warp & 3, kp = warp >> 2;
+  const int r = rs * 32 + lane;
   float acc[MT];
 #pragma unroll
   for (int j = 0; j < MT; j++) acc[j] = 0.0f;
-
-  const int8_t *tile0 = qs + (g * nb) * SC_TILE_BYTES + r * 16;
-  const __half *sc0 = scl + (g * nb) * SC_GROUP_ROWS + r;
-
-  // Blocks of this warp: b0 + warp, b0 + warp + 4, ...  Loads for kUnroll
-  // blocks are issued before their math so each lane keeps 128 bytes in
-  // flight.
-  for (int bb = warp; bb < nbl; bb += kSmallWarps * kUnroll) {
-    int4 w0[kUnroll], w1[kUnroll];
-    float dw[kUnroll];
+#pragma unroll 2
+  for (int bb = kp; bb < nbl; bb += 2) {
+    const unsigned char *t = wbuf + (size_t)bb * SC_TILE_BYTES + r * 16;
+    const int4 w0 = *(const int4 *)t, w1 = *(const int4 *)(t + 2048);
+    const float dw = __half2float(sbuf[bb * SC_GROUP_ROWS + r]);
 #pragma unroll
-    for (int u = 0; u < kUnroll; u++) {
-      int bu = bb + u * kSmallWarps;
-      if (bu < nbl) {
-        const int8_t *t = tile0 + (b0 + bu) * SC_TILE_BYTES;
-        w0[u] = ldg_stream(t);
-        w1[u] = ldg_stream(t + 2048);
-        dw[u] = __half2float(sc0[(b0 + bu) * SC_GROUP_ROWS]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; u++) {
-      int bu = bb + u * kSmallWarps;
-      if (bu < nbl) {
-#pragma unroll
-        for (int j = 0; j < MT; j++) {
-          const int4 *xp = (const int4 *)(xs + (size_t)j * nbl * 32 + bu * 32);
-          int d = dot32(w0[u], w1[u], xp[0], xp[1]);
-          if constexpr (kDumpDots) {
-            int64_t n = g * SC_GROUP_ROWS + r, col = col0 + j;
-            if (n < n_rows && col < m) dots[(n * m + col) * nb + b0 + bu] = d;
-          } else {
-            float s = dw[u] * dxs[bu * MT + j];
-            acc[j] = fmaf(s, (float)d, acc[j]);
-          }
-        }
+    for (int j = 0; j < MT; j++) {
+      const int4 *xp = (const int4 *)(xs + (size_t)j * nbl * 32 + bb * 32);
+      const int d = dot32(w0, w1, xp[0], xp[1]);
+      if constexpr (kDump) {
+        const int64_t n = g * SC_GROUP_ROWS + r, col = col0 + j;
+        if (n < p.n_rows && col < p.m) p.dots[(n * p.m + col) * p.nb + b0 + bb] = d;
+      } else {
+        acc[j] = fmaf(dw * dxs[bb * MT + j], (float)d, acc[j]);
       }
     }
   }
-  if constexpr (!kDumpDots) {
-    // Reduce the 4 warps' partials.
+  if constexpr (!kDump) {
+  // ---- reductions: block parities, then the cluster's K splits ----
 #pragma unroll
-    for (int j = 0; j < MT; j++) part[(warp * MT + j) * 32 + lane] = acc[j];
+  for (int j = 0; j < MT; j++) part[(warp * MT + j) * 32 + lane] = acc[j];
+  __syncthreads();
+  if (warp < 4) {
+#pragma unroll
+    for (int j = 0; j < MT; j++)
+      part[(warp * MT + j) * 32 + lane] += part[((warp + 4) * MT + j) * 32 + lane];
+  }
+  if (p.ks > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (split == 0 && warp < 4) {
+      for (int q = 1; q < p.ks; q++) {
+        const float *rp = cluster.map_shared_rank(part, q);
+#pragma unroll
+        for (int j = 0; j < MT; j++) part[(warp * MT + j) * 32 + lane] += rp[(warp * MT + j) * 32 + lane];
+      }
+    }
+    cluster.sync();
+  } else {
     __syncthreads();
-    if (warp == 0) {
+  }
+  if (split != 0 || warp >= 4) return;
+  const int64_t n = g * SC_GROUP_ROWS + r;
+  if (n >= p.n_rows) return;
+  const float bn = p.bias ? p.bias[n] : 0.0f;
 #pragma unroll
-      for (int j = 0; j < MT; j++) {
-        float v = part[j * 32 + lane];
-#pragma unroll
-        for (int w = 1; w < kSmallWarps; w++) v += part[(w * MT + j) * 32 + lane];
-        part[j * 32 + lane] = v;
-      }
+  for (int j = 0; j < MT; j++) {
+    const int64_t col = col0 + j;
+    if (col < p.m) {
+      const float v = part[(warp * MT + j) * 32 + lane] + bn;
+      if (p.y_time_major)
+        p.y[col * p.ldy + n] = v;
+      else
+        p.y[n * p.ldy + col] = v;
     }
-    // Reduce over the cluster's K splits (rank 0 collects).
-    if (ks > 1) {
-      cg::cluster_group cluster = cg::this_cluster();
-      cluster.sync();
-      if (split == 0 && warp == 0) {
-        for (int q = 1; q < ks; q++) {
-          float *rp = cluster.map_shared_rank(part, q);
-#pragma unroll
-          for (int j = 0; j < MT; j++) part[j * 32 + lane] += rp[j * 32 + lane];
-        }
-      }
-      cluster.sync();
-    } else {
-      __syncthreads();
-    }
-    if (split != 0 || warp != 0) return;
-    const int64_t n = g * SC_GROUP_ROWS + r;
-    if (n >= n_rows) return;
-    const float bn = bias ? bias[n] : 0.0f;
-#pragma unroll
-    for (int j = 0; j < MT; j++) {
-      int64_t col = col0 + j;
-      if (col < m) {
-        float v = part[j * 32 + lane] + bn;
-        if (y_time_major)
-          y[col * ldy + n] = v;
-        else
-          y[n * ldy + col] = v;
-      }
-    }
+  }
   }
 }
 
-static int pick_ks(int64_t row_groups, int64_t nb, int64_t mtiles, int sm_count) {
-  // Aim for about two CTAs per SM with at least 8 K blocks per CTA (two per
-  // warp); the split is a cluster dimension, so at most 8.
-  int ks = 1;
-  while (ks < 8 && row_groups * mtiles * ks < 2 * sm_count && nb / (ks * 2) >= 8) ks *= 2;
-  return ks;
+static size_t stream_smem(int mt, int nbl_max) {
+  return (size_t)nbl_max * (SC_TILE_BYTES + SC_GROUP_ROWS * 2) + (size_t)mt * nbl_max * 32 +
+         (size_t)nbl_max * mt * 4 + (size_t)8 * mt * 32 * 4 + 16;
 }
 
 template <int MT, bool kDump>
-static int launch_small(const SmallGemmArgs &a, int ks, cudaStream_t st) {
-  const Q8Weights *w = a.w;
-  int64_t row_groups = w->rows_pad / 32;
-  int64_t mtiles = ceil_div(a.m, MT);
-  int64_t nbl_max = ceil_div(w->nb, ks);
-  size_t smem = (size_t)MT * nbl_max * 32 + (size_t)nbl_max * MT * 4 +
-                (size_t)kSmallWarps * MT * 32 * 4;
-  auto kern = q8_gemm_small_kernel<MT, kDump>;
-  // Raise the dynamic shared-memory limit once per device (not inside every
-  // launch, so graph capture sees only the launch itself).
+static int launch_stream(StreamParams &p, int64_t groups, int64_t mtiles, cudaStream_t st) {
+  auto kern = q8_gemm_stream_kernel<MT, kDump>;
+  const size_t smem = stream_smem(MT, p.nbl_max);
   static size_t smem_set[64] = {};
   int dev = 0;
   SC_CUDA(cudaGetDevice(&dev));
-  if (smem > 48 * 1024 && dev < 64 && smem_set[dev] < smem) {
+  if (dev < 64 && smem_set[dev] < smem) {
     SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     smem_set[dev] = smem;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)row_groups, (unsigned)ks, (unsigned)mtiles);
-  cfg.blockDim = dim3(kSmallWarps * 32, 1, 1);
+  cfg.gridDim = dim3((unsigned)groups, (unsigned)p.ks, (unsigned)mtiles);
+  cfg.blockDim = dim3(kStreamThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = (unsigned)ks;
+  attr[0].val.clusterDim.y = (unsigned)p.ks;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  SC_CUDA(cudaLaunchKernelEx(&cfg, kern, (const int8_t *)w->qs, (const __half *)w->sc,
-                             w->nb, a.xq, a.dx, a.k_pad, a.m_pad, a.m, a.bias, a.y,
-                             w->rows, a.y_time_major, a.ldy, ks, a.dots));
+  cfg.numAttrs = 2;
+  SC_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
+  return kOk;
+}
+
+static unsigned *small_status_ptr() {
+  static unsigned *ptr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return nullptr;
+  if (!ptr[dev]) {
+    void *q = nullptr;
+    if (cudaGetSymbolAddress(&q, g_small_status) != cudaSuccess) return nullptr;
+    ptr[dev] = (unsigned *)q;
+  }
+  return ptr[dev];
+}
+
+int small_gemm_status(unsigned *out) {
+  unsigned v = 0, zero = 0;
+  SC_CUDA(cudaMemcpyFromSymbol(&v, g_small_status, sizeof(v)));
+  SC_CUDA(cudaMemcpyToSymbol(g_small_status, &zero, sizeof(zero)));
+  *out = v;
   return kOk;
 }
 
 int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st) {
-  int mt = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : a.m <= 8 ? 8 : 16;
-  int64_t mtiles = ceil_div(a.m, mt);
-  int ks = pick_ks(a.w->rows_pad / 32, a.w->nb, mtiles, sm_count);
-  // Shared memory must hold the K slice of xq for MT columns.
-  while (ks < 8 && (size_t)mt * ceil_div(a.w->nb, ks) * 36 > 160 * 1024) ks *= 2;
-  if ((size_t)mt * ceil_div(a.w->nb, ks) * 36 > 200 * 1024) {
-    set_error("q8_gemm: K=%lld too large for the small-M kernel", (long long)a.w->k);
+  const Q8Weights *w = a.w;
+  const int mt = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : a.m <= 8 ? 8 : 16;
+  const int64_t mtiles = ceil_div(a.m, mt);
+  const int64_t groups = w->rows_pad / SC_GROUP_ROWS;
+  // K split (a cluster dimension, at most 8): smallest power of two that
+  // fills the GPU, keeps at least two blocks per CTA and fits shared memory.
+  int ks = 1;
+  while (ks < 8 && (ceil_div(w->nb, ks) > kNblCap ||
+                    (groups * mtiles * ks < sm_count && w->nb / (ks * 2) >= 2)))
+    ks *= 2;
+  if (ceil_div(w->nb, ks) > kNblCap) {
+    set_error("q8_gemm: K=%lld too large for the streaming kernel", (long long)w->k);
     return kErrUnsupported;
   }
+  unsigned *status = small_status_ptr();
+  if (!status) {
+    set_error("q8_gemm: status word lookup failed");
+    return kErrCuda;
+  }
+  StreamParams p{};
+  p.qs = w->qs;
+  p.sc = w->sc;
+  p.nb = w->nb;
+  p.n_rows = w->rows;
+  p.k = w->k;
+  p.x = a.x;
+  p.ldx = a.ldx;
+  p.x_feature_major = a.x_feature_major;
+  p.xq = a.xq;
+  p.dx = a.dx;
+  p.k_pad = a.k_pad;
+  p.m_pad = a.m_pad;
+  p.m = a.m;
+  p.bias = a.bias;
+  p.y = a.y;
+  p.y_time_major = a.y_time_major;
+  p.ldy = a.ldy;
+  p.ks = ks;
+  p.nbl_max = (int)ceil_div(w->nb, ks);
+  p.dots = a.dots;
+  p.status = status;
   if (a.dots) {
     switch (mt) {
-      case 1: return launch_small<1, true>(a, ks, st);
-      case 2: return launch_small<2, true>(a, ks, st);
-      case 4: return launch_small<4, true>(a, ks, st);
-      case 8: return launch_small<8, true>(a, ks, st);
-      default: return launch_small<16, true>(a, ks, st);
+      case 1: return launch_stream<1, true>(p, groups, mtiles, st);
+      case 2: return launch_stream<2, true>(p, groups, mtiles, st);
+      case 4: return launch_stream<4, true>(p, groups, mtiles, st);
+      case 8: return launch_stream<8, true>(p, groups, mtiles, st);
+      default: return launch_stream<16, true>(p, groups, mtiles, st);
     }
   }
   switch (mt) {
-    case 1: return launch_small<1, false>(a, ks, st);
-    case 2: return launch_small<2, false>(a, ks, st);
-    case 4: return launch_small<4, false>(a, ks, st);
-    case 8: return launch_small<8, false>(a, ks, st);
-    default: return launch_small<16, false>(a, ks, st);
+    case 1: return launch_stream<1, false>(p, groups, mtiles, st);
+    case 2: return launch_stream<2, false>(p, groups, mtiles, st);
+    case 4: return launch_stream<4, false>(p, groups, mtiles, st);
+    case 8: return launch_stream<8, false>(p, groups, mtiles, st);
+    default: return launch_stream<16, false>(p, groups, mtiles, st);
   }
 }
 

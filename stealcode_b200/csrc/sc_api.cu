@@ -64,7 +64,7 @@ size_t gemm_ws_bytes(int64_t m, int64_t k) {
   return a + (size_t)nb * m_pad * 4 + 256;
 }
 
-static int default_ws(size_t bytes, void **out) {
+[[maybe_unused]] static int default_ws(size_t bytes, void **out) {
   int dev;
   int rc = current_device(&dev, nullptr);
   if (rc) return rc;
@@ -117,20 +117,14 @@ int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, i
     return kErrInvalid;
   }
   size_t need = gemm_ws_bytes(t, w->k);
-  if (!ws) {
-    rc = default_ws(need, &ws);
-    if (rc) return rc;
-  } else if (ws_bytes < need || ((uintptr_t)ws & 255)) {
+  if (ws && (ws_bytes < need || ((uintptr_t)ws & 255))) {
     set_error("q8_gemm: workspace needs %zu bytes at 256-byte alignment", need);
     return kErrInvalid;
   }
-  int64_t nb = w->nb, k_pad = nb * 32, m_pad = ceil_div(t, 16) * 16;
-  int8_t *xq = (int8_t *)ws;
-  size_t off = ((size_t)m_pad * k_pad + 255) / 256 * 256;
-  float *dx = (float *)((char *)ws + off);
-  rc = quantize_act(x, t, w->k, ldx, x_layout == SC_LAYOUT_FEATURE_MAJOR, m_pad, xq, dx, st);
-  if (rc) return rc;
-  SmallGemmArgs a{w, xq, dx, k_pad, m_pad, t, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy, dots};
+  // The streaming kernel quantises the activations itself; the workspace is
+  // validated for callers that pass one but not needed by this path.
+  SmallGemmArgs a{w, x, ldx, x_layout == SC_LAYOUT_FEATURE_MAJOR, nullptr, nullptr, 0, 0, t, bias, y,
+                  y_layout == SC_LAYOUT_TIME_MAJOR, ldy, dots};
   return gemm_small(a, sms, st);
 }
 
@@ -255,6 +249,15 @@ int sc_q8w_device_layout(const sc_q8w *w, const int8_t **quants, const uint16_t 
   return kOk;
 }
 
+int sc_device_status(uint32_t *flags) {
+  if (!flags) { set_error("device_status: null pointer"); return kErrInvalid; }
+  unsigned v = 0;
+  int rc = small_gemm_status(&v);
+  if (rc) return rc;
+  *flags = v;
+  return kOk;
+}
+
 int64_t sc_q8_gemm_workspace_bytes(int64_t t, int64_t k) {
   if (t <= 0 || k <= 0) return 0;
   return (int64_t)gemm_ws_bytes(t, k);
@@ -341,7 +344,8 @@ int sc_q8_gemm_q(const sc_q8w *w, const int8_t *xq, const float *dx, int64_t t, 
   int dev, sms;
   int rc = current_device(&dev, &sms);
   if (rc) return rc;
-  SmallGemmArgs a{&W, xq, dx, W.nb * 32, t_pad, t, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy, nullptr};
+  SmallGemmArgs a{&W, nullptr, 0, 0, xq, dx, W.nb * 32, t_pad, t, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy,
+                  nullptr};
   return gemm_small(a, sms, (cudaStream_t)stream);
 }
 

@@ -15,8 +15,11 @@ int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx, bool feature
 // q8_gemm_small.cu
 struct SmallGemmArgs {
   const Q8Weights *w;
-  const int8_t *xq;   // [m_pad][k_pad] quantised activations
-  const float *dx;    // [nb][m_pad] activation block scales
+  const float *x;     // f32 activations quantised inside the kernel, or nullptr
+  int64_t ldx;
+  int x_feature_major;
+  const int8_t *xq;   // else: pre-quantised [m_pad][k_pad] activations
+  const float *dx;    // and their block scales [nb][m_pad]
   int64_t k_pad, m_pad, m;
   const float *bias;  // [rows] or nullptr
   float *y;
@@ -25,6 +28,7 @@ struct SmallGemmArgs {
   int32_t *dots;      // non-null: write raw int32 block dots instead of y
 };
 int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st);
+int small_gemm_status(unsigned *out);  // read and clear the kernels' status word
 
 // attn_stream.cu
 struct AttnParams {

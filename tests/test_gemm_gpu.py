@@ -218,3 +218,9 @@ def test_caller_workspace(torch):
     x = torch.from_numpy(synth.normal(72, (8, 1024))).cuda()
     ws = torch.empty(mat.workspace_bytes(8), dtype=torch.uint8, device="cuda")
     assert torch.equal(mat.gemm(x, workspace=ws), mat.gemm(x))
+
+
+def test_no_device_wait_timed_out(torch):
+    """No bounded device-side wait gave up during the tests above."""
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
