@@ -30,6 +30,14 @@ namespace cg = cooperative_groups;
 
 namespace sc {
 
+// Build-time tuning knobs (defaults are the measured best).
+#ifndef SC_STREAM_KS_MAX
+#define SC_STREAM_KS_MAX 8  // largest K split (cluster size)
+#endif
+#ifndef SC_STREAM_PDL
+#define SC_STREAM_PDL 1     // launch with programmatic stream serialization
+#endif
+
 constexpr int kStreamThreads = 256;
 constexpr int kNblCap = 40;  // K blocks per CTA slice (shared-memory bound)
 
@@ -104,17 +112,33 @@ __global__ void __launch_bounds__(kStreamThreads)
   pdl_wait();
 
   // ---- activations of this CTA's frames and K slice -> shared memory ----
+  // Each warp first issues the loads of up to 8 (frame, block) pairs, then
+  // quantises them, so the loads' latencies overlap instead of adding up.
   if (p.x) {
-    for (int pair = warp; pair < MT * nbl; pair += kStreamThreads / 32) {
-      const int j = pair / nbl, bb = pair % nbl;
-      const int64_t col = col0 + j, kk = (b0 + bb) * 32 + lane;
-      const bool valid = col < p.m && kk < p.k;
-      float v = 0.0f;
-      if (valid) v = p.x_feature_major ? p.x[kk * p.ldx + col] : p.x[col * p.ldx + kk];
-      float s;
-      const int8_t q = warp_quantize_block(v, valid, s);
-      xs[(size_t)j * nbl * 32 + bb * 32 + lane] = q;
-      if (lane == 0) dxs[bb * MT + j] = col < p.m ? s : 0.0f;
+    constexpr int kPairs = 8;
+    const int npairs = MT * nbl;
+    for (int base = warp; base < npairs; base += kPairs * (kStreamThreads / 32)) {
+      float v[kPairs];
+      bool valid[kPairs];
+#pragma unroll
+      for (int i = 0; i < kPairs; i++) {
+        const int pair = base + i * (kStreamThreads / 32);
+        const int j = pair / nbl, bb = pair % nbl;
+        const int64_t col = col0 + j, kk = (b0 + bb) * 32 + lane;
+        valid[i] = pair < npairs && col < p.m && kk < p.k;
+        v[i] = 0.0f;
+        if (valid[i]) v[i] = p.x_feature_major ? p.x[kk * p.ldx + col] : p.x[col * p.ldx + kk];
+      }
+#pragma unroll
+      for (int i = 0; i < kPairs; i++) {
+        const int pair = base + i * (kStreamThreads / 32);
+        if (pair >= npairs) break;
+        const int j = pair / nbl, bb = pair % nbl;
+        float sblk;
+        const int8_t q = warp_quantize_block(v[i], valid[i], sblk);
+        xs[(size_t)j * nbl * 32 + bb * 32 + lane] = q;
+        if (lane == 0) dxs[bb * MT + j] = col0 + j < p.m ? sblk : 0.0f;
+      }
     }
   } else {
     for (int i = tid; i < MT * nbl * 2; i += kStreamThreads) {
@@ -166,35 +190,37 @@ __global__ void __launch_bounds__(kStreamThreads)
     for (int j = 0; j < MT; j++)
       part[(warp * MT + j) * 32 + lane] += part[((warp + 4) * MT + j) * 32 + lane];
   }
-  if (p.ks > 1) {
-    cg::cluster_group cluster = cg::this_cluster();
+  // Reduce-scatter over the cluster's K splits: rank q sums rows
+  // [q*128/ks, (q+1)*128/ks) of every split (all remote loads in flight at
+  // once) and writes them, so no rank gathers the whole tile serially.
+  cg::cluster_group cluster = cg::this_cluster();
+  if (p.ks > 1)
     cluster.sync();
-    if (split == 0 && warp < 4) {
-      for (int q = 1; q < p.ks; q++) {
-        const float *rp = cluster.map_shared_rank(part, q);
-#pragma unroll
-        for (int j = 0; j < MT; j++) part[(warp * MT + j) * 32 + lane] += rp[(warp * MT + j) * 32 + lane];
-      }
-    }
-    cluster.sync();
-  } else {
+  else
     __syncthreads();
-  }
-  if (split != 0 || warp >= 4) return;
-  const int64_t n = g * SC_GROUP_ROWS + r;
-  if (n >= p.n_rows) return;
-  const float bn = p.bias ? p.bias[n] : 0.0f;
+  const int rows_per = SC_GROUP_ROWS / p.ks;
+  for (int e = tid; e < rows_per * MT; e += kStreamThreads) {
+    const int rr = split * rows_per + e / MT, j = e % MT;  // row in tile, frame
+    const int idx = ((rr >> 5) * MT + j) * 32 + (rr & 31);
+    float v = part[idx];
+    if (p.ks > 1) {
+      float rv[8];
 #pragma unroll
-  for (int j = 0; j < MT; j++) {
-    const int64_t col = col0 + j;
-    if (col < p.m) {
-      const float v = part[(warp * MT + j) * 32 + lane] + bn;
+      for (int q = 0; q < 8; q++) rv[q] = (q < p.ks && q != split) ? cluster.map_shared_rank(part, q)[idx] : 0.0f;
+      v = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 8; q++) v += q == split ? part[idx] : rv[q];
+    }
+    const int64_t n = g * SC_GROUP_ROWS + rr, col = col0 + j;
+    if (n < p.n_rows && col < p.m) {
+      v += p.bias ? p.bias[n] : 0.0f;
       if (p.y_time_major)
         p.y[col * p.ldy + n] = v;
       else
         p.y[n * p.ldy + col] = v;
     }
   }
+  if (p.ks > 1) cluster.sync();  // keep this CTA's partials alive for its peers
   }
 }
 
@@ -227,7 +253,7 @@ static int launch_stream(StreamParams &p, int64_t groups, int64_t mtiles, cudaSt
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = SC_STREAM_PDL ? 2 : 1;
   SC_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
   return kOk;
 }
@@ -260,10 +286,10 @@ int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st) {
   // K split (a cluster dimension, at most 8): smallest power of two that
   // fills the GPU, keeps at least two blocks per CTA and fits shared memory.
   int ks = 1;
-  while (ks < 8 && (ceil_div(w->nb, ks) > kNblCap ||
+  while (ks < SC_STREAM_KS_MAX && (ceil_div(w->nb, ks) > kNblCap ||
                     (groups * mtiles * ks < sm_count && w->nb / (ks * 2) >= 2)))
     ks *= 2;
-  if (ceil_div(w->nb, ks) > kNblCap) {
+  if (ceil_div(w->nb, ks) > kNblCap || ks > 8) {
     set_error("q8_gemm: K=%lld too large for the streaming kernel", (long long)w->k);
     return kErrUnsupported;
   }
