@@ -1,0 +1,334 @@
+// q8_gemm_tc.cu -- large-M Q8_0 GEMM on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8, int32 accumulators in tensor memory).
+//
+// Same arithmetic as the reference (sgemm_kernel.rs:156-201): for every 32-wide
+// K block the exact int32 dot of int8 weights and int8 activation codes, scaled
+// by dw[n, b] * dx[col, b] and accumulated in f32.  Because each K block has
+// its own pair of scales, the int32 accumulator cannot run across blocks:
+// every tcgen05.mma covers exactly one block (M = 128 weight rows, N = FT
+// frames, K = 32) into a fresh TMEM buffer, and drain warps read it back
+// (tcgen05.ld), scale it and add it to f32 accumulators in registers while the
+// tensor core already computes the next block into the other buffer.
+//
+// CTA roles (warp-specialised, one CTA per 128-row group x FT-frame tile):
+//   warp 0       producer: 1-D bulk copies (TMA engine, no multicast) of the
+//                block's weight tile (the row-group tile layout is already the
+//                no-swizzle K-major UMMA operand layout), the activation tile,
+//                and the block's weight and activation scales, into a ring of
+//                shared-memory stages;
+//   warp 1       allocates TMEM and issues one tcgen05.mma per block (single
+//                thread), committing to the stage's "empty" barrier and the
+//                TMEM buffer's "full" barrier;
+//   warps 2..    drain warpgroups: each thread owns one weight row (TMEM lane)
+//                and FT/DWG frame columns.
+// Every mbarrier wait is bounded; a wait that gives up sets a status bit and
+// the kernel runs to its end without waiting again, so it cannot hang.
+#include "sc_device.cuh"
+#include "sc_kernels.cuh"
+
+namespace sc {
+
+constexpr int kTcStages = 6;
+constexpr int kTcAccBufs = 2;
+
+static __device__ unsigned g_tc_status;
+
+struct TcParams {
+  const int8_t *qs;      // weight tiles
+  const __half *sc;      // weight scales [g][b][128]
+  int64_t nb, n_rows;
+  const int8_t *xq;      // activation tiles [t_pad/FT][nb][2][FT][16]
+  const float *dx;       // activation scales [nb][t_pad]
+  int64_t t, t_pad;
+  const float *bias;
+  float *y;
+  int y_time_major;
+  int64_t ldy;
+  unsigned *status;
+};
+
+// ---- tcgen05 wrappers -----------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, no swizzle, K-major canonical layout:
+// core matrices of 8 rows x 16 bytes, `lbo` bytes between the two 16-byte
+// K halves, `sbo` bytes between consecutive 8-row groups.
+__device__ __forceinline__ uint64_t umma_desc(const void *smem, uint32_t lbo, uint32_t sbo) {
+  const uint32_t a = smem_u32(smem);
+  uint64_t d = 0;
+  d |= (uint64_t)((a >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  return d;               // base offset 0, layout type 0 = no swizzle
+}
+
+// Instruction descriptor: kind::i8, D = s32, A = B = signed int8, both
+// K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int FT, int DWG>
+struct TcSmem {
+  static constexpr int kA = SC_TILE_BYTES;          // 128 x 32 int8
+  static constexpr int kB = FT * 32;                // FT x 32 int8
+  static constexpr int kS = SC_GROUP_ROWS * 2;      // 128 f16 weight scales
+  static constexpr int kD = FT * 4;                 // FT f32 activation scales
+  static constexpr int kStage = kA + kB + kS + kD;  // all multiples of 16
+  static constexpr int kBars = 8 * (2 * kTcStages + 2 * kTcAccBufs) + 16;
+  static constexpr int kBytes = kTcStages * kStage + kBars;
+};
+
+template <int FT, int DWG>
+__global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __grid_constant__ TcParams p) {
+  using L = TcSmem<FT, DWG>;
+  constexpr int CPT = FT / DWG;  // frame columns per drain thread
+  static_assert(CPT % 32 == 0, "drain chunk is 32 columns");
+  extern __shared__ __align__(1024) unsigned char smem[];
+  uint64_t *full = (uint64_t *)(smem + kTcStages * L::kStage);
+  uint64_t *empty = full + kTcStages;
+  uint64_t *tfull = empty + kTcStages;
+  uint64_t *tempty = tfull + kTcAccBufs;
+  uint32_t *tmem_slot = (uint32_t *)(tempty + kTcAccBufs);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t g = blockIdx.x, ft = blockIdx.y;
+  const int nb = (int)p.nb;
+  constexpr uint32_t kTmemCols = FT * kTcAccBufs < 32 ? 32 : FT * kTcAccBufs;
+
+  // All inputs are read after the previous kernel on the stream completes;
+  // TMEM is allocated after that too, so a CTA never holds tensor memory
+  // while it waits on another grid.
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + 4 * DWG);  // MMA commit + one arrival per drain warp
+    }
+    for (int b = 0; b < kTcAccBufs; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4 * DWG);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  bool ok = true;
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int b = 0; b < nb && ok; b++) {
+        const int s = b % kTcStages;
+        const uint32_t ph = (uint32_t)(b / kTcStages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u)) { ok = false; break; }
+        unsigned char *st = smem + s * L::kStage;
+        mbar_arrive_expect_tx(&full[s], L::kStage);
+        bulk_g2s(st, p.qs + (g * p.nb + b) * SC_TILE_BYTES, L::kA, &full[s]);
+        bulk_g2s(st + L::kA, p.xq + (ft * p.nb + b) * (int64_t)(FT * 32), L::kB, &full[s]);
+        bulk_g2s(st + L::kA + L::kB, p.sc + (g * p.nb + b) * SC_GROUP_ROWS, L::kS, &full[s]);
+        bulk_g2s(st + L::kA + L::kB + L::kS, p.dx + (int64_t)b * p.t_pad + ft * FT, L::kD, &full[s]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_i8(FT);
+      for (int b = 0; b < nb && ok; b++) {
+        const int s = b % kTcStages, buf = b % kTcAccBufs;
+        if (!mbar_wait(&full[s], (uint32_t)(b / kTcStages) & 1u)) { ok = false; break; }
+        if (!mbar_wait(&tempty[buf], ((uint32_t)(b / kTcAccBufs) & 1u) ^ 1u)) { ok = false; break; }
+        tc_fence_after();
+        const unsigned char *st = smem + s * L::kStage;
+        const uint64_t ad = umma_desc(st, 2048, 128);
+        const uint64_t bd = umma_desc(st + L::kA, FT * 16, 128);
+        tc_mma_i8(tmem_base + (uint32_t)(buf * FT), ad, bd, idesc, 0u);
+        tc_commit(&empty[s]);
+        tc_commit(&tfull[buf]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- drain warpgroups ----
+    const int dw_idx = warp - 2;
+    const int wg = dw_idx >> 2;         // column slice
+    const int quarter = warp & 3;       // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const int col_base = wg * CPT;
+    float acc[CPT];
+#pragma unroll
+    for (int j = 0; j < CPT; j++) acc[j] = 0.0f;
+    for (int b = 0; b < nb && ok; b++) {
+      const int s = b % kTcStages, buf = b % kTcAccBufs;
+      // warp-uniform waits: tcgen05.ld below needs the whole warp
+      bool got = mbar_wait(&full[s], (uint32_t)(b / kTcStages) & 1u);
+      got = got && mbar_wait(&tfull[buf], (uint32_t)(b / kTcAccBufs) & 1u);
+      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t d[CPT];
+#pragma unroll
+      for (int c = 0; c < CPT / 32; c++) {
+        uint32_t r[32];
+        tc_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * FT + col_base + c * 32), r);
+#pragma unroll
+        for (int i = 0; i < 32; i++) d[c * 32 + i] = r[i];
+      }
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      const unsigned char *st = smem + s * L::kStage;
+      const float dwv = __half2float(((const __half *)(st + L::kA + L::kB))[row]);
+      const float *dxs = (const float *)(st + L::kA + L::kB + L::kS) + col_base;
+#pragma unroll
+      for (int j = 0; j < CPT; j++) acc[j] = fmaf(dwv * dxs[j], (float)(int)d[j], acc[j]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // ---- epilogue: y (+ bias) ----
+    const int64_t n = g * SC_GROUP_ROWS + row;
+    if (n < p.n_rows) {
+      const float bn = p.bias ? p.bias[n] : 0.0f;
+#pragma unroll
+      for (int j = 0; j < CPT; j++) {
+        const int64_t f = ft * FT + col_base + j;
+        if (f < p.t) {
+          if (p.y_time_major)
+            p.y[f * p.ldy + n] = acc[j] + bn;
+          else
+            p.y[n * p.ldy + f] = acc[j] + bn;
+        }
+      }
+    }
+  }
+  if (!ok) atomicOr(p.status, kStatusWaitTimeout);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+static unsigned *tc_status_ptr() {
+  static unsigned *ptr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return nullptr;
+  if (!ptr[dev]) {
+    void *q = nullptr;
+    if (cudaGetSymbolAddress(&q, g_tc_status) != cudaSuccess) return nullptr;
+    ptr[dev] = (unsigned *)q;
+  }
+  return ptr[dev];
+}
+
+int tc_gemm_status(unsigned *out) {
+  unsigned v = 0, zero = 0;
+  SC_CUDA(cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(v)));
+  SC_CUDA(cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(zero)));
+  *out = v;
+  return kOk;
+}
+
+template <int FT, int DWG>
+static int launch_tc(const TcParams &p, int64_t groups, cudaStream_t st) {
+  using L = TcSmem<FT, DWG>;
+  auto kern = q8_gemm_tc_kernel<FT, DWG>;
+  static bool configured[64] = {};
+  int dev = 0;
+  SC_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !configured[dev]) {
+    SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)groups, (unsigned)(p.t_pad / FT), 1);
+  cfg.blockDim = dim3(64 + 128 * DWG, 1, 1);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SC_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
+  return kOk;
+}
+
+int tc_frame_tile(int64_t t) { return t <= 32 ? 32 : t <= 64 ? 64 : 128; }
+
+int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
+  const Q8Weights *w = a.w;
+  TcParams p{};
+  p.qs = w->qs;
+  p.sc = w->sc;
+  p.nb = w->nb;
+  p.n_rows = w->rows;
+  p.xq = a.xq;
+  p.dx = a.dx;
+  p.t = a.t;
+  p.t_pad = a.t_pad;
+  p.bias = a.bias;
+  p.y = a.y;
+  p.y_time_major = a.y_time_major;
+  p.ldy = a.ldy;
+  p.status = tc_status_ptr();
+  if (!p.status) {
+    set_error("q8_gemm_tc: status word lookup failed");
+    return kErrCuda;
+  }
+  const int ft = tc_frame_tile(a.t);
+  if (a.t_pad % ft != 0) {
+    set_error("q8_gemm_tc: t_pad %lld is not a multiple of the frame tile %d", (long long)a.t_pad, ft);
+    return kErrInvalid;
+  }
+  const int64_t groups = w->rows_pad / SC_GROUP_ROWS;
+  switch (ft) {
+    case 32: return launch_tc<32, 1>(p, groups, st);
+    case 64: return launch_tc<64, 2>(p, groups, st);
+    default: return launch_tc<128, 2>(p, groups, st);
+  }
+}
+
+}  // namespace sc

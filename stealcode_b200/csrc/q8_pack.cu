@@ -86,7 +86,7 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t m,
                                     int64_t k, int64_t ldx, int64_t nb,
                                     int64_t m_pad, int64_t k_pad,
                                     int8_t *__restrict__ xq,
-                                    float *__restrict__ dx) {
+                                    float *__restrict__ dx, int tile_ft) {
   int lane = threadIdx.x & 31;
   int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (wid >= m_pad * nb) return;
@@ -107,22 +107,26 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t m,
     float inv = __fdiv_rn(1.0f, s);
     q = rust_round_i8(__fmul_rn(v, inv));
   }
-  xq[col * k_pad + kk] = q;
+  if (tile_ft)
+    xq[((col / tile_ft) * nb + b) * (int64_t)tile_ft * 32 + (lane >> 4) * tile_ft * 16 + (col % tile_ft) * 16 +
+       (lane & 15)] = q;
+  else
+    xq[col * k_pad + kk] = q;
   if (lane == 0) dx[b * m_pad + col] = s;
 }
 
 int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx,
                  bool feature_major, int64_t m_pad, int8_t *xq, float *dx,
-                 cudaStream_t st) {
+                 cudaStream_t st, int tile_ft) {
   int64_t nb = ceil_div(k, 32);
   int64_t k_pad = nb * 32;
   int64_t warps = m_pad * nb;
   int threads = 256;
   unsigned grid = (unsigned)ceil_div(warps * 32, threads);
   if (feature_major)
-    quantize_act_kernel<true><<<grid, threads, 0, st>>>(x, m, k, ldx, nb, m_pad, k_pad, xq, dx);
+    quantize_act_kernel<true><<<grid, threads, 0, st>>>(x, m, k, ldx, nb, m_pad, k_pad, xq, dx, tile_ft);
   else
-    quantize_act_kernel<false><<<grid, threads, 0, st>>>(x, m, k, ldx, nb, m_pad, k_pad, xq, dx);
+    quantize_act_kernel<false><<<grid, threads, 0, st>>>(x, m, k, ldx, nb, m_pad, k_pad, xq, dx, tile_ft);
   SC_CUDA(cudaGetLastError());
   return kOk;
 }

@@ -58,13 +58,13 @@ int current_device(int *dev, int *sm_count) {
 // Workspace of a GEMM call: quantised activations [m_pad][k_pad] int8 then
 // their scales [nb][m_pad] f32.
 size_t gemm_ws_bytes(int64_t m, int64_t k) {
-  int64_t nb = ceil_div(k, 32), m_pad = ceil_div(m, 16) * 16;
+  int64_t nb = ceil_div(k, 32), m_pad = ceil_div(m, 128) * 128;
   size_t a = (size_t)m_pad * nb * 32;
   a = (a + 255) / 256 * 256;
   return a + (size_t)nb * m_pad * 4 + 256;
 }
 
-[[maybe_unused]] static int default_ws(size_t bytes, void **out) {
+static int default_ws(size_t bytes, void **out) {
   int dev;
   int rc = current_device(&dev, nullptr);
   if (rc) return rc;
@@ -92,6 +92,10 @@ size_t gemm_ws_bytes(int64_t m, int64_t k) {
 }
 
 static bool layout_ok(int32_t l) { return l == SC_LAYOUT_FEATURE_MAJOR || l == SC_LAYOUT_TIME_MAJOR; }
+
+// Frames up to which the weight-streaming kernel runs; above it the
+// tensor-core kernel takes over.
+constexpr int64_t kSmallMaxFrames = 16;
 
 // Quantise + GEMM on device pointers.
 int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
@@ -121,8 +125,22 @@ int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, i
     set_error("q8_gemm: workspace needs %zu bytes at 256-byte alignment", need);
     return kErrInvalid;
   }
-  // The streaming kernel quantises the activations itself; the workspace is
-  // validated for callers that pass one but not needed by this path.
+  if (t > kSmallMaxFrames && !dots) {
+    // Tensor-core path: quantise into the tiled operand layout, then tcgen05.
+    if (!ws) {
+      rc = default_ws(need, &ws);
+      if (rc) return rc;
+    }
+    const int ft = tc_frame_tile(t);
+    const int64_t t_pad = ceil_div(t, ft) * ft, k_pad = w->nb * 32;
+    int8_t *xq = (int8_t *)ws;
+    float *dx = (float *)((char *)ws + ((size_t)t_pad * k_pad + 255) / 256 * 256);
+    rc = quantize_act(x, t, w->k, ldx, x_layout == SC_LAYOUT_FEATURE_MAJOR, t_pad, xq, dx, st, ft);
+    if (rc) return rc;
+    TcGemmArgs ta{w, xq, dx, t, t_pad, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy};
+    return gemm_tc(ta, st);
+  }
+  // The streaming kernel quantises the activations itself.
   SmallGemmArgs a{w, x, ldx, x_layout == SC_LAYOUT_FEATURE_MAJOR, nullptr, nullptr, 0, 0, t, bias, y,
                   y_layout == SC_LAYOUT_TIME_MAJOR, ldy, dots};
   return gemm_small(a, sms, st);
@@ -251,10 +269,11 @@ int sc_q8w_device_layout(const sc_q8w *w, const int8_t **quants, const uint16_t 
 
 int sc_device_status(uint32_t *flags) {
   if (!flags) { set_error("device_status: null pointer"); return kErrInvalid; }
-  unsigned v = 0;
+  unsigned v = 0, v2 = 0;
   int rc = small_gemm_status(&v);
+  if (!rc) rc = tc_gemm_status(&v2);
   if (rc) return rc;
-  *flags = v;
+  *flags = v | v2;
   return kOk;
 }
 

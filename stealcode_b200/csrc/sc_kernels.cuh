@@ -9,8 +9,11 @@ namespace sc {
 // q8_pack.cu
 int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k, int64_t block_bytes,
                      int64_t qoff, Q8Weights *w, cudaStream_t st);
+// tile_ft == 0: xq is [m_pad][k_pad]; tile_ft > 0: xq is the tensor-core
+// operand layout [m_pad/tile_ft][nb][2][tile_ft][16] (frame tiles of
+// tile_ft rows, one no-swizzle K-major tile per 32-wide block).
 int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx, bool feature_major,
-                 int64_t m_pad, int8_t *xq, float *dx, cudaStream_t st);
+                 int64_t m_pad, int8_t *xq, float *dx, cudaStream_t st, int tile_ft = 0);
 
 // q8_gemm_small.cu
 struct SmallGemmArgs {
@@ -29,6 +32,21 @@ struct SmallGemmArgs {
 };
 int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st);
 int small_gemm_status(unsigned *out);  // read and clear the kernels' status word
+
+// q8_gemm_tc.cu
+struct TcGemmArgs {
+  const Q8Weights *w;
+  const int8_t *xq;   // tiled activation codes (quantize_act with tile_ft = tc_frame_tile(t))
+  const float *dx;    // [nb][t_pad]
+  int64_t t, t_pad;   // t_pad: multiple of tc_frame_tile(t)
+  const float *bias;
+  float *y;
+  int y_time_major;
+  int64_t ldy;
+};
+int tc_frame_tile(int64_t t);
+int gemm_tc(const TcGemmArgs &a, cudaStream_t st);
+int tc_gemm_status(unsigned *out);
 
 // attn_stream.cu
 struct AttnParams {

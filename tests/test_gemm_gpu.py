@@ -224,3 +224,47 @@ def test_no_device_wait_timed_out(torch):
     """No bounded device-side wait gave up during the tests above."""
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
+
+
+# ---- tensor-core path (tcgen05 kind::i8), t > 16 frames -------------------
+@pytest.mark.parametrize("t,k,n", [(17, 1024, 256), (33, 1000, 37), (64, 1024, 384), (100, 4096, 128),
+                                   (129, 1024, 256), (300, 4352, 128)])
+@pytest.mark.parametrize("layout", [SC_LAYOUT_TIME_MAJOR, SC_LAYOUT_FEATURE_MAJOR])
+def test_tensor_core_path_matches_oracle(torch, t, k, n, layout):
+    w = synth.q8_weights(1000 + t + k, n, k)
+    x_tk = synth.normal(2000 + t, (t, k))
+    bias = synth.normal(3000 + n, (n,), std=0.02)
+    ref = oracle.q8_gemm(n, k, t, w, ((k + 31) // 32) * 34, 34, 2, np.ascontiguousarray(x_tk.T)) + bias[:, None]
+    mat = Q8Mat(w, n, k)
+    xd = torch.from_numpy(x_tk if layout == SC_LAYOUT_TIME_MAJOR else np.ascontiguousarray(x_tk.T)).cuda()
+    y = mat.gemm(xd, x_layout=layout, bias=torch.from_numpy(bias).cuda(), y_layout=layout)
+    torch.cuda.synchronize()
+    y = y.cpu().numpy()
+    got = y.T if layout == SC_LAYOUT_TIME_MAJOR else y
+    assert rms_err(got, ref) <= TOL_RMS
+
+
+def test_tensor_core_path_config3_frames(torch):
+    """M = 256 streams x 7 frames = 1792 (the batched encoder step), full
+    FFN-up shape; checked on a column subset against the oracle plus the
+    size-independent scaling and permutation properties on all of it."""
+    t, k, n = 1792, 1024, 4096
+    mat = Q8Mat(synth.q8_weights(77, n, k), n, k)
+    x = torch.from_numpy(synth.normal(78, (t, k))).cuda()
+    y1 = mat.gemm(x)
+    y2 = mat.gemm(2 * x)
+    perm = torch.randperm(t, generator=torch.Generator().manual_seed(1)).cuda()
+    y3 = mat.gemm(x[perm].contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(y2, 2 * y1)
+    assert torch.equal(y3, y1[perm])
+    cols = [0, 1, 127, 128, 1000, 1791]
+    xs = x[cols].cpu().numpy()
+    w = synth.q8_weights(77, n, k)
+    ref = oracle.q8_gemm(n, k, len(cols), w, 32 * 34, 34, 2, np.ascontiguousarray(xs.T))
+    assert rms_err(y1[cols].cpu().numpy().T, ref) <= TOL_RMS
+
+
+def test_tensor_core_no_timeouts(torch):
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
