@@ -56,7 +56,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--profile", default=None, choices=["gemm", "attn"],
+    ap.add_argument("--profile", default=None, choices=["gemm", "attn", "tc"],
                     help="small eager case for ncu captures (no timing, no JSON line)")
     return ap.parse_args()
 
@@ -332,11 +332,11 @@ def run_profile(args):
     from stealcode_b200.ops import SC_LAYOUT_TIME_MAJOR, Q8Mat, attn_stream_ring
 
     dev = torch.device("cuda", 0)
-    if args.profile == "gemm":
+    if args.profile in ("gemm", "tc"):
         wh = host_weights()
         for name, k, n in SHAPES:
             mat = Q8Mat(wh[name], n, k)
-            for m in (8, 128):
+            for m in ((8, 128) if args.profile == "gemm" else (1792,)):
                 x = torch.from_numpy(synth.normal(synth.SEED_BASE + 100 + m + k, (m, k))).to(dev)
                 for _ in range(3):
                     mat.gemm(x, x_layout=SC_LAYOUT_TIME_MAJOR, y_layout=SC_LAYOUT_TIME_MAJOR)
