@@ -1,0 +1,75 @@
+/*
+ * sc_oracle_enc.h -- CPU oracle (TEST INFRASTRUCTURE ONLY) for the streaming
+ * Nemotron/FastConformer encoder step: a plain-C restatement of the
+ * reference's StreamingEncoder (streaming.rs:42-383), block_new
+ * (streaming.rs:395-680), the causal pre-encode stack
+ * (nemotron/encoder.rs:400-482) and the helper kernels they call
+ * (simd_kernel.rs:734-910, 1160-1235; nemotron/weights.rs:345-579).
+ * Paths are relative to the reference's crates/audio_engine/src/.
+ *
+ * Weights come as a table of named tensors using the GGUF tensor names the
+ * reference loads (nemotron/encoder.rs:89-245): f32 tensors (dtype 0) and
+ * Q8_0 tensors with f16 block scales (dtype 8, 34-byte blocks).
+ */
+#ifndef SC_ORACLE_ENC_H
+#define SC_ORACLE_ENC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    const char *name;
+    int32_t dtype;      /* 0 = f32, 8 = Q8_0 (f16 scale, 34-byte blocks) */
+    int32_t n_dims;
+    int64_t dims[4];    /* GGUF order: fastest axis first */
+    const void *data;
+} orc_tensor;
+
+typedef struct {
+    int32_t d_model, n_layers, n_heads, d_ff;
+    int32_t feat_in;        /* mel bins */
+    int32_t conv_channels;  /* pre-encode channels */
+    int32_t conv_kernel;    /* conformer depthwise kernel */
+    int32_t conv_left;      /* causal left context = kernel - 1 */
+    int32_t att_left;       /* att_context_left (frames) */
+    int32_t att_right;      /* att_context_right; chunk = att_right + 1 */
+    float ln_eps;
+} orc_enc_config;
+
+typedef struct orc_enc orc_enc;
+
+/* Returns NULL (and fills err) when a tensor is missing or mis-shaped. */
+orc_enc *orc_enc_create(const orc_enc_config *cfg, const orc_tensor *tensors,
+                        int n_tensors, char *err, size_t err_len);
+void orc_enc_destroy(orc_enc *e);
+/* streaming.rs:137-383.  mel is time-major [mel_frames, n_mels] (all mel
+ * frames of the stream so far); returns 0, -6 when t0 is out of sync. */
+int orc_enc_encode_new(orc_enc *e, const float *mel, size_t mel_frames,
+                       size_t n_mels, size_t t0, size_t t1, int fin);
+size_t orc_enc_total(const orc_enc *e);
+/* streaming.rs:111-127: copy frames [from, to) of the last block output. */
+int orc_enc_frames(const orc_enc *e, size_t from, size_t to, float *out);
+/* Stage outputs of the last step, for debugging parity: which = 0 pre-encode
+ * output of the new frames [c, d]; 1 + b = block b output [c, d]. */
+int orc_enc_last(const orc_enc *e, int which, float *out, size_t *c_out);
+
+/* Helper kernels, exposed for unit checks. */
+void orc_ln_forward(const float *x, const float *w, const float *b,
+                    float eps, float *out, size_t d);
+void orc_silu_inplace(float *v, size_t n);
+void orc_glu_from(const float *h, size_t t, size_t d, float *out);
+void orc_dwconv_forward(const float *x, size_t t, size_t dim, size_t kh,
+                        size_t pad_left, size_t pad_right, const float *w,
+                        float *out);
+/* streaming.rs:236-261: pos rows for pos in [1-chunk, (left_chunks+1)*chunk-1]
+ * before the linear_pos projection: [n_pos, d] sin/cos rows. */
+void orc_pos_rows(size_t n_pos, size_t d, long pos_lo, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

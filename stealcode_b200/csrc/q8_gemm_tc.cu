@@ -20,7 +20,8 @@
 //                thread), committing to the stage's "empty" barrier and the
 //                TMEM buffer's "full" barrier;
 //   warps 2..    drain warpgroups: each thread owns one weight row (TMEM lane)
-//                and FT/DWG frame columns.
+//                and 32 frame columns; the scaling runs in packed f32x2 FMAs
+//                and the int32 -> f32 conversion is an exact integer add.
 // Every mbarrier wait is bounded; a wait that gives up sets a status bit and
 // the kernel runs to its end without waiting again, so it cannot hang.
 #include "sc_device.cuh"
@@ -110,11 +111,32 @@ struct TcSmem {
   static constexpr int kBytes = kTcStages * kStage + kBars;
 };
 
+// Packed f32x2 arithmetic (two lanes of f32 per 64-bit register pair).
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 template <int FT, int DWG>
 __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __grid_constant__ TcParams p) {
   using L = TcSmem<FT, DWG>;
-  constexpr int CPT = FT / DWG;  // frame columns per drain thread
-  static_assert(CPT % 32 == 0, "drain chunk is 32 columns");
+  static_assert(FT == 32 * DWG, "each drain warpgroup owns 32 frame columns");
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t *full = (uint64_t *)(smem + kTcStages * L::kStage);
   uint64_t *empty = full + kTcStages;
@@ -189,15 +211,18 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
     }
     __syncwarp();
   } else {
-    // ---- drain warpgroups ----
+    // ---- drain warpgroups: 32 frame columns per thread ----
     const int dw_idx = warp - 2;
     const int wg = dw_idx >> 2;         // column slice
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
-    const int col_base = wg * CPT;
-    float acc[CPT];
+    const int col_base = wg * 32;
+    // int32 -> f32 without I2F: for |d| < 2^22, the float with bit pattern
+    // d + 0x4B400000 is exactly 1.5 * 2^23 + d (block dots are below 2^20).
+    const uint64_t neg_magic = pack2(-12582912.0f, -12582912.0f);
+    uint64_t acc[16];
 #pragma unroll
-    for (int j = 0; j < CPT; j++) acc[j] = 0.0f;
+    for (int j = 0; j < 16; j++) acc[j] = 0ull;
     for (int b = 0; b < nb && ok; b++) {
       const int s = b % kTcStages, buf = b % kTcAccBufs;
       // warp-uniform waits: tcgen05.ld below needs the whole warp
@@ -205,23 +230,24 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
       got = got && mbar_wait(&tfull[buf], (uint32_t)(b / kTcAccBufs) & 1u);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
       tc_fence_after();
-      uint32_t d[CPT];
-#pragma unroll
-      for (int c = 0; c < CPT / 32; c++) {
-        uint32_t r[32];
-        tc_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * FT + col_base + c * 32), r);
-#pragma unroll
-        for (int i = 0; i < 32; i++) d[c * 32 + i] = r[i];
-      }
+      uint32_t r[32];
+      tc_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * FT + col_base), r);
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
       const unsigned char *st = smem + s * L::kStage;
       const float dwv = __half2float(((const __half *)(st + L::kA + L::kB))[row]);
-      const float *dxs = (const float *)(st + L::kA + L::kB + L::kS) + col_base;
+      const uint64_t dw2 = pack2(dwv, dwv);
+      const uint64_t *dx2 = (const uint64_t *)(st + L::kA + L::kB + L::kS) + col_base / 2;
 #pragma unroll
-      for (int j = 0; j < CPT; j++) acc[j] = fmaf(dwv * dxs[j], (float)(int)d[j], acc[j]);
+      for (int j = 0; j < 16; j++) {
+        const uint64_t s2 = fmul2(dw2, dx2[j]);  // dw * dx per column
+        const uint64_t f2 = fadd2(pack2(__uint_as_float(r[2 * j] + 0x4B400000u),
+                                        __uint_as_float(r[2 * j + 1] + 0x4B400000u)),
+                                  neg_magic);   // exact block dots as f32
+        acc[j] = ffma2(s2, f2, acc[j]);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -230,13 +256,14 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
     if (n < p.n_rows) {
       const float bn = p.bias ? p.bias[n] : 0.0f;
 #pragma unroll
-      for (int j = 0; j < CPT; j++) {
+      for (int j = 0; j < 32; j++) {
         const int64_t f = ft * FT + col_base + j;
+        const float v = (j & 1) ? hi_of(acc[j >> 1]) : lo_of(acc[j >> 1]);
         if (f < p.t) {
           if (p.y_time_major)
-            p.y[f * p.ldy + n] = acc[j] + bn;
+            p.y[f * p.ldy + n] = v + bn;
           else
-            p.y[n * p.ldy + f] = acc[j] + bn;
+            p.y[n * p.ldy + f] = v + bn;
         }
       }
     }
@@ -327,7 +354,7 @@ int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
   switch (ft) {
     case 32: return launch_tc<32, 1>(p, groups, st);
     case 64: return launch_tc<64, 2>(p, groups, st);
-    default: return launch_tc<128, 2>(p, groups, st);
+    default: return launch_tc<128, 4>(p, groups, st);
   }
 }
 

@@ -115,11 +115,74 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t m,
   if (lane == 0) dx[b * m_pad + col] = s;
 }
 
+// Time-major variant with 16-byte loads: one warp per (frame, 4 blocks); the
+// 8 lanes of a block each hold 4 consecutive elements, reduce amax over the
+// 8-lane group and store their 4 codes with one 32-bit store.  Same
+// arithmetic per element as quantize_act_kernel.
+__global__ void quantize_act_v4_kernel(const float *__restrict__ x, int64_t m, int64_t k, int64_t ldx,
+                                       int64_t nb, int64_t m_pad, int64_t k_pad, int8_t *__restrict__ xq,
+                                       float *__restrict__ dx, int tile_ft) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nq = ceil_div(nb, 4);
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (wid >= m_pad * nq) return;
+  const int64_t col = wid / nq;
+  const int64_t b = (wid % nq) * 4 + (lane >> 3);
+  const int sub = lane & 7;
+  const int64_t kk = b * 32 + sub * 4;
+  float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  bool valid[4];
+  const bool blk_ok = b < nb;
+  if (blk_ok && col < m && kk + 3 < k) {
+    const float4 t4 = *(const float4 *)(x + col * ldx + kk);
+    v[0] = t4.x, v[1] = t4.y, v[2] = t4.z, v[3] = t4.w;
+#pragma unroll
+    for (int e = 0; e < 4; e++) valid[e] = true;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      valid[e] = blk_ok && col < m && kk + e < k;
+      if (valid[e]) v[e] = x[col * ldx + kk + e];
+    }
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 4; e++) amax = fmaxf(amax, valid[e] ? fabsf(v[e]) : 0.0f);
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (amax != amax) amax = 0.0f;
+  const float s = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
+  uint32_t packed = 0;
+  if (amax != 0.0f) {
+    const float inv = __fdiv_rn(1.0f, s);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int8_t q = valid[e] ? rust_round_i8(__fmul_rn(v[e], inv)) : (int8_t)0;
+      packed |= (uint32_t)(uint8_t)q << (8 * e);
+    }
+  }
+  if (!blk_ok) return;
+  if (tile_ft)
+    *(uint32_t *)(xq + ((col / tile_ft) * nb + b) * (int64_t)tile_ft * 32 + (sub >> 2) * tile_ft * 16 +
+                  (col % tile_ft) * 16 + (sub & 3) * 4) = packed;
+  else
+    *(uint32_t *)(xq + col * k_pad + kk) = packed;
+  if (sub == 0) dx[b * m_pad + col] = s;
+}
+
 int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx,
                  bool feature_major, int64_t m_pad, int8_t *xq, float *dx,
                  cudaStream_t st, int tile_ft) {
   int64_t nb = ceil_div(k, 32);
   int64_t k_pad = nb * 32;
+  if (!feature_major && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0) {
+    const int64_t warps = m_pad * ceil_div(nb, 4);
+    const int threads = 256;
+    quantize_act_v4_kernel<<<(unsigned)ceil_div(warps * 32, threads), threads, 0, st>>>(
+        x, m, k, ldx, nb, m_pad, k_pad, xq, dx, tile_ft);
+    SC_CUDA(cudaGetLastError());
+    return kOk;
+  }
   int64_t warps = m_pad * nb;
   int threads = 256;
   unsigned grid = (unsigned)ceil_div(warps * 32, threads);

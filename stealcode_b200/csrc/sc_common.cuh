@@ -54,6 +54,6 @@ int cuda_fail(cudaError_t e, const char *what);
     if (_e != cudaSuccess) return sc::cuda_fail(_e, #call); \
   } while (0)
 
-static inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ static inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace sc
