@@ -209,6 +209,66 @@ int sc_attn_stream_ring(const float *q, int64_t ldq, const float *k_new,
                         int64_t k_hi, int64_t pos_off, float *out,
                         int64_t ldo, void *stream);
 
+/* ---- streaming encoder (StreamEncoder) --------------------------------- */
+
+/* A named tensor of the model, with the GGUF tensor names the reference
+ * loads (nemotron/encoder.rs:89-245, e.g. "encoder.layers.3.self_attn.linear_q
+ * .weight").  dtype 0 = f32, 8 = Q8_0 with f16 block scales (34-byte blocks);
+ * dims in GGUF order (fastest axis first); data is host memory. */
+typedef struct {
+  const char *name;
+  int32_t dtype;
+  int32_t n_dims;
+  int64_t dims[4];
+  const void *data;
+} sc_tensor;
+
+/* EncoderConfig (nemotron/config.rs:19-39) plus max_frames, the largest
+ * number of encoder frames one encode_new call may add (1..16).
+ * att_right is the chunk's right context: chunk = att_right + 1 (the
+ * reference fixes it to 6, nemotron/config.rs:164). */
+typedef struct {
+  int32_t d_model, n_layers, n_heads, d_ff;
+  int32_t feat_in;        /* mel bins */
+  int32_t conv_channels;  /* pre-encode channels */
+  int32_t conv_kernel;    /* conformer depthwise kernel */
+  int32_t conv_left;      /* causal left context = conv_kernel - 1 */
+  int32_t att_left;       /* attention left context in frames */
+  int32_t att_right;
+  float ln_eps;
+  int32_t max_frames;
+} sc_encoder_config;
+
+typedef struct sc_stream_encoder sc_stream_encoder;
+
+/* Build a device streaming encoder for n_streams streams from the model's
+ * tensors (Encoder::load, nemotron/encoder.rs:249-282, then the weights'
+ * one-time device repack).  Synchronous. */
+int sc_stream_encoder_create(const sc_encoder_config *cfg,
+                             const sc_tensor *tensors, int n_tensors,
+                             int64_t n_streams, sc_stream_encoder **out);
+/* StreamEncoder::encode_new (streaming.rs:687-699, 137-383) for every
+ * stream at once: mel_new (device) holds each stream's new mel frames
+ * [t0, t1) as [n_streams][t1 - t0][feat_in]; the encoder keeps the mel left
+ * context itself, so the whole mel history is not passed.  t0 must equal 8 *
+ * the frames encoded so far (else SC_ERR_STATE, as the reference's "out of
+ * sync" bail); fin marks a stream's last batch.  Async on stream. */
+int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new,
+                                 int64_t t0, int64_t t1, int32_t fin,
+                                 void *stream);
+/* StreamEncoder::total (streaming.rs:702-703). */
+int64_t sc_stream_encoder_total(const sc_stream_encoder *e);
+/* StreamEncoder::frames (streaming.rs:700-701, 111-127) for one stream,
+ * copied to a host buffer [to - from][d_model]; the last 64 frames are kept.
+ * Synchronous. */
+int sc_stream_encoder_frames(const sc_stream_encoder *e, int64_t stream_idx,
+                             int64_t from, int64_t to, float *out_host);
+/* Device pointer to the last call's output frames, [n_streams * c][d]
+ * (stream-major); valid until the next encode_new. */
+int sc_stream_encoder_output(const sc_stream_encoder *e, const float **frames,
+                             int64_t *rows, int64_t *d);
+int sc_stream_encoder_destroy(sc_stream_encoder *e);
+
 #ifdef __cplusplus
 }
 #endif

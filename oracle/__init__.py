@@ -45,6 +45,16 @@ for _name, _res, _args in [
     ("orc_attn_stream_testloop", None, [_P, _P, _P, _P, _P, _P, _S, _S, _S, c_float, _S, _S, _S, _S,
                                         _S, _S, _P]),
     ("orc_num_cpus", c_int, []),
+    ("orc_enc_create", c_void_p, [_P, _P, c_int, ctypes.c_char_p, _S]),
+    ("orc_enc_destroy", None, [_P]),
+    ("orc_enc_encode_new", c_int, [_P, _P, _S, _S, _S, _S, c_int]),
+    ("orc_enc_total", _S, [_P]),
+    ("orc_enc_frames", c_int, [_P, _S, _S, _P]),
+    ("orc_enc_last", c_int, [_P, c_int, _P, ctypes.POINTER(_S)]),
+    ("orc_ln_forward", None, [_P, _P, _P, c_float, _P, _S]),
+    ("orc_dwconv_forward", None, [_P, _S, _S, _S, _S, _S, _P, _P]),
+    ("orc_glu_from", None, [_P, _S, _S, _P]),
+    ("orc_silu_inplace", None, [_P, _S]),
 ]:
     _f = getattr(lib, _name)
     _f.restype = _res
@@ -148,3 +158,53 @@ def attn_stream_testloop(q, kv, vv, pos_p, q_bias, v_bias, c, d, n_heads, scale,
 
 def num_cpus() -> int:
     return lib.orc_num_cpus()
+
+
+class OrcEncConfig(ctypes.Structure):
+    _fields_ = [("d_model", ctypes.c_int32), ("n_layers", ctypes.c_int32), ("n_heads", ctypes.c_int32),
+                ("d_ff", ctypes.c_int32), ("feat_in", ctypes.c_int32), ("conv_channels", ctypes.c_int32),
+                ("conv_kernel", ctypes.c_int32), ("conv_left", ctypes.c_int32), ("att_left", ctypes.c_int32),
+                ("att_right", ctypes.c_int32), ("ln_eps", ctypes.c_float)]
+
+
+class StreamingEncoder:
+    """The reference's single-stream CPU StreamingEncoder (streaming.rs:42-383),
+    restated in C.  `model` is a stealcode_b200.model.Model."""
+
+    def __init__(self, model):
+        c = model.config
+        self.model = model
+        self._table = model.table()
+        self._cfg = OrcEncConfig(c.d_model, c.n_layers, c.n_heads, c.d_ff, c.feat_in, c.conv_channels,
+                                 c.conv_kernel, c.conv_left, c.att_left, c.att_right, c.ln_eps)
+        err = ctypes.create_string_buffer(256)
+        self._h = lib.orc_enc_create(ctypes.byref(self._cfg), self._table, len(model.tensors), err, 256)
+        if not self._h:
+            raise RuntimeError(err.value.decode())
+        self.d = c.d_model
+
+    def encode_new(self, mel: np.ndarray, t0: int, t1: int, fin: bool = False) -> int:
+        """mel: all mel frames of the stream so far, [n_frames, n_mels]."""
+        mel = np.ascontiguousarray(mel, dtype=np.float32)
+        return lib.orc_enc_encode_new(self._h, _p(mel), mel.shape[0], mel.shape[1], t0, t1, int(fin))
+
+    def total(self) -> int:
+        return lib.orc_enc_total(self._h)
+
+    def frames(self, frm: int, to: int) -> np.ndarray:
+        out = np.empty((to - frm, self.d), dtype=np.float32)
+        if lib.orc_enc_frames(self._h, frm, to, _p(out)):
+            raise ValueError("frames out of range")
+        return out
+
+    def last(self, which: int) -> np.ndarray:
+        c = ctypes.c_size_t()
+        out = np.empty((16, self.d), dtype=np.float32)
+        if lib.orc_enc_last(self._h, which, _p(out), ctypes.byref(c)):
+            raise ValueError("no such stage")
+        return out[: c.value].copy()
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib.orc_enc_destroy(self._h)
+            self._h = None

@@ -10,7 +10,7 @@ Operator names are resolved lazily so that ``python -m stealcode_b200.build``
 works before the library exists; any use of an operator imports ``_lib``,
 which raises ImportError when the library is missing (there is no fallback).
 """
-_OPS = {"AttnStreamKernel", "Lin", "Q8Mat", "attn_stream_ring", "q8_gemm", "quantize"}
+_OPS = {"AttnStreamKernel", "Lin", "Q8Mat", "StreamEncoder", "attn_stream_ring", "q8_gemm", "quantize"}
 
 
 def __getattr__(name):

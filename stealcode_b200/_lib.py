@@ -69,6 +69,12 @@ SIGNATURES = {
     "sc_q8_gemm_host": (c_int, [c_size_t, c_size_t, c_size_t, _P, c_size_t, c_size_t, c_size_t, _P, _P]),
     "sc_q8_quantize": (c_int, [_P, _I, _I, c_int32, _I, _P, _P, _P]),
     "sc_q8_block_dots": (c_int, [_P, _P, _I, c_int32, _I, _P, _P]),
+    "sc_stream_encoder_create": (c_int, [_P, _P, c_int, _I, POINTER(c_void_p)]),
+    "sc_stream_encoder_encode_new": (c_int, [_P, _P, _I, _I, c_int32, _P]),
+    "sc_stream_encoder_total": (c_int64, [_P]),
+    "sc_stream_encoder_frames": (c_int, [_P, _I, _I, _I, _P]),
+    "sc_stream_encoder_output": (c_int, [_P, POINTER(c_void_p), POINTER(c_int64), POINTER(c_int64)]),
+    "sc_stream_encoder_destroy": (c_int, [_P]),
     "sc_attn_stream": (c_int, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, c_float,
                                _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "sc_attn_stream_host": (c_int, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, c_float,

@@ -24,7 +24,7 @@ size_t gemm_ws_bytes(int64_t m, int64_t k);
 int current_device(int *dev, int *sm_count);
 int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
               const float *bias, float *y, int32_t y_layout, int64_t ldy, void *ws, size_t ws_bytes,
-              int32_t *dots, cudaStream_t st);
+              int32_t *dots, cudaStream_t st, Epilogue epi);
 const Q8Weights *q8w_weights(const sc_q8w *w);
 
 // The scratch: quantised activations [t_pad][k_pad] int8, then their block
@@ -83,5 +83,6 @@ extern "C" int sc_q8_gemm_noalloc(const sc_q8w *w, const float *x, int64_t t, in
   // (the quantiser fills all t_pad rows, padding rows with zero codes), so
   // nothing is cleared; leftovers of the previous call are never read.
   return gemm_impl(W, x, t, x_layout, ldx, bias, y, y_layout, ldy, scratch,
-                   (size_t)SC_Q8_GEMM_NOALLOC_SCRATCH_BYTES, nullptr, (cudaStream_t)stream);
+                   (size_t)SC_Q8_GEMM_NOALLOC_SCRATCH_BYTES, nullptr, (cudaStream_t)stream,
+                   Epilogue{});
 }

@@ -61,6 +61,7 @@ struct StreamParams {
   int ks, nbl_max;
   int32_t *dots;
   unsigned *status;
+  Epilogue epi;
 };
 
 __device__ __forceinline__ int dot32(const int4 w0, const int4 w1, const int4 x0, const int4 x1) {
@@ -214,10 +215,8 @@ __global__ void __launch_bounds__(kStreamThreads)
     const int64_t n = g * SC_GROUP_ROWS + rr, col = col0 + j;
     if (n < p.n_rows && col < p.m) {
       v += p.bias ? p.bias[n] : 0.0f;
-      if (p.y_time_major)
-        p.y[col * p.ldy + n] = v;
-      else
-        p.y[n * p.ldy + col] = v;
+      const int64_t idx = p.y_time_major ? col * p.ldy + n : n * p.ldy + col;
+      p.y[idx] = apply_epilogue(p.epi, v, idx);
     }
   }
   if (p.ks > 1) cluster.sync();  // keep this CTA's partials alive for its peers
@@ -320,6 +319,7 @@ int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st) {
   p.nbl_max = (int)ceil_div(w->nb, ks);
   p.dots = a.dots;
   p.status = status;
+  p.epi = a.epi;
   if (a.dots) {
     switch (mt) {
       case 1: return launch_stream<1, true>(p, groups, mtiles, st);

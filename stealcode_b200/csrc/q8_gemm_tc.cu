@@ -46,6 +46,7 @@ struct TcParams {
   int y_time_major;
   int64_t ldy;
   unsigned *status;
+  Epilogue epi;
 };
 
 // ---- tcgen05 wrappers -----------------------------------------------------
@@ -260,10 +261,8 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
         const int64_t f = ft * FT + col_base + j;
         const float v = (j & 1) ? hi_of(acc[j >> 1]) : lo_of(acc[j >> 1]);
         if (f < p.t) {
-          if (p.y_time_major)
-            p.y[f * p.ldy + n] = v + bn;
-          else
-            p.y[n * p.ldy + f] = v + bn;
+          const int64_t idx = p.y_time_major ? f * p.ldy + n : n * p.ldy + f;
+          p.y[idx] = apply_epilogue(p.epi, v + bn, idx);
         }
       }
     }
@@ -341,6 +340,7 @@ int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
   p.y_time_major = a.y_time_major;
   p.ldy = a.ldy;
   p.status = tc_status_ptr();
+  p.epi = a.epi;
   if (!p.status) {
     set_error("q8_gemm_tc: status word lookup failed");
     return kErrCuda;

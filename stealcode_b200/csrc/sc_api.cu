@@ -100,7 +100,7 @@ constexpr int64_t kSmallMaxFrames = 16;
 // Quantise + GEMM on device pointers.
 int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
               const float *bias, float *y, int32_t y_layout, int64_t ldy, void *ws,
-              size_t ws_bytes, int32_t *dots, cudaStream_t st) {
+              size_t ws_bytes, int32_t *dots, cudaStream_t st, Epilogue epi) {
   if (!w || !x || (!y && !dots) || t < 0 || !layout_ok(x_layout) || !layout_ok(y_layout)) {
     set_error("q8_gemm: invalid argument");
     return kErrInvalid;
@@ -137,12 +137,12 @@ int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, i
     float *dx = (float *)((char *)ws + ((size_t)t_pad * k_pad + 255) / 256 * 256);
     rc = quantize_act(x, t, w->k, ldx, x_layout == SC_LAYOUT_FEATURE_MAJOR, t_pad, xq, dx, st, ft);
     if (rc) return rc;
-    TcGemmArgs ta{w, xq, dx, t, t_pad, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy};
+    TcGemmArgs ta{w, xq, dx, t, t_pad, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy, epi};
     return gemm_tc(ta, st);
   }
   // The streaming kernel quantises the activations itself.
   SmallGemmArgs a{w, x, ldx, x_layout == SC_LAYOUT_FEATURE_MAJOR, nullptr, nullptr, 0, 0, t, bias, y,
-                  y_layout == SC_LAYOUT_TIME_MAJOR, ldy, dots};
+                  y_layout == SC_LAYOUT_TIME_MAJOR, ldy, dots, epi};
   return gemm_small(a, sms, st);
 }
 
@@ -287,14 +287,14 @@ int sc_q8_gemm(const sc_q8w *w, const float *x, int64_t t, int32_t x_layout, int
                int64_t workspace_bytes, void *stream) {
   if (!w) { set_error("q8_gemm: null weights"); return kErrInvalid; }
   return gemm_impl(&w->w, x, t, x_layout, ldx, bias, y, y_layout, ldy, workspace,
-                   (size_t)(workspace_bytes < 0 ? 0 : workspace_bytes), nullptr, (cudaStream_t)stream);
+                   (size_t)(workspace_bytes < 0 ? 0 : workspace_bytes), nullptr, (cudaStream_t)stream, Epilogue{});
 }
 
 int sc_q8_block_dots(const sc_q8w *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
                      int32_t *dots, void *stream) {
   if (!w || !dots) { set_error("q8_block_dots: invalid argument"); return kErrInvalid; }
   return gemm_impl(&w->w, x, t, x_layout, ldx, nullptr, nullptr, SC_LAYOUT_TIME_MAJOR, 0, nullptr, 0,
-                   dots, (cudaStream_t)stream);
+                   dots, (cudaStream_t)stream, Epilogue{});
 }
 
 int sc_q8_quantize(const float *x, int64_t m, int64_t k, int32_t x_layout, int64_t ldx, int8_t *xq,
@@ -337,7 +337,7 @@ int sc_q8mat_gemm_t(const sc_q8w *w, const float *x_host, int64_t t, float *y_ho
   cudaError_t e = cudaMemcpyAsync(xd, x_host, (size_t)W.k * t * 4, cudaMemcpyHostToDevice, 0);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(x)");
   rc = gemm_impl(&W, xd, t, SC_LAYOUT_FEATURE_MAJOR, t, nullptr, yd, SC_LAYOUT_FEATURE_MAJOR, t, nullptr, 0,
-                 nullptr, 0);
+                 nullptr, 0, Epilogue{});
   if (rc) return rc;
   e = cudaMemcpyAsync(y_host, yd, yb, cudaMemcpyDeviceToHost, 0);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(y)");
@@ -364,7 +364,7 @@ int sc_q8_gemm_q(const sc_q8w *w, const int8_t *xq, const float *dx, int64_t t, 
   int rc = current_device(&dev, &sms);
   if (rc) return rc;
   SmallGemmArgs a{&W, nullptr, 0, 0, xq, dx, W.nb * 32, t_pad, t, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy,
-                  nullptr};
+                  nullptr, Epilogue{}};
   return gemm_small(a, sms, (cudaStream_t)stream);
 }
 

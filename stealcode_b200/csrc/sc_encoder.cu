@@ -1,0 +1,550 @@
+// sc_encoder.cu -- the device streaming encoder: the B200 counterpart of the
+// reference's StreamEncoder trait (streaming.rs:687-729) and its CPU
+// implementation StreamingEncoder::encode_new (streaming.rs:137-383) with
+// block_new (streaming.rs:395-680) and the causal pre-encode stack
+// (nemotron/encoder.rs:400-482), for n_streams streams advanced in lockstep.
+//
+// One encode_new call is one streaming step for every stream: M = n_streams x
+// c frames flow through the 24 conformer blocks as time-major [M, d] rows.
+// All per-stream state lives in HBM: per layer a K ring and a V ring
+// (cap >= the attention band), a GLU ring (the depthwise conv's causal
+// context), the last 24 mel frames for the next pre-encode window and an
+// output ring for frames().  The reference's Vec caches with drain/extend
+// (streaming.rs:263-277, 307-312, 345-361) become ring slots, so no per-step
+// host<->device traffic remains besides the new mel frames.
+//
+// Weights come as a table of named tensors with the reference's GGUF names
+// (nemotron/encoder.rs:89-245); linear_q/k/v are fused row-wise into one Q8
+// matrix (each output row is computed independently, so the result is the
+// same as three GEMMs over the same quantised input).
+#include <cublas_v2.h>
+
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "sc_kernels.cuh"
+#include "../../include/stealcode_b200.h"
+
+namespace sc {
+
+size_t gemm_ws_bytes(int64_t m, int64_t k);
+int current_device(int *dev, int *sm_count);
+int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
+              const float *bias, float *y, int32_t y_layout, int64_t ldy, void *ws, size_t ws_bytes,
+              int32_t *dots, cudaStream_t st, Epilogue epi);
+int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k, int64_t block_bytes, int64_t qoff,
+                     Q8Weights *w, cudaStream_t st);
+int launch_ln_rows(const float *x, int64_t ldx, const float *w, const float *b, float eps, float *out, int64_t ldo,
+                   int64_t rows, int d, cudaStream_t st);
+int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st);
+int launch_dwconv_ln_silu(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s, const float *w,
+                          const float *lnw, const float *lnb, float eps, float *out, cudaStream_t st);
+int launch_mel_window(const float *hist, int hist_cap, int hist_frames, const float *mel_new, int n_new,
+                      int n_mels, int t_mel, float *win, int64_t n_streams, cudaStream_t st);
+int launch_mel_hist(const float *old_hist, int hist_cap, int hist_frames, const float *mel_new, int n_new,
+                    int n_mels, float *new_hist, int64_t n_streams, cudaStream_t st);
+int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int f_in, int c_in, const float *w,
+                        const float *b, int c_out, int t_out, int f_out, int relu, float *out, cudaStream_t st);
+int launch_bias_relu(float *x, const float *b, int c, int64_t n, cudaStream_t st);
+int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int start_rel, int c, float *out,
+                   cudaStream_t st);
+int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st);
+
+constexpr int kMelHistory = 24;  // mel frames of left context (streaming.rs:188)
+
+struct Lin {
+  Q8Weights w{};
+  float *bias = nullptr;
+};
+
+struct Layer {
+  float *ln_ff1_w, *ln_ff1_b, *ln_att_w, *ln_att_b, *ln_conv_w, *ln_conv_b, *conv_ln_w, *conv_ln_b;
+  float *ln_ff2_w, *ln_ff2_b, *ln_out_w, *ln_out_b;
+  Lin ff1_1, ff1_2, qkv, pos, out, pw1, pw2, ff2_1, ff2_2;
+  float *pos_u, *pos_v, *dw;
+  float *pos_p = nullptr;              // [n_pos][d], after the first step
+  float *k_ring, *v_ring, *glu_ring;   // [n_streams][cap][d]
+};
+
+struct Conv {
+  float *w, *b;
+};
+
+}  // namespace sc
+
+using namespace sc;
+
+struct sc_stream_encoder {
+  sc_encoder_config cfg{};
+  int64_t n_streams = 0;
+  int device = 0;
+  int64_t chunk = 0, left_chunks = 0, n_pos = 0, kv_cap = 0, glu_cap = 0, out_cap = 0, t_mel_max = 0;
+  std::vector<Layer> layers;
+  Conv c0{}, c2{}, c3{}, c5{}, c6{};
+  Lin pre_out;
+  std::vector<void *> allocs;
+  // state
+  int64_t total = 0;
+  int64_t last_c = 0;
+  int hist_frames = 0;
+  float *hist[2] = {nullptr, nullptr};
+  int hist_cur = 0;
+  bool pos_ready = false;
+  // scratch
+  float *x, *y, *xn, *h, *qkv, *attn, *h2, *o2, *out_ring;
+  float *win, *p0, *p1, *p2, *flat, *pos_in;
+  void *ws = nullptr;
+  size_t ws_bytes = 0;
+  cublasHandle_t cublas = nullptr;
+
+  ~sc_stream_encoder() {
+    for (auto &l : layers)
+      for (Lin *q : {&l.ff1_1, &l.ff1_2, &l.qkv, &l.pos, &l.out, &l.pw1, &l.pw2, &l.ff2_1, &l.ff2_2}) {
+        cudaFree(q->w.qs);
+        cudaFree(q->w.sc);
+      }
+    cudaFree(pre_out.w.qs);
+    cudaFree(pre_out.w.sc);
+    for (void *p : allocs) cudaFree(p);
+    if (cublas) cublasDestroy(cublas);
+  }
+};
+
+namespace {
+
+struct Loader {
+  const sc_tensor *t;
+  int n;
+  sc_stream_encoder *e;
+  std::string err;
+
+  const sc_tensor *find(const std::string &name) const {
+    for (int i = 0; i < n; i++)
+      if (name == t[i].name) return &t[i];
+    return nullptr;
+  }
+  static int64_t numel(const sc_tensor *x) {
+    int64_t c = 1;
+    for (int i = 0; i < x->n_dims; i++) c *= x->dims[i];
+    return c;
+  }
+  float *dev_alloc(size_t bytes) {
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes < 16 ? 16 : bytes) != cudaSuccess) {
+      cudaGetLastError();
+      err = "cudaMalloc failed";
+      return nullptr;
+    }
+    e->allocs.push_back(p);
+    return (float *)p;
+  }
+  float *f32(const std::string &name, int64_t count, bool optional = false) {
+    const sc_tensor *x = find(name);
+    if (!x) {
+      if (!optional && err.empty()) err = "tensor " + name + " not found";
+      return nullptr;
+    }
+    if (x->dtype != 0 || numel(x) != count) {
+      if (err.empty()) err = "tensor " + name + " is not f32 with " + std::to_string(count) + " elements";
+      return nullptr;
+    }
+    float *d = dev_alloc((size_t)count * 4);
+    if (d && cudaMemcpy(d, x->data, (size_t)count * 4, cudaMemcpyHostToDevice) != cudaSuccess) err = "upload failed";
+    return d;
+  }
+  // Q8 linear [out, inp] (GGUF dims [inp, out]); `parts` tensors are stacked
+  // row-wise (QKV fusion).
+  bool lin(const std::vector<std::string> &bases, int64_t inp, int64_t out_each, Lin *l, bool bias_optional) {
+    const int64_t nb = (inp + 31) / 32, padded = nb * 34, rows = out_each * (int64_t)bases.size();
+    std::vector<uint8_t> raw((size_t)(rows * padded));
+    std::vector<float> bias((size_t)rows, 0.0f);
+    bool have_bias = false;  // missing parts of a fused bias are zero
+    for (size_t p = 0; p < bases.size(); p++) {
+      const sc_tensor *x = find(bases[p] + ".weight");
+      if (!x || x->dtype != 8 || x->n_dims != 2 || x->dims[0] != inp || x->dims[1] != out_each) {
+        if (err.empty()) err = "tensor " + bases[p] + ".weight missing or not Q8_0 [" + std::to_string(inp) + " -> " +
+                               std::to_string(out_each) + "]";
+        return false;
+      }
+      memcpy(raw.data() + p * out_each * padded, x->data, (size_t)(out_each * padded));
+      const sc_tensor *b = find(bases[p] + ".bias");
+      if (b) {
+        if (b->dtype != 0 || numel(b) != out_each) {
+          if (err.empty()) err = "tensor " + bases[p] + ".bias mis-shaped";
+          return false;
+        }
+        memcpy(bias.data() + p * out_each, b->data, (size_t)out_each * 4);
+        have_bias = true;
+      }
+    }
+    (void)bias_optional;  // a linear without bias is allowed (Lin::bias is optional)
+    uint8_t *draw = nullptr;
+    if (cudaMalloc(&draw, raw.size()) != cudaSuccess) {
+      cudaGetLastError();
+      err = "cudaMalloc failed";
+      return false;
+    }
+    Q8Weights &w = l->w;
+    w.rows = rows;
+    w.k = inp;
+    w.nb = nb;
+    w.rows_pad = (rows + SC_GROUP_ROWS - 1) / SC_GROUP_ROWS * SC_GROUP_ROWS;
+    w.device = e->device;
+    bool ok = cudaMemcpy(draw, raw.data(), raw.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMalloc(&w.qs, (size_t)w.rows_pad * nb * 32) == cudaSuccess &&
+              cudaMalloc(&w.sc, (size_t)w.rows_pad * nb * 2) == cudaSuccess &&
+              repack_q8_device(draw, rows, inp, 34, 2, &w, 0) == kOk && cudaDeviceSynchronize() == cudaSuccess;
+    cudaFree(draw);
+    if (!ok) {
+      cudaGetLastError();
+      if (err.empty()) err = "Q8 upload/repack failed";
+      return false;
+    }
+    if (have_bias) {
+      l->bias = dev_alloc(bias.size() * 4);
+      if (!l->bias || cudaMemcpy(l->bias, bias.data(), bias.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return false;
+    }
+    return true;
+  }
+};
+
+#define TRY(call)         \
+  do {                    \
+    int _rc = (call);     \
+    if (_rc) return _rc;  \
+  } while (0)
+
+int64_t conv_out(int64_t in) { return (in + 3 - 3) / 2 + 1; }  // k 3, pads (2, 1), stride 2
+
+}  // namespace
+
+extern "C" {
+
+int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tensors, int n_tensors,
+                             int64_t n_streams, sc_stream_encoder **out) {
+  if (!cfg || !tensors || !out || n_tensors <= 0 || n_streams <= 0) {
+    set_error("stream_encoder_create: invalid argument");
+    return kErrInvalid;
+  }
+  *out = nullptr;
+  const sc_encoder_config &c = *cfg;
+  if (c.d_model % 256 || c.d_model > 4096 || c.n_heads <= 0 || c.d_model % c.n_heads || c.att_right < 0 ||
+      c.conv_kernel < 1 || c.conv_left != c.conv_kernel - 1 || c.max_frames < 1 || c.max_frames > 16 ||
+      c.feat_in <= 0 || c.conv_channels <= 0 || c.n_layers <= 0) {
+    set_error("stream_encoder_create: unsupported config (d_model %d, heads %d, conv %d/%d, max_frames %d)",
+              c.d_model, c.n_heads, c.conv_kernel, c.conv_left, c.max_frames);
+    return kErrUnsupported;
+  }
+  int dev;
+  int rc = current_device(&dev, nullptr);
+  if (rc) return rc;
+  sc_stream_encoder *e = new (std::nothrow) sc_stream_encoder();
+  if (!e) {
+    set_error("stream_encoder_create: host allocation failed");
+    return kErrAlloc;
+  }
+  e->cfg = c;
+  e->n_streams = n_streams;
+  e->device = dev;
+  e->chunk = c.att_right + 1;
+  e->left_chunks = c.att_left / e->chunk;
+  e->n_pos = (e->left_chunks + 2) * e->chunk - 1;
+  e->kv_cap = e->left_chunks * e->chunk + (e->chunk - 1) + c.max_frames;
+  e->glu_cap = c.conv_left + c.max_frames;
+  e->out_cap = 64;
+  e->t_mel_max = kMelHistory + 8 * (int64_t)c.max_frames + 8;
+  const int64_t d = c.d_model, dff = c.d_ff, C = c.conv_channels;
+  Loader L{tensors, n_tensors, e, {}};
+  // pre-encode (nemotron/encoder.rs:89-160)
+  const std::string pc = "encoder.pre_encode.conv.";
+  e->c0 = {L.f32(pc + "0.weight", C * 9), L.f32(pc + "0.bias", C)};
+  e->c2 = {L.f32(pc + "2.weight", C * 9), L.f32(pc + "2.bias", C)};
+  e->c3 = {L.f32(pc + "3.weight", C * C), L.f32(pc + "3.bias", C)};
+  e->c5 = {L.f32(pc + "5.weight", C * 9), L.f32(pc + "5.bias", C)};
+  e->c6 = {L.f32(pc + "6.weight", C * C), L.f32(pc + "6.bias", C)};
+  const int64_t f_final = conv_out(conv_out(conv_out(c.feat_in)));
+  bool ok = L.err.empty() && L.lin({"encoder.pre_encode.out"}, f_final * C, d, &e->pre_out, true);
+  // conformer blocks (nemotron/encoder.rs:171-245)
+  e->layers.resize(c.n_layers);
+  for (int i = 0; ok && i < c.n_layers; i++) {
+    Layer &ly = e->layers[i];
+    const std::string p = "encoder.layers." + std::to_string(i) + ".";
+    ly.ln_ff1_w = L.f32(p + "norm_feed_forward1.weight", d);
+    ly.ln_ff1_b = L.f32(p + "norm_feed_forward1.bias", d);
+    ly.ln_att_w = L.f32(p + "norm_self_att.weight", d);
+    ly.ln_att_b = L.f32(p + "norm_self_att.bias", d);
+    ly.ln_conv_w = L.f32(p + "norm_conv.weight", d);
+    ly.ln_conv_b = L.f32(p + "norm_conv.bias", d);
+    ly.conv_ln_w = L.f32(p + "conv.batch_norm.weight", d);
+    ly.conv_ln_b = L.f32(p + "conv.batch_norm.bias", d);
+    ly.ln_ff2_w = L.f32(p + "norm_feed_forward2.weight", d);
+    ly.ln_ff2_b = L.f32(p + "norm_feed_forward2.bias", d);
+    ly.ln_out_w = L.f32(p + "norm_out.weight", d);
+    ly.ln_out_b = L.f32(p + "norm_out.bias", d);
+    ly.pos_u = L.f32(p + "self_attn.pos_bias_u", d);
+    ly.pos_v = L.f32(p + "self_attn.pos_bias_v", d);
+    ly.dw = L.f32(p + "conv.depthwise_conv.weight", d * c.conv_kernel);
+    ok = L.err.empty() && L.lin({p + "feed_forward1.linear1"}, d, dff, &ly.ff1_1, true) &&
+         L.lin({p + "feed_forward1.linear2"}, dff, d, &ly.ff1_2, true) &&
+         L.lin({p + "self_attn.linear_q", p + "self_attn.linear_k", p + "self_attn.linear_v"}, d, d, &ly.qkv, true) &&
+         L.lin({p + "self_attn.linear_pos"}, d, d, &ly.pos, true) &&
+         L.lin({p + "self_attn.linear_out"}, d, d, &ly.out, true) &&
+         L.lin({p + "conv.pointwise_conv1"}, d, 2 * d, &ly.pw1, true) &&
+         L.lin({p + "conv.pointwise_conv2"}, d, d, &ly.pw2, true) &&
+         L.lin({p + "feed_forward2.linear1"}, d, dff, &ly.ff2_1, true) &&
+         L.lin({p + "feed_forward2.linear2"}, dff, d, &ly.ff2_2, true);
+    if (ok) {
+      ly.pos_p = L.dev_alloc((size_t)(e->n_pos * d * 4));
+      ly.k_ring = L.dev_alloc((size_t)(n_streams * e->kv_cap * d * 4));
+      ly.v_ring = L.dev_alloc((size_t)(n_streams * e->kv_cap * d * 4));
+      ly.glu_ring = L.dev_alloc((size_t)(n_streams * e->glu_cap * d * 4));
+      ok = L.err.empty();
+    }
+  }
+  const int64_t M = n_streams * c.max_frames;
+  if (ok) {
+    e->x = L.dev_alloc(M * d * 4);
+    e->y = L.dev_alloc(M * d * 4);
+    e->xn = L.dev_alloc(M * d * 4);
+    e->h = L.dev_alloc(M * dff * 4);
+    e->qkv = L.dev_alloc(M * 3 * d * 4);
+    e->attn = L.dev_alloc(M * d * 4);
+    e->h2 = L.dev_alloc(M * 2 * d * 4);
+    e->o2 = L.dev_alloc(M * d * 4);
+    e->out_ring = L.dev_alloc((size_t)(n_streams * e->out_cap * d * 4));
+    e->hist[0] = L.dev_alloc((size_t)(n_streams * kMelHistory * c.feat_in * 4));
+    e->hist[1] = L.dev_alloc((size_t)(n_streams * kMelHistory * c.feat_in * 4));
+    const int64_t t0 = conv_out(e->t_mel_max), f0 = conv_out(c.feat_in);
+    e->win = L.dev_alloc((size_t)(n_streams * e->t_mel_max * c.feat_in * 4));
+    e->p0 = L.dev_alloc((size_t)(n_streams * t0 * f0 * C * 4));
+    e->p1 = L.dev_alloc((size_t)(n_streams * t0 * f0 * C * 4));
+    e->p2 = L.dev_alloc((size_t)(n_streams * t0 * f0 * C * 4));
+    e->flat = L.dev_alloc((size_t)(M * f_final * C * 4));
+    e->pos_in = L.dev_alloc((size_t)(e->n_pos * d * 4));
+    const int64_t kmax = std::max<int64_t>(std::max<int64_t>(dff, f_final * C), d);
+    const int64_t tmax = std::max<int64_t>(M, e->n_pos);
+    e->ws_bytes = gemm_ws_bytes(tmax, kmax);
+    e->ws = L.dev_alloc(e->ws_bytes);
+    ok = L.err.empty();
+  }
+  if (ok && cublasCreate(&e->cublas) != CUBLAS_STATUS_SUCCESS) {
+    L.err = "cublasCreate failed";
+    ok = false;
+  }
+  if (!ok) {
+    set_error("stream_encoder_create: %s", L.err.c_str());
+    delete e;
+    return L.err.find("cudaMalloc") != std::string::npos ? kErrAlloc : kErrInvalid;
+  }
+  *out = e;
+  return kOk;
+}
+
+int sc_stream_encoder_destroy(sc_stream_encoder *e) {
+  if (e) {
+    cudaDeviceSynchronize();
+    delete e;
+  }
+  return kOk;
+}
+
+int64_t sc_stream_encoder_total(const sc_stream_encoder *e) { return e ? e->total : -1; }
+
+int sc_stream_encoder_frames(const sc_stream_encoder *e, int64_t stream_idx, int64_t from, int64_t to,
+                             float *out_host) {
+  if (!e || !out_host || stream_idx < 0 || stream_idx >= e->n_streams) {
+    set_error("stream_encoder_frames: invalid argument");
+    return kErrInvalid;
+  }
+  if (e->total == 0) {
+    set_error("stream_encoder_frames: nothing encoded yet");
+    return kErrState;
+  }
+  if (to <= from || to > e->total || from < e->total - e->out_cap || from < 0) {
+    set_error("frames [%lld, %lld) outside cache [%lld, %lld)", (long long)from, (long long)to,
+              (long long)std::max<int64_t>(0, e->total - e->out_cap), (long long)e->total);
+    return kErrInvalid;
+  }
+  const int64_t d = e->cfg.d_model;
+  SC_CUDA(cudaDeviceSynchronize());
+  for (int64_t f = from; f < to; f++)
+    SC_CUDA(cudaMemcpy(out_host + (f - from) * d, e->out_ring + (stream_idx * e->out_cap + f % e->out_cap) * d,
+                       d * 4, cudaMemcpyDeviceToHost));
+  return kOk;
+}
+
+int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int64_t t0, int64_t t1, int32_t fin,
+                                 void *stream) {
+  if (!e || (!mel_new && t1 > t0) || t0 < 0 || t1 < t0 || t0 % 8) {
+    set_error("stream_encoder_encode_new: invalid argument (t0 must be a multiple of 8)");
+    return kErrInvalid;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const sc_encoder_config &c = e->cfg;
+  const int64_t d = c.d_model, dff = c.d_ff, C = c.conv_channels, Z = e->n_streams;
+  const float eps = c.ln_eps;
+  // ---- frames of this step (streaming.rs:160-180) ----
+  const int64_t s = t0 / 8, n_new = t1 - t0, ecount = s + (n_new + 7) / 8;
+  if (s != e->total) {
+    set_error("streaming encoder out of sync: expected frame %lld, cache has %lld", (long long)s,
+              (long long)e->total);
+    return kErrState;
+  }
+  const int64_t t_new = fin ? s + (((n_new / 2 + 1) / 2 + 1) / 2 + 1) : ecount;
+  if (t_new <= s) return kOk;
+  const int64_t cf = t_new - s;
+  if (cf > c.max_frames) {
+    set_error("stream_encoder_encode_new: %lld new frames exceed max_frames %d", (long long)cf, c.max_frames);
+    return kErrUnsupported;
+  }
+  const int64_t M = Z * cf;
+  // ---- pre-encode window (streaming.rs:182-218) ----
+  const int64_t mel_lo = s * 8, win_start = mel_lo > kMelHistory ? mel_lo - kMelHistory : 0;
+  const int64_t start_rel = (mel_lo - win_start) / 8, rel_max = start_rel + cf - 1;
+  const int64_t avail = t1 - win_start;
+  const int64_t want = std::max<int64_t>(8 * rel_max + 1, t_new * 8 - win_start);
+  const int64_t t_mel = std::min<int64_t>(avail, want);
+  if (mel_lo - win_start != e->hist_frames || t_mel > e->t_mel_max) {
+    set_error("stream_encoder_encode_new: window of %lld mel frames unsupported", (long long)t_mel);
+    return kErrUnsupported;
+  }
+  TRY(launch_mel_window(e->hist[e->hist_cur], kMelHistory, e->hist_frames, mel_new, (int)n_new, c.feat_in,
+                        (int)t_mel, e->win, Z, st));
+  // ---- pre-encode stack (nemotron/encoder.rs:400-482) ----
+  const int64_t ta = conv_out(t_mel), fa = conv_out(c.feat_in);
+  const int64_t tb = conv_out(ta), fb = conv_out(fa);
+  const int64_t tc = conv_out(tb), fc = conv_out(fb);
+  if (tc < start_rel + cf) {
+    set_error("pre_encode produced too few frames: %lld < %lld", (long long)tc, (long long)(start_rel + cf));
+    return kErrInvalid;
+  }
+  TRY(launch_conv2d_3x3s2(e->win, Z, (int)t_mel, c.feat_in, 1, e->c0.w, e->c0.b, (int)C, (int)ta, (int)fa, 1, e->p0,
+                          st));
+  TRY(launch_conv2d_3x3s2(e->p0, Z, (int)ta, (int)fa, (int)C, e->c2.w, e->c2.b, (int)C, (int)tb, (int)fb, 0, e->p1,
+                          st));
+  const float one = 1.0f, zero = 0.0f;
+  if (cublasSetStream(e->cublas, st) != CUBLAS_STATUS_SUCCESS ||
+      cublasSgemm(e->cublas, CUBLAS_OP_T, CUBLAS_OP_N, (int)C, (int)(Z * tb * fb), (int)C, &one, e->c3.w, (int)C,
+                  e->p1, (int)C, &zero, e->p2, (int)C) != CUBLAS_STATUS_SUCCESS) {
+    set_error("pre_encode pointwise conv: cuBLAS sgemm failed");
+    return kErrCuda;
+  }
+  TRY(launch_bias_relu(e->p2, e->c3.b, (int)C, Z * tb * fb * C, st));
+  TRY(launch_conv2d_3x3s2(e->p2, Z, (int)tb, (int)fb, (int)C, e->c5.w, e->c5.b, (int)C, (int)tc, (int)fc, 0, e->p1,
+                          st));
+  if (cublasSgemm(e->cublas, CUBLAS_OP_T, CUBLAS_OP_N, (int)C, (int)(Z * tc * fc), (int)C, &one, e->c6.w, (int)C,
+                  e->p1, (int)C, &zero, e->p0, (int)C) != CUBLAS_STATUS_SUCCESS) {
+    set_error("pre_encode pointwise conv: cuBLAS sgemm failed");
+    return kErrCuda;
+  }
+  TRY(launch_bias_relu(e->p0, e->c6.b, (int)C, Z * tc * fc * C, st));
+  TRY(launch_flatten(e->p0, Z, (int)tc, (int)fc, (int)C, (int)start_rel, (int)cf, e->flat, st));
+  TRY(gemm_impl(&e->pre_out.w, e->flat, M, SC_LAYOUT_TIME_MAJOR, 0, e->pre_out.bias, e->x, SC_LAYOUT_TIME_MAJOR, d,
+                e->ws, e->ws_bytes, nullptr, st, Epilogue{}));
+  // history for the next window
+  TRY(launch_mel_hist(e->hist[e->hist_cur], kMelHistory, e->hist_frames, mel_new, (int)n_new, c.feat_in,
+                      e->hist[e->hist_cur ^ 1], Z, st));
+  // ---- band and pos rows (streaming.rs:226-261) ----
+  const int64_t k_lo = (s / e->chunk > e->left_chunks ? s / e->chunk - e->left_chunks : 0) * e->chunk;
+  const int64_t k_hi = t_new, pos_off = e->chunk - 1;
+  if (!e->pos_ready) {
+    // sinusoid rows computed on the host in f32 exactly as the reference does
+    std::vector<float> pet((size_t)(e->n_pos * d));
+    const float ln10000 = logf(10000.0f);
+    for (int64_t i = 0; i < e->n_pos; i++) {
+      const float pos = (float)i + (float)(1 - e->chunk);
+      for (int64_t k = 0; k < d / 2; k++) {
+        const float div = expf(-2.0f * (float)k * ln10000 / (float)d);
+        pet[i * d + 2 * k] = sinf(pos * div);
+        pet[i * d + 2 * k + 1] = cosf(pos * div);
+      }
+    }
+    SC_CUDA(cudaMemcpyAsync(e->pos_in, pet.data(), pet.size() * 4, cudaMemcpyHostToDevice, st));
+    for (auto &ly : e->layers)
+      TRY(gemm_impl(&ly.pos.w, e->pos_in, e->n_pos, SC_LAYOUT_TIME_MAJOR, 0, ly.pos.bias, ly.pos_p,
+                    SC_LAYOUT_TIME_MAJOR, d, e->ws, e->ws_bytes, nullptr, st, Epilogue{}));
+    SC_CUDA(cudaStreamSynchronize(st));  // pet must outlive the copy
+    e->pos_ready = true;
+  }
+  // ---- conformer blocks (streaming.rs:279-318, block_new :395-680) ----
+  Epilogue silu{kEpiSilu, nullptr, 1.0f};
+  for (auto &ly : e->layers) {
+    auto gemm = [&](const Lin &l, const float *in, float *out, int64_t ldo, Epilogue epi) {
+      return gemm_impl(&l.w, in, M, SC_LAYOUT_TIME_MAJOR, 0, l.bias, out, SC_LAYOUT_TIME_MAJOR, ldo, e->ws,
+                       e->ws_bytes, nullptr, st, epi);
+    };
+    // macaron FF1: y = x + 0.5 * FF(LN(x))
+    TRY(launch_ln_rows(e->x, d, ly.ln_ff1_w, ly.ln_ff1_b, eps, e->xn, d, M, (int)d, st));
+    TRY(gemm(ly.ff1_1, e->xn, e->h, dff, silu));
+    TRY(gemm(ly.ff1_2, e->h, e->y, d, Epilogue{kEpiResidual, e->x, 0.5f}));
+    // rel-pos MHSA over the band, K/V from the rings
+    TRY(launch_ln_rows(e->y, d, ly.ln_att_w, ly.ln_att_b, eps, e->xn, d, M, (int)d, st));
+    TRY(gemm(ly.qkv, e->xn, e->qkv, 3 * d, Epilogue{}));
+    {
+      AttnParams p{};
+      p.q = e->qkv;
+      p.ldq = 3 * d;
+      p.k_new = e->qkv + d;
+      p.v_new = e->qkv + 2 * d;
+      p.ld_new = 3 * d;
+      p.rows_new = cf;
+      p.new_lo = s;
+      p.k_ring = ly.k_ring;
+      p.v_ring = ly.v_ring;
+      p.cap = e->kv_cap;
+      p.pos_p = ly.pos_p;
+      p.u = ly.pos_u;
+      p.v = ly.pos_v;
+      p.out = e->attn;
+      p.ldo = d;
+      p.c = (int)cf;
+      p.d = (int)d;
+      p.n_heads = c.n_heads;
+      p.scale = 1.0f / sqrtf((float)(d / c.n_heads));
+      p.s = s;
+      p.k_lo = k_lo;
+      p.k_hi = k_hi;
+      p.chunk = e->chunk;
+      p.left_chunks = e->left_chunks;
+      p.pos_off = pos_off;
+      TRY(attn_prepare(p, e->n_pos));
+      TRY(launch_attn(p, Z, st));
+    }
+    TRY(gemm(ly.out, e->attn, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}));
+    // conv module: LN, pw1, GLU (ring), causal dw conv, LN, SiLU, pw2
+    TRY(launch_ln_rows(e->y, d, ly.ln_conv_w, ly.ln_conv_b, eps, e->xn, d, M, (int)d, st));
+    TRY(gemm(ly.pw1, e->xn, e->h2, 2 * d, Epilogue{}));
+    TRY(launch_glu_ring(e->h2, M, (int)cf, (int)d, ly.glu_ring, (int)e->glu_cap, s, st));
+    TRY(launch_dwconv_ln_silu(ly.glu_ring, (int)e->glu_cap, M, (int)cf, (int)d, c.conv_kernel, s, ly.dw,
+                              ly.conv_ln_w, ly.conv_ln_b, eps, e->o2, st));
+    TRY(gemm(ly.pw2, e->o2, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}));
+    // macaron FF2 and the block's final LN
+    TRY(launch_ln_rows(e->y, d, ly.ln_ff2_w, ly.ln_ff2_b, eps, e->xn, d, M, (int)d, st));
+    TRY(gemm(ly.ff2_1, e->xn, e->h, dff, silu));
+    TRY(gemm(ly.ff2_2, e->h, e->y, d, Epilogue{kEpiResidual, e->y, 0.5f}));
+    TRY(launch_ln_rows(e->y, d, ly.ln_out_w, ly.ln_out_b, eps, e->x, d, M, (int)d, st));
+  }
+  TRY(launch_out_ring(e->x, M, (int)cf, (int)d, e->out_ring, (int)e->out_cap, s, st));
+  e->hist_cur ^= 1;
+  e->hist_frames = (int)std::min<int64_t>(kMelHistory, e->hist_frames + n_new);
+  e->total = t_new;
+  e->last_c = cf;
+  return kOk;
+}
+
+int sc_stream_encoder_output(const sc_stream_encoder *e, const float **frames, int64_t *rows, int64_t *d) {
+  if (!e || !frames) {
+    set_error("stream_encoder_output: invalid argument");
+    return kErrInvalid;
+  }
+  *frames = e->x;
+  if (rows) *rows = e->n_streams * e->last_c;
+  if (d) *d = e->cfg.d_model;
+  return kOk;
+}
+
+}  // extern "C"

@@ -6,6 +6,23 @@
 
 namespace sc {
 
+// GEMM epilogue applied to v = W x + bias, element-wise on the output:
+//   kEpiNone:     y = v
+//   kEpiSilu:     y = v * (1 / (1 + exp(-v)))        (simd_kernel.rs:817-839)
+//   kEpiResidual: y = res + alpha * v                 (res may alias y)
+enum : int { kEpiNone = 0, kEpiSilu = 1, kEpiResidual = 2 };
+struct Epilogue {
+  int op = kEpiNone;
+  const float *res = nullptr;
+  float alpha = 1.0f;
+};
+
+__device__ __forceinline__ float apply_epilogue(const Epilogue &e, float v, int64_t idx) {
+  if (e.op == kEpiSilu) return v * (1.0f / (1.0f + expf(-v)));
+  if (e.op == kEpiResidual) return e.res[idx] + e.alpha * v;
+  return v;
+}
+
 // q8_pack.cu
 int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k, int64_t block_bytes,
                      int64_t qoff, Q8Weights *w, cudaStream_t st);
@@ -29,6 +46,7 @@ struct SmallGemmArgs {
   int y_time_major;   // 1: y[col*ldy + n]; 0: y[n*ldy + col]
   int64_t ldy;
   int32_t *dots;      // non-null: write raw int32 block dots instead of y
+  Epilogue epi;
 };
 int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st);
 int small_gemm_status(unsigned *out);  // read and clear the kernels' status word
@@ -43,6 +61,7 @@ struct TcGemmArgs {
   float *y;
   int y_time_major;
   int64_t ldy;
+  Epilogue epi;
 };
 int tc_frame_tile(int64_t t);
 int gemm_tc(const TcGemmArgs &a, cudaStream_t st);

@@ -221,5 +221,53 @@ def attn_stream_ring(q, k_new, v_new, k_ring, v_ring, pos_p, q_bias, v_bias, *, 
     return out
 
 
-__all__ = ["q8_gemm", "Q8Mat", "Lin", "quantize", "AttnStreamKernel", "attn_stream_ring",
+class StreamEncoder:
+    """Device streaming encoder for n_streams lockstep streams -- the
+    StreamEncoder trait (streaming.rs:687-704): encode_new, frames, total."""
+
+    def __init__(self, model, n_streams: int):
+        from .model import ScEncoderConfig
+
+        self.model = model
+        self._table = model.table()
+        self._cfg = ScEncoderConfig.of(model.config)
+        h = ctypes.c_void_p()
+        check(lib.sc_stream_encoder_create(ctypes.byref(self._cfg), self._table, len(model.tensors), n_streams,
+                                           ctypes.byref(h)))
+        self._h = h
+        self.n_streams = n_streams
+        self.d = model.config.d_model
+
+    def encode_new(self, mel_new, t0: int, t1: int, fin: bool = False, stream=None) -> None:
+        """mel_new: CUDA tensor [n_streams, t1 - t0, feat_in] (f32)."""
+        check(lib.sc_stream_encoder_encode_new(self._h, mel_new.data_ptr() if mel_new is not None else None, t0, t1,
+                                               int(fin), _stream_ptr(stream)))
+
+    def total(self) -> int:
+        return int(lib.sc_stream_encoder_total(self._h))
+
+    def frames(self, stream_idx: int, frm: int, to: int) -> np.ndarray:
+        out = np.empty((to - frm, self.d), dtype=np.float32)
+        check(lib.sc_stream_encoder_frames(self._h, stream_idx, frm, to, _hp(out)))
+        return out
+
+    def output(self):
+        """(device pointer, rows, d) of the last step's frames [n_streams * c, d]."""
+        ptr, rows, d = ctypes.c_void_p(), ctypes.c_int64(), ctypes.c_int64()
+        check(lib.sc_stream_encoder_output(self._h, ctypes.byref(ptr), ctypes.byref(rows), ctypes.byref(d)))
+        return ptr.value, rows.value, d.value
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib.sc_stream_encoder_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+__all__ = ["StreamEncoder", "q8_gemm", "Q8Mat", "Lin", "quantize", "AttnStreamKernel", "attn_stream_ring",
            "SC_LAYOUT_FEATURE_MAJOR", "SC_LAYOUT_TIME_MAJOR", "_lib"]
