@@ -267,6 +267,16 @@ int sc_stream_encoder_frames(const sc_stream_encoder *e, int64_t stream_idx,
  * (stream-major); valid until the next encode_new. */
 int sc_stream_encoder_output(const sc_stream_encoder *e, const float **frames,
                              int64_t *rows, int64_t *d);
+/* Stage dumps of one layer, the device twin of the reference's
+ * STEALCODE_DUMP_DIR block dumps (streaming.rs:426-434, 462-631): after
+ * set_dump(layer) (-1 = off) every encode_new records, for that layer and
+ * all rows [n_streams * c][d]: 0 after FF1, 1 attention LayerNorm, 2
+ * attention output, 3 after the attention residual, 4 q projection, 5 conv
+ * module after dw conv + LN + SiLU, 6 after the conv residual, 7 block
+ * output.  dump() copies one stage to a host buffer; synchronous. */
+int sc_stream_encoder_set_dump(sc_stream_encoder *e, int32_t layer);
+int sc_stream_encoder_dump(const sc_stream_encoder *e, int32_t stage,
+                           float *out_host, int64_t *rows);
 int sc_stream_encoder_destroy(sc_stream_encoder *e);
 
 #ifdef __cplusplus

@@ -37,6 +37,7 @@ for _name, _res, _args in [
     ("orc_q8_gemm_scalar", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P]),
     ("orc_q8_gemm_simd_order", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P]),
     ("orc_q8_gemm", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P, c_int]),
+    ("orc_q8_gemm_order", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P, c_int, c_int]),
     ("orc_q8_block_dots", None, [_S, _S, _S, _P, _S, _S, _S, _P, _P]),
     ("orc_score_dot", c_float, [_P, _P, _P, _P, _P, _P, _S, c_float]),
     ("orc_softmax_v", None, [_P, _S, _S, _S, _S, _P, _S, _P]),
@@ -51,6 +52,13 @@ for _name, _res, _args in [
     ("orc_enc_total", _S, [_P]),
     ("orc_enc_frames", c_int, [_P, _S, _S, _P]),
     ("orc_enc_last", c_int, [_P, c_int, _P, ctypes.POINTER(_S)]),
+    ("orc_enc_set_dump", None, [_P, c_int]),
+    ("orc_enc_set_gemm_order", None, [_P, c_int]),
+    ("orc_enc_set_exp_mode", None, [_P, c_int]),
+    ("orc_set_exp_mode", None, [c_int]),
+    ("orc_get_exp_mode", c_int, []),
+    ("orc_expf", c_float, [c_float]),
+    ("orc_enc_dump", c_int, [_P, c_int, _P, ctypes.POINTER(_S)]),
     ("orc_ln_forward", None, [_P, _P, _P, c_float, _P, _S]),
     ("orc_dwconv_forward", None, [_P, _S, _S, _S, _S, _S, _P, _P]),
     ("orc_glu_from", None, [_P, _S, _S, _P]),
@@ -156,6 +164,21 @@ def attn_stream_testloop(q, kv, vv, pos_p, q_bias, v_bias, c, d, n_heads, scale,
     return out
 
 
+def set_exp_mode(correctly_rounded: bool) -> None:
+    """Exp of the standalone softmax/attention/SiLU functions in this thread
+    (False: libm expf as the reference; True: correctly rounded)."""
+    lib.orc_set_exp_mode(1 if correctly_rounded else 0)
+
+
+def expf(x: float, correctly_rounded: bool = False) -> float:
+    saved = lib.orc_get_exp_mode()
+    lib.orc_set_exp_mode(1 if correctly_rounded else 0)
+    try:
+        return lib.orc_expf(x)
+    finally:
+        lib.orc_set_exp_mode(saved)
+
+
 def num_cpus() -> int:
     return lib.orc_num_cpus()
 
@@ -178,6 +201,7 @@ class StreamingEncoder:
         self._cfg = OrcEncConfig(c.d_model, c.n_layers, c.n_heads, c.d_ff, c.feat_in, c.conv_channels,
                                  c.conv_kernel, c.conv_left, c.att_left, c.att_right, c.ln_eps)
         err = ctypes.create_string_buffer(256)
+        self._destroy = lib.orc_enc_destroy
         self._h = lib.orc_enc_create(ctypes.byref(self._cfg), self._table, len(model.tensors), err, 256)
         if not self._h:
             raise RuntimeError(err.value.decode())
@@ -204,7 +228,36 @@ class StreamingEncoder:
             raise ValueError("no such stage")
         return out[: c.value].copy()
 
+    def set_gemm_order(self, scalar: bool) -> None:
+        """False: the reference's GEMM dispatch (8-lane SIMD order for chunks
+        of <= 16 frames); True: q8_gemm_scalar's arithmetic for every linear."""
+        lib.orc_enc_set_gemm_order(self._h, 1 if scalar else 0)
+
+    def set_exp_mode(self, correctly_rounded: bool) -> None:
+        """False: libm expf (the reference on glibc); True: correctly rounded
+        exp, as the device computes it."""
+        lib.orc_enc_set_exp_mode(self._h, 1 if correctly_rounded else 0)
+
+    def set_device_rounding(self) -> None:
+        """Scalar-order linears and correctly rounded exp: the device's
+        rounding, one ulp away from the reference's dispatch in rare places."""
+        self.set_gemm_order(True)
+        self.set_exp_mode(True)
+
+    def set_dump(self, layer: int) -> None:
+        lib.orc_enc_set_dump(self._h, layer)
+
+    def dump(self, stage: int) -> np.ndarray:
+        c = ctypes.c_size_t()
+        out = np.empty((16, self.d), dtype=np.float32)
+        if lib.orc_enc_dump(self._h, stage, _p(out), ctypes.byref(c)):
+            raise ValueError("no dump recorded")
+        return out[: c.value].copy()
+
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib.orc_enc_destroy(self._h)
+        # the destroy function is held by the instance: module globals may
+        # already be gone when this runs at interpreter exit
+        h, destroy = getattr(self, "_h", None), getattr(self, "_destroy", None)
+        if h and destroy:
+            destroy(h)
             self._h = None

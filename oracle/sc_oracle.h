@@ -26,6 +26,14 @@
 extern "C" {
 #endif
 
+/* exp as the oracle evaluates it: mode 0 (default) is libm expf, what the
+ * reference's f32::exp and Simd::exp call on Linux/glibc; mode 1 is the
+ * correctly rounded exp, (float)exp((double)x), which differs from glibc's
+ * expf by one ulp for about 6 inputs in 10^4.  The mode is per thread. */
+void orc_set_exp_mode(int correctly_rounded);
+int orc_get_exp_mode(void);
+float orc_expf(float x);
+
 /* gguf.rs:365-397 */
 float orc_f16_to_f32(uint16_t h);
 /* sgemm_kernel.rs:209-221 (test helper half_f32_to_u16: truncating) */
@@ -63,6 +71,12 @@ void orc_q8_gemm_simd_order(size_t m, size_t k, size_t n, const uint8_t *w,
 void orc_q8_gemm(size_t m, size_t k, size_t n, const uint8_t *w,
                  size_t padded_row, size_t block_bytes, size_t qoff,
                  const float *x, float *y, int nthreads);
+/* orc_q8_gemm with the dispatch pinned: scalar = 0 is the reference's own
+ * dispatch (above); scalar = 1 always takes q8_gemm_scalar's arithmetic
+ * (sgemm_kernel.rs:185-196), threaded over rows. */
+void orc_q8_gemm_order(size_t m, size_t k, size_t n, const uint8_t *w,
+                       size_t padded_row, size_t block_bytes, size_t qoff,
+                       const float *x, float *y, int nthreads, int scalar);
 
 /* Per-block integer dot products dots[(i*n + nj)*nblocks + b] =
  * sum_j w[i, 32b+j] * xq[nj, 32b+j] (the exact integer that the scalar

@@ -44,7 +44,7 @@ void orc_softmax_v(const float *srow, size_t k0, size_t k1, size_t n_heads,
     float *e = malloc((band ? band : 1) * sizeof(float));
     float sum = 0.0f;
     for (size_t kk = k0, i = 0; kk < k1; kk++, i++) {
-        float val = expf(srow[kk * n_heads + h] - maxv);
+        float val = orc_expf(srow[kk * n_heads + h] - maxv);
         e[i] = val;
         sum += val;
     }
@@ -153,7 +153,7 @@ void orc_attn_stream_testloop(const float *q, const float *kv,
                 exps[kk] = sc;
             }
             for (size_t kk = k0; kk < k1; kk++) {
-                exps[kk] = expf(exps[kk] - maxv);
+                exps[kk] = orc_expf(exps[kk] - maxv);
                 sum += exps[kk];
             }
             float inv = 1.0f / sum;

@@ -60,7 +60,7 @@ void orc_ln_forward(const float *x, const float *w, const float *b, float eps,
 
 /* simd_kernel.rs:817-839: v * (1 + exp(-v)).recip() */
 void orc_silu_inplace(float *v, size_t n) {
-    for (size_t i = 0; i < n; i++) v[i] = v[i] * (1.0f / (1.0f + expf(-v[i])));
+    for (size_t i = 0; i < n; i++) v[i] = v[i] * (1.0f / (1.0f + orc_expf(-v[i])));
 }
 
 static void relu_inplace(float *v, size_t n) {
@@ -72,7 +72,7 @@ void orc_glu_from(const float *h, size_t t, size_t d, float *out) {
     for (size_t tt = 0; tt < t; tt++)
         for (size_t i = 0; i < d; i++) {
             float gate = h[tt * 2 * d + i], val = h[tt * 2 * d + d + i];
-            out[tt * d + i] = gate * (1.0f / (1.0f + expf(-val)));
+            out[tt * d + i] = gate * (1.0f / (1.0f + orc_expf(-val)));
         }
 }
 
@@ -157,8 +157,12 @@ struct orc_enc {
     fcache out;    /* last block output frames */
     size_t total;
     size_t last_c;
+    int scalar_gemm; /* 1: every linear in q8_gemm_scalar's arithmetic */
+    int exp_cr;      /* exp mode of this encoder's steps (orc_set_exp_mode) */
     float *last_pre; /* [c, d] */
     float **last_blk;
+    int dump_layer;
+    float *dump[8]; /* stages of dump_layer, [c, d] each */
 };
 
 static const orc_tensor *find(const orc_tensor *t, int n, const char *name) {
@@ -231,19 +235,19 @@ static int get_conv(const orc_tensor *t, int n, const char *base, size_t inp,
 }
 
 /* Lin::forward_t (nemotron/weights.rs:305-337): y_t [out, t] = W x_t [inp, t] + b */
-static void lin_forward_t(const lin_t *l, const float *x_t, size_t t, float *y_t) {
+static void lin_forward_t(const orc_enc *e, const lin_t *l, const float *x_t, size_t t, float *y_t) {
     size_t padded_row = (l->row_len + 31) / 32 * 34;
-    orc_q8_gemm(l->rows, l->row_len, t, l->w, padded_row, 34, 2, x_t, y_t, 0);
+    orc_q8_gemm_order(l->rows, l->row_len, t, l->w, padded_row, 34, 2, x_t, y_t, 0, e->scalar_gemm);
     if (l->bias)
         for (size_t j = 0; j < l->rows; j++)
             for (size_t tt = 0; tt < t; tt++) y_t[j * t + tt] += l->bias[j];
 }
 
 /* time-major [t, inp] -> time-major [t, out] through forward_t's layout */
-static void lin_tm(const lin_t *l, const float *x, size_t t, float *y, float *scratch_a,
+static void lin_tm(const orc_enc *e, const lin_t *l, const float *x, size_t t, float *y, float *scratch_a,
                    float *scratch_b) {
     transpose(x, t, l->row_len, scratch_a);
-    lin_forward_t(l, scratch_a, t, scratch_b);
+    lin_forward_t(e, l, scratch_a, t, scratch_b);
     transpose(scratch_b, l->rows, t, y);
 }
 
@@ -325,7 +329,7 @@ static float *pre_encode_forward(const orc_enc *e, const float *mel, size_t t_me
     free(x6);
     float *y = malloc(t * d * sizeof(float));
     float *sa = malloc(t * flat * sizeof(float)), *sb = malloc(t * d * sizeof(float));
-    lin_tm(&e->pre_out, flat_x, t, y, sa, sb);
+    lin_tm(e, &e->pre_out, flat_x, t, y, sa, sb);
     free(sa);
     free(sb);
     free(flat_x);
@@ -428,6 +432,7 @@ orc_enc *orc_enc_create(const orc_enc_config *cfg, const orc_tensor *t, int n, c
         fc_init(&e->glu[i], d);
     }
     fc_init(&e->out, d);
+    e->dump_layer = -1;
     return e;
 }
 
@@ -449,12 +454,21 @@ void orc_enc_destroy(orc_enc *e) {
     free(e->out.data);
     free(e->last_pre);
     free(e->layers);
+    for (int i = 0; i < 8; i++) free(e->dump[i]);
     free(e);
 }
 
 /* ------------------------------------------------------------------ */
 /* block_new: streaming.rs:395-680                                      */
 /* ------------------------------------------------------------------ */
+static void dump_stage(orc_enc *e, size_t li, int stage, const float *src, size_t c, size_t width) {
+    if ((int)li != e->dump_layer) return;
+    size_t d = (size_t)e->cfg.d_model;
+    free(e->dump[stage]);
+    e->dump[stage] = malloc(c * d * sizeof(float));
+    for (size_t j = 0; j < c; j++) memcpy(e->dump[stage] + j * d, src + j * width, d * sizeof(float));
+}
+
 static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_t t_new,
                       size_t k_lo, size_t k_hi, long pos_lo, float *out) {
     const layer_t *L = &e->layers[li];
@@ -469,20 +483,23 @@ static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_
     /* macaron FF1 (:436-462) */
     for (size_t j = 0; j < c; j++) orc_ln_forward(input + j * d, L->norm_ff1.w, L->norm_ff1.b, eps, y + j * d, d);
     transpose(y, c, d, sa);
-    lin_forward_t(&L->ff1_1, sa, c, h); /* [dff, c] */
+    lin_forward_t(e, &L->ff1_1, sa, c, h); /* [dff, c] */
     orc_silu_inplace(h, dff * c);
-    lin_forward_t(&L->ff1_2, h, c, sb); /* [d, c] */
+    lin_forward_t(e, &L->ff1_2, h, c, sb); /* [d, c] */
     transpose(sb, d, c, f);
     for (size_t i = 0; i < c * d; i++) y[i] = input[i] + 0.5f * f[i];
+    dump_stage(e, li, 0, y, c, d);
 
     /* rel-pos MHSA (:464-600) */
     float *ln_new = malloc(c * d * sizeof(float));
     float *k_new = malloc(c * d * sizeof(float)), *v_new = malloc(c * d * sizeof(float)),
           *q_new = malloc(c * d * sizeof(float));
     for (size_t j = 0; j < c; j++) orc_ln_forward(y + j * d, L->norm_att.w, L->norm_att.b, eps, ln_new + j * d, d);
-    lin_tm(&L->k, ln_new, c, k_new, sa, sb);
-    lin_tm(&L->v, ln_new, c, v_new, sa, sb);
-    lin_tm(&L->q, ln_new, c, q_new, sa, sb);
+    lin_tm(e, &L->k, ln_new, c, k_new, sa, sb);
+    lin_tm(e, &L->v, ln_new, c, v_new, sa, sb);
+    lin_tm(e, &L->q, ln_new, c, q_new, sa, sb);
+    dump_stage(e, li, 1, ln_new, c, d);
+    dump_stage(e, li, 4, q_new, c, d);
     size_t band = k_hi - k_lo;
     float *scores = calloc(c * band * nh, sizeof(float));
     const float **vrows = malloc(band * sizeof(float *));
@@ -513,8 +530,10 @@ static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_
             orc_softmax_v(row, k0, k1, nh, hh, vrows, hd, attn + qi * d + ho);
         }
     }
-    lin_tm(&L->out, attn, c, tmp, sa, sb);
+    dump_stage(e, li, 2, attn, c, d);
+    lin_tm(e, &L->out, attn, c, tmp, sa, sb);
     for (size_t i = 0; i < c * d; i++) y[i] += tmp[i];
+    dump_stage(e, li, 3, y, c, d);
 
     /* conv module (:602-646) */
     size_t conv_left = (size_t)e->cfg.conv_left, kh = (size_t)e->cfg.conv_kernel;
@@ -522,7 +541,7 @@ static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_
     float *lnc = malloc(c * d * sizeof(float)), *h2 = malloc(c * 2 * d * sizeof(float));
     float *glu_new = malloc(c * d * sizeof(float));
     for (size_t j = 0; j < c; j++) orc_ln_forward(y + j * d, L->norm_conv.w, L->norm_conv.b, eps, lnc + j * d, d);
-    lin_tm(&L->pw1, lnc, c, h2, sa, sb);
+    lin_tm(e, &L->pw1, lnc, c, h2, sa, sb);
     orc_glu_from(h2, c, d, glu_new);
     float *glu = malloc(n_glu * d * sizeof(float));
     for (size_t fr = conv_lo; fr < s; fr++) memcpy(glu + (fr - conv_lo) * d, fc_row(&e->glu[li], fr), d * sizeof(float));
@@ -535,19 +554,22 @@ static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_
         orc_ln_forward(conv + (old_glu + j) * d, L->conv_ln.w, L->conv_ln.b, eps, o2 + j * d, d);
         orc_silu_inplace(o2 + j * d, d);
     }
-    lin_tm(&L->pw2, o2, c, tmp, sa, sb);
+    dump_stage(e, li, 5, o2, c, d);
+    lin_tm(e, &L->pw2, o2, c, tmp, sa, sb);
     for (size_t i = 0; i < c * d; i++) y[i] += tmp[i];
+    dump_stage(e, li, 6, y, c, d);
 
     /* macaron FF2 + final LN (:648-679) */
     float *y2 = malloc(c * d * sizeof(float));
     for (size_t j = 0; j < c; j++) orc_ln_forward(y + j * d, L->norm_ff2.w, L->norm_ff2.b, eps, y2 + j * d, d);
     transpose(y2, c, d, sa);
-    lin_forward_t(&L->ff2_1, sa, c, h);
+    lin_forward_t(e, &L->ff2_1, sa, c, h);
     orc_silu_inplace(h, dff * c);
-    lin_forward_t(&L->ff2_2, h, c, sb);
+    lin_forward_t(e, &L->ff2_2, h, c, sb);
     transpose(sb, d, c, f);
     for (size_t i = 0; i < c * d; i++) y2[i] = y[i] + 0.5f * f[i];
     for (size_t j = 0; j < c; j++) orc_ln_forward(y2 + j * d, L->norm_out.w, L->norm_out.b, eps, out + j * d, d);
+    dump_stage(e, li, 7, out, c, d);
 
     /* caches: the caller appends K/V and GLU after the block (:307-312) */
     fc_append(&e->kc[li], k_new, c);
@@ -562,8 +584,20 @@ static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_
 /* ------------------------------------------------------------------ */
 /* encode_new: streaming.rs:137-383                                     */
 /* ------------------------------------------------------------------ */
+static int encode_new(orc_enc *e, const float *mel, size_t mel_frames, size_t n_mels, size_t t0,
+                      size_t t1, int fin);
+
 int orc_enc_encode_new(orc_enc *e, const float *mel, size_t mel_frames, size_t n_mels, size_t t0,
                        size_t t1, int fin) {
+    int saved = orc_get_exp_mode();
+    orc_set_exp_mode(e->exp_cr);
+    int rc = encode_new(e, mel, mel_frames, n_mels, t0, t1, fin);
+    orc_set_exp_mode(saved);
+    return rc;
+}
+
+static int encode_new(orc_enc *e, const float *mel, size_t mel_frames, size_t n_mels, size_t t0,
+                      size_t t1, int fin) {
     size_t d = (size_t)e->cfg.d_model, nl = (size_t)e->cfg.n_layers;
     size_t s = t0 / 8, ecount = s + (t1 - t0 + 7) / 8;
     if (s != e->total) return -6;
@@ -603,7 +637,7 @@ int orc_enc_encode_new(orc_enc *e, const float *mel, size_t mel_frames, size_t n
         float *sa = malloc(e->n_pos * d * sizeof(float)), *sb = malloc(e->n_pos * d * sizeof(float));
         for (size_t b = 0; b < nl; b++) {
             e->pos_p[b] = malloc(e->n_pos * d * sizeof(float));
-            lin_tm(&e->layers[b].pos, pet, e->n_pos, e->pos_p[b], sa, sb);
+            lin_tm(e, &e->layers[b].pos, pet, e->n_pos, e->pos_p[b], sa, sb);
         }
         free(sa), free(sb), free(pet);
     }
@@ -651,5 +685,18 @@ int orc_enc_last(const orc_enc *e, int which, float *out, size_t *c_out) {
     const float *src = which == 0 ? e->last_pre : (which - 1 < e->cfg.n_layers ? e->last_blk[which - 1] : NULL);
     if (!src) return -1;
     memcpy(out, src, e->last_c * d * sizeof(float));
+    return 0;
+}
+
+void orc_enc_set_gemm_order(orc_enc *e, int scalar) { e->scalar_gemm = scalar ? 1 : 0; }
+
+void orc_enc_set_exp_mode(orc_enc *e, int correctly_rounded) { e->exp_cr = correctly_rounded ? 1 : 0; }
+
+void orc_enc_set_dump(orc_enc *e, int layer) { e->dump_layer = layer; }
+
+int orc_enc_dump(const orc_enc *e, int stage, float *out, size_t *c_out) {
+    if (stage < 0 || stage >= 8 || !e->dump[stage]) return -1;
+    *c_out = e->last_c;
+    memcpy(out, e->dump[stage], e->last_c * (size_t)e->cfg.d_model * sizeof(float));
     return 0;
 }

@@ -57,6 +57,21 @@ int orc_enc_frames(const orc_enc *e, size_t from, size_t to, float *out);
  * output of the new frames [c, d]; 1 + b = block b output [c, d]. */
 int orc_enc_last(const orc_enc *e, int which, float *out, size_t *c_out);
 
+/* Arithmetic of the Q8_0 linears: 0 (default) the reference's dispatch
+ * (the 8-lane SIMD order for 7-frame chunks, simd_kernel.rs:93-230),
+ * 1 the scalar oracle's order (sgemm_kernel.rs:185-196) for every linear. */
+void orc_enc_set_gemm_order(orc_enc *e, int scalar);
+/* exp of this encoder's SiLU, GLU and softmax: 0 (default) libm expf as the
+ * reference on glibc, 1 correctly rounded (orc_set_exp_mode). */
+void orc_enc_set_exp_mode(orc_enc *e, int correctly_rounded);
+
+/* Stage dumps of one layer of the last step (the reference's
+ * STEALCODE_DUMP_DIR block dumps): 0 after FF1, 1 attention LN, 2 attention
+ * output, 3 after the attention residual, 4 q projection, 5 conv module
+ * after dw + LN + SiLU, 6 after the conv residual, 7 block output. */
+void orc_enc_set_dump(orc_enc *e, int layer);
+int orc_enc_dump(const orc_enc *e, int stage, float *out, size_t *c_out);
+
 /* Helper kernels, exposed for unit checks. */
 void orc_ln_forward(const float *x, const float *w, const float *b,
                     float eps, float *out, size_t d);

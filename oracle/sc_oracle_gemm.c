@@ -17,6 +17,14 @@
 
 /* ------------------------------------------------------------------ */
 /* f16 decode: gguf.rs:365-397                                         */
+static __thread int g_exp_cr;
+
+void orc_set_exp_mode(int correctly_rounded) { g_exp_cr = correctly_rounded ? 1 : 0; }
+
+int orc_get_exp_mode(void) { return g_exp_cr; }
+
+float orc_expf(float x) { return g_exp_cr ? (float)exp((double)x) : expf(x); }
+
 /* ------------------------------------------------------------------ */
 float orc_f16_to_f32(uint16_t h) {
     uint32_t sign = (uint32_t)(h >> 15);
@@ -427,6 +435,12 @@ static void quant_chunk(void *vctx, size_t nj) {
 void orc_q8_gemm(size_t m, size_t k, size_t n, const uint8_t *w,
                  size_t padded_row, size_t block_bytes, size_t qoff,
                  const float *x, float *y, int nthreads) {
+    orc_q8_gemm_order(m, k, n, w, padded_row, block_bytes, qoff, x, y, nthreads, 0);
+}
+
+void orc_q8_gemm_order(size_t m, size_t k, size_t n, const uint8_t *w,
+                       size_t padded_row, size_t block_bytes, size_t qoff,
+                       const float *x, float *y, int nthreads, int scalar) {
     if (m == 0 || k == 0 || n == 0) return;
     int threads = nthreads > 0 ? nthreads : orc_num_cpus();
     size_t nblocks = (k + 31) / 32;
@@ -434,7 +448,7 @@ void orc_q8_gemm(size_t m, size_t k, size_t n, const uint8_t *w,
     float *dx = calloc(n * nblocks, sizeof(float));
     gemm_ctx g = {m, k, n, padded_row, block_bytes, qoff, nblocks, 0,
                   w, xq, dx, x, xq, dx, y};
-    int fast = (m % 8 == 0) && (k % 32 == 0) && (n <= 16);
+    int fast = !scalar && (m % 8 == 0) && (k % 32 == 0) && (n <= 16);
     /* simd_kernel.rs:129-144: columns quantised in parallel when
      * n*nblocks >= 1024; the scalar path quantises serially. */
     if (fast && n * nblocks >= 1024)

@@ -74,6 +74,8 @@ SIGNATURES = {
     "sc_stream_encoder_total": (c_int64, [_P]),
     "sc_stream_encoder_frames": (c_int, [_P, _I, _I, _I, _P]),
     "sc_stream_encoder_output": (c_int, [_P, POINTER(c_void_p), POINTER(c_int64), POINTER(c_int64)]),
+    "sc_stream_encoder_set_dump": (c_int, [_P, c_int32]),
+    "sc_stream_encoder_dump": (c_int, [_P, c_int32, _P, POINTER(c_int64)]),
     "sc_stream_encoder_destroy": (c_int, [_P]),
     "sc_attn_stream": (c_int, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, c_float,
                                _I, _I, _I, _I, _I, _I, _I, _P, _P]),

@@ -10,53 +10,25 @@
 //
 // with the chunk-aligned band [sat(q/chunk - left_chunks)*chunk,
 // min((q/chunk + 1)*chunk, k_hi)).  One CTA per (head, stream), one thread
-// per head-dim element.  Each K, V and pos row of the head is read exactly
-// once per CTA and used by all the chunk's queries:
-//   A. QK^T: warps take band rows; each lane holds HD/32 dims of every
-//      query's (q + u); one multi-value butterfly reduces all queries'
-//      partials;
-//   B. pos term R[q, p] = (q + v) . pos_p[p] over the pos rows the chunk
-//      touches (the Toeplitz structure: c + band - 1 rows, not c * band);
-//   C. band mask + softmax per query (exp, max, 1/sum as the reference);
-//   D. P.V with one thread per dim, V rows streamed once.
+// per head-dim element.  Every value is rounded exactly as the reference's
+// CPU kernels round it, so the output is bit-equal to score_dot + softmax_v
+// (simd_kernel.rs:930-1104):
+//   A. scores: a half-warp owns a tile of KT keys x CQ queries; its lane l is
+//      the reference's SIMD lane l (dims l, l+16, ...) and keeps one
+//      accumulator per (query, key) with the reference's two chained FMAs
+//      acc = fma(q+u, k, fma(q+v, p, acc)); the 16 lane accumulators are
+//      then summed in lane order and scaled.  Each K row is read once per
+//      CTA, pos rows about twice (neighbouring tiles share a diagonal).
+//   C. band mask + softmax per query: max, exp, the sum taken sequentially
+//      over the band, inv = 1/sum, weights e*inv.
+//   D. P.V with one thread per dim: acc = fma(w, v, acc) over the band in
+//      order, V rows streamed once.
 // In ring mode the K/V of the chunk's new frames come from the projection
 // output and are written into the stream's HBM ring (slot = frame % cap);
 // older band frames are read from the ring.
 #include "sc_kernels.cuh"
 
 namespace sc {
-
-// Reduce NV per-lane values over the warp in log2(NV) exchange steps (each
-// step halves the values a lane carries), then plain xor steps.  Afterwards
-// the lane holds the full sum of value index multi_idx(lane).
-template <int NV>
-__device__ __forceinline__ float multi_reduce(float (&v)[NV], int lane) {
-#pragma unroll
-  for (int cnt = NV, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
-    const int half = cnt >> 1;
-    const bool up = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < half; i++) {
-      float send = up ? v[i] : v[i + half];
-      float keep = up ? v[i + half] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  float r = v[0];
-  constexpr int steps = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : NV == 16 ? 4 : 5;
-#pragma unroll
-  for (int off = 16 >> steps; off > 0; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
-  return r;
-}
-
-template <int NV>
-__device__ __forceinline__ int multi_idx(int lane) {
-  int idx = 0;
-#pragma unroll
-  for (int cnt = NV, off = 16; cnt > 1; cnt >>= 1, off >>= 1)
-    if (lane & off) idx += cnt >> 1;
-  return idx;
-}
 
 __device__ __forceinline__ void band_of(int64_t qq, int64_t chunk, int64_t left_chunks,
                                         int64_t k_hi, int64_t &kmin, int64_t &kmax) {
@@ -66,15 +38,33 @@ __device__ __forceinline__ void band_of(int64_t qq, int64_t chunk, int64_t left_
   kmax = hi < k_hi ? hi : k_hi;
 }
 
-// HD = head_dim (one thread per dim, HD/32 warps); CQ = queries padded.
+constexpr int kLanes = 16;        // the reference's SIMD width for score_dot
+constexpr int kRedStride = 17;    // padded row of the lane-sum buffer
+
+template <int CQ>
+struct AttnTile {
+  static constexpr int KT = 64 / CQ;  // keys per half-warp tile
+};
+
+template <int HD, int CQ>
+__host__ __device__ constexpr size_t attn_smem_floats(int band) {
+  return (size_t)CQ * band + 2 * (size_t)CQ * HD + (size_t)(HD / kLanes) * CQ * AttnTile<CQ>::KT * kRedStride;
+}
+
+// HD = head_dim (one thread per dim); CQ = queries padded (8 or 16).
 template <int HD, int CQ>
 __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
   constexpr int NW = HD / 32;
-  constexpr int VPL = HD / 32;  // dims per lane in phases A/B
+  constexpr int NHW = HD / kLanes;  // half-warps
+  constexpr int KT = AttnTile<CQ>::KT;
+  constexpr int NCH = HD / kLanes;  // 16-dim chunks per head row
+  constexpr int NPV = CQ + KT - 1;  // pos rows one tile touches
   extern __shared__ __align__(16) float sm[];
   const int band = (int)(p.k_hi - p.k_lo);
-  float *s_qk = sm;                      // [CQ][band]  scores, then probabilities
-  float *s_r = sm + CQ * band;           // [CQ][np]
+  float *s_qk = sm;                   // [CQ][band]  scores, then weights
+  float *s_qu = sm + CQ * band;       // [CQ][HD]    q + u
+  float *s_qv = s_qu + CQ * HD;       // [CQ][HD]    q + v
+  float *s_red = s_qv + CQ * HD;      // [NHW][CQ*KT][kRedStride]
   const int h = blockIdx.x;
   const int64_t z = blockIdx.y;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -86,95 +76,102 @@ __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
     return ring + (z * p.cap + fr % p.cap) * (int64_t)p.d + hoff;
   };
 
-  // ---- A: QK^T over the band ----
-  {
-    float qa[CQ][VPL];
-#pragma unroll
-    for (int j = 0; j < CQ; j++)
-#pragma unroll
-      for (int e = 0; e < VPL; e++) {
-        int dim = lane * VPL + e;
-        qa[j][e] = j < c ? p.q[(z * c + j) * p.ldq + hoff + dim] + p.u[hoff + dim] : 0.0f;
-      }
-    for (int kk = warp; kk < band; kk += NW) {
-      int64_t fr = p.k_lo + kk;
-      const float *kr = key_row(p.k_ring, p.k_new, fr);
-      float kv[VPL];
-#pragma unroll
-      for (int e = 0; e < VPL; e++) kv[e] = kr[lane * VPL + e];
-      if (p.k_ring && fr >= p.s) {
-        float *dst = p.k_ring + (z * p.cap + fr % p.cap) * (int64_t)p.d + hoff;
-#pragma unroll
-        for (int e = 0; e < VPL; e++) dst[lane * VPL + e] = kv[e];
-      }
-      float part[CQ];
-#pragma unroll
-      for (int j = 0; j < CQ; j++) {
-        float a = 0.0f;
-#pragma unroll
-        for (int e = 0; e < VPL; e++) a = fmaf(qa[j][e], kv[e], a);
-        part[j] = a;
-      }
-      float r = multi_reduce<CQ>(part, lane);
-      int idx = multi_idx<CQ>(lane);
-      constexpr int lowmask = (32 / CQ) - 1;
-      if ((lane & lowmask) == 0 && idx < c) s_qk[idx * band + kk] = r;
-    }
+  for (int j = 0; j < CQ; j++) {
+    float qd = j < c ? p.q[(z * c + j) * p.ldq + hoff + t] : 0.0f;
+    s_qu[j * HD + t] = j < c ? __fadd_rn(qd, p.u[hoff + t]) : 0.0f;
+    s_qv[j * HD + t] = j < c ? __fadd_rn(qd, p.v[hoff + t]) : 0.0f;
   }
-  // ---- B: pos term over the touched pos rows ----
+  __syncthreads();
+
+  // ---- A: scores, half-warp tiles of KT keys x CQ queries ----
   {
-    float qb[CQ][VPL];
+    const int hw = t / kLanes, l = t % kLanes;
+    float *red = s_red + hw * (CQ * KT * kRedStride);
+    // pos row of (query j, key kt0 + b) is prow0 - kt0 + j - b
+    const int64_t prow0 = p.s + p.pos_off - p.k_lo - p.pr_lo;
+    // Every half-warp takes the same number of rounds (the __syncwarp()s
+    // below need both halves of the warp); a tile past the band computes
+    // on clamped rows and stores nothing.
+    for (int base = 0; base < band; base += NHW * KT) {
+      const int kt0 = base + hw * KT;
+      float acc[CQ][KT];
 #pragma unroll
-    for (int j = 0; j < CQ; j++)
+      for (int j = 0; j < CQ; j++)
 #pragma unroll
-      for (int e = 0; e < VPL; e++) {
-        int dim = lane * VPL + e;
-        qb[j][e] = j < c ? p.q[(z * c + j) * p.ldq + hoff + dim] + p.v[hoff + dim] : 0.0f;
+        for (int b = 0; b < KT; b++) acc[j][b] = 0.0f;
+      const float *krow[KT];
+      float *kdst[KT];
+#pragma unroll
+      for (int b = 0; b < KT; b++) {
+        const int64_t fr = p.k_lo + (kt0 + b < band ? kt0 + b : band - 1);
+        krow[b] = key_row(p.k_ring, p.k_new, fr);
+        kdst[b] = (p.k_ring && fr >= p.s && kt0 + b < band)
+                      ? p.k_ring + (z * p.cap + fr % p.cap) * (int64_t)p.d + hoff
+                      : nullptr;
       }
-    for (int pi = warp; pi < p.np; pi += NW) {
-      const float *pr = p.pos_p + (p.pr_lo + pi) * (int64_t)p.d + hoff;
-      float pv[VPL];
+      const float *prow[NPV];
 #pragma unroll
-      for (int e = 0; e < VPL; e++) pv[e] = pr[lane * VPL + e];
-      float part[CQ];
-#pragma unroll
-      for (int j = 0; j < CQ; j++) {
-        float a = 0.0f;
-#pragma unroll
-        for (int e = 0; e < VPL; e++) a = fmaf(qb[j][e], pv[e], a);
-        part[j] = a;
+      for (int m = 0; m < NPV; m++) {
+        int64_t pi = prow0 - kt0 - (KT - 1) + m;  // masked pairs may fall outside
+        pi = pi < 0 ? 0 : (pi >= p.np ? p.np - 1 : pi);
+        prow[m] = p.pos_p + (p.pr_lo + pi) * (int64_t)p.d + hoff;
       }
-      float r = multi_reduce<CQ>(part, lane);
-      int idx = multi_idx<CQ>(lane);
-      constexpr int lowmask = (32 / CQ) - 1;
-      if ((lane & lowmask) == 0 && idx < c) s_r[idx * p.np + pi] = r;
+#pragma unroll 1
+      for (int ch = 0; ch < NCH; ch++) {
+        const int i = ch * kLanes + l;
+        float kv[KT], pv[NPV];
+#pragma unroll
+        for (int b = 0; b < KT; b++) kv[b] = krow[b][i];
+#pragma unroll
+        for (int m = 0; m < NPV; m++) pv[m] = prow[m][i];
+#pragma unroll
+        for (int b = 0; b < KT; b++)
+          if (kdst[b]) kdst[b][i] = kv[b];
+#pragma unroll
+        for (int j = 0; j < CQ; j++) {
+          const float qu = s_qu[j * HD + i], qv = s_qv[j * HD + i];
+#pragma unroll
+          for (int b = 0; b < KT; b++) {
+            const float inner = __fmaf_rn(qv, pv[j - b + KT - 1], acc[j][b]);
+            acc[j][b] = __fmaf_rn(qu, kv[b], inner);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < CQ; j++)
+#pragma unroll
+        for (int b = 0; b < KT; b++) red[(j * KT + b) * kRedStride + l] = acc[j][b];
+      __syncwarp();
+      for (int pr = l; pr < CQ * KT; pr += kLanes) {
+        const int j = pr / KT, b = pr % KT;
+        float sum = red[pr * kRedStride];
+#pragma unroll
+        for (int q = 1; q < kLanes; q++) sum = __fadd_rn(sum, red[pr * kRedStride + q]);
+        if (j < c && kt0 + b < band) s_qk[j * band + kt0 + b] = __fmul_rn(sum, p.scale);
+      }
+      __syncwarp();
     }
   }
   __syncthreads();
-  // ---- C: band mask + softmax per query ----
+  // ---- C: band mask + softmax per query (simd_kernel.rs:1010-1104) ----
   for (int j = warp; j < c; j += NW) {
     int64_t qq = p.s + j, kmin, kmax;
     band_of(qq, p.chunk, p.left_chunks, p.k_hi, kmin, kmax);
     int k0 = (int)(kmin - p.k_lo), k1 = (int)(kmax - p.k_lo);
     float mx = -INFINITY;
-    for (int kk = k0 + lane; kk < k1; kk += 32) {
-      int pi = (int)(qq + p.pos_off - (p.k_lo + kk) - p.pr_lo);
-      float sc = (s_qk[j * band + kk] + s_r[j * p.np + pi]) * p.scale;
-      s_qk[j * band + kk] = sc;
-      mx = fmaxf(mx, sc);
-    }
+    for (int kk = k0 + lane; kk < k1; kk += 32) mx = fmaxf(mx, s_qk[j * band + kk]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.0f;
-    for (int kk = k0 + lane; kk < k1; kk += 32) {
-      float e = expf(s_qk[j * band + kk] - mx);
-      s_qk[j * band + kk] = e;
-      sum += e;
+    for (int kk = k0 + lane; kk < k1; kk += 32) s_qk[j * band + kk] = exp_rn(__fsub_rn(s_qk[j * band + kk], mx));
+    __syncwarp();
+    float inv = 0.0f;
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (int kk = k0; kk < k1; kk++) sum = __fadd_rn(sum, s_qk[j * band + kk]);
+      inv = __fdiv_rn(1.0f, sum);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    float inv = 1.0f / sum;
-    for (int kk = k0 + lane; kk < k1; kk += 32) s_qk[j * band + kk] *= inv;
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int kk = k0 + lane; kk < k1; kk += 32) s_qk[j * band + kk] = __fmul_rn(s_qk[j * band + kk], inv);
   }
   __syncthreads();
   // ---- D: P.V, one thread per head dim ----
@@ -196,7 +193,7 @@ __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
       if (p.v_ring && fr >= p.s) p.v_ring[(z * p.cap + fr % p.cap) * (int64_t)p.d + hoff + t] = vv;
 #pragma unroll
       for (int j = 0; j < CQ; j++)
-        if (kk >= k0s[j] && kk < k1s[j]) acc[j] = fmaf(s_qk[j * band + kk], vv, acc[j]);
+        if (kk >= k0s[j] && kk < k1s[j]) acc[j] = __fmaf_rn(s_qk[j * band + kk], vv, acc[j]);
     }
 #pragma unroll
     for (int j = 0; j < CQ; j++)
@@ -257,7 +254,7 @@ int attn_prepare(AttnParams &p, int64_t n_pos) {
 template <int HD, int CQ>
 static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
   int band = (int)(p.k_hi - p.k_lo);
-  size_t smem = (size_t)CQ * (band + p.np) * sizeof(float);
+  size_t smem = attn_smem_floats<HD, CQ>(band) * sizeof(float);
   auto kern = attn_stream_kernel<HD, CQ>;
   static size_t smem_set[64] = {};
   int dev = 0;

@@ -10,7 +10,8 @@
 //   mel_window_kernel         pre-encode mel window     (streaming.rs:182-207)
 //   conv2d_3x3s2_kernel       conv0 and the depthwise convs 2/5
 //                                                       (nemotron/weights.rs:418-523)
-//   bias_relu_kernel          bias + ReLU after the pointwise convs
+//   pw_conv_relu_kernel       pointwise convs 3/6 as an f32 GEMM + bias + ReLU
+//                                                       (nemotron/weights.rs:345-417)
 //   flatten_kernel            [t, f, C] -> [t, C*f] of the needed frames
 //                                                       (nemotron/encoder.rs:460-470)
 // Frame rows are time-major [stream][frame][d]; one CTA handles one row for
@@ -23,45 +24,75 @@ namespace sc {
 constexpr int kRowThreads = 256;
 constexpr int kMaxRowVals = 16;  // d up to 4096
 
-// Sum over the CTA (256 threads): warp shuffles, then the 8 warp sums.
-__device__ __forceinline__ float block_sum(float v, float *red) {
+constexpr int kLnLanes = 16;  // the reference's SIMD width for ln_forward
+
+// Shared scratch of the row kernels: the row padded to 17 floats per
+// 16-element chunk (conflict-free chunk walks), the chunk sums and the
+// broadcast scalar.
+struct RowScratch {
+  float row[kMaxRowVals * kRowThreads / kLnLanes * (kLnLanes + 1)];
+  float part[kMaxRowVals * kRowThreads / kLnLanes];
+  float bcast;
+};
+
+__device__ __forceinline__ int row_slot(int i) { return i + i / kLnLanes; }
+
+// Sum of the row's 16-element chunk sums in the reference's order
+// (simd_kernel.rs:734-776): each chunk summed lane 0..15 in sequence, then
+// the chunk sums in sequence.  sq = true sums (x - mean)^2 with the square
+// rounded before the add, as the reference's (diff * diff).reduce_sum().
+template <bool kSq>
+__device__ __forceinline__ float ordered_row_sum(RowScratch &sh, int d, float mean) {
+  const int nchunks = d / kLnLanes;
+  for (int ci = threadIdx.x; ci < nchunks; ci += kRowThreads) {
+    const float *r = sh.row + ci * (kLnLanes + 1);
+    float cs;
+    if (kSq) {
+      float df = __fsub_rn(r[0], mean);
+      cs = __fmul_rn(df, df);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.0f;
+      for (int q = 1; q < kLnLanes; q++) {
+        df = __fsub_rn(r[q], mean);
+        cs = __fadd_rn(cs, __fmul_rn(df, df));
+      }
+    } else {
+      cs = r[0];
 #pragma unroll
-  for (int w = 0; w < kRowThreads / 32; w++) t += red[w];
+      for (int q = 1; q < kLnLanes; q++) cs = __fadd_rn(cs, r[q]);
+    }
+    sh.part[ci] = cs;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int ci = 0; ci < nchunks; ci++) t = __fadd_rn(t, sh.part[ci]);
+    sh.bcast = t;
+  }
+  __syncthreads();
+  const float t = sh.bcast;
+  __syncthreads();  // bcast and part are reused by the next call
   return t;
 }
 
-// LayerNorm of the row values held by this thread (element i = tid + k*256):
-// mean = sum/d, var = sum (x-mean)^2 / d, out = (x-mean) * (w * inv) + b
-// with inv = 1 / sqrt(var + eps) -- the reference's formula.
+// LayerNorm of the row values held by this thread (element i = tid + k*256),
+// rounded as the reference's ln_forward (simd_kernel.rs:734-805):
+// mean = sum/d, var = sum (x-mean)^2 / d, inv = 1 / sqrt(var/d + eps),
+// out = fma(x - mean, w * inv, b).
 __device__ __forceinline__ void ln_vals(float (&v)[kMaxRowVals], int d, const float *w, const float *b, float eps,
-                                        float *red) {
+                                        RowScratch &sh) {
   const int nv = d / kRowThreads;
-  float s = 0.0f;
 #pragma unroll
   for (int k = 0; k < kMaxRowVals; k++)
-    if (k < nv) s += v[k];
-  const float mean = block_sum(s, red) / (float)d;
-  float q = 0.0f;
-#pragma unroll
-  for (int k = 0; k < kMaxRowVals; k++)
-    if (k < nv) {
-      const float df = v[k] - mean;
-      q += df * df;
-    }
-  const float var = block_sum(q, red);
-  const float inv = 1.0f / sqrtf(var / (float)d + eps);
+    if (k < nv) sh.row[row_slot(threadIdx.x + k * kRowThreads)] = v[k];
+  __syncthreads();
+  const float mean = __fdiv_rn(ordered_row_sum<false>(sh, d, 0.0f), (float)d);
+  const float var = ordered_row_sum<true>(sh, d, mean);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(var, (float)d), eps)));
 #pragma unroll
   for (int k = 0; k < kMaxRowVals; k++)
     if (k < nv) {
       const int i = threadIdx.x + k * kRowThreads;
-      v[k] = fmaf(v[k] - mean, w[i] * inv, b[i]);
+      v[k] = __fmaf_rn(__fsub_rn(v[k], mean), __fmul_rn(w[i], inv), b[i]);
     }
 }
 
@@ -69,14 +100,14 @@ __global__ void __launch_bounds__(kRowThreads) ln_rows_kernel(const float *__res
                                                               const float *__restrict__ w,
                                                               const float *__restrict__ b, float eps,
                                                               float *__restrict__ out, int64_t ldo, int d) {
-  __shared__ float red[kRowThreads / 32];
+  __shared__ RowScratch sh;
   const int64_t row = blockIdx.x;
   const int nv = d / kRowThreads;
   float v[kMaxRowVals];
 #pragma unroll
   for (int k = 0; k < kMaxRowVals; k++)
     if (k < nv) v[k] = x[row * ldx + threadIdx.x + k * kRowThreads];
-  ln_vals(v, d, w, b, eps, red);
+  ln_vals(v, d, w, b, eps, sh);
 #pragma unroll
   for (int k = 0; k < kMaxRowVals; k++)
     if (k < nv) out[row * ldo + threadIdx.x + k * kRowThreads] = v[k];
@@ -91,7 +122,7 @@ __global__ void glu_ring_kernel(const float *__restrict__ h2, int c, int d, floa
   float *dst = ring + (z * cap + (s + j) % cap) * (int64_t)d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
     const float gate = h2[row * 2 * d + i], val = h2[row * 2 * d + d + i];
-    dst[i] = gate * (1.0f / (1.0f + expf(-val)));
+    dst[i] = __fmul_rn(gate, __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-val))));
   }
 }
 
@@ -102,7 +133,7 @@ __global__ void __launch_bounds__(kRowThreads)
     dwconv_ln_silu_kernel(const float *__restrict__ ring, int cap, int c, int d, int kh, int64_t s,
                           const float *__restrict__ w, const float *__restrict__ lnw,
                           const float *__restrict__ lnb, float eps, float *__restrict__ out) {
-  __shared__ float red[kRowThreads / 32];
+  __shared__ RowScratch sh;
   const int64_t row = blockIdx.x;
   const int64_t z = row / c, fr = s + row % c;
   const int nv = d / kRowThreads;
@@ -115,17 +146,14 @@ __global__ void __launch_bounds__(kRowThreads)
       for (int t = 0; t < kh; t++) {
         const int64_t ti = fr - (kh - 1) + t;
         if (ti < 0) continue;
-        acc = fmaf(ring[(z * cap + ti % cap) * (int64_t)d + ch], w[ch * kh + t], acc);
+        acc = __fmaf_rn(ring[(z * cap + ti % cap) * (int64_t)d + ch], w[ch * kh + t], acc);
       }
       v[k] = acc;
     }
-  ln_vals(v, d, lnw, lnb, eps, red);
+  ln_vals(v, d, lnw, lnb, eps, sh);
 #pragma unroll
   for (int k = 0; k < kMaxRowVals; k++)
-    if (k < nv) {
-      const float a = v[k];
-      out[row * d + threadIdx.x + k * kRowThreads] = a * (1.0f / (1.0f + expf(-a)));
-    }
+    if (k < nv) out[row * d + threadIdx.x + k * kRowThreads] = silu_ref(v[k]);
 }
 
 // Pre-encode window of stream z: `hist` held frames of history (the last
@@ -189,15 +217,81 @@ __global__ void conv2d_3x3s2_kernel(const float *__restrict__ x, int t_in, int f
     for (int kf = 0; kf < 3; kf++) {
       const int fi = of * 2 + kf - 2;
       if (fi < 0 || fi >= f_in) continue;
-      acc += x[((z * t_in + ti) * f_in + fi) * c_in + ic] * w[oc * 9 + kt * 3 + kf];
+      acc = __fadd_rn(acc, __fmul_rn(x[((z * t_in + ti) * f_in + fi) * c_in + ic], w[oc * 9 + kt * 3 + kf]));
     }
   }
   out[i] = relu ? fmaxf(acc, 0.0f) : acc;
 }
 
-__global__ void bias_relu_kernel(float *__restrict__ x, const float *__restrict__ b, int c, int64_t n) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) x[i] = fmaxf(x[i] + b[i % c], 0.0f);
+// Pointwise conv: Y[m][n] = max(sum_k W[n][k] X[m][k] + b[n], 0) over all
+// spatial positions m of all streams (X, Y channels-last).  Each output's
+// k-sum is one fused multiply-add chain from k = 0 upwards, then the bias
+// is added -- the reference's rounding for its pointwise convs.  128 x 128
+// tile per CTA, 8 x 8 outputs per thread, k staged 8 at a time.
+constexpr int kPwBM = 128, kPwBN = 128, kPwBK = 8, kPwThreads = 256;
+
+__global__ void __launch_bounds__(kPwThreads)
+    pw_conv_relu_kernel(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
+                        float *__restrict__ y, int64_t m_rows, int n, int k) {
+  __shared__ __align__(16) float as[2][kPwBK][kPwBM];
+  __shared__ __align__(16) float bs[2][kPwBK][kPwBN];
+  const int tid = threadIdx.x;
+  const int64_t m0 = (int64_t)blockIdx.x * kPwBM;
+  const int n0 = blockIdx.y * kPwBN;
+  // loader: thread -> (row tid / 2, k quad (tid % 2) * 4) of both tiles
+  const int lr = tid >> 1, lk = (tid & 1) * 4;
+  const int64_t am = m0 + lr;
+  const int bn = n0 + lr;
+  auto load = [&](int kb, float (&ra)[4], float (&rb)[4]) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int kk = kb + lk + q;
+      ra[q] = (am < m_rows && kk < k) ? x[am * k + kk] : 0.0f;
+      rb[q] = (bn < n && kk < k) ? w[(int64_t)bn * k + kk] : 0.0f;
+    }
+  };
+  const int ty = tid / 16, tx = tid % 16;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+  float ra[4], rb[4];
+  load(0, ra, rb);
+  int buf = 0;
+  for (int kb = 0; kb < k; kb += kPwBK) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      as[buf][lk + q][lr] = ra[q];
+      bs[buf][lk + q][lr] = rb[q];
+    }
+    __syncthreads();
+    if (kb + kPwBK < k) load(kb + kPwBK, ra, rb);
+#pragma unroll
+    for (int kq = 0; kq < kPwBK; kq++) {
+      const float4 a0 = *reinterpret_cast<const float4 *>(&as[buf][kq][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&as[buf][kq][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&bs[buf][kq][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&bs[buf][kq][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = __fmaf_rn(bv[j], av[i], acc[i][j]);
+    }
+    buf ^= 1;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (m >= m_rows) continue;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int nn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+      if (nn < n) y[m * n + nn] = fmaxf(__fadd_rn(acc[i][j], b[nn]), 0.0f);
+    }
+  }
 }
 
 // [z][t][f][C] -> rows (z, j) of [C*f] (channel-major, frequency fastest)
@@ -271,8 +365,11 @@ int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int f_in, i
   return kOk;
 }
 
-int launch_bias_relu(float *x, const float *b, int c, int64_t n, cudaStream_t st) {
-  bias_relu_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(x, b, c, n);
+int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t m_rows, int n, int k,
+                        cudaStream_t st) {
+  if (m_rows <= 0) return kOk;
+  dim3 grid((unsigned)ceil_div(m_rows, kPwBM), (unsigned)ceil_div(n, kPwBN));
+  pw_conv_relu_kernel<<<grid, kPwThreads, 0, st>>>(x, w, b, y, m_rows, n, k);
   SC_CUDA(cudaGetLastError());
   return kOk;
 }

@@ -20,11 +20,6 @@
 
 namespace sc {
 
-size_t gemm_ws_bytes(int64_t m, int64_t k);
-int current_device(int *dev, int *sm_count);
-int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
-              const float *bias, float *y, int32_t y_layout, int64_t ldy, void *ws, size_t ws_bytes,
-              int32_t *dots, cudaStream_t st, Epilogue epi);
 const Q8Weights *q8w_weights(const sc_q8w *w);
 
 // The scratch: quantised activations [t_pad][k_pad] int8, then their block

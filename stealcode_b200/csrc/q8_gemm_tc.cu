@@ -20,8 +20,10 @@
 //                thread), committing to the stage's "empty" barrier and the
 //                TMEM buffer's "full" barrier;
 //   warps 2..    drain warpgroups: each thread owns one weight row (TMEM lane)
-//                and 32 frame columns; the scaling runs in packed f32x2 FMAs
-//                and the int32 -> f32 conversion is an exact integer add.
+//                and 32 frame columns; the scales multiply in packed f32x2,
+//                the accumulation runs in the reference scalar oracle's
+//                order with unfused scalar multiply + add, and the int32 ->
+//                f32 conversion is an exact integer add.
 // Every mbarrier wait is bounded; a wait that gives up sets a status bit and
 // the kernel runs to its end without waiting again, so it cannot hang.
 #include "sc_device.cuh"
@@ -118,11 +120,6 @@ __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
 }
 __device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
 __device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
 __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -241,13 +238,19 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
       const float dwv = __half2float(((const __half *)(st + L::kA + L::kB))[row]);
       const uint64_t dw2 = pack2(dwv, dwv);
       const uint64_t *dx2 = (const uint64_t *)(st + L::kA + L::kB + L::kS) + col_base / 2;
+      // acc += (dw * dx) * dot with the three roundings of the reference's
+      // scalar oracle (sgemm_kernel.rs:185-196), so each output is bit-equal
+      // to q8_gemm_scalar's.  The product and the sum are scalar __fmul_rn /
+      // __fadd_rn, which are never fused into an FMA (a packed f32x2 multiply
+      // followed by a packed add was, measurably).
 #pragma unroll
       for (int j = 0; j < 16; j++) {
         const uint64_t s2 = fmul2(dw2, dx2[j]);  // dw * dx per column
         const uint64_t f2 = fadd2(pack2(__uint_as_float(r[2 * j] + 0x4B400000u),
                                         __uint_as_float(r[2 * j + 1] + 0x4B400000u)),
                                   neg_magic);   // exact block dots as f32
-        acc[j] = ffma2(s2, f2, acc[j]);
+        acc[j] = pack2(__fadd_rn(lo_of(acc[j]), __fmul_rn(lo_of(s2), lo_of(f2))),
+                       __fadd_rn(hi_of(acc[j]), __fmul_rn(hi_of(s2), hi_of(f2))));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);

@@ -100,7 +100,7 @@ constexpr int64_t kSmallMaxFrames = 16;
 // Quantise + GEMM on device pointers.
 int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
               const float *bias, float *y, int32_t y_layout, int64_t ldy, void *ws,
-              size_t ws_bytes, int32_t *dots, cudaStream_t st, Epilogue epi) {
+              size_t ws_bytes, int32_t *dots, cudaStream_t st, Epilogue epi, bool force_tc) {
   if (!w || !x || (!y && !dots) || t < 0 || !layout_ok(x_layout) || !layout_ok(y_layout)) {
     set_error("q8_gemm: invalid argument");
     return kErrInvalid;
@@ -125,7 +125,7 @@ int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, i
     set_error("q8_gemm: workspace needs %zu bytes at 256-byte alignment", need);
     return kErrInvalid;
   }
-  if (t > kSmallMaxFrames && !dots) {
+  if ((t > kSmallMaxFrames || force_tc) && !dots) {
     // Tensor-core path: quantise into the tiled operand layout, then tcgen05.
     if (!ws) {
       rc = default_ws(need, &ws);

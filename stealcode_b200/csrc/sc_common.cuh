@@ -56,4 +56,17 @@ int cuda_fail(cudaError_t e, const char *what);
 
 __host__ __device__ static inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+#ifdef __CUDACC__
+// exp(x) rounded once to f32 from a double-precision exp: the correctly
+// rounded value except in vanishingly rare ties, i.e. what glibc's expf
+// (which Rust's f32::exp calls) returns for all but about one input in 10^5.
+__device__ __forceinline__ float exp_rn(float x) { return (float)exp((double)x); }
+
+// SiLU exactly as the reference writes it: v * (1 + exp(-v)).recip()
+// (simd_kernel.rs:817-839), with IEEE rounding at every step.
+__device__ __forceinline__ float silu_ref(float v) {
+  return __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-v))));
+}
+#endif
+
 }  // namespace sc

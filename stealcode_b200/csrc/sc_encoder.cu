@@ -17,7 +17,6 @@
 // (nemotron/encoder.rs:89-245); linear_q/k/v are fused row-wise into one Q8
 // matrix (each output row is computed independently, so the result is the
 // same as three GEMMs over the same quantised input).
-#include <cublas_v2.h>
 
 #include <cmath>
 #include <cstring>
@@ -30,11 +29,6 @@
 
 namespace sc {
 
-size_t gemm_ws_bytes(int64_t m, int64_t k);
-int current_device(int *dev, int *sm_count);
-int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
-              const float *bias, float *y, int32_t y_layout, int64_t ldy, void *ws, size_t ws_bytes,
-              int32_t *dots, cudaStream_t st, Epilogue epi);
 int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k, int64_t block_bytes, int64_t qoff,
                      Q8Weights *w, cudaStream_t st);
 int launch_ln_rows(const float *x, int64_t ldx, const float *w, const float *b, float eps, float *out, int64_t ldo,
@@ -48,12 +42,14 @@ int launch_mel_hist(const float *old_hist, int hist_cap, int hist_frames, const 
                     int n_mels, float *new_hist, int64_t n_streams, cudaStream_t st);
 int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int f_in, int c_in, const float *w,
                         const float *b, int c_out, int t_out, int f_out, int relu, float *out, cudaStream_t st);
-int launch_bias_relu(float *x, const float *b, int c, int64_t n, cudaStream_t st);
+int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t m_rows, int n, int k,
+                        cudaStream_t st);
 int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int start_rel, int c, float *out,
                    cudaStream_t st);
 int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st);
 
 constexpr int kMelHistory = 24;  // mel frames of left context (streaming.rs:188)
+constexpr int kDumpStages = 8;
 
 struct Lin {
   Q8Weights w{};
@@ -98,7 +94,11 @@ struct sc_stream_encoder {
   float *win, *p0, *p1, *p2, *flat, *pos_in;
   void *ws = nullptr;
   size_t ws_bytes = 0;
-  cublasHandle_t cublas = nullptr;
+  // stage dumps of one layer (the reference's STEALCODE_DUMP_DIR senc_b*_*
+  // files, streaming.rs:426-434): -1 = off
+  int dump_layer = -1;
+  float *dump = nullptr;  // [kDumpStages][M][2d]
+  int64_t dump_rows = 0;
 
   ~sc_stream_encoder() {
     for (auto &l : layers)
@@ -109,7 +109,6 @@ struct sc_stream_encoder {
     cudaFree(pre_out.w.qs);
     cudaFree(pre_out.w.sc);
     for (void *p : allocs) cudaFree(p);
-    if (cublas) cublasDestroy(cublas);
   }
 };
 
@@ -234,7 +233,7 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
   const sc_encoder_config &c = *cfg;
   if (c.d_model % 256 || c.d_model > 4096 || c.n_heads <= 0 || c.d_model % c.n_heads || c.att_right < 0 ||
       c.conv_kernel < 1 || c.conv_left != c.conv_kernel - 1 || c.max_frames < 1 || c.max_frames > 16 ||
-      c.feat_in <= 0 || c.conv_channels <= 0 || c.n_layers <= 0) {
+      c.feat_in <= 0 || c.conv_channels <= 0 || c.n_layers < 0) {
     set_error("stream_encoder_create: unsupported config (d_model %d, heads %d, conv %d/%d, max_frames %d)",
               c.d_model, c.n_heads, c.conv_kernel, c.conv_left, c.max_frames);
     return kErrUnsupported;
@@ -331,10 +330,6 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     e->ws = L.dev_alloc(e->ws_bytes);
     ok = L.err.empty();
   }
-  if (ok && cublasCreate(&e->cublas) != CUBLAS_STATUS_SUCCESS) {
-    L.err = "cublasCreate failed";
-    ok = false;
-  }
   if (!ok) {
     set_error("stream_encoder_create: %s", L.err.c_str());
     delete e;
@@ -426,25 +421,13 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
                           st));
   TRY(launch_conv2d_3x3s2(e->p0, Z, (int)ta, (int)fa, (int)C, e->c2.w, e->c2.b, (int)C, (int)tb, (int)fb, 0, e->p1,
                           st));
-  const float one = 1.0f, zero = 0.0f;
-  if (cublasSetStream(e->cublas, st) != CUBLAS_STATUS_SUCCESS ||
-      cublasSgemm(e->cublas, CUBLAS_OP_T, CUBLAS_OP_N, (int)C, (int)(Z * tb * fb), (int)C, &one, e->c3.w, (int)C,
-                  e->p1, (int)C, &zero, e->p2, (int)C) != CUBLAS_STATUS_SUCCESS) {
-    set_error("pre_encode pointwise conv: cuBLAS sgemm failed");
-    return kErrCuda;
-  }
-  TRY(launch_bias_relu(e->p2, e->c3.b, (int)C, Z * tb * fb * C, st));
+  TRY(launch_pw_conv_relu(e->p1, e->c3.w, e->c3.b, e->p2, Z * tb * fb, (int)C, (int)C, st));
   TRY(launch_conv2d_3x3s2(e->p2, Z, (int)tb, (int)fb, (int)C, e->c5.w, e->c5.b, (int)C, (int)tc, (int)fc, 0, e->p1,
                           st));
-  if (cublasSgemm(e->cublas, CUBLAS_OP_T, CUBLAS_OP_N, (int)C, (int)(Z * tc * fc), (int)C, &one, e->c6.w, (int)C,
-                  e->p1, (int)C, &zero, e->p0, (int)C) != CUBLAS_STATUS_SUCCESS) {
-    set_error("pre_encode pointwise conv: cuBLAS sgemm failed");
-    return kErrCuda;
-  }
-  TRY(launch_bias_relu(e->p0, e->c6.b, (int)C, Z * tc * fc * C, st));
+  TRY(launch_pw_conv_relu(e->p1, e->c6.w, e->c6.b, e->p0, Z * tc * fc, (int)C, (int)C, st));
   TRY(launch_flatten(e->p0, Z, (int)tc, (int)fc, (int)C, (int)start_rel, (int)cf, e->flat, st));
   TRY(gemm_impl(&e->pre_out.w, e->flat, M, SC_LAYOUT_TIME_MAJOR, 0, e->pre_out.bias, e->x, SC_LAYOUT_TIME_MAJOR, d,
-                e->ws, e->ws_bytes, nullptr, st, Epilogue{}));
+                e->ws, e->ws_bytes, nullptr, st, Epilogue{}, true));
   // history for the next window
   TRY(launch_mel_hist(e->hist[e->hist_cur], kMelHistory, e->hist_frames, mel_new, (int)n_new, c.feat_in,
                       e->hist[e->hist_cur ^ 1], Z, st));
@@ -466,23 +449,33 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
     SC_CUDA(cudaMemcpyAsync(e->pos_in, pet.data(), pet.size() * 4, cudaMemcpyHostToDevice, st));
     for (auto &ly : e->layers)
       TRY(gemm_impl(&ly.pos.w, e->pos_in, e->n_pos, SC_LAYOUT_TIME_MAJOR, 0, ly.pos.bias, ly.pos_p,
-                    SC_LAYOUT_TIME_MAJOR, d, e->ws, e->ws_bytes, nullptr, st, Epilogue{}));
+                    SC_LAYOUT_TIME_MAJOR, d, e->ws, e->ws_bytes, nullptr, st, Epilogue{}, true));
     SC_CUDA(cudaStreamSynchronize(st));  // pet must outlive the copy
     e->pos_ready = true;
   }
   // ---- conformer blocks (streaming.rs:279-318, block_new :395-680) ----
   Epilogue silu{kEpiSilu, nullptr, 1.0f};
-  for (auto &ly : e->layers) {
+  e->dump_rows = M;
+  for (size_t li = 0; li < e->layers.size(); li++) {
+    Layer &ly = e->layers[li];
+    auto dump = [&](int stage, const float *src, int64_t width) -> int {
+      if ((int)li != e->dump_layer || !e->dump) return kOk;
+      SC_CUDA(cudaMemcpy2DAsync(e->dump + (size_t)stage * M * 2 * d, 2 * d * 4, src, width * 4, d * 4, M,
+                                cudaMemcpyDeviceToDevice, st));
+      return kOk;
+    };
     auto gemm = [&](const Lin &l, const float *in, float *out, int64_t ldo, Epilogue epi) {
       return gemm_impl(&l.w, in, M, SC_LAYOUT_TIME_MAJOR, 0, l.bias, out, SC_LAYOUT_TIME_MAJOR, ldo, e->ws,
-                       e->ws_bytes, nullptr, st, epi);
+                       e->ws_bytes, nullptr, st, epi, true);
     };
     // macaron FF1: y = x + 0.5 * FF(LN(x))
     TRY(launch_ln_rows(e->x, d, ly.ln_ff1_w, ly.ln_ff1_b, eps, e->xn, d, M, (int)d, st));
     TRY(gemm(ly.ff1_1, e->xn, e->h, dff, silu));
     TRY(gemm(ly.ff1_2, e->h, e->y, d, Epilogue{kEpiResidual, e->x, 0.5f}));
+    TRY(dump(0, e->y, d));
     // rel-pos MHSA over the band, K/V from the rings
     TRY(launch_ln_rows(e->y, d, ly.ln_att_w, ly.ln_att_b, eps, e->xn, d, M, (int)d, st));
+    TRY(dump(1, e->xn, d));
     TRY(gemm(ly.qkv, e->xn, e->qkv, 3 * d, Epilogue{}));
     {
       AttnParams p{};
@@ -514,25 +507,62 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
       TRY(attn_prepare(p, e->n_pos));
       TRY(launch_attn(p, Z, st));
     }
+    TRY(dump(2, e->attn, d));
     TRY(gemm(ly.out, e->attn, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}));
+    TRY(dump(3, e->y, d));
     // conv module: LN, pw1, GLU (ring), causal dw conv, LN, SiLU, pw2
     TRY(launch_ln_rows(e->y, d, ly.ln_conv_w, ly.ln_conv_b, eps, e->xn, d, M, (int)d, st));
     TRY(gemm(ly.pw1, e->xn, e->h2, 2 * d, Epilogue{}));
     TRY(launch_glu_ring(e->h2, M, (int)cf, (int)d, ly.glu_ring, (int)e->glu_cap, s, st));
     TRY(launch_dwconv_ln_silu(ly.glu_ring, (int)e->glu_cap, M, (int)cf, (int)d, c.conv_kernel, s, ly.dw,
                               ly.conv_ln_w, ly.conv_ln_b, eps, e->o2, st));
+    TRY(dump(4, e->qkv, 3 * d));  // q of the new frames
+    TRY(dump(5, e->o2, d));
     TRY(gemm(ly.pw2, e->o2, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}));
+    TRY(dump(6, e->y, d));
     // macaron FF2 and the block's final LN
     TRY(launch_ln_rows(e->y, d, ly.ln_ff2_w, ly.ln_ff2_b, eps, e->xn, d, M, (int)d, st));
     TRY(gemm(ly.ff2_1, e->xn, e->h, dff, silu));
     TRY(gemm(ly.ff2_2, e->h, e->y, d, Epilogue{kEpiResidual, e->y, 0.5f}));
     TRY(launch_ln_rows(e->y, d, ly.ln_out_w, ly.ln_out_b, eps, e->x, d, M, (int)d, st));
+    TRY(dump(7, e->x, d));
   }
   TRY(launch_out_ring(e->x, M, (int)cf, (int)d, e->out_ring, (int)e->out_cap, s, st));
   e->hist_cur ^= 1;
   e->hist_frames = (int)std::min<int64_t>(kMelHistory, e->hist_frames + n_new);
   e->total = t_new;
   e->last_c = cf;
+  return kOk;
+}
+
+int sc_stream_encoder_set_dump(sc_stream_encoder *e, int32_t layer) {
+  if (!e || layer >= (int32_t)e->layers.size()) {
+    set_error("stream_encoder_set_dump: invalid layer");
+    return kErrInvalid;
+  }
+  if (layer >= 0 && !e->dump) {
+    const size_t bytes = (size_t)kDumpStages * e->n_streams * e->cfg.max_frames * 2 * e->cfg.d_model * 4;
+    if (cudaMalloc(&e->dump, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("stream_encoder_set_dump: cudaMalloc failed");
+      return kErrAlloc;
+    }
+    e->allocs.push_back(e->dump);
+  }
+  e->dump_layer = layer;
+  return kOk;
+}
+
+int sc_stream_encoder_dump(const sc_stream_encoder *e, int32_t stage, float *out_host, int64_t *rows) {
+  if (!e || !e->dump || stage < 0 || stage >= kDumpStages || !out_host) {
+    set_error("stream_encoder_dump: no dump recorded or bad stage");
+    return kErrInvalid;
+  }
+  SC_CUDA(cudaDeviceSynchronize());
+  const int64_t d = e->cfg.d_model;
+  SC_CUDA(cudaMemcpy2D(out_host, d * 4, e->dump + (size_t)stage * e->dump_rows * 2 * d, 2 * d * 4, d * 4,
+                       e->dump_rows, cudaMemcpyDeviceToHost));
+  if (rows) *rows = e->dump_rows;
   return kOk;
 }
 

@@ -6,10 +6,12 @@
 
 namespace sc {
 
-// GEMM epilogue applied to v = W x + bias, element-wise on the output:
+// GEMM epilogue applied to v = W x + bias, element-wise on the output,
+// rounding like the reference's element loops (no fused multiply-add):
 //   kEpiNone:     y = v
 //   kEpiSilu:     y = v * (1 / (1 + exp(-v)))        (simd_kernel.rs:817-839)
-//   kEpiResidual: y = res + alpha * v                 (res may alias y)
+//   kEpiResidual: y = res + alpha * v                 (res may alias y;
+//                 streaming.rs:458-460, 596-598, 643-645, 667-669)
 enum : int { kEpiNone = 0, kEpiSilu = 1, kEpiResidual = 2 };
 struct Epilogue {
   int op = kEpiNone;
@@ -18,8 +20,8 @@ struct Epilogue {
 };
 
 __device__ __forceinline__ float apply_epilogue(const Epilogue &e, float v, int64_t idx) {
-  if (e.op == kEpiSilu) return v * (1.0f / (1.0f + expf(-v)));
-  if (e.op == kEpiResidual) return e.res[idx] + e.alpha * v;
+  if (e.op == kEpiSilu) return silu_ref(v);
+  if (e.op == kEpiResidual) return __fadd_rn(e.res[idx], __fmul_rn(e.alpha, v));
   return v;
 }
 
@@ -66,6 +68,17 @@ struct TcGemmArgs {
 int tc_frame_tile(int64_t t);
 int gemm_tc(const TcGemmArgs &a, cudaStream_t st);
 int tc_gemm_status(unsigned *out);
+
+// sc_api.cu: the shared dispatch behind the Q8_0 GEMM entry points.
+// t <= 16 frames run the weight-streaming kernel, more frames (or force_tc)
+// the tensor-core kernel, whose accumulation follows the reference scalar
+// oracle's order (sgemm_kernel.rs:185-196) -- the encoder's linears set
+// force_tc so that every output is rounded the same way at any frame count.
+size_t gemm_ws_bytes(int64_t m, int64_t k);
+int current_device(int *dev, int *sm_count);
+int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
+              const float *bias, float *y, int32_t y_layout, int64_t ldy, void *ws, size_t ws_bytes,
+              int32_t *dots, cudaStream_t st, Epilogue epi, bool force_tc = false);
 
 // attn_stream.cu
 struct AttnParams {

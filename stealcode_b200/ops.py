@@ -257,6 +257,15 @@ class StreamEncoder:
         check(lib.sc_stream_encoder_output(self._h, ctypes.byref(ptr), ctypes.byref(rows), ctypes.byref(d)))
         return ptr.value, rows.value, d.value
 
+    def set_dump(self, layer: int) -> None:
+        check(lib.sc_stream_encoder_set_dump(self._h, layer))
+
+    def dump(self, stage: int) -> np.ndarray:
+        rows = ctypes.c_int64()
+        out = np.empty((self.n_streams * 16, self.d), dtype=np.float32)
+        check(lib.sc_stream_encoder_dump(self._h, stage, _hp(out), ctypes.byref(rows)))
+        return out[: rows.value].copy()
+
     def close(self):
         if getattr(self, "_h", None):
             lib.sc_stream_encoder_destroy(self._h)

@@ -1,7 +1,19 @@
 """GPU parity of the device streaming encoder (one encode_new call = one
 streaming step for all streams) against the oracle StreamingEncoder
 (streaming.rs:137-680), one oracle instance per stream, on the same seeded
-random-init model and mel input."""
+random-init model and mel input.
+
+The device rounds every value as the reference's CPU code does, with its
+Q8_0 linears in q8_gemm_scalar's order (sgemm_kernel.rs:185-196) and a
+correctly rounded exp.  Against the oracle with that rounding the bar is
+the stated f32 tolerance (max |d| <= 1e-4 x RMS; in practice the outputs
+are bit-equal).  The reference's own dispatch runs 7-frame chunks through
+its 8-lane SIMD order and glibc's expf (one ulp off the correctly rounded
+value for ~6 inputs in 10^4); those last-ulp differences become whole-code
+flips in the next layer's int8 re-quantisation, so against that dispatch
+the device must be no further off than the oracle with the device's
+rounding is.  Both are the reference's arithmetic; they differ only in
+which of its CPU paths and which libm the reference would have run on."""
 import numpy as np
 import pytest
 
@@ -26,7 +38,13 @@ def _err(got, ref):
     return float(d.max() / rms), float(d.mean() / rms)
 
 
-def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11):
+TOL = 1e-4  # max |d| / RMS(reference), f32 outputs
+
+
+def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11, simd_too=False):
+    """Runs the device encoder and per-stream oracles side by side; returns
+    (t0, stream, max/RMS, mean/RMS, exact fraction[, oracle scalar-vs-SIMD
+    max/RMS, device-vs-SIMD max/RMS]) per step and stream."""
     from stealcode_b200.ops import StreamEncoder
 
     m = model.random_model(cfg, seed=seed)
@@ -34,6 +52,9 @@ def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11):
     mel = model.mel_stream(seed + 1, n_streams, n_mel, cfg.feat_in)
     dev = StreamEncoder(m, n_streams)
     refs = [oracle.StreamingEncoder(m) for _ in range(n_streams)]
+    for r in refs:
+        r.set_device_rounding()
+    simd = [oracle.StreamingEncoder(m) for _ in range(n_streams)] if simd_too else []
     stats = []
     batches = [(56 * i, 56 * (i + 1), False) for i in range(n_steps)]
     if tail:
@@ -47,24 +68,54 @@ def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11):
             assert dev.total() == refs[z].total()
             got = dev.frames(z, s, dev.total())
             ref = refs[z].frames(s, refs[z].total())
-            stats.append((t0, z) + _err(got, ref))
+            row = (t0, z) + _err(got, ref) + (float(np.mean(got == ref)),)
+            if simd:
+                assert simd[z].encode_new(mel[z, :t1], t0, t1, fin) == 0
+                alt = simd[z].frames(s, simd[z].total())
+                row += (_err(ref, alt)[0], _err(got, alt)[0])
+            stats.append(row)
     dev.close()
     return stats
+
+
+def _report(name, stats):
+    print("%s: worst max/RMS %.3g, worst mean/RMS %.3g, min exact fraction %.6f"
+          % (name, max(s[2] for s in stats), max(s[3] for s in stats), min(s[4] for s in stats)))
+    for s in stats:
+        print("  t0=%d stream %d: max/RMS %.3g mean/RMS %.3g exact %.6f" % s[:5]
+              + ("  [oracle device-rounding vs reference dispatch %.3g, device vs reference dispatch %.3g]" % s[5:] if len(s) > 5 else ""))
+
+
+def test_pre_encode_matches_oracle(torch):
+    """0 conformer blocks: the output frames are the pre-encode stack's
+    (convs, flatten, the 4352 -> 1024 Q8_0 linear), first window, steady
+    windows and a short final window."""
+    cfg = model.EncoderConfig(n_layers=0)
+    stats = run_steps(torch, cfg, 2, 3, tail=24)
+    _report("pre-encode", stats)
+    assert max(s[2] for s in stats) <= TOL
 
 
 def test_encoder_two_layers_matches_oracle(torch):
     """2 conformer blocks at full width (d 1024, 8 heads, FF 4096, conv 9):
     13 steady 56-mel steps (the band reaches its 77-frame steady state at
-    step 11) and a 24-mel final tail."""
+    step 11) and a 24-mel final tail, 3 streams (M = 21 frames per GEMM)."""
     cfg = model.EncoderConfig(n_layers=2)
     stats = run_steps(torch, cfg, 3, 13, tail=24)
-    worst = max(s[2] for s in stats)
-    mean = max(s[3] for s in stats)
-    print("encoder 2-layer: worst max/RMS %.3g, worst mean/RMS %.3g" % (worst, mean))
+    _report("encoder 2-layer", stats)
+    assert max(s[2] for s in stats) <= TOL
+
+
+def test_encoder_24_layers_matches_oracle(torch):
+    """The full 24-layer encoder (the 256-stream workload's model) for 2
+    streams over 4 steps, checked against both oracle GEMM orders."""
+    cfg = model.EncoderConfig(n_layers=24)
+    stats = run_steps(torch, cfg, 2, 4, seed=5, simd_too=True)
+    _report("encoder 24-layer", stats)
+    assert max(s[2] for s in stats) <= TOL
+    # against the reference's own dispatch: within its scalar path's spread
     for s in stats:
-        print("step t0=%d stream %d: max/RMS %.3g mean/RMS %.3g" % s)
-    assert mean <= 1e-4
-    assert worst <= 1e-2
+        assert s[6] <= s[5] + TOL
 
 
 def test_encoder_out_of_sync_is_rejected(torch):

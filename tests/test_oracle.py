@@ -180,3 +180,26 @@ def test_attn_band_mask_is_exact():
                                                                  "pos_off")])
     assert np.array_equal(a[:4], b[:4])
     assert not np.allclose(a[4:], b[4:])
+
+
+def test_exp_modes():
+    """orc_expf: mode 0 is libm expf (the reference's f32::exp on glibc), mode
+    1 the correctly rounded exp; they agree except in rare last-ulp cases."""
+    import ctypes
+
+    libm = ctypes.CDLL("libm.so.6")
+    libm.expf.restype = ctypes.c_float
+    libm.expf.argtypes = [ctypes.c_float]
+    xs = np.random.default_rng(5).uniform(-20, 20, 20000).astype(np.float32)
+    differ = 0
+    for x in xs:
+        x = float(x)
+        glibc = oracle.expf(x, correctly_rounded=False)
+        cr = oracle.expf(x, correctly_rounded=True)
+        assert glibc == libm.expf(x)
+        assert cr == np.float32(np.exp(np.float64(np.float32(x))))
+        if glibc != cr:
+            assert abs(np.float32(glibc).view(np.int32) - np.float32(cr).view(np.int32)) == 1
+            differ += 1
+    assert differ < 0.005 * len(xs)
+    assert oracle.lib.orc_get_exp_mode() == 0
