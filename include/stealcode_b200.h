@@ -59,6 +59,11 @@ int sc_abi_version(void);
 #define SC_STATUS_WAIT_TIMEOUT 1u
 int sc_device_status(uint32_t *flags);
 
+/* Number of CUDA kernel launches this library has issued in this process
+ * (all devices, all entry points).  Diagnostic; no counterpart in the
+ * reference. */
+long long sc_launch_count(void);
+
 /* ---- weights --------------------------------------------------------- */
 
 /* Repack a GGUF Q8_0 tensor once into the device layout: int8 quants in

@@ -55,6 +55,7 @@ SIGNATURES = {
     "sc_last_error": (c_char_p, []),
     "sc_abi_version": (c_int, []),
     "sc_device_status": (c_int, [POINTER(ctypes.c_uint32)]),
+    "sc_launch_count": (ctypes.c_longlong, []),
     "sc_q8_repack": (c_int, [_P, _I, _I, _I, _I, POINTER(c_void_p)]),
     "sc_q8_repack_device": (c_int, [_P, _I, _I, _I, _I, _P, POINTER(c_void_p)]),
     "sc_q8w_free": (c_int, [_P]),
@@ -97,6 +98,11 @@ def device_status() -> int:
     v = ctypes.c_uint32(0)
     check(lib.sc_device_status(ctypes.byref(v)))
     return v.value
+
+
+def launch_count() -> int:
+    """Kernel launches this library has issued in this process."""
+    return int(lib.sc_launch_count())
 
 
 def last_error() -> str:

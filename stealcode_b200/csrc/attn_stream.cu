@@ -264,6 +264,7 @@ static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st
     smem_set[dev] = smem;
   }
   kern<<<dim3((unsigned)p.n_heads, (unsigned)n_streams), HD, smem, st>>>(p);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }

@@ -323,12 +323,14 @@ int launch_ln_rows(const float *x, int64_t ldx, const float *w, const float *b, 
     return kErrUnsupported;
   }
   ln_rows_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(x, ldx, w, b, eps, out, ldo, d);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
 
 int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st) {
   glu_ring_kernel<<<(unsigned)rows, 256, 0, st>>>(h2, c, d, ring, cap, s);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -336,6 +338,7 @@ int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, in
 int launch_dwconv_ln_silu(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s, const float *w,
                           const float *lnw, const float *lnb, float eps, float *out, cudaStream_t st) {
   dwconv_ln_silu_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(ring, cap, c, d, kh, s, w, lnw, lnb, eps, out);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -344,6 +347,7 @@ int launch_mel_window(const float *hist, int hist_cap, int hist_frames, const fl
                       int n_mels, int t_mel, float *win, int64_t n_streams, cudaStream_t st) {
   dim3 grid((unsigned)ceil_div((int64_t)t_mel * n_mels, 256), (unsigned)n_streams);
   mel_window_kernel<<<grid, 256, 0, st>>>(hist, hist_cap, hist_frames, mel_new, n_new, n_mels, t_mel, win);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -352,6 +356,7 @@ int launch_mel_hist(const float *old_hist, int hist_cap, int hist_frames, const 
                     int n_mels, float *new_hist, int64_t n_streams, cudaStream_t st) {
   dim3 grid((unsigned)ceil_div((int64_t)hist_cap * n_mels, 256), (unsigned)n_streams);
   mel_hist_kernel<<<grid, 256, 0, st>>>(old_hist, hist_cap, hist_frames, mel_new, n_new, n_mels, new_hist);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -361,6 +366,7 @@ int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int f_in, i
   const int64_t n = n_streams * t_out * f_out * c_out;
   conv2d_3x3s2_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(x, t_in, f_in, c_in, w, b, c_out, t_out, f_out,
                                                                    relu, out, n);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -370,6 +376,7 @@ int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y
   if (m_rows <= 0) return kOk;
   dim3 grid((unsigned)ceil_div(m_rows, kPwBM), (unsigned)ceil_div(n, kPwBN));
   pw_conv_relu_kernel<<<grid, kPwThreads, 0, st>>>(x, w, b, y, m_rows, n, k);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -378,12 +385,14 @@ int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int s
                    cudaStream_t st) {
   dim3 grid((unsigned)ceil_div((int64_t)C * f, 256), (unsigned)(n_streams * c));
   flatten_kernel<<<grid, 256, 0, st>>>(x, t, f, C, start_rel, c, out);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
 
 int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st) {
   out_ring_kernel<<<(unsigned)rows, 256, 0, st>>>(x, c, d, ring, cap, s);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }

@@ -253,6 +253,7 @@ static int launch_stream(StreamParams &p, int64_t groups, int64_t mtiles, cudaSt
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = SC_STREAM_PDL ? 2 : 1;
+  note_launch();
   SC_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
   return kOk;
 }

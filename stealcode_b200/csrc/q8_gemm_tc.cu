@@ -120,6 +120,14 @@ __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
 }
 __device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
 __device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+#ifndef SC_TC_DRAIN
+#define SC_TC_DRAIN 0
+#endif
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
 __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -218,6 +226,9 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
     // int32 -> f32 without I2F: for |d| < 2^22, the float with bit pattern
     // d + 0x4B400000 is exactly 1.5 * 2^23 + d (block dots are below 2^20).
     const uint64_t neg_magic = pack2(-12582912.0f, -12582912.0f);
+    const uint64_t neg_zero = pack2(-0.0f, -0.0f), one2 = pack2(1.0f, 1.0f);
+    (void)neg_zero;
+    (void)one2;
     uint64_t acc[16];
 #pragma unroll
     for (int j = 0; j < 16; j++) acc[j] = 0ull;
@@ -249,8 +260,22 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
         const uint64_t f2 = fadd2(pack2(__uint_as_float(r[2 * j] + 0x4B400000u),
                                         __uint_as_float(r[2 * j + 1] + 0x4B400000u)),
                                   neg_magic);   // exact block dots as f32
+#if SC_TC_DRAIN == 0
         acc[j] = pack2(__fadd_rn(lo_of(acc[j]), __fmul_rn(lo_of(s2), lo_of(f2))),
                        __fadd_rn(hi_of(acc[j]), __fmul_rn(hi_of(s2), hi_of(f2))));
+#elif SC_TC_DRAIN == 1
+        acc[j] = fadd2(acc[j], ffma2(s2, f2, neg_zero));
+#elif SC_TC_DRAIN == 2
+        acc[j] = ffma2(fmul2(s2, f2), one2, acc[j]);
+#elif SC_TC_DRAIN == 4
+        acc[j] = ffma2(s2, f2, acc[j]);
+#else
+        {
+          uint64_t p2 = fmul2(s2, f2);
+          asm volatile("" : "+l"(p2));
+          acc[j] = fadd2(acc[j], p2);
+        }
+#endif
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -321,6 +346,7 @@ static int launch_tc(const TcParams &p, int64_t groups, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  note_launch();
   SC_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
   return kOk;
 }

@@ -56,6 +56,7 @@ int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k,
   repack_q8f16_kernel<<<(unsigned)ceil_div(n, threads), threads, 0, st>>>(
       raw_dev, rows, k, padded_row, block_bytes, qoff, rows_pad, nb, w->qs,
       w->sc);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -180,6 +181,7 @@ int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx,
     const int threads = 256;
     quantize_act_v4_kernel<<<(unsigned)ceil_div(warps * 32, threads), threads, 0, st>>>(
         x, m, k, ldx, nb, m_pad, k_pad, xq, dx, tile_ft);
+    note_launch();
     SC_CUDA(cudaGetLastError());
     return kOk;
   }
@@ -190,6 +192,7 @@ int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx,
     quantize_act_kernel<true><<<grid, threads, 0, st>>>(x, m, k, ldx, nb, m_pad, k_pad, xq, dx, tile_ft);
   else
     quantize_act_kernel<false><<<grid, threads, 0, st>>>(x, m, k, ldx, nb, m_pad, k_pad, xq, dx, tile_ft);
+  note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }

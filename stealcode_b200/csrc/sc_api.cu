@@ -2,6 +2,7 @@
 // include/stealcode_b200.h).  Every entry point validates its arguments,
 // returns 0 or a negative error code and never aborts; sc_last_error() gives
 // the message of the calling thread's last failure.
+#include <atomic>
 #include <mutex>
 #include <new>
 #include <stdarg.h>
@@ -38,6 +39,9 @@ struct DeviceState {
   std::mutex stage_mu;
 };
 static DeviceState g_dev[64];
+
+static std::atomic<long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int current_device(int *dev, int *sm_count) {
   SC_CUDA(cudaGetDevice(dev));
@@ -159,6 +163,8 @@ const Q8Weights *q8w_weights(const sc_q8w *w) { return &w->w; }
 }  // namespace sc
 
 extern "C" {
+
+long long sc_launch_count(void) { return sc::g_launches.load(std::memory_order_relaxed); }
 
 const char *sc_last_error(void) { return g_err; }
 

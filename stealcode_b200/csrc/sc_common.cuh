@@ -47,6 +47,8 @@ enum : int {
 
 void set_error(const char *fmt, ...);
 int cuda_fail(cudaError_t e, const char *what);
+// Counts one kernel launch issued by this library (sc_launch_count).
+void note_launch();
 
 #define SC_CUDA(call)                                       \
   do {                                                      \
@@ -58,8 +60,9 @@ __host__ __device__ static inline int64_t ceil_div(int64_t a, int64_t b) { retur
 
 #ifdef __CUDACC__
 // exp(x) rounded once to f32 from a double-precision exp: the correctly
-// rounded value except in vanishingly rare ties, i.e. what glibc's expf
-// (which Rust's f32::exp calls) returns for all but about one input in 10^5.
+// rounded value (a double-rounding miss needs the exact value within 2^-29
+// of a float midpoint).  glibc's expf, which Rust's f32::exp calls on
+// Linux, is one ulp off this for about 6 inputs in 10^4.
 __device__ __forceinline__ float exp_rn(float x) { return (float)exp((double)x); }
 
 // SiLU exactly as the reference writes it: v * (1 + exp(-v)).recip()
