@@ -196,31 +196,52 @@ __global__ void mel_hist_kernel(const float *__restrict__ old_hist, int hist_cap
 
 // 3x3 stride-2 conv with causal pads (2, 1) on both axes, groups = c_in
 // (depthwise, c_in == c_out) or c_in == 1 (conv0): acc = bias, then taps in
-// (kt, kf) order; input [z][t_in][f_in][c_in], output [z][t_out][f_out][c_out].
-__global__ void conv2d_3x3s2_kernel(const float *__restrict__ x, int t_in, int f_in, int c_in,
-                                    const float *__restrict__ w, const float *__restrict__ b, int c_out,
-                                    int t_out, int f_out, int relu, float *__restrict__ out, int64_t n_total) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n_total) return;
-  const int oc = (int)(i % c_out);
-  const int64_t r = i / c_out;
-  const int of = (int)(r % f_out);
-  const int ot = (int)((r / f_out) % t_out);
-  const int64_t z = r / ((int64_t)f_out * t_out);
+// (kt, kf) order, each product and sum rounded on its own (the reference's
+// scalar loop, nemotron/weights.rs:418-523).  Only output rows
+// [out_row0, out_row0 + out_rows) are computed -- the rows the step's new
+// frames depend on; the input holds rows [x_row0, x_row0 + x_rows) of the
+// t_in-row map, and rows outside [0, t_in) are the zero padding.
+// Layouts: x [z][x_rows][f_in][c_in], out [z][out_rows][f_out][c_out].
+// One CTA per (output row, stream), one thread per output channel, looping
+// over the row's f_out positions: loads are coalesced over channels (conv0
+// reads one broadcast mel value per tap).
+__global__ void conv2d_3x3s2_kernel(const float *__restrict__ x, int t_in, int x_row0, int x_rows, int f_in,
+                                    int c_in, const float *__restrict__ w, const float *__restrict__ b, int c_out,
+                                    int out_row0, int out_rows, int f_out, int relu, float *__restrict__ out) {
+  const int oc = threadIdx.x;
+  if (oc >= c_out) return;
+  const int r = blockIdx.x, z = blockIdx.y;
+  const int ot = out_row0 + r;
   const int ic = c_in == 1 ? 0 : oc;  // depthwise: channel oc only
-  float acc = b[oc];
+  float wr[9];
+#pragma unroll
+  for (int tap = 0; tap < 9; tap++) wr[tap] = w[oc * 9 + tap];
+  const float bias = b[oc];
+  const float *xz = x + (size_t)z * x_rows * f_in * c_in + ic;
+  float *o = out + ((size_t)z * out_rows + r) * f_out * c_out + oc;
+  bool row_ok[3];
+  const float *xr[3];
 #pragma unroll
   for (int kt = 0; kt < 3; kt++) {
     const int ti = ot * 2 + kt - 2;
-    if (ti < 0 || ti >= t_in) continue;
-#pragma unroll
-    for (int kf = 0; kf < 3; kf++) {
-      const int fi = of * 2 + kf - 2;
-      if (fi < 0 || fi >= f_in) continue;
-      acc = __fadd_rn(acc, __fmul_rn(x[((z * t_in + ti) * f_in + fi) * c_in + ic], w[oc * 9 + kt * 3 + kf]));
-    }
+    const int li = ti - x_row0;
+    row_ok[kt] = ti >= 0 && ti < t_in && li >= 0 && li < x_rows;
+    xr[kt] = xz + (size_t)(row_ok[kt] ? li : 0) * f_in * c_in;
   }
-  out[i] = relu ? fmaxf(acc, 0.0f) : acc;
+  for (int of = 0; of < f_out; of++) {
+    float acc = bias;
+#pragma unroll
+    for (int kt = 0; kt < 3; kt++) {
+      if (!row_ok[kt]) continue;
+#pragma unroll
+      for (int kf = 0; kf < 3; kf++) {
+        const int fi = of * 2 + kf - 2;
+        if (fi < 0 || fi >= f_in) continue;
+        acc = __fadd_rn(acc, __fmul_rn(xr[kt][(size_t)fi * c_in], wr[kt * 3 + kf]));
+      }
+    }
+    o[(size_t)of * c_out] = relu ? fmaxf(acc, 0.0f) : acc;
+  }
 }
 
 // Pointwise conv: Y[m][n] = max(sum_k W[n][k] X[m][k] + b[n], 0) over all
@@ -361,11 +382,16 @@ int launch_mel_hist(const float *old_hist, int hist_cap, int hist_frames, const 
   return kOk;
 }
 
-int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int f_in, int c_in, const float *w,
-                        const float *b, int c_out, int t_out, int f_out, int relu, float *out, cudaStream_t st) {
-  const int64_t n = n_streams * t_out * f_out * c_out;
-  conv2d_3x3s2_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(x, t_in, f_in, c_in, w, b, c_out, t_out, f_out,
-                                                                   relu, out, n);
+int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int x_row0, int x_rows, int f_in, int c_in,
+                        const float *w, const float *b, int c_out, int out_row0, int out_rows, int f_out, int relu,
+                        float *out, cudaStream_t st) {
+  if (c_out > 1024 || (c_in != 1 && c_in != c_out)) {
+    set_error("pre_encode conv: c_in %d / c_out %d unsupported (c_out <= 1024, depthwise or c_in 1)", c_in, c_out);
+    return kErrUnsupported;
+  }
+  if (out_rows <= 0 || n_streams <= 0) return kOk;
+  conv2d_3x3s2_kernel<<<dim3((unsigned)out_rows, (unsigned)n_streams), (unsigned)c_out, 0, st>>>(
+      x, t_in, x_row0, x_rows, f_in, c_in, w, b, c_out, out_row0, out_rows, f_out, relu, out);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;

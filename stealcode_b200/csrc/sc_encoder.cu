@@ -40,8 +40,9 @@ int launch_mel_window(const float *hist, int hist_cap, int hist_frames, const fl
                       int n_mels, int t_mel, float *win, int64_t n_streams, cudaStream_t st);
 int launch_mel_hist(const float *old_hist, int hist_cap, int hist_frames, const float *mel_new, int n_new,
                     int n_mels, float *new_hist, int64_t n_streams, cudaStream_t st);
-int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int f_in, int c_in, const float *w,
-                        const float *b, int c_out, int t_out, int f_out, int relu, float *out, cudaStream_t st);
+int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int x_row0, int x_rows, int f_in, int c_in,
+                        const float *w, const float *b, int c_out, int out_row0, int out_rows, int f_out, int relu,
+                        float *out, cudaStream_t st);
 int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t m_rows, int n, int k,
                         cudaStream_t st);
 int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int start_rel, int c, float *out,
@@ -417,15 +418,26 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
     set_error("pre_encode produced too few frames: %lld < %lld", (long long)tc, (long long)(start_rel + cf));
     return kErrInvalid;
   }
-  TRY(launch_conv2d_3x3s2(e->win, Z, (int)t_mel, c.feat_in, 1, e->c0.w, e->c0.b, (int)C, (int)ta, (int)fa, 1, e->p0,
-                          st));
-  TRY(launch_conv2d_3x3s2(e->p0, Z, (int)ta, (int)fa, (int)C, e->c2.w, e->c2.b, (int)C, (int)tb, (int)fb, 0, e->p1,
-                          st));
-  TRY(launch_pw_conv_relu(e->p1, e->c3.w, e->c3.b, e->p2, Z * tb * fb, (int)C, (int)C, st));
-  TRY(launch_conv2d_3x3s2(e->p2, Z, (int)tb, (int)fb, (int)C, e->c5.w, e->c5.b, (int)C, (int)tc, (int)fc, 0, e->p1,
-                          st));
-  TRY(launch_pw_conv_relu(e->p1, e->c6.w, e->c6.b, e->p0, Z * tc * fc, (int)C, (int)C, st));
-  TRY(launch_flatten(e->p0, Z, (int)tc, (int)fc, (int)C, (int)start_rel, (int)cf, e->flat, st));
+  // Rows each stage must produce for output frames [start_rel, start_rel + cf)
+  // (a 3x3 stride-2 conv with top pad 2 maps output row r to input rows
+  // 2r - 2 .. 2r); the convs compute only those rows.
+  auto need = [](int64_t lo, int64_t hi, int64_t t_in, int64_t &in_lo, int64_t &in_hi) {
+    in_lo = std::max<int64_t>(2 * lo - 2, 0);
+    in_hi = std::min<int64_t>(2 * (hi - 1) + 1, t_in);
+  };
+  const int64_t r5 = start_rel, n5 = cf;  // conv5 / conv6 rows
+  int64_t r3, e3, r0, e0;
+  need(r5, r5 + n5, tb, r3, e3);          // conv2 / conv3 rows
+  need(r3, e3, ta, r0, e0);               // conv0 rows
+  TRY(launch_conv2d_3x3s2(e->win, Z, (int)t_mel, 0, (int)t_mel, c.feat_in, 1, e->c0.w, e->c0.b, (int)C, (int)r0,
+                          (int)(e0 - r0), (int)fa, 1, e->p0, st));
+  TRY(launch_conv2d_3x3s2(e->p0, Z, (int)ta, (int)r0, (int)(e0 - r0), (int)fa, (int)C, e->c2.w, e->c2.b, (int)C,
+                          (int)r3, (int)(e3 - r3), (int)fb, 0, e->p1, st));
+  TRY(launch_pw_conv_relu(e->p1, e->c3.w, e->c3.b, e->p2, Z * (e3 - r3) * fb, (int)C, (int)C, st));
+  TRY(launch_conv2d_3x3s2(e->p2, Z, (int)tb, (int)r3, (int)(e3 - r3), (int)fb, (int)C, e->c5.w, e->c5.b, (int)C,
+                          (int)r5, (int)n5, (int)fc, 0, e->p1, st));
+  TRY(launch_pw_conv_relu(e->p1, e->c6.w, e->c6.b, e->p0, Z * n5 * fc, (int)C, (int)C, st));
+  TRY(launch_flatten(e->p0, Z, (int)n5, (int)fc, (int)C, 0, (int)cf, e->flat, st));
   TRY(gemm_impl(&e->pre_out.w, e->flat, M, SC_LAYOUT_TIME_MAJOR, 0, e->pre_out.bias, e->x, SC_LAYOUT_TIME_MAJOR, d,
                 e->ws, e->ws_bytes, nullptr, st, Epilogue{}, true));
   // history for the next window
