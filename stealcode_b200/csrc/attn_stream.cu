@@ -26,6 +26,7 @@
 // In ring mode the K/V of the chunk's new frames come from the projection
 // output and are written into the stream's HBM ring (slot = frame % cap);
 // older band frames are read from the ring.
+#include "sc_device.cuh"
 #include "sc_kernels.cuh"
 
 namespace sc {
@@ -38,6 +39,9 @@ __device__ __forceinline__ void band_of(int64_t qq, int64_t chunk, int64_t left_
   kmax = hi < k_hi ? hi : k_hi;
 }
 
+#ifndef SC_ATTN_PREFETCH
+#define SC_ATTN_PREFETCH 1
+#endif
 constexpr int kLanes = 16;        // the reference's SIMD width for score_dot
 constexpr int kRedStride = 17;    // padded row of the lane-sum buffer
 
@@ -71,10 +75,22 @@ __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
   const int hoff = h * HD;
   const int c = p.c;
 
-  auto key_row = [&](const float *ring, const float *nw, int64_t fr) -> const float * {
-    if (fr >= p.new_lo) return nw + (z * p.rows_new + (fr - p.new_lo)) * p.ld_new + hoff;
-    return ring + (z * p.cap + fr % p.cap) * (int64_t)p.d + hoff;
+  // Band key kk is frame k_lo + kk: from the projection output when
+  // kk >= kk_new, else from ring slot (k_lo + kk) % cap (band <= cap, so one
+  // wrap at most).  Int32 index math, no 64-bit modulo in the loops.
+  const int kk_new = (int)(p.new_lo - p.k_lo);
+  const int slot0 = p.cap > 0 ? (int)(p.k_lo % p.cap) : 0;
+  const int cap = (int)p.cap;
+  auto ring_row = [&](float *ring, int kk) -> float * {
+    int slot = slot0 + kk;
+    slot = slot >= cap ? slot - cap : slot;
+    return ring + (z * cap + slot) * (int64_t)p.d + hoff;
   };
+  auto key_row = [&](float *ring, const float *nw, int kk) -> const float * {
+    if (kk >= kk_new) return nw + (z * p.rows_new + (kk - kk_new)) * p.ld_new + hoff;
+    return ring_row(ring, kk);
+  };
+  const int kk_s = (int)(p.s - p.k_lo);  // keys >= kk_s are this chunk's new frames
 
   for (int j = 0; j < CQ; j++) {
     float qd = j < c ? p.q[(z * c + j) * p.ldq + hoff + t] : 0.0f;
@@ -103,11 +119,9 @@ __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
       float *kdst[KT];
 #pragma unroll
       for (int b = 0; b < KT; b++) {
-        const int64_t fr = p.k_lo + (kt0 + b < band ? kt0 + b : band - 1);
-        krow[b] = key_row(p.k_ring, p.k_new, fr);
-        kdst[b] = (p.k_ring && fr >= p.s && kt0 + b < band)
-                      ? p.k_ring + (z * p.cap + fr % p.cap) * (int64_t)p.d + hoff
-                      : nullptr;
+        const int kk = kt0 + b < band ? kt0 + b : band - 1;
+        krow[b] = key_row(p.k_ring, p.k_new, kk);
+        kdst[b] = (p.k_ring && kt0 + b >= kk_s && kt0 + b < band) ? ring_row(p.k_ring, kk) : nullptr;
       }
       const float *prow[NPV];
 #pragma unroll
@@ -116,14 +130,28 @@ __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
         pi = pi < 0 ? 0 : (pi >= p.np ? p.np - 1 : pi);
         prow[m] = p.pos_p + (p.pr_lo + pi) * (int64_t)p.d + hoff;
       }
+      // operands of chunk ch + 1 are loaded while chunk ch computes
+      float kv[KT], pv[NPV];
+#pragma unroll
+      for (int b = 0; b < KT; b++) kv[b] = krow[b][l];
+#pragma unroll
+      for (int m = 0; m < NPV; m++) pv[m] = prow[m][l];
 #pragma unroll 1
       for (int ch = 0; ch < NCH; ch++) {
         const int i = ch * kLanes + l;
-        float kv[KT], pv[NPV];
+#if SC_ATTN_PREFETCH
+        const int in = ch + 1 < NCH ? i + kLanes : i;
+        float kn[KT], pn[NPV];
+#pragma unroll
+        for (int b = 0; b < KT; b++) kn[b] = krow[b][in];
+#pragma unroll
+        for (int m = 0; m < NPV; m++) pn[m] = prow[m][in];
+#else
 #pragma unroll
         for (int b = 0; b < KT; b++) kv[b] = krow[b][i];
 #pragma unroll
         for (int m = 0; m < NPV; m++) pv[m] = prow[m][i];
+#endif
 #pragma unroll
         for (int b = 0; b < KT; b++)
           if (kdst[b]) kdst[b][i] = kv[b];
@@ -136,6 +164,12 @@ __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
             acc[j][b] = __fmaf_rn(qu, kv[b], inner);
           }
         }
+#if SC_ATTN_PREFETCH
+#pragma unroll
+        for (int b = 0; b < KT; b++) kv[b] = kn[b];
+#pragma unroll
+        for (int m = 0; m < NPV; m++) pv[m] = pn[m];
+#endif
       }
 #pragma unroll
       for (int j = 0; j < CQ; j++)
@@ -187,13 +221,231 @@ __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
     float acc[CQ];
 #pragma unroll
     for (int j = 0; j < CQ; j++) acc[j] = 0.0f;
+#pragma unroll 4
     for (int kk = 0; kk < band; kk++) {
-      int64_t fr = p.k_lo + kk;
-      float vv = key_row(p.v_ring, p.v_new, fr)[t];
-      if (p.v_ring && fr >= p.s) p.v_ring[(z * p.cap + fr % p.cap) * (int64_t)p.d + hoff + t] = vv;
+      float vv = key_row(p.v_ring, p.v_new, kk)[t];
+      if (p.v_ring && kk >= kk_s) ring_row(p.v_ring, kk)[t] = vv;
 #pragma unroll
       for (int j = 0; j < CQ; j++)
         if (kk >= k0s[j] && kk < k1s[j]) acc[j] = __fmaf_rn(s_qk[j * band + kk], vv, acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < CQ; j++)
+      if (j < c) p.out[(z * c + j) * p.ldo + hoff + t] = acc[j];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Staged variant (the path every band that fits in shared memory takes):
+// the same arithmetic in the same order, with the head's K band, its pos
+// rows and q+u / q+v staged once in shared memory in a lane-major order --
+// element i = 16*ch + l of a row sits at (ch/4)*64 + 4l + ch%4 -- so that
+// SIMD lane l reads four consecutive chunks of a row with one 16-byte load.
+// A warp takes KT keys, each half-warp a group of 4 queries.  After the
+// scores, the V band replaces K in shared memory (cp.async, overlapped with
+// the softmax) and P.V runs from there with the weights outside each
+// query's band set to zero (fma(0, v, acc) == acc, so the sum over the band
+// in order is unchanged).
+constexpr int kStageKT = 8;
+
+__device__ __forceinline__ int lane_major(int i) { return (i >> 6) * 64 + (i & 15) * 4 + ((i >> 4) & 3); }
+
+__device__ __forceinline__ float f4c(const float4 &v, int c) {
+  return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+__host__ __device__ constexpr int stage_band_pad(int band) { return (band + 3) & ~3; }
+
+template <int HD, int CQ>
+__host__ __device__ constexpr size_t attn_stage_smem_floats(int band, int np) {
+  return (size_t)band * HD + (size_t)np * HD + 2 * (size_t)CQ * HD + (size_t)CQ * stage_band_pad(band) +
+         (size_t)(HD / 16) * 4 * kStageKT * kRedStride;
+}
+
+template <int HD, int CQ>
+__global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
+  constexpr int NW = HD / 32;
+  constexpr int NQG = CQ / 4;        // query groups of 4
+  constexpr int KT = kStageKT;
+  constexpr int NPV = 4 + KT - 1;    // pos rows of one (group, tile)
+  constexpr int NHALF = HD / 64;     // 4-chunk slices per row
+  extern __shared__ __align__(16) float sm[];
+  const int band = (int)(p.k_hi - p.k_lo), np = p.np, bp = stage_band_pad(band);
+  float *s_k = sm;                   // [band][HD] K lane-major, later V natural
+  float *s_p = s_k + band * HD;      // [np][HD]   pos rows lane-major
+  float *s_qu = s_p + np * HD;       // [CQ][HD]   q + u lane-major
+  float *s_qv = s_qu + CQ * HD;      // [CQ][HD]   q + v lane-major
+  float *s_w = s_qv + CQ * HD;       // [CQ][bp]   scores, then weights
+  float *s_red = s_w + CQ * bp;      // [2*NW][4*KT][kRedStride]
+  const int h = blockIdx.x;
+  const int64_t z = blockIdx.y;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int hoff = h * HD;
+  const int c = p.c;
+  const int kk_new = (int)(p.new_lo - p.k_lo);
+  const int slot0 = p.cap > 0 ? (int)(p.k_lo % p.cap) : 0;
+  const int cap = (int)p.cap;
+  auto ring_row = [&](float *ring, int kk) -> float * {
+    int slot = slot0 + kk;
+    slot = slot >= cap ? slot - cap : slot;
+    return ring + (z * cap + slot) * (int64_t)p.d + hoff;
+  };
+  auto key_row = [&](float *ring, const float *nw, int kk) -> const float * {
+    if (kk >= kk_new) return nw + (z * p.rows_new + (kk - kk_new)) * p.ld_new + hoff;
+    return ring_row(ring, kk);
+  };
+  const int kk_s = (int)(p.s - p.k_lo);
+
+  // ---- stage K (and write the new K rows to the ring), pos rows, q ----
+  for (int kk = warp; kk < band; kk += NW) {
+    const float *src = key_row(p.k_ring, p.k_new, kk);
+    float *dst_ring = (p.k_ring && kk >= kk_s) ? ring_row(p.k_ring, kk) : nullptr;
+    for (int e4 = lane; e4 < HD / 4; e4 += 32) {
+      const float4 v = *reinterpret_cast<const float4 *>(src + e4 * 4);
+      if (dst_ring) *reinterpret_cast<float4 *>(dst_ring + e4 * 4) = v;
+      float *d = s_k + kk * HD + lane_major(e4 * 4);
+      d[0] = v.x, d[4] = v.y, d[8] = v.z, d[12] = v.w;
+    }
+  }
+  for (int r = warp; r < np; r += NW) {
+    const float *src = p.pos_p + (p.pr_lo + r) * (int64_t)p.d + hoff;
+    for (int e4 = lane; e4 < HD / 4; e4 += 32) {
+      const float4 v = *reinterpret_cast<const float4 *>(src + e4 * 4);
+      float *d = s_p + r * HD + lane_major(e4 * 4);
+      d[0] = v.x, d[4] = v.y, d[8] = v.z, d[12] = v.w;
+    }
+  }
+  for (int j = 0; j < CQ; j++) {
+    const float qd = j < c ? p.q[(z * c + j) * p.ldq + hoff + t] : 0.0f;
+    s_qu[j * HD + lane_major(t)] = j < c ? __fadd_rn(qd, p.u[hoff + t]) : 0.0f;
+    s_qv[j * HD + lane_major(t)] = j < c ? __fadd_rn(qd, p.v[hoff + t]) : 0.0f;
+  }
+  __syncthreads();
+
+  // ---- A: scores (score_dot order) ----
+  {
+    const int hw2 = lane >> 4, l = lane & 15;
+    float *red = s_red + (warp * 2 + hw2) * (4 * KT * kRedStride);
+    // pos row of (query j, key kk) is prow0 + j - kk
+    const int prow0 = (int)(p.s + p.pos_off - p.k_lo - p.pr_lo);
+    for (int kt0 = warp * KT; kt0 < band; kt0 += NW * KT) {
+      for (int qg = hw2; qg < NQG; qg += 2) {
+        float acc[4][KT];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+          for (int b = 0; b < KT; b++) acc[j][b] = 0.0f;
+        int koff[KT], poff[NPV];
+#pragma unroll
+        for (int b = 0; b < KT; b++) koff[b] = min(kt0 + b, band - 1) * HD + l * 4;
+#pragma unroll
+        for (int m = 0; m < NPV; m++) {
+          int pi = prow0 - kt0 + 4 * qg - (KT - 1) + m;  // masked pairs may fall outside
+          pi = pi < 0 ? 0 : (pi >= np ? np - 1 : pi);
+          poff[m] = pi * HD + l * 4;
+        }
+        const int qoff = 4 * qg * HD + l * 4;
+#pragma unroll
+        for (int hh = 0; hh < NHALF; hh++) {
+          float4 kv[KT], pv[NPV], qu[4], qv[4];
+#pragma unroll
+          for (int b = 0; b < KT; b++) kv[b] = *reinterpret_cast<const float4 *>(s_k + koff[b] + hh * 64);
+#pragma unroll
+          for (int m = 0; m < NPV; m++) pv[m] = *reinterpret_cast<const float4 *>(s_p + poff[m] + hh * 64);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            qu[j] = *reinterpret_cast<const float4 *>(s_qu + qoff + j * HD + hh * 64);
+            qv[j] = *reinterpret_cast<const float4 *>(s_qv + qoff + j * HD + hh * 64);
+          }
+#pragma unroll
+          for (int cc = 0; cc < 4; cc++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+              for (int b = 0; b < KT; b++) {
+                const float inner = __fmaf_rn(f4c(qv[j], cc), f4c(pv[j - b + KT - 1], cc), acc[j][b]);
+                acc[j][b] = __fmaf_rn(f4c(qu[j], cc), f4c(kv[b], cc), inner);
+              }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+          for (int b = 0; b < KT; b++) red[(j * KT + b) * kRedStride + l] = acc[j][b];
+        __syncwarp();
+        for (int pr = l; pr < 4 * KT; pr += kLanes) {
+          const int j = 4 * qg + pr / KT, b = pr % KT;
+          float sum = red[pr * kRedStride];
+#pragma unroll
+          for (int q = 1; q < kLanes; q++) sum = __fadd_rn(sum, red[pr * kRedStride + q]);
+          if (j < c && kt0 + b < band) s_w[j * bp + kt0 + b] = __fmul_rn(sum, p.scale);
+        }
+        __syncwarp();
+      }
+    }
+  }
+  __syncthreads();
+  // ---- V band into shared memory (natural order), overlapped with C ----
+  for (int kk = warp; kk < band; kk += NW) {
+    const float *src = key_row(p.v_ring, p.v_new, kk);
+    for (int e4 = lane; e4 < HD / 4; e4 += 32) cp_async16(s_k + kk * HD + e4 * 4, src + e4 * 4);
+    if (p.v_ring && kk >= kk_s) {
+      float *dst = ring_row(p.v_ring, kk);
+      for (int e4 = lane; e4 < HD / 4; e4 += 32)
+        *reinterpret_cast<float4 *>(dst + e4 * 4) = *reinterpret_cast<const float4 *>(src + e4 * 4);
+    }
+  }
+  // ---- C: band mask + softmax per query (simd_kernel.rs:1010-1104) ----
+  for (int j = warp; j < CQ; j += NW) {
+    float *row = s_w + j * bp;
+    if (j >= c) {
+      for (int kk = lane; kk < bp; kk += 32) row[kk] = 0.0f;
+      continue;
+    }
+    int64_t kmin, kmax;
+    band_of(p.s + j, p.chunk, p.left_chunks, p.k_hi, kmin, kmax);
+    const int k0 = (int)(kmin - p.k_lo), k1 = (int)(kmax - p.k_lo);
+    float mx = -INFINITY;
+    for (int kk = k0 + lane; kk < k1; kk += 32) mx = fmaxf(mx, row[kk]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int kk = lane; kk < bp; kk += 32)
+      row[kk] = (kk >= k0 && kk < k1) ? exp_rn(__fsub_rn(row[kk], mx)) : 0.0f;
+    __syncwarp();
+    float inv = 0.0f;
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (int kk = k0; kk < k1; kk++) sum = __fadd_rn(sum, row[kk]);
+      inv = __fdiv_rn(1.0f, sum);
+    }
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int kk = lane; kk < bp; kk += 32) row[kk] = __fmul_rn(row[kk], inv);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  // ---- D: P.V over the band in order, one thread per head dim ----
+  {
+    float acc[CQ];
+#pragma unroll
+    for (int j = 0; j < CQ; j++) acc[j] = 0.0f;
+    for (int kk0 = 0; kk0 < bp; kk0 += 4) {
+      float4 w[CQ];
+#pragma unroll
+      for (int j = 0; j < CQ; j++) w[j] = *reinterpret_cast<const float4 *>(s_w + j * bp + kk0);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int kk = kk0 + e;
+        if (kk >= band) break;
+        const float vv = s_k[kk * HD + t];
+#pragma unroll
+        for (int j = 0; j < CQ; j++) acc[j] = __fmaf_rn(f4c(w[j], e), vv, acc[j]);
+      }
     }
 #pragma unroll
     for (int j = 0; j < CQ; j++)
@@ -251,8 +503,38 @@ int attn_prepare(AttnParams &p, int64_t n_pos) {
   return kOk;
 }
 
+// The staged kernel needs 16-byte aligned rows and its shared-memory
+// footprint within the 227 KB a CTA may use.
+template <int HD, int CQ>
+static bool stage_fits(const AttnParams &p) {
+  const int band = (int)(p.k_hi - p.k_lo);
+  auto al = [](const void *q) { return ((uintptr_t)q & 15) == 0; };
+  const bool aligned = al(p.q) && al(p.k_new) && al(p.v_new) && al(p.pos_p) && p.d % 4 == 0 && p.ldq % 4 == 0 &&
+                       p.ld_new % 4 == 0 && (!p.k_ring || (al(p.k_ring) && al(p.v_ring)));
+  return aligned && attn_stage_smem_floats<HD, CQ>(band, p.np) * sizeof(float) <= 227 * 1024;
+}
+
+template <int HD, int CQ>
+static int launch_stage_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
+  const int band = (int)(p.k_hi - p.k_lo);
+  const size_t smem = attn_stage_smem_floats<HD, CQ>(band, p.np) * sizeof(float);
+  auto kern = attn_stage_kernel<HD, CQ>;
+  static size_t smem_set[64] = {};
+  int dev = 0;
+  SC_CUDA(cudaGetDevice(&dev));
+  if (smem > 48 * 1024 && dev < 64 && smem_set[dev] < smem) {
+    SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    smem_set[dev] = smem;
+  }
+  kern<<<dim3((unsigned)p.n_heads, (unsigned)n_streams), HD, smem, st>>>(p);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
 template <int HD, int CQ>
 static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
+  if (stage_fits<HD, CQ>(p)) return launch_stage_t<HD, CQ>(p, n_streams, st);
   int band = (int)(p.k_hi - p.k_lo);
   size_t smem = attn_smem_floats<HD, CQ>(band) * sizeof(float);
   auto kern = attn_stream_kernel<HD, CQ>;
