@@ -257,6 +257,9 @@ __device__ __forceinline__ float f4c(const float4 &v, int c) {
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
@@ -303,30 +306,43 @@ __global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
   };
   const int kk_s = (int)(p.s - p.k_lo);
 
-  // ---- stage K (and write the new K rows to the ring), pos rows, q ----
-  for (int kk = warp; kk < band; kk += NW) {
-    const float *src = key_row(p.k_ring, p.k_new, kk);
-    float *dst_ring = (p.k_ring && kk >= kk_s) ? ring_row(p.k_ring, kk) : nullptr;
-    for (int e4 = lane; e4 < HD / 4; e4 += 32) {
-      const float4 v = *reinterpret_cast<const float4 *>(src + e4 * 4);
-      if (dst_ring) *reinterpret_cast<float4 *>(dst_ring + e4 * 4) = v;
-      float *d = s_k + kk * HD + lane_major(e4 * 4);
-      d[0] = v.x, d[4] = v.y, d[8] = v.z, d[12] = v.w;
+  // ---- stage K, pos rows (async copies, all in flight at once), q; the
+  // new K rows also go to the ring.  Rows already in lane-major order are
+  // copied 16 bytes at a time; natural rows element by element into their
+  // lane-major slots. ----
+  if (p.lane_major) {
+    constexpr int V4 = HD / 4;  // 16-byte pieces per row
+    for (int x = t; x < band * V4; x += HD) {
+      const int kk = x / V4, e4 = x % V4;
+      cp_async16(s_k + kk * HD + e4 * 4, key_row(p.k_ring, p.k_new, kk) + e4 * 4);
+    }
+    const float *prow = p.pos_p + p.pr_lo * (int64_t)p.d + hoff;
+    for (int x = t; x < np * V4; x += HD) {
+      const int r = x / V4, e4 = x % V4;
+      cp_async16(s_p + r * HD + e4 * 4, prow + (int64_t)r * p.d + e4 * 4);
+    }
+  } else {
+    const int dt = lane_major(t);
+    for (int kk = 0; kk < band; kk++) cp_async4(s_k + kk * HD + dt, key_row(p.k_ring, p.k_new, kk) + t);
+    const float *prow = p.pos_p + p.pr_lo * (int64_t)p.d + hoff + t;
+    for (int r = 0; r < np; r++) cp_async4(s_p + r * HD + dt, prow + (int64_t)r * p.d);
+  }
+  if (p.k_ring)
+    for (int kk = max(kk_s, 0) + warp; kk < band; kk += NW) {
+      const float *src = key_row(p.k_ring, p.k_new, kk);
+      float *dst = ring_row(p.k_ring, kk);
+      for (int e4 = lane; e4 < HD / 4; e4 += 32)
+        *reinterpret_cast<float4 *>(dst + e4 * 4) = *reinterpret_cast<const float4 *>(src + e4 * 4);
+    }
+  {
+    const int dt = p.lane_major ? t : lane_major(t);
+    for (int j = 0; j < CQ; j++) {
+      const float qd = j < c ? p.q[(z * c + j) * p.ldq + hoff + t] : 0.0f;
+      s_qu[j * HD + dt] = j < c ? __fadd_rn(qd, p.u[hoff + t]) : 0.0f;
+      s_qv[j * HD + dt] = j < c ? __fadd_rn(qd, p.v[hoff + t]) : 0.0f;
     }
   }
-  for (int r = warp; r < np; r += NW) {
-    const float *src = p.pos_p + (p.pr_lo + r) * (int64_t)p.d + hoff;
-    for (int e4 = lane; e4 < HD / 4; e4 += 32) {
-      const float4 v = *reinterpret_cast<const float4 *>(src + e4 * 4);
-      float *d = s_p + r * HD + lane_major(e4 * 4);
-      d[0] = v.x, d[4] = v.y, d[8] = v.z, d[12] = v.w;
-    }
-  }
-  for (int j = 0; j < CQ; j++) {
-    const float qd = j < c ? p.q[(z * c + j) * p.ldq + hoff + t] : 0.0f;
-    s_qu[j * HD + lane_major(t)] = j < c ? __fadd_rn(qd, p.u[hoff + t]) : 0.0f;
-    s_qv[j * HD + lane_major(t)] = j < c ? __fadd_rn(qd, p.v[hoff + t]) : 0.0f;
-  }
+  cp_async_wait_all();
   __syncthreads();
 
   // ---- A: scores (score_dot order) ----
@@ -535,6 +551,11 @@ static int launch_stage_t(const AttnParams &p, int64_t n_streams, cudaStream_t s
 template <int HD, int CQ>
 static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
   if (stage_fits<HD, CQ>(p)) return launch_stage_t<HD, CQ>(p, n_streams, st);
+  if (p.lane_major) {
+    set_error("attn_stream: lane-major rows need the staged kernel (band %lld too large or rows unaligned)",
+              (long long)(p.k_hi - p.k_lo));
+    return kErrUnsupported;
+  }
   int band = (int)(p.k_hi - p.k_lo);
   size_t smem = attn_smem_floats<HD, CQ>(band) * sizeof(float);
   auto kern = attn_stream_kernel<HD, CQ>;

@@ -22,6 +22,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <algorithm>
 #include <vector>
 
 #include "sc_kernels.cuh"
@@ -51,6 +52,10 @@ int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int
 
 constexpr int kMelHistory = 24;  // mel frames of left context (streaming.rs:188)
 constexpr int kDumpStages = 8;
+
+// Position of head element i in the attention's lane-major row order:
+// element 16*ch + l at (ch/4)*64 + 4l + ch%4 (head_dim a multiple of 64).
+static int64_t lane_major_h(int64_t i) { return (i >> 6) * 64 + (i & 15) * 4 + ((i >> 4) & 3); }
 
 struct Lin {
   Q8Weights w{};
@@ -141,7 +146,12 @@ struct Loader {
     e->allocs.push_back(p);
     return (float *)p;
   }
-  float *f32(const std::string &name, int64_t count, bool optional = false) {
+  // Rows (or elements) of a [.., d] part permuted into lane-major order
+  // within each head: source index h*hd + i goes to h*hd + lane_major(i).
+  static int64_t head_perm(int64_t n, int64_t hd) {
+    return hd > 0 ? (n / hd) * hd + lane_major_h(n % hd) : n;
+  }
+  float *f32(const std::string &name, int64_t count, bool optional = false, int64_t perm_hd = 0) {
     const sc_tensor *x = find(name);
     if (!x) {
       if (!optional && err.empty()) err = "tensor " + name + " not found";
@@ -152,12 +162,22 @@ struct Loader {
       return nullptr;
     }
     float *d = dev_alloc((size_t)count * 4);
-    if (d && cudaMemcpy(d, x->data, (size_t)count * 4, cudaMemcpyHostToDevice) != cudaSuccess) err = "upload failed";
+    const float *src = (const float *)x->data;
+    std::vector<float> perm;
+    if (perm_hd > 0) {
+      perm.resize((size_t)count);
+      for (int64_t i = 0; i < count; i++) perm[(size_t)head_perm(i, perm_hd)] = src[i];
+      src = perm.data();
+    }
+    if (d && cudaMemcpy(d, src, (size_t)count * 4, cudaMemcpyHostToDevice) != cudaSuccess) err = "upload failed";
     return d;
   }
   // Q8 linear [out, inp] (GGUF dims [inp, out]); `parts` tensors are stacked
-  // row-wise (QKV fusion).
-  bool lin(const std::vector<std::string> &bases, int64_t inp, int64_t out_each, Lin *l, bool bias_optional) {
+  // row-wise (QKV fusion).  Parts listed in perm_parts get their output rows
+  // (and bias) permuted lane-major within each head of perm_hd rows: the
+  // same per-row arithmetic, outputs in the attention's staging order.
+  bool lin(const std::vector<std::string> &bases, int64_t inp, int64_t out_each, Lin *l, bool bias_optional,
+           const std::vector<int> &perm_parts = {}, int64_t perm_hd = 0) {
     const int64_t nb = (inp + 31) / 32, padded = nb * 34, rows = out_each * (int64_t)bases.size();
     std::vector<uint8_t> raw((size_t)(rows * padded));
     std::vector<float> bias((size_t)rows, 0.0f);
@@ -169,14 +189,19 @@ struct Loader {
                                std::to_string(out_each) + "]";
         return false;
       }
-      memcpy(raw.data() + p * out_each * padded, x->data, (size_t)(out_each * padded));
+      const bool perm = std::find(perm_parts.begin(), perm_parts.end(), (int)p) != perm_parts.end();
+      const int64_t hd = perm ? perm_hd : 0;
+      for (int64_t r = 0; r < out_each; r++)
+        memcpy(raw.data() + (p * out_each + head_perm(r, hd)) * padded, (const uint8_t *)x->data + r * padded,
+               (size_t)padded);
       const sc_tensor *b = find(bases[p] + ".bias");
       if (b) {
         if (b->dtype != 0 || numel(b) != out_each) {
           if (err.empty()) err = "tensor " + bases[p] + ".bias mis-shaped";
           return false;
         }
-        memcpy(bias.data() + p * out_each, b->data, (size_t)out_each * 4);
+        for (int64_t r = 0; r < out_each; r++)
+          bias[(size_t)(p * out_each + head_perm(r, hd))] = ((const float *)b->data)[r];
         have_bias = true;
       }
     }
@@ -234,8 +259,10 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
   const sc_encoder_config &c = *cfg;
   if (c.d_model % 256 || c.d_model > 4096 || c.n_heads <= 0 || c.d_model % c.n_heads || c.att_right < 0 ||
       c.conv_kernel < 1 || c.conv_left != c.conv_kernel - 1 || c.max_frames < 1 || c.max_frames > 16 ||
-      c.feat_in <= 0 || c.conv_channels <= 0 || c.n_layers < 0) {
-    set_error("stream_encoder_create: unsupported config (d_model %d, heads %d, conv %d/%d, max_frames %d)",
+      c.feat_in <= 0 || c.conv_channels <= 0 || c.n_layers < 0 ||
+      (c.d_model / c.n_heads != 64 && c.d_model / c.n_heads != 128)) {
+    set_error("stream_encoder_create: unsupported config (d_model %d, heads %d (head_dim 64 or 128), conv %d/%d, "
+              "max_frames %d)",
               c.d_model, c.n_heads, c.conv_kernel, c.conv_left, c.max_frames);
     return kErrUnsupported;
   }
@@ -257,7 +284,7 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
   e->glu_cap = c.conv_left + c.max_frames;
   e->out_cap = 64;
   e->t_mel_max = kMelHistory + 8 * (int64_t)c.max_frames + 8;
-  const int64_t d = c.d_model, dff = c.d_ff, C = c.conv_channels;
+  const int64_t d = c.d_model, dff = c.d_ff, C = c.conv_channels, hd = d / c.n_heads;
   Loader L{tensors, n_tensors, e, {}};
   // pre-encode (nemotron/encoder.rs:89-160)
   const std::string pc = "encoder.pre_encode.conv.";
@@ -285,13 +312,16 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     ly.ln_ff2_b = L.f32(p + "norm_feed_forward2.bias", d);
     ly.ln_out_w = L.f32(p + "norm_out.weight", d);
     ly.ln_out_b = L.f32(p + "norm_out.bias", d);
-    ly.pos_u = L.f32(p + "self_attn.pos_bias_u", d);
-    ly.pos_v = L.f32(p + "self_attn.pos_bias_v", d);
+    // q, k, pos rows and the pos biases live in lane-major head order (the
+    // attention kernel's staging order); v and everything else stay natural
+    ly.pos_u = L.f32(p + "self_attn.pos_bias_u", d, false, hd);
+    ly.pos_v = L.f32(p + "self_attn.pos_bias_v", d, false, hd);
     ly.dw = L.f32(p + "conv.depthwise_conv.weight", d * c.conv_kernel);
     ok = L.err.empty() && L.lin({p + "feed_forward1.linear1"}, d, dff, &ly.ff1_1, true) &&
          L.lin({p + "feed_forward1.linear2"}, dff, d, &ly.ff1_2, true) &&
-         L.lin({p + "self_attn.linear_q", p + "self_attn.linear_k", p + "self_attn.linear_v"}, d, d, &ly.qkv, true) &&
-         L.lin({p + "self_attn.linear_pos"}, d, d, &ly.pos, true) &&
+         L.lin({p + "self_attn.linear_q", p + "self_attn.linear_k", p + "self_attn.linear_v"}, d, d, &ly.qkv, true,
+               {0, 1}, hd) &&
+         L.lin({p + "self_attn.linear_pos"}, d, d, &ly.pos, true, {0}, hd) &&
          L.lin({p + "self_attn.linear_out"}, d, d, &ly.out, true) &&
          L.lin({p + "conv.pointwise_conv1"}, d, 2 * d, &ly.pw1, true) &&
          L.lin({p + "conv.pointwise_conv2"}, d, d, &ly.pw2, true) &&
@@ -516,6 +546,7 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
       p.chunk = e->chunk;
       p.left_chunks = e->left_chunks;
       p.pos_off = pos_off;
+      p.lane_major = 1;  // q, k, pos rows and biases in lane-major head order
       TRY(attn_prepare(p, e->n_pos));
       TRY(launch_attn(p, Z, st));
     }
@@ -574,6 +605,15 @@ int sc_stream_encoder_dump(const sc_stream_encoder *e, int32_t stage, float *out
   const int64_t d = e->cfg.d_model;
   SC_CUDA(cudaMemcpy2D(out_host, d * 4, e->dump + (size_t)stage * e->dump_rows * 2 * d, 2 * d * 4, d * 4,
                        e->dump_rows, cudaMemcpyDeviceToHost));
+  if (stage == 4) {  // q is held in lane-major head order: back to natural
+    const int64_t hd = d / e->cfg.n_heads;
+    std::vector<float> row((size_t)d);
+    for (int64_t r = 0; r < e->dump_rows; r++) {
+      float *q = out_host + r * d;
+      for (int64_t i = 0; i < d; i++) row[(size_t)i] = q[(i / hd) * hd + lane_major_h(i % hd)];
+      memcpy(q, row.data(), (size_t)d * 4);
+    }
+  }
   if (rows) *rows = e->dump_rows;
   return kOk;
 }

@@ -100,6 +100,9 @@ struct AttnParams {
   int64_t s, k_lo, k_hi, chunk, left_chunks, pos_off;
   int64_t pr_lo;        // first pos row the chunk touches (attn_prepare)
   int np;               // number of pos rows touched (attn_prepare)
+  int lane_major;       // q, k (new and ring), u, v and pos rows are stored
+                        // lane-major within each head (element 16*ch + l
+                        // at (ch/4)*64 + 4l + ch%4); v_new / v_ring natural
 };
 int attn_prepare(AttnParams &p, int64_t n_pos);
 int launch_attn(const AttnParams &p, int64_t n_streams, cudaStream_t st);
