@@ -465,7 +465,15 @@ __global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
     }
 #pragma unroll
     for (int j = 0; j < CQ; j++)
-      if (j < c) p.out[(z * c + j) * p.ldo + hoff + t] = acc[j];
+      if (j < c) {
+        if (p.out) p.out[(z * c + j) * p.ldo + hoff + t] = acc[j];
+        if (p.qout.xq) {  // the warp's 32 dims are one block of the out-proj input
+          float sblk;
+          const int8_t q = warp_quantize_block(acc[j], true, sblk);
+          p.qout.xq[qout_code_index(p.qout, z * c + j, hoff + t)] = q;
+          if (lane == 0) p.qout.dx[((hoff + t) >> 5) * p.qout.t_pad + z * c + j] = sblk;
+        }
+      }
   }
 }
 
@@ -551,8 +559,9 @@ static int launch_stage_t(const AttnParams &p, int64_t n_streams, cudaStream_t s
 template <int HD, int CQ>
 static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
   if (stage_fits<HD, CQ>(p)) return launch_stage_t<HD, CQ>(p, n_streams, st);
-  if (p.lane_major) {
-    set_error("attn_stream: lane-major rows need the staged kernel (band %lld too large or rows unaligned)",
+  if (p.lane_major || p.qout.xq) {
+    set_error("attn_stream: lane-major rows / quantised output need the staged kernel (band %lld too large or "
+              "rows unaligned)",
               (long long)(p.k_hi - p.k_lo));
     return kErrUnsupported;
   }

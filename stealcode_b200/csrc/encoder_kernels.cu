@@ -113,6 +113,169 @@ __global__ void __launch_bounds__(kRowThreads) ln_rows_kernel(const float *__res
     if (k < nv) out[row * ldo + threadIdx.x + k * kRowThreads] = v[k];
 }
 
+// ---- row kernels with fused quantisation (one row per L lanes) -----------
+// A row of d = 32 * L * ... floats is held by L lanes of a warp, lane l of
+// the group owning the E = d / L consecutive elements [l*E, l*E + E), E a
+// multiple of 32: its E/16 LayerNorm chunks and E/32 quantisation blocks are
+// lane-local, and the reference's ordered chunk sums become a walk over the
+// group's lanes in order (every lane computes the same total).
+template <int E, int L>
+__device__ __forceinline__ float ordered_group_sum(const float (&cs)[E / 16], int lead) {
+  float t = 0.0f;
+#pragma unroll
+  for (int l = 0; l < L; l++)
+#pragma unroll
+    for (int c = 0; c < E / 16; c++) t = __fadd_rn(t, __shfl_sync(0xffffffffu, cs[c], lead + l));
+  return t;
+}
+
+// LayerNorm of v (the lane's E elements) in ln_forward's rounding
+// (simd_kernel.rs:734-805).
+template <int E, int L>
+__device__ __forceinline__ void ln_lane(float (&v)[E], int lead, const float *w, const float *b, float eps,
+                                        int i0) {
+  constexpr int d = E * L;
+  float cs[E / 16];
+#pragma unroll
+  for (int c = 0; c < E / 16; c++) {
+    cs[c] = v[16 * c];
+#pragma unroll
+    for (int q = 1; q < 16; q++) cs[c] = __fadd_rn(cs[c], v[16 * c + q]);
+  }
+  const float mean = __fdiv_rn(ordered_group_sum<E, L>(cs, lead), (float)d);
+#pragma unroll
+  for (int c = 0; c < E / 16; c++) {
+    float df = __fsub_rn(v[16 * c], mean);
+    cs[c] = __fmul_rn(df, df);
+#pragma unroll
+    for (int q = 1; q < 16; q++) {
+      df = __fsub_rn(v[16 * c + q], mean);
+      cs[c] = __fadd_rn(cs[c], __fmul_rn(df, df));
+    }
+  }
+  const float var = ordered_group_sum<E, L>(cs, lead);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(var, (float)d), eps)));
+#pragma unroll
+  for (int e4 = 0; e4 < E / 4; e4++) {
+    const float4 w4 = *reinterpret_cast<const float4 *>(w + i0 + 4 * e4);
+    const float4 b4 = *reinterpret_cast<const float4 *>(b + i0 + 4 * e4);
+    const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      float &x = v[4 * e4 + q];
+      x = __fmaf_rn(__fsub_rn(x, mean), __fmul_rn(wv[q], inv), bv[q]);
+    }
+  }
+}
+
+// quantize_col of the lane's E elements (features i0 .. i0 + E - 1 of frame
+// f), E/32 whole blocks, into the tiled codes of qo.
+template <int E>
+__device__ __forceinline__ void quant_lane(const float (&v)[E], const QOut &qo, int64_t f, int i0) {
+#pragma unroll
+  for (int blk = 0; blk < E / 32; blk++) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 32; e++) amax = fmaxf(amax, fabsf(v[32 * blk + e]));
+    const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
+    const float inv = __fdiv_rn(1.0f, sc);
+    uint32_t words[8];
+#pragma unroll
+    for (int w4 = 0; w4 < 8; w4++) {
+      uint32_t wd = 0;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int8_t code = amax != 0.0f ? rust_round_i8(__fmul_rn(v[32 * blk + 4 * w4 + q], inv)) : (int8_t)0;
+        wd |= (uint32_t)(uint8_t)code << (8 * q);
+      }
+      words[w4] = wd;
+    }
+    const int i = i0 + 32 * blk;
+    int8_t *dst = qo.xq + qout_code_index(qo, f, i);
+    *reinterpret_cast<uint4 *>(dst) = make_uint4(words[0], words[1], words[2], words[3]);
+    *reinterpret_cast<uint4 *>(dst + (int64_t)qo.ft * 16) = make_uint4(words[4], words[5], words[6], words[7]);
+    qo.dx[(i / 32) * qo.t_pad + f] = sc;
+  }
+}
+
+// LayerNorm of each row, written as codes for the next GEMM (and as f32
+// when out != nullptr).  rows_per_warp = 32 / L.
+template <int E, int L>
+__global__ void __launch_bounds__(128) ln_quant_kernel(const float *__restrict__ x, int64_t ldx,
+                                                       const float *__restrict__ w, const float *__restrict__ b,
+                                                       float eps, int64_t rows, QOut qo, float *__restrict__ out,
+                                                       int64_t ldo) {
+  const int lane = threadIdx.x & 31, sub = lane / L, lead = sub * L, l = lane % L;
+  const int64_t row = ((int64_t)blockIdx.x * 4 + (threadIdx.x >> 5)) * (32 / L) + sub;
+  const bool live = row < rows;
+  const int i0 = l * E;
+  float v[E];
+  const float *xr = x + (live ? row : 0) * ldx + i0;
+#pragma unroll
+  for (int e4 = 0; e4 < E / 4; e4++) {
+    const float4 t = *reinterpret_cast<const float4 *>(xr + 4 * e4);
+    v[4 * e4] = t.x, v[4 * e4 + 1] = t.y, v[4 * e4 + 2] = t.z, v[4 * e4 + 3] = t.w;
+  }
+  ln_lane<E, L>(v, lead, w, b, eps, i0);  // all lanes take part in the shuffles
+  if (!live) return;
+  if (out)
+#pragma unroll
+    for (int e4 = 0; e4 < E / 4; e4++)
+      *reinterpret_cast<float4 *>(out + row * ldo + i0 + 4 * e4) =
+          make_float4(v[4 * e4], v[4 * e4 + 1], v[4 * e4 + 2], v[4 * e4 + 3]);
+  quant_lane<E>(v, qo, row, i0);
+}
+
+// Causal depthwise conv over the GLU ring (taps in order, fused multiply-
+// adds as the reference's S-lane loop), the conv module's LayerNorm and
+// SiLU, then codes for pw2.  wt is the depthwise weight transposed to
+// [kh][d].  rows = n_streams * c, frame of row r: s + r % c.
+template <int E, int L, int KH>
+__global__ void __launch_bounds__(128)
+    dwconv_ln_silu_quant_kernel(const float *__restrict__ ring, int cap, int c, int kh_rt, int64_t s,
+                                const float *__restrict__ wt, const float *__restrict__ lnw,
+                                const float *__restrict__ lnb, float eps, int64_t rows, QOut qo,
+                                float *__restrict__ out) {
+  constexpr int d = E * L;
+  const int kh = KH > 0 ? KH : kh_rt;
+  const int lane = threadIdx.x & 31, sub = lane / L, lead = sub * L, l = lane % L;
+  const int64_t row = ((int64_t)blockIdx.x * 4 + (threadIdx.x >> 5)) * (32 / L) + sub;
+  const bool live = row < rows;
+  const int64_t rr = live ? row : 0;
+  const int64_t z = rr / c, fr = s + rr % c;
+  const int i0 = l * E;
+  float v[E];
+#pragma unroll
+  for (int e = 0; e < E; e++) v[e] = 0.0f;
+#pragma unroll
+  for (int t = 0; t < (KH > 0 ? KH : 64); t++) {
+    if (KH == 0 && t >= kh) break;
+    const int64_t ti = fr - (kh - 1) + t;
+    if (ti < 0) continue;
+    const float *rw = ring + (z * cap + ti % cap) * (int64_t)d + i0;
+    const float *ww = wt + (int64_t)t * d + i0;
+#pragma unroll
+    for (int e4 = 0; e4 < E / 4; e4++) {
+      const float4 a = *reinterpret_cast<const float4 *>(rw + 4 * e4);
+      const float4 k = *reinterpret_cast<const float4 *>(ww + 4 * e4);
+      v[4 * e4] = __fmaf_rn(a.x, k.x, v[4 * e4]);
+      v[4 * e4 + 1] = __fmaf_rn(a.y, k.y, v[4 * e4 + 1]);
+      v[4 * e4 + 2] = __fmaf_rn(a.z, k.z, v[4 * e4 + 2]);
+      v[4 * e4 + 3] = __fmaf_rn(a.w, k.w, v[4 * e4 + 3]);
+    }
+  }
+  ln_lane<E, L>(v, lead, lnw, lnb, eps, i0);
+  if (!live) return;
+#pragma unroll
+  for (int e = 0; e < E; e++) v[e] = silu_ref(v[e]);
+  if (out)
+#pragma unroll
+    for (int e4 = 0; e4 < E / 4; e4++)
+      *reinterpret_cast<float4 *>(out + row * d + i0 + 4 * e4) =
+          make_float4(v[4 * e4], v[4 * e4 + 1], v[4 * e4 + 2], v[4 * e4 + 3]);
+  quant_lane<E>(v, qo, row, i0);
+}
+
 // GLU of the new frames (h2 = [M][2d] time-major, gate first, value second)
 // stored into ring slot (s + j) % cap of stream z.
 __global__ void glu_ring_kernel(const float *__restrict__ h2, int c, int d, float *__restrict__ ring, int cap,
@@ -318,13 +481,22 @@ __global__ void __launch_bounds__(kPwThreads)
 // [z][t][f][C] -> rows (z, j) of [C*f] (channel-major, frequency fastest)
 // for frames start_rel .. start_rel + c - 1.
 __global__ void flatten_kernel(const float *__restrict__ x, int t, int f, int C, int start_rel, int c,
-                               float *__restrict__ out) {
+                               float *__restrict__ out, QOut qo) {
   const int64_t row = blockIdx.y;  // z * c + j
   const int64_t z = row / c, j = row % c;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)C * f) return;
-  const int ch = (int)(i / f), ff = (int)(i % f);
-  out[row * C * f + i] = x[((z * t + start_rel + j) * f + ff) * C + ch];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // blockDim 256: whole warps of one block
+  const bool valid = i < C * f;
+  const int ch = valid ? i / f : 0, ff = valid ? i % f : 0;
+  const float v = valid ? x[((z * t + start_rel + j) * f + ff) * C + ch] : 0.0f;
+  if (out && valid) out[row * C * f + i] = v;
+  if (qo.xq) {  // one warp = one 32-feature block of the pre-encode linear
+    float sblk;
+    const int8_t q = warp_quantize_block(v, valid, sblk);
+    if (i < (C * f + 31) / 32 * 32) {
+      qo.xq[qout_code_index(qo, row, i)] = q;
+      if ((threadIdx.x & 31) == 0) qo.dx[(i / 32) * qo.t_pad + row] = sblk;
+    }
+  }
 }
 
 // Output frames into the per-stream output ring (slot = frame % cap).
@@ -408,12 +580,69 @@ int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y
 }
 
 int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int start_rel, int c, float *out,
-                   cudaStream_t st) {
+                   cudaStream_t st, QOut qo) {
   dim3 grid((unsigned)ceil_div((int64_t)C * f, 256), (unsigned)(n_streams * c));
-  flatten_kernel<<<grid, 256, 0, st>>>(x, t, f, C, start_rel, c, out);
+  flatten_kernel<<<grid, 256, 0, st>>>(x, t, f, C, start_rel, c, out, qo);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
+}
+
+template <int E, int L>
+static int launch_ln_quant_t(const float *x, int64_t ldx, const float *w, const float *b, float eps, int64_t rows,
+                             const QOut &qo, float *out, int64_t ldo, cudaStream_t st) {
+  const int64_t warps = ceil_div(rows, 32 / L);
+  ln_quant_kernel<E, L><<<(unsigned)ceil_div(warps, 4), 128, 0, st>>>(x, ldx, w, b, eps, rows, qo, out, ldo);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+int launch_ln_quant(const float *x, int64_t ldx, const float *w, const float *b, float eps, int d, int64_t rows,
+                    const QOut &qo, float *out, int64_t ldo, cudaStream_t st) {
+  switch (d) {
+    case 256: return launch_ln_quant_t<32, 8>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
+    case 512: return launch_ln_quant_t<32, 16>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
+    case 1024: return launch_ln_quant_t<32, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
+    case 2048: return launch_ln_quant_t<64, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
+    case 4096: return launch_ln_quant_t<128, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
+    default:
+      set_error("layernorm+quantise: d=%d must be 256, 512, 1024, 2048 or 4096", d);
+      return kErrUnsupported;
+  }
+}
+
+template <int E, int L>
+static int launch_dwq_t(const float *ring, int cap, int64_t rows, int c, int kh, int64_t s, const float *wt,
+                        const float *lnw, const float *lnb, float eps, const QOut &qo, float *out, cudaStream_t st) {
+  const int64_t warps = ceil_div(rows, 32 / L);
+  const unsigned grid = (unsigned)ceil_div(warps, 4);
+  if (kh == 9)
+    dwconv_ln_silu_quant_kernel<E, L, 9><<<grid, 128, 0, st>>>(ring, cap, c, kh, s, wt, lnw, lnb, eps, rows, qo, out);
+  else if (kh <= 64)
+    dwconv_ln_silu_quant_kernel<E, L, 0><<<grid, 128, 0, st>>>(ring, cap, c, kh, s, wt, lnw, lnb, eps, rows, qo, out);
+  else {
+    set_error("conv module: kernel %d > 64 unsupported", kh);
+    return kErrUnsupported;
+  }
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+int launch_dwconv_ln_silu_quant(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s,
+                                const float *wt, const float *lnw, const float *lnb, float eps, const QOut &qo,
+                                float *out, cudaStream_t st) {
+  switch (d) {
+    case 256: return launch_dwq_t<32, 8>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
+    case 512: return launch_dwq_t<32, 16>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
+    case 1024: return launch_dwq_t<32, 32>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
+    case 2048: return launch_dwq_t<64, 32>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
+    case 4096: return launch_dwq_t<128, 32>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
+    default:
+      set_error("conv module: d=%d must be 256, 512, 1024, 2048 or 4096", d);
+      return kErrUnsupported;
+  }
 }
 
 int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st) {

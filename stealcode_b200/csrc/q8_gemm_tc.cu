@@ -49,6 +49,7 @@ struct TcParams {
   int64_t ldy;
   unsigned *status;
   Epilogue epi;
+  QOut qout;
 };
 
 // ---- tcgen05 wrappers -----------------------------------------------------
@@ -280,9 +281,54 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-    // ---- epilogue: y (+ bias) ----
+    // ---- epilogue: y (+ bias); or the next GEMM's codes, one block of 32
+    // output features per warp (the warp's lanes are 32 consecutive rows) ----
     const int64_t n = g * SC_GROUP_ROWS + row;
-    if (n < p.n_rows) {
+    if (p.qout.xq) {
+      const float bn = p.bias ? p.bias[n] : 0.0f;
+      float v[32], a[32];
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        v[j] = apply_epilogue(p.epi, __fadd_rn((j & 1) ? hi_of(acc[j >> 1]) : lo_of(acc[j >> 1]), bn), 0);
+        a[j] = fabsf(v[j]);
+      }
+      // block amax of every column over the warp's 32 rows: a butterfly that
+      // leaves column col_of(lane) in a[0] of this lane (max ignores order;
+      // fmaxf skips NaN like quantize_col's amax)
+#pragma unroll
+      for (int cnt = 32, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
+        const bool up = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < cnt / 2; i++) {
+          const float send = up ? a[i] : a[i + cnt / 2];
+          const float keep = up ? a[i + cnt / 2] : a[i];
+          a[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, off));
+        }
+      }
+      int mycol = 0;  // column whose amax this lane holds
+#pragma unroll
+      for (int cnt = 32, off = 16; cnt > 1; cnt >>= 1, off >>= 1)
+        if (lane & off) mycol += cnt / 2;
+      const float amax = a[0];
+      const float sblk = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
+      const float inv = __fdiv_rn(1.0f, sblk);
+      const int64_t fbase = ft * FT + col_base;  // frames of this thread's columns (< t_pad)
+      p.qout.dx[(n >> 5) * p.qout.t_pad + fbase + mycol] = sblk;
+      // codes: row n is element n % 32 of block n / 32 of the next GEMM's K
+      int8_t *dst = p.qout.xq + ((int64_t)ft * p.qout.nb + (n >> 5)) * (FT * 32) + ((n & 31) >> 4) * (FT * 16) +
+                    (int64_t)col_base * 16 + (n & 15);
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        int src = 0;  // lane holding column j: bit-reverse of the butterfly's split order
+#pragma unroll
+        for (int cnt = 32, off = 16, jj = j; cnt > 1; cnt >>= 1, off >>= 1)
+          if (jj >= cnt / 2) { src |= off; jj -= cnt / 2; }
+        const float ij = __shfl_sync(0xffffffffu, inv, src);
+        const float aj = __shfl_sync(0xffffffffu, amax, src);
+        dst[j * 16] = aj != 0.0f ? rust_round_i8(__fmul_rn(v[j], ij)) : (int8_t)0;
+        if (p.y && fbase + j < p.t) p.y[p.y_time_major ? (fbase + j) * p.ldy + n : n * p.ldy + fbase + j] = v[j];
+      }
+    } else if (n < p.n_rows) {
       const float bn = p.bias ? p.bias[n] : 0.0f;
 #pragma unroll
       for (int j = 0; j < 32; j++) {
@@ -290,7 +336,7 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
         const float v = (j & 1) ? hi_of(acc[j >> 1]) : lo_of(acc[j >> 1]);
         if (f < p.t) {
           const int64_t idx = p.y_time_major ? f * p.ldy + n : n * p.ldy + f;
-          p.y[idx] = apply_epilogue(p.epi, v + bn, idx);
+          p.y[idx] = apply_epilogue(p.epi, __fadd_rn(v, bn), idx);
         }
       }
     }
@@ -370,6 +416,12 @@ int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
   p.ldy = a.ldy;
   p.status = tc_status_ptr();
   p.epi = a.epi;
+  p.qout = a.qout;
+  if (p.qout.xq && (w->rows % SC_GROUP_ROWS || p.epi.op == kEpiResidual || p.qout.t_pad != a.t_pad ||
+                    p.qout.ft != tc_frame_tile(a.t) || p.qout.nb * 32 != w->rows)) {
+    set_error("q8_gemm_tc: quantised output needs rows %% 128 == 0, no residual and the same frame tiling");
+    return kErrInvalid;
+  }
   if (!p.status) {
     set_error("q8_gemm_tc: status word lookup failed");
     return kErrCuda;

@@ -47,7 +47,12 @@ int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int x_row0,
 int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t m_rows, int n, int k,
                         cudaStream_t st);
 int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int start_rel, int c, float *out,
-                   cudaStream_t st);
+                   cudaStream_t st, QOut qo);
+int launch_ln_quant(const float *x, int64_t ldx, const float *w, const float *b, float eps, int d, int64_t rows,
+                    const QOut &qo, float *out, int64_t ldo, cudaStream_t st);
+int launch_dwconv_ln_silu_quant(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s,
+                                const float *wt, const float *lnw, const float *lnb, float eps, const QOut &qo,
+                                float *out, cudaStream_t st);
 int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st);
 
 constexpr int kMelHistory = 24;  // mel frames of left context (streaming.rs:188)
@@ -67,6 +72,7 @@ struct Layer {
   float *ln_ff2_w, *ln_ff2_b, *ln_out_w, *ln_out_b;
   Lin ff1_1, ff1_2, qkv, pos, out, pw1, pw2, ff2_1, ff2_2;
   float *pos_u, *pos_v, *dw;
+  float *dw_t = nullptr;               // depthwise weight transposed to [kh][d]
   float *pos_p = nullptr;              // [n_pos][d], after the first step
   float *k_ring, *v_ring, *glu_ring;   // [n_streams][cap][d]
 };
@@ -98,6 +104,10 @@ struct sc_stream_encoder {
   // scratch
   float *x, *y, *xn, *h, *qkv, *attn, *h2, *o2, *out_ring;
   float *win, *p0, *p1, *p2, *flat, *pos_in;
+  // GEMM inputs as codes in the tensor-core tiled layout (two, so that a
+  // GEMM can write its successor's codes while reading its own)
+  int8_t *qx[2] = {nullptr, nullptr};
+  float *qd[2] = {nullptr, nullptr};
   void *ws = nullptr;
   size_t ws_bytes = 0;
   // stage dumps of one layer (the reference's STEALCODE_DUMP_DIR senc_b*_*
@@ -260,9 +270,10 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
   if (c.d_model % 256 || c.d_model > 4096 || c.n_heads <= 0 || c.d_model % c.n_heads || c.att_right < 0 ||
       c.conv_kernel < 1 || c.conv_left != c.conv_kernel - 1 || c.max_frames < 1 || c.max_frames > 16 ||
       c.feat_in <= 0 || c.conv_channels <= 0 || c.n_layers < 0 ||
-      (c.d_model / c.n_heads != 64 && c.d_model / c.n_heads != 128)) {
-    set_error("stream_encoder_create: unsupported config (d_model %d, heads %d (head_dim 64 or 128), conv %d/%d, "
-              "max_frames %d)",
+      (c.d_model / c.n_heads != 64 && c.d_model / c.n_heads != 128) || (c.d_model & (c.d_model - 1)) ||
+      c.d_ff % 128) {
+    set_error("stream_encoder_create: unsupported config (d_model %d (a power of two, 256..4096), heads %d "
+              "(head_dim 64 or 128), d_ff a multiple of 128, conv %d/%d, max_frames %d)",
               c.d_model, c.n_heads, c.conv_kernel, c.conv_left, c.max_frames);
     return kErrUnsupported;
   }
@@ -317,6 +328,17 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     ly.pos_u = L.f32(p + "self_attn.pos_bias_u", d, false, hd);
     ly.pos_v = L.f32(p + "self_attn.pos_bias_v", d, false, hd);
     ly.dw = L.f32(p + "conv.depthwise_conv.weight", d * c.conv_kernel);
+    if (const sc_tensor *dwx = L.find(p + "conv.depthwise_conv.weight")) {
+      if (dwx->dtype == 0 && L.numel(dwx) == d * c.conv_kernel) {
+        std::vector<float> tr((size_t)(d * c.conv_kernel));
+        const float *src = (const float *)dwx->data;
+        for (int64_t ch = 0; ch < d; ch++)
+          for (int64_t t = 0; t < c.conv_kernel; t++) tr[(size_t)(t * d + ch)] = src[ch * c.conv_kernel + t];
+        ly.dw_t = L.dev_alloc(tr.size() * 4);
+        if (ly.dw_t && cudaMemcpy(ly.dw_t, tr.data(), tr.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+          L.err = "upload failed";
+      }
+    }
     ok = L.err.empty() && L.lin({p + "feed_forward1.linear1"}, d, dff, &ly.ff1_1, true) &&
          L.lin({p + "feed_forward1.linear2"}, dff, d, &ly.ff1_2, true) &&
          L.lin({p + "self_attn.linear_q", p + "self_attn.linear_k", p + "self_attn.linear_v"}, d, d, &ly.qkv, true,
@@ -359,6 +381,11 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     const int64_t tmax = std::max<int64_t>(M, e->n_pos);
     e->ws_bytes = gemm_ws_bytes(tmax, kmax);
     e->ws = L.dev_alloc(e->ws_bytes);
+    const int64_t tp = std::max<int64_t>(ceil_div(M, 128) * 128, 64), kp = ceil_div(kmax, 32) * 32;
+    for (int i = 0; i < 2; i++) {
+      e->qx[i] = (int8_t *)L.dev_alloc((size_t)(tp * kp));
+      e->qd[i] = L.dev_alloc((size_t)(kp / 32 * tp * 4));
+    }
     ok = L.err.empty();
   }
   if (!ok) {
@@ -467,9 +494,17 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
   TRY(launch_conv2d_3x3s2(e->p2, Z, (int)tb, (int)r3, (int)(e3 - r3), (int)fb, (int)C, e->c5.w, e->c5.b, (int)C,
                           (int)r5, (int)n5, (int)fc, 0, e->p1, st));
   TRY(launch_pw_conv_relu(e->p1, e->c6.w, e->c6.b, e->p0, Z * n5 * fc, (int)C, (int)C, st));
-  TRY(launch_flatten(e->p0, Z, (int)n5, (int)fc, (int)C, 0, (int)cf, e->flat, st));
-  TRY(gemm_impl(&e->pre_out.w, e->flat, M, SC_LAYOUT_TIME_MAJOR, 0, e->pre_out.bias, e->x, SC_LAYOUT_TIME_MAJOR, d,
-                e->ws, e->ws_bytes, nullptr, st, Epilogue{}, true));
+  // GEMM inputs are quantised by their producers straight into the
+  // tensor-core operand layout (code buffers qx/qd, ping-pong)
+  const int ft = tc_frame_tile(M);
+  const int64_t t_pad = ceil_div(M, ft) * ft;
+  auto qbuf = [&](int i, int64_t k) { return QOut{e->qx[i], e->qd[i], ceil_div(k, 32), t_pad, ft}; };
+  auto gemm_q = [&](const Lin &l, const QOut &in, float *out, int64_t ldo, Epilogue epi, QOut next) {
+    TcGemmArgs ta{&l.w, in.xq, in.dx, M, t_pad, l.bias, out, 1, ldo, epi, next};
+    return gemm_tc(ta, st);
+  };
+  TRY(launch_flatten(e->p0, Z, (int)n5, (int)fc, (int)C, 0, (int)cf, nullptr, st, qbuf(0, C * fc)));
+  TRY(gemm_q(e->pre_out, qbuf(0, C * fc), e->x, d, Epilogue{}, QOut{}));
   // history for the next window
   TRY(launch_mel_hist(e->hist[e->hist_cur], kMelHistory, e->hist_frames, mel_new, (int)n_new, c.feat_in,
                       e->hist[e->hist_cur ^ 1], Z, st));
@@ -506,19 +541,18 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
                                 cudaMemcpyDeviceToDevice, st));
       return kOk;
     };
-    auto gemm = [&](const Lin &l, const float *in, float *out, int64_t ldo, Epilogue epi) {
-      return gemm_impl(&l.w, in, M, SC_LAYOUT_TIME_MAJOR, 0, l.bias, out, SC_LAYOUT_TIME_MAJOR, ldo, e->ws,
-                       e->ws_bytes, nullptr, st, epi, true);
-    };
-    // macaron FF1: y = x + 0.5 * FF(LN(x))
-    TRY(launch_ln_rows(e->x, d, ly.ln_ff1_w, ly.ln_ff1_b, eps, e->xn, d, M, (int)d, st));
-    TRY(gemm(ly.ff1_1, e->xn, e->h, dff, silu));
-    TRY(gemm(ly.ff1_2, e->h, e->y, d, Epilogue{kEpiResidual, e->x, 0.5f}));
+    const bool dumping = (int)li == e->dump_layer && e->dump;
+    const QOut qa = qbuf(0, d), qb_ff = qbuf(1, dff), qb_d = qbuf(1, d);
+    // macaron FF1: y = x + 0.5 * FF(LN(x)); the SiLU output goes to ff1_2 as codes
+    TRY(launch_ln_quant(e->x, d, ly.ln_ff1_w, ly.ln_ff1_b, eps, (int)d, M, qa, nullptr, d, st));
+    TRY(gemm_q(ly.ff1_1, qa, nullptr, dff, silu, qb_ff));
+    TRY(gemm_q(ly.ff1_2, qb_ff, e->y, d, Epilogue{kEpiResidual, e->x, 0.5f}, QOut{}));
     TRY(dump(0, e->y, d));
-    // rel-pos MHSA over the band, K/V from the rings
-    TRY(launch_ln_rows(e->y, d, ly.ln_att_w, ly.ln_att_b, eps, e->xn, d, M, (int)d, st));
+    // rel-pos MHSA over the band, K/V from the rings; its output goes to
+    // the out projection as codes
+    TRY(launch_ln_quant(e->y, d, ly.ln_att_w, ly.ln_att_b, eps, (int)d, M, qa, dumping ? e->xn : nullptr, d, st));
     TRY(dump(1, e->xn, d));
-    TRY(gemm(ly.qkv, e->xn, e->qkv, 3 * d, Epilogue{}));
+    TRY(gemm_q(ly.qkv, qa, e->qkv, 3 * d, Epilogue{}, QOut{}));
     {
       AttnParams p{};
       p.q = e->qkv;
@@ -534,8 +568,9 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
       p.pos_p = ly.pos_p;
       p.u = ly.pos_u;
       p.v = ly.pos_v;
-      p.out = e->attn;
+      p.out = dumping ? e->attn : nullptr;
       p.ldo = d;
+      p.qout = qb_d;
       p.c = (int)cf;
       p.d = (int)d;
       p.n_heads = c.n_heads;
@@ -551,22 +586,22 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
       TRY(launch_attn(p, Z, st));
     }
     TRY(dump(2, e->attn, d));
-    TRY(gemm(ly.out, e->attn, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}));
+    TRY(gemm_q(ly.out, qb_d, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}, QOut{}));
     TRY(dump(3, e->y, d));
-    // conv module: LN, pw1, GLU (ring), causal dw conv, LN, SiLU, pw2
-    TRY(launch_ln_rows(e->y, d, ly.ln_conv_w, ly.ln_conv_b, eps, e->xn, d, M, (int)d, st));
-    TRY(gemm(ly.pw1, e->xn, e->h2, 2 * d, Epilogue{}));
+    // conv module: LN, pw1, GLU (ring), causal dw conv + LN + SiLU (codes), pw2
+    TRY(launch_ln_quant(e->y, d, ly.ln_conv_w, ly.ln_conv_b, eps, (int)d, M, qa, nullptr, d, st));
+    TRY(gemm_q(ly.pw1, qa, e->h2, 2 * d, Epilogue{}, QOut{}));
     TRY(launch_glu_ring(e->h2, M, (int)cf, (int)d, ly.glu_ring, (int)e->glu_cap, s, st));
-    TRY(launch_dwconv_ln_silu(ly.glu_ring, (int)e->glu_cap, M, (int)cf, (int)d, c.conv_kernel, s, ly.dw,
-                              ly.conv_ln_w, ly.conv_ln_b, eps, e->o2, st));
+    TRY(launch_dwconv_ln_silu_quant(ly.glu_ring, (int)e->glu_cap, M, (int)cf, (int)d, c.conv_kernel, s, ly.dw_t,
+                                    ly.conv_ln_w, ly.conv_ln_b, eps, qb_d, dumping ? e->o2 : nullptr, st));
     TRY(dump(4, e->qkv, 3 * d));  // q of the new frames
     TRY(dump(5, e->o2, d));
-    TRY(gemm(ly.pw2, e->o2, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}));
+    TRY(gemm_q(ly.pw2, qb_d, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}, QOut{}));
     TRY(dump(6, e->y, d));
     // macaron FF2 and the block's final LN
-    TRY(launch_ln_rows(e->y, d, ly.ln_ff2_w, ly.ln_ff2_b, eps, e->xn, d, M, (int)d, st));
-    TRY(gemm(ly.ff2_1, e->xn, e->h, dff, silu));
-    TRY(gemm(ly.ff2_2, e->h, e->y, d, Epilogue{kEpiResidual, e->y, 0.5f}));
+    TRY(launch_ln_quant(e->y, d, ly.ln_ff2_w, ly.ln_ff2_b, eps, (int)d, M, qa, nullptr, d, st));
+    TRY(gemm_q(ly.ff2_1, qa, nullptr, dff, silu, qb_ff));
+    TRY(gemm_q(ly.ff2_2, qb_ff, e->y, d, Epilogue{kEpiResidual, e->y, 0.5f}, QOut{}));
     TRY(launch_ln_rows(e->y, d, ly.ln_out_w, ly.ln_out_b, eps, e->x, d, M, (int)d, st));
     TRY(dump(7, e->x, d));
   }

@@ -54,6 +54,22 @@ int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st);
 int small_gemm_status(unsigned *out);  // read and clear the kernels' status word
 
 // q8_gemm_tc.cu
+// Activation codes quantised by the kernel that produces them, written in
+// the tensor-core GEMM's tiled operand layout (ft = tc_frame_tile(t)): the
+// code of frame f, feature i at
+//   ((f / ft) * nb + i / 32) * ft * 32 + ((i % 32) / 16) * ft * 16 + (f % ft) * 16 + i % 16
+// and the block scale at dx[(i / 32) * t_pad + f].  xq == nullptr: unused.
+struct QOut {
+  int8_t *xq;
+  float *dx;
+  int64_t nb, t_pad;
+  int ft;
+};
+__host__ __device__ inline int64_t qout_code_index(const QOut &q, int64_t f, int64_t i) {
+  return ((f / q.ft) * q.nb + i / 32) * (int64_t)q.ft * 32 + ((i & 31) >> 4) * (int64_t)q.ft * 16 +
+         (f % q.ft) * 16 + (i & 15);
+}
+
 struct TcGemmArgs {
   const Q8Weights *w;
   const int8_t *xq;   // tiled activation codes (quantize_act with tile_ft = tc_frame_tile(t))
@@ -64,6 +80,8 @@ struct TcGemmArgs {
   int y_time_major;
   int64_t ldy;
   Epilogue epi;
+  QOut qout;          // quantise the epilogue output for the next GEMM (rows % 128 == 0;
+                      // y may then be nullptr)
 };
 int tc_frame_tile(int64_t t);
 int gemm_tc(const TcGemmArgs &a, cudaStream_t st);
@@ -100,6 +118,7 @@ struct AttnParams {
   int64_t s, k_lo, k_hi, chunk, left_chunks, pos_off;
   int64_t pr_lo;        // first pos row the chunk touches (attn_prepare)
   int np;               // number of pos rows touched (attn_prepare)
+  QOut qout;            // also write the output as codes for the next GEMM (out may be nullptr)
   int lane_major;       // q, k (new and ring), u, v and pos rows are stored
                         // lane-major within each head (element 16*ch + l
                         // at (ch/4)*64 + 4l + ch%4); v_new / v_ring natural
