@@ -31,8 +31,25 @@
 
 namespace sc {
 
-constexpr int kTcStages = 6;
-constexpr int kTcAccBufs = 2;
+#ifndef SC_TC_STAGES
+#define SC_TC_STAGES 8
+#endif
+#ifndef SC_TC_PHASES
+#define SC_TC_PHASES 4
+#endif
+constexpr int kTcStages = SC_TC_STAGES;
+// Bulk copies issued by one thread complete one after another (about half
+// a microsecond each, whatever their size), so the producer spreads them:
+// 4 lanes per block (one per copy), and kTcPhases block phases, lane
+// (phase, copy) handling blocks b = phase (mod kTcPhases).
+constexpr int kTcPhases = SC_TC_PHASES;
+static_assert(kTcStages >= kTcPhases, "every producer phase needs a stage in flight");
+#ifndef SC_TC_ACC_BUFS
+#define SC_TC_ACC_BUFS 2
+#endif
+// TMEM accumulator buffers (FT columns each, at most 512 columns in all):
+// a block's MMA may start once the drain has emptied the buffer it reuses.
+constexpr int kTcAccBufs = SC_TC_ACC_BUFS;
 
 static __device__ unsigned g_tc_status;
 
@@ -164,7 +181,7 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; s++) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 4);             // one arrive.expect_tx per copy lane
       mbar_init(&empty[s], 1 + 4 * DWG);  // MMA commit + one arrival per drain warp
     }
     for (int b = 0; b < kTcAccBufs; b++) {
@@ -186,17 +203,28 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
 
   bool ok = true;
   if (warp == 0) {
-    if (lane == 0) {
-      for (int b = 0; b < nb && ok; b++) {
+    if (lane < 4 * kTcPhases) {
+      const int cp = lane & 3, phase = lane >> 2;  // copy kind, block phase
+      for (int b = phase; b < nb && ok; b += kTcPhases) {
         const int s = b % kTcStages;
         const uint32_t ph = (uint32_t)(b / kTcStages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u)) { ok = false; break; }
         unsigned char *st = smem + s * L::kStage;
-        mbar_arrive_expect_tx(&full[s], L::kStage);
-        bulk_g2s(st, p.qs + (g * p.nb + b) * SC_TILE_BYTES, L::kA, &full[s]);
-        bulk_g2s(st + L::kA, p.xq + (ft * p.nb + b) * (int64_t)(FT * 32), L::kB, &full[s]);
-        bulk_g2s(st + L::kA + L::kB, p.sc + (g * p.nb + b) * SC_GROUP_ROWS, L::kS, &full[s]);
-        bulk_g2s(st + L::kA + L::kB + L::kS, p.dx + (int64_t)b * p.t_pad + ft * FT, L::kD, &full[s]);
+        // each copy lane arrives with its own byte count before its copy, so
+        // the stage completes only when all four have arrived and landed
+        if (cp == 0) {
+          mbar_arrive_expect_tx(&full[s], L::kA);
+          bulk_g2s(st, p.qs + (g * p.nb + b) * SC_TILE_BYTES, L::kA, &full[s]);
+        } else if (cp == 1) {
+          mbar_arrive_expect_tx(&full[s], L::kB);
+          bulk_g2s(st + L::kA, p.xq + (ft * p.nb + b) * (int64_t)(FT * 32), L::kB, &full[s]);
+        } else if (cp == 2) {
+          mbar_arrive_expect_tx(&full[s], L::kS);
+          bulk_g2s(st + L::kA + L::kB, p.sc + (g * p.nb + b) * SC_GROUP_ROWS, L::kS, &full[s]);
+        } else {
+          mbar_arrive_expect_tx(&full[s], L::kD);
+          bulk_g2s(st + L::kA + L::kB + L::kS, p.dx + (int64_t)b * p.t_pad + ft * FT, L::kD, &full[s]);
+        }
       }
     }
     __syncwarp();
