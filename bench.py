@@ -74,8 +74,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the GEMM shape sweep block")
     ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--profile", default=None, choices=["gemm", "attn", "tc", "encoder"],
-                    help="small eager case for ncu captures (no timing, no JSON line)")
+    ap.add_argument("--profile", default=None, choices=["gemm", "attn", "tc", "encoder", "breakdown"],
+                    help="small eager case for ncu captures (no timing, no JSON line); breakdown: per-kernel "
+                         "device time of 3 steady headline steps (CUPTI through torch.profiler)")
     return ap.parse_args()
 
 
@@ -121,6 +122,27 @@ class ClockSampler:
                           and "Not" not in r[5 + i]})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
+
+
+def reduce_max(value: float, device) -> float:
+    """Max of `value` over the ranks of the default process group (the value
+    itself without one); every rank must call it at the same point."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def stream_shard(global_streams: int, world: int, rank: int):
+    """Contiguous streams [lo, hi) of `rank` when `global_streams` independent
+    streams are spread over `world` GPUs (the first ranks take the remainder)."""
+    base, extra = divmod(global_streams, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
 
 
 def peaks():
@@ -226,11 +248,7 @@ def time_steps(fn, steps, warmup, world, dev, stream):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = reduce_max(e0.elapsed_time(e1), dev)
     return ms / steps
 
 
@@ -475,11 +493,7 @@ def run_ours(args, rank, world, local_rank):
     t0 = time.perf_counter()
     for _ in range(args.e2e_steps):
         e2e_step()
-    e2e_s = (time.perf_counter() - t0) / args.e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = reduce_max((time.perf_counter() - t0) / args.e2e_steps, dev)
     e2e = {"value": world * Z * AUDIO_S_PER_STEP / e2e_s, "unit": UNIT,
            "h2d_bytes_per_step": Z * MEL_PER_STEP * cfg.feat_in * 4, "d2h_bytes_per_step": rows * cfg.d_model * 4,
            "api": "sc_stream_encoder_encode_new + sc_stream_encoder_output, pinned host mel in / frames out, "
@@ -547,6 +561,34 @@ def run_profile(args):
         for _ in range(3):
             attn_stream_ring(q, kn, vn, rk, rv, pos, u, v, c=c, d=d, n_heads=nh, scale=1 / math.sqrt(128), s=s,
                              k_lo=k_lo, chunk=chunk, left_chunks=lc, pos_off=chunk - 1)
+    elif args.profile == "breakdown":
+        import collections
+
+        from torch.profiler import ProfilerActivity, profile
+
+        m = encoder_model()
+        enc = StreamEncoder(m, args.streams)
+        mel = torch.randn((args.streams, MEL_PER_STEP, m.config.feat_in), device=dev)
+        for i in range(PRIME_STEPS + 2):
+            enc.encode_new(mel, MEL_PER_STEP * i, MEL_PER_STEP * (i + 1))
+        torch.cuda.synchronize()
+        steps = 3
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for i in range(PRIME_STEPS + 2, PRIME_STEPS + 2 + steps):
+                enc.encode_new(mel, MEL_PER_STEP * i, MEL_PER_STEP * (i + 1))
+            torch.cuda.synchronize()
+        tot, cnt = collections.defaultdict(float), collections.Counter()
+        for ev in prof.events():
+            if ev.device_type == torch.autograd.DeviceType.CUDA:
+                name = ev.name.split("(")[0].replace("void ", "")
+                tot[name] += ev.device_time_total
+                cnt[name] += 1
+        total = sum(tot.values())
+        print(f"{args.streams} streams, {N_LAYERS} layers: kernel time per step {total / steps / 1e3:.2f} ms")
+        for k, v in sorted(tot.items(), key=lambda x: -x[1]):
+            print(f"{k[:56]:56s} launches/step {cnt[k] // steps:4d}  us/step {v / steps:9.1f}  "
+                  f"share {100 * v / total:5.1f}%  us/launch {v / cnt[k]:8.2f}")
+        enc.close()
     else:
         # the encoder step with 2 layers at the headline's stream count
         from stealcode_b200 import model
