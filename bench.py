@@ -621,6 +621,9 @@ def main():
         import torch
         import torch.distributed as dist
 
+        # rank 0 prints exactly one line: keep NCCL's version banner off stdout
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
