@@ -272,8 +272,11 @@ __host__ __device__ constexpr size_t attn_stage_smem_floats(int band, int np) {
          (size_t)(HD / 16) * 4 * kStageKT * kRedStride;
 }
 
-template <int HD, int CQ>
-__global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
+// LM: rows arrive lane-major (the encoder's layout); pos rows are then read
+// straight from global memory (they are shared by every stream, so L1/L2
+// keep them) instead of being staged, which leaves room for 3 CTAs per SM.
+template <int HD, int CQ, bool LM>
+__global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnParams p) {
   constexpr int NW = HD / 32;
   constexpr int NQG = CQ / 4;        // query groups of 4
   constexpr int KT = kStageKT;
@@ -282,8 +285,8 @@ __global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
   extern __shared__ __align__(16) float sm[];
   const int band = (int)(p.k_hi - p.k_lo), np = p.np, bp = stage_band_pad(band);
   float *s_k = sm;                   // [band][HD] K lane-major, later V natural
-  float *s_p = s_k + band * HD;      // [np][HD]   pos rows lane-major
-  float *s_qu = s_p + np * HD;       // [CQ][HD]   q + u lane-major
+  float *s_p = s_k + band * HD;      // [np][HD]   pos rows lane-major (natural inputs only)
+  float *s_qu = s_p + (LM ? 0 : np) * HD;  // [CQ][HD]   q + u lane-major
   float *s_qv = s_qu + CQ * HD;      // [CQ][HD]   q + v lane-major
   float *s_w = s_qv + CQ * HD;       // [CQ][bp]   scores, then weights
   float *s_red = s_w + CQ * bp;      // [2*NW][4*KT][kRedStride]
@@ -310,16 +313,11 @@ __global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
   // new K rows also go to the ring.  Rows already in lane-major order are
   // copied 16 bytes at a time; natural rows element by element into their
   // lane-major slots. ----
-  if (p.lane_major) {
+  if (LM) {
     constexpr int V4 = HD / 4;  // 16-byte pieces per row
     for (int x = t; x < band * V4; x += HD) {
       const int kk = x / V4, e4 = x % V4;
       cp_async16(s_k + kk * HD + e4 * 4, key_row(p.k_ring, p.k_new, kk) + e4 * 4);
-    }
-    const float *prow = p.pos_p + p.pr_lo * (int64_t)p.d + hoff;
-    for (int x = t; x < np * V4; x += HD) {
-      const int r = x / V4, e4 = x % V4;
-      cp_async16(s_p + r * HD + e4 * 4, prow + (int64_t)r * p.d + e4 * 4);
     }
   } else {
     const int dt = lane_major(t);
@@ -335,7 +333,7 @@ __global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
         *reinterpret_cast<float4 *>(dst + e4 * 4) = *reinterpret_cast<const float4 *>(src + e4 * 4);
     }
   {
-    const int dt = p.lane_major ? t : lane_major(t);
+    const int dt = LM ? t : lane_major(t);
     for (int j = 0; j < CQ; j++) {
       const float qd = j < c ? p.q[(z * c + j) * p.ldq + hoff + t] : 0.0f;
       s_qu[j * HD + dt] = j < c ? __fadd_rn(qd, p.u[hoff + t]) : 0.0f;
@@ -373,8 +371,13 @@ __global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
           float4 kv[KT], pv[NPV], qu[4], qv[4];
 #pragma unroll
           for (int b = 0; b < KT; b++) kv[b] = *reinterpret_cast<const float4 *>(s_k + koff[b] + hh * 64);
+          const float *pbase = LM ? p.pos_p + p.pr_lo * (int64_t)p.d + hoff : s_p;
+          const int pstride = LM ? p.d : HD;
 #pragma unroll
-          for (int m = 0; m < NPV; m++) pv[m] = *reinterpret_cast<const float4 *>(s_p + poff[m] + hh * 64);
+          for (int m = 0; m < NPV; m++)
+            pv[m] = LM ? __ldg(reinterpret_cast<const float4 *>(pbase + (poff[m] / HD) * pstride + poff[m] % HD +
+                                                                hh * 64))
+                       : *reinterpret_cast<const float4 *>(s_p + poff[m] + hh * 64);
 #pragma unroll
           for (int j = 0; j < 4; j++) {
             qu[j] = *reinterpret_cast<const float4 *>(s_qu + qoff + j * HD + hh * 64);
@@ -535,14 +538,14 @@ static bool stage_fits(const AttnParams &p) {
   auto al = [](const void *q) { return ((uintptr_t)q & 15) == 0; };
   const bool aligned = al(p.q) && al(p.k_new) && al(p.v_new) && al(p.pos_p) && p.d % 4 == 0 && p.ldq % 4 == 0 &&
                        p.ld_new % 4 == 0 && (!p.k_ring || (al(p.k_ring) && al(p.v_ring)));
-  return aligned && attn_stage_smem_floats<HD, CQ>(band, p.np) * sizeof(float) <= 227 * 1024;
+  return aligned && attn_stage_smem_floats<HD, CQ>(band, p.lane_major ? 0 : p.np) * sizeof(float) <= 227 * 1024;
 }
 
-template <int HD, int CQ>
-static int launch_stage_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
+template <int HD, int CQ, bool LM>
+static int launch_stage_lm(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
   const int band = (int)(p.k_hi - p.k_lo);
-  const size_t smem = attn_stage_smem_floats<HD, CQ>(band, p.np) * sizeof(float);
-  auto kern = attn_stage_kernel<HD, CQ>;
+  const size_t smem = attn_stage_smem_floats<HD, CQ>(band, LM ? 0 : p.np) * sizeof(float);
+  auto kern = attn_stage_kernel<HD, CQ, LM>;
   static size_t smem_set[64] = {};
   int dev = 0;
   SC_CUDA(cudaGetDevice(&dev));
@@ -554,6 +557,12 @@ static int launch_stage_t(const AttnParams &p, int64_t n_streams, cudaStream_t s
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
+}
+
+template <int HD, int CQ>
+static int launch_stage_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
+  return p.lane_major ? launch_stage_lm<HD, CQ, true>(p, n_streams, st)
+                      : launch_stage_lm<HD, CQ, false>(p, n_streams, st);
 }
 
 template <int HD, int CQ>
