@@ -243,6 +243,18 @@ class StreamEncoder:
         check(lib.sc_stream_encoder_encode_new(self._h, mel_new.data_ptr() if mel_new is not None else None, t0, t1,
                                                int(fin), _stream_ptr(stream)))
 
+    @classmethod
+    def from_gguf(cls, path: str, n_streams: int, max_frames: int = 8) -> "StreamEncoder":
+        """Build from a GGUF checkpoint in the reference's layout
+        (`Encoder::load`, nemotron/encoder.rs:249-282): the file is memory-
+        mapped and its tensors go to the device without a host copy."""
+        from . import gguf
+
+        g = gguf.open_gguf(path)
+        enc = cls(gguf.model_from_gguf(g, max_frames), n_streams)
+        enc._gguf = g  # the mapping backs the model's arrays
+        return enc
+
     def total(self) -> int:
         return int(lib.sc_stream_encoder_total(self._h))
 

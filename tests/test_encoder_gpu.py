@@ -132,3 +132,26 @@ def test_encoder_out_of_sync_is_rejected(torch):
     with pytest.raises(_lib.ScError):
         dev.frames(0, 0, 8)  # past the encoded frames
     dev.close()
+
+
+def test_encoder_from_gguf_file_matches_memory(torch, tmp_path):
+    """A device encoder built from a GGUF checkpoint (memory-mapped, the
+    reference's file layout) computes the same bits as one built in memory."""
+    from stealcode_b200 import gguf
+    from stealcode_b200.ops import StreamEncoder
+
+    cfg = model.EncoderConfig(n_layers=2)
+    m = model.random_model(cfg, seed=13)
+    path = str(tmp_path / "enc.gguf")
+    gguf.save_model(m, path)
+    mel = model.mel_stream(14, 2, 112, cfg.feat_in)
+    a, b = StreamEncoder(m, 2), StreamEncoder.from_gguf(path, 2)
+    for t0, t1 in ((0, 56), (56, 112)):
+        x = torch.from_numpy(np.ascontiguousarray(mel[:, t0:t1])).cuda()
+        a.encode_new(x, t0, t1)
+        b.encode_new(x, t0, t1)
+    torch.cuda.synchronize()
+    for z in range(2):
+        assert np.array_equal(a.frames(z, 0, a.total()), b.frames(z, 0, b.total()))
+    a.close()
+    b.close()
