@@ -55,6 +55,15 @@ for _name, _res, _args in [
     ("orc_enc_set_dump", None, [_P, c_int]),
     ("orc_enc_set_gemm_order", None, [_P, c_int]),
     ("orc_enc_set_exp_mode", None, [_P, c_int]),
+    ("orc_enc_set_prompt", c_int, [_P, c_int]),
+    ("orc_rnnt_create", c_void_p, [_P, _P, c_int, ctypes.c_char_p, _S]),
+    ("orc_rnnt_destroy", None, [_P]),
+    ("orc_rnnt_set_order", None, [_P, c_int, c_int]),
+    ("orc_rnnt_state_new", c_void_p, [_P]),
+    ("orc_rnnt_state_free", None, [_P]),
+    ("orc_rnnt_state_get", None, [_P, _P, _P, _P]),
+    ("orc_rnnt_decode_frames", c_int, [_P, _P, _P, _S, _P, _P, c_int]),
+    ("orc_tanhf", c_float, [c_float]),
     ("orc_set_exp_mode", None, [c_int]),
     ("orc_get_exp_mode", c_int, []),
     ("orc_expf", c_float, [c_float]),
@@ -244,6 +253,13 @@ class StreamingEncoder:
         self.set_gemm_order(True)
         self.set_exp_mode(True)
 
+    def set_prompt(self, prompt_id) -> None:
+        """Prompt of the multilingual prompt MLP (streaming.rs:320-342);
+        None = no prompt.  Raises when the model has no prompt MLP or the id
+        is out of range."""
+        if lib.orc_enc_set_prompt(self._h, -1 if prompt_id is None else int(prompt_id)):
+            raise ValueError(f"prompt {prompt_id}: no prompt MLP or out of range")
+
     def set_dump(self, layer: int) -> None:
         lib.orc_enc_set_dump(self._h, layer)
 
@@ -257,6 +273,81 @@ class StreamingEncoder:
     def __del__(self):
         # the destroy function is held by the instance: module globals may
         # already be gone when this runs at interpreter exit
+        h, destroy = getattr(self, "_h", None), getattr(self, "_destroy", None)
+        if h and destroy:
+            destroy(h)
+            self._h = None
+
+
+class OrcRnntConfig(ctypes.Structure):
+    _fields_ = [("d_enc", ctypes.c_int32), ("hidden", ctypes.c_int32), ("n_layers", ctypes.c_int32),
+                ("joint", ctypes.c_int32), ("vocab", ctypes.c_int32), ("blank", ctypes.c_int32),
+                ("max_symbols", ctypes.c_int32)]
+
+
+class RnntState:
+    """StreamState (live.rs:24-50) of one stream: LSTM h/c per layer and the
+    last emitted token."""
+
+    def __init__(self, dec: "RnntDecoder"):
+        self._dec = dec
+        self._free = lib.orc_rnnt_state_free
+        self._h = lib.orc_rnnt_state_new(dec._h)
+
+    def get(self):
+        c = self._dec.config
+        h = np.empty((c.n_layers, c.hidden), dtype=np.float32)
+        cc = np.empty_like(h)
+        last = ctypes.c_int32()
+        lib.orc_rnnt_state_get(self._h, _p(h), _p(cc), ctypes.byref(last))
+        return h, cc, last.value
+
+    def __del__(self):
+        h, free = getattr(self, "_h", None), getattr(self, "_free", None)
+        if h and free:
+            free(h)
+            self._h = None
+
+
+class RnntDecoder:
+    """The reference's greedy RNN-T decoder (nemotron/decoder.rs:75-235,
+    live.rs:56-145) restated in C.  `model` is a stealcode_b200.model.Model
+    whose config is an RnntConfig."""
+
+    def __init__(self, model):
+        c = model.config
+        self.config = c
+        self.model = model
+        self._table = model.table()
+        self._cfg = OrcRnntConfig(c.d_enc, c.hidden, c.n_layers, c.joint, c.vocab, c.blank, c.max_symbols)
+        err = ctypes.create_string_buffer(256)
+        self._destroy = lib.orc_rnnt_destroy
+        self._h = lib.orc_rnnt_create(ctypes.byref(self._cfg), self._table, len(model.tensors), err, 256)
+        if not self._h:
+            raise RuntimeError(err.value.decode())
+
+    def set_order(self, scalar_gemm: bool = False, exp_cr: bool = False) -> None:
+        """scalar_gemm: q8_gemm_scalar's arithmetic for every matvec instead
+        of the reference's dispatch; exp_cr: correctly rounded exp/tanh."""
+        lib.orc_rnnt_set_order(self._h, int(scalar_gemm), int(exp_cr))
+
+    def new_state(self) -> RnntState:
+        return RnntState(self)
+
+    def decode_frames(self, frames: np.ndarray, state: RnntState):
+        """decode_frames (live.rs:56-145) over frames [n, d_enc]: returns
+        the (ids, steps) emitted; raises on the iteration cap."""
+        frames = np.ascontiguousarray(frames, dtype=np.float32)
+        n = frames.shape[0]
+        cap = 16 * n + 64
+        ids = np.empty(cap, dtype=np.int32)
+        steps = np.empty(cap, dtype=np.int32)
+        k = lib.orc_rnnt_decode_frames(self._h, state._h, _p(frames), n, _p(ids), _p(steps), cap)
+        if k < 0:
+            raise RuntimeError("rnnt decode: iteration cap hit")
+        return ids[:k].copy(), steps[:k].copy()
+
+    def __del__(self):
         h, destroy = getattr(self, "_h", None), getattr(self, "_destroy", None)
         if h and destroy:
             destroy(h)

@@ -33,6 +33,9 @@ extern "C" {
 void orc_set_exp_mode(int correctly_rounded);
 int orc_get_exp_mode(void);
 float orc_expf(float x);
+/* tanh under the same mode: libm tanhf (the reference's f32::tanh), or
+ * (float)tanh((double)x). */
+float orc_tanhf(float x);
 
 /* gguf.rs:365-397 */
 float orc_f16_to_f32(uint16_t h);

@@ -152,6 +152,9 @@ struct orc_enc {
     layer_t *layers;
     conv2d_t conv0, conv2, conv3, conv5, conv6;
     lin_t pre_out;
+    lin_t prompt0, prompt2; /* prompt MLP (optional): [d + n_prompts -> hidden], [hidden -> d] */
+    size_t n_prompts;       /* 0: the model has no prompt MLP */
+    int prompt_id;          /* -1: none */
     float **pos_p; /* per layer [n_pos, d], NULL until the first step */
     fcache *kc, *vc, *glu;
     fcache out;    /* last block output frames */
@@ -385,6 +388,17 @@ orc_enc *orc_enc_create(const orc_enc_config *cfg, const orc_tensor *t, int n, c
     size_t f_out = (size_t)cfg->feat_in;
     for (int i = 0; i < 3; i++) f_out = (f_out + 3 - 3) / 2 + 1;
     rc |= get_lin(t, n, "encoder.pre_encode.out", f_out * C, d, &e->pre_out, err, err_len);
+    /* optional multilingual prompt MLP (nemotron/encoder.rs:260-270) */
+    e->prompt_id = -1;
+    {
+        const orc_tensor *p0 = find(t, n, "prompt_kernel.0.weight");
+        if (p0 && p0->n_dims == 2 && (size_t)p0->dims[0] > d) {
+            size_t np = (size_t)p0->dims[0] - d, hid = (size_t)p0->dims[1];
+            rc |= get_lin(t, n, "prompt_kernel.0", d + np, hid, &e->prompt0, err, err_len);
+            rc |= get_lin(t, n, "prompt_kernel.2", hid, d, &e->prompt2, err, err_len);
+            e->n_prompts = np;
+        }
+    }
     for (int i = 0; i < cfg->n_layers && !rc; i++) {
         layer_t *L = &e->layers[i];
         snprintf(b, sizeof b, "encoder.layers.%d", i);
@@ -663,6 +677,25 @@ static int encode_new(orc_enc *e, const float *mel, size_t mel_frames, size_t n_
         size_t keep = t_new > (size_t)e->cfg.conv_left ? t_new - (size_t)e->cfg.conv_left : 0;
         fc_drop_before(&e->glu[b], keep);
     }
+    /* prompt MLP on the new frames (streaming.rs:320-342):
+     * out = prompt2(relu(prompt0([x ; onehot(prompt_id)]))) */
+    if (e->n_prompts && e->prompt_id >= 0 && (size_t)e->prompt_id < e->n_prompts) {
+        size_t np = e->n_prompts, cat_in = d + np, hid = e->prompt0.rows;
+        float *cat = calloc(cat_in * c, sizeof(float));
+        for (size_t j = 0; j < c; j++) {
+            memcpy(cat + j * cat_in, in + j * d, d * sizeof(float));
+            cat[j * cat_in + d + (size_t)e->prompt_id] = 1.0f;
+        }
+        float *sa = malloc((cat_in > hid ? cat_in : hid) * c * sizeof(float));
+        float *sb = malloc((hid > d ? hid : d) * c * sizeof(float));
+        float *h = malloc(hid * c * sizeof(float));
+        transpose(cat, c, cat_in, sa);
+        lin_forward_t(e, &e->prompt0, sa, c, h); /* [hid, c] */
+        for (size_t i = 0; i < hid * c; i++) h[i] = h[i] > 0.0f ? h[i] : 0.0f; /* relu_into: v.max(0) */
+        lin_forward_t(e, &e->prompt2, h, c, sb); /* [d, c] */
+        transpose(sb, d, c, in);
+        free(cat), free(sa), free(sb), free(h);
+    }
     if (e->out.n == 0) e->out.lo = s;
     fc_append(&e->out, in, c);
     free(in), free(outb);
@@ -689,6 +722,12 @@ int orc_enc_last(const orc_enc *e, int which, float *out, size_t *c_out) {
 }
 
 void orc_enc_set_gemm_order(orc_enc *e, int scalar) { e->scalar_gemm = scalar ? 1 : 0; }
+
+int orc_enc_set_prompt(orc_enc *e, int prompt_id) {
+    if (prompt_id >= 0 && (!e->n_prompts || (size_t)prompt_id >= e->n_prompts)) return -1;
+    e->prompt_id = prompt_id;
+    return 0;
+}
 
 void orc_enc_set_exp_mode(orc_enc *e, int correctly_rounded) { e->exp_cr = correctly_rounded ? 1 : 0; }
 

@@ -65,6 +65,12 @@ void orc_enc_set_gemm_order(orc_enc *e, int scalar);
  * reference on glibc, 1 correctly rounded (orc_set_exp_mode). */
 void orc_enc_set_exp_mode(orc_enc *e, int correctly_rounded);
 
+/* Prompt of the multilingual prompt MLP applied to every new frame
+ * (streaming.rs:320-342; tensors prompt_kernel.0 / prompt_kernel.2, whose
+ * input width d + n_prompts gives n_prompts).  -1 = none (the default).
+ * Returns -1 when the model has no prompt MLP or the id is out of range. */
+int orc_enc_set_prompt(orc_enc *e, int prompt_id);
+
 /* Stage dumps of one layer of the last step (the reference's
  * STEALCODE_DUMP_DIR block dumps): 0 after FF1, 1 attention LN, 2 attention
  * output, 3 after the attention residual, 4 q projection, 5 conv module
@@ -83,6 +89,37 @@ void orc_dwconv_forward(const float *x, size_t t, size_t dim, size_t kh,
 /* streaming.rs:236-261: pos rows for pos in [1-chunk, (left_chunks+1)*chunk-1]
  * before the linear_pos projection: [n_pos, d] sin/cos rows. */
 void orc_pos_rows(size_t n_pos, size_t d, long pos_lo, float *out);
+
+/* ------------------------------------------------------------------ */
+/* RNN-T greedy decoder (sc_oracle_rnnt.c): predictor LSTM + joint +
+ * live.rs:56-145 decode_frames with a carried per-stream state.  Tensors:
+ * decoder.prediction.embed.weight (f32 [vocab][hidden]),
+ * decoder.prediction.dec_rnn.lstm.{ih,hh}_l<i>.{weight,bias} (Q8 [hidden ->
+ * 4 hidden], f32 biases), joint.enc / joint.pred / joint.joint_net.2 (Q8,
+ * optional f32 biases). */
+typedef struct {
+    int32_t d_enc, hidden, n_layers, joint, vocab, blank, max_symbols;
+} orc_rnnt_config;
+
+typedef struct orc_rnnt orc_rnnt;
+typedef struct orc_rnnt_state orc_rnnt_state;
+
+orc_rnnt *orc_rnnt_create(const orc_rnnt_config *cfg, const orc_tensor *tensors,
+                          int n_tensors, char *err, size_t err_len);
+void orc_rnnt_destroy(orc_rnnt *r);
+/* scalar_gemm: every matvec in q8_gemm_scalar's order instead of the
+ * reference's dispatch; exp_cr: correctly rounded exp/tanh. */
+void orc_rnnt_set_order(orc_rnnt *r, int scalar_gemm, int exp_cr);
+/* StreamState::new (live.rs:35-50): zero h/c, last_token -1. */
+orc_rnnt_state *orc_rnnt_state_new(const orc_rnnt *r);
+void orc_rnnt_state_free(orc_rnnt_state *s);
+/* h, c: [n_layers][hidden] */
+void orc_rnnt_state_get(const orc_rnnt_state *s, float *h, float *c, int32_t *last_token);
+/* decode_frames over n frames [n][d_enc]: writes up to cap (id, step)
+ * pairs and returns the number emitted, or -1 when the iteration cap
+ * 16 n + 64 is hit (the reference's bail). */
+int orc_rnnt_decode_frames(orc_rnnt *r, orc_rnnt_state *st, const float *frames, size_t n,
+                           int32_t *ids, int32_t *steps, int cap);
 
 #ifdef __cplusplus
 }

@@ -25,6 +25,8 @@ int orc_get_exp_mode(void) { return g_exp_cr; }
 
 float orc_expf(float x) { return g_exp_cr ? (float)exp((double)x) : expf(x); }
 
+float orc_tanhf(float x) { return g_exp_cr ? (float)tanh((double)x) : tanhf(x); }
+
 /* ------------------------------------------------------------------ */
 float orc_f16_to_f32(uint16_t h) {
     uint32_t sign = (uint32_t)(h >> 15);

@@ -37,6 +37,7 @@ class EncoderConfig:
     att_right: int = 6
     ln_eps: float = 1e-5
     max_frames: int = 8
+    n_prompts: int = 0      # asr.rnnt.num_prompts: > 0 adds the prompt MLP
 
     @property
     def conv_left(self) -> int:
@@ -95,8 +96,14 @@ class Model:
         raise KeyError(name)
 
 
+PROMPT_HIDDEN = 2048  # prompt_intermediate (nemotron/config.rs:181, encoder.rs:268)
+
+
 def random_model(cfg: EncoderConfig, seed: int = synth.SEED_BASE + 3, linear_pos_bias: bool = False) -> Model:
-    """Random-init model of `cfg`, bit-identical for a given seed."""
+    """Random-init model of `cfg`, bit-identical for a given seed.  With
+    cfg.n_prompts > 0 it also holds the multilingual prompt MLP
+    prompt_kernel.0 [d + n_prompts -> 2048] and prompt_kernel.2 [2048 -> d]
+    (nemotron/encoder.rs:260-270)."""
     d, dff, C, k = cfg.d_model, cfg.d_ff, cfg.conv_channels, cfg.conv_kernel
     m = Model(cfg)
     ctr = [seed * 1000]
@@ -156,6 +163,66 @@ def random_model(cfg: EncoderConfig, seed: int = synth.SEED_BASE + 3, linear_pos
         lin(p + "feed_forward2.linear1", d, dff)
         lin(p + "feed_forward2.linear2", dff, d)
         ln(p + "norm_out", d)
+    if cfg.n_prompts > 0:
+        lin("prompt_kernel.0", d + cfg.n_prompts, PROMPT_HIDDEN)
+        lin("prompt_kernel.2", PROMPT_HIDDEN, d)
+    return m
+
+
+@dataclass
+class RnntConfig:
+    """RnntConfig (nemotron/config.rs:41-53) of the greedy RNN-T decoder:
+    the predictor's embedding and LSTM width `hidden`, its layers, the joint
+    width, the classes (vocabulary + blank) and max symbols per frame."""
+    d_enc: int = 1024
+    hidden: int = 640
+    n_layers: int = 2
+    joint: int = 640
+    vocab: int = 1025
+    blank: int = 1024
+    max_symbols: int = 10
+
+
+def random_decoder(cfg: RnntConfig, seed: int = synth.SEED_BASE + 5, blank_bias: float = 0.8,
+                   lstm_std: float = 0.08, pred_std: float = 0.1) -> Model:
+    """Random-init RNN-T decoder with the reference's tensor names
+    (nemotron/decoder.rs:75-235): embedding ~N(0, 1) (f32), LSTM linears
+    Q8_0 ~N(0, lstm_std), joint.pred ~N(0, pred_std), joint.enc and the
+    output linear ~N(0, 0.02), biases ~N(0, 0.02).  The wider LSTM and
+    joint.pred weights give the predictor's output a weight in the joint
+    comparable to the encoder frame's, as in a trained model; `blank_bias`
+    is added to the blank class's output bias so that greedy decoding of
+    N(0, 1) frames mixes blanks and emissions (random weights otherwise
+    almost never pick the blank class)."""
+    H, J = cfg.hidden, cfg.joint
+    m = Model(cfg)
+    ctr = [seed * 1000]
+
+    def nxt():
+        ctr[0] += 1
+        return ctr[0]
+
+    def f32(name, dims, std, add=None):
+        n = int(np.prod(dims))
+        v = synth.normal(nxt(), (n,), std=std)
+        if add is not None:
+            v[add[0]] += np.float32(add[1])
+        m.tensors.append(Tensor(name, 0, tuple(dims), v))
+
+    def lin(name, inp, out, bias=True, bias_add=None, std=0.02):
+        q = synth.q8_weights(nxt(), out, inp, std=std)
+        m.tensors.append(Tensor(name + ".weight", 8, (inp, out), np.ascontiguousarray(q)))
+        if bias:
+            f32(name + ".bias", (out,), 0.02, bias_add)
+
+    f32("decoder.prediction.embed.weight", (H, cfg.vocab), 1.0)
+    for i in range(cfg.n_layers):
+        p = f"decoder.prediction.dec_rnn.lstm."
+        lin(p + f"ih_l{i}", H, 4 * H, std=lstm_std)
+        lin(p + f"hh_l{i}", H, 4 * H, std=lstm_std)
+    lin("joint.enc", cfg.d_enc, J)
+    lin("joint.pred", H, J, std=pred_std)
+    lin("joint.joint_net.2", J, cfg.vocab, bias_add=(cfg.blank, blank_bias))
     return m
 
 
