@@ -272,6 +272,15 @@ int sc_stream_encoder_frames(const sc_stream_encoder *e, int64_t stream_idx,
  * (stream-major); valid until the next encode_new. */
 int sc_stream_encoder_output(const sc_stream_encoder *e, const float **frames,
                              int64_t *rows, int64_t *d);
+/* Prompt of each stream for the multilingual prompt MLP that encode_new
+ * applies to the new frames (streaming.rs:320-342, the prompt_id argument of
+ * StreamEncoder::encode_new): prompt_ids is a host array [n_streams]; an id
+ * < 0 or >= n_prompts means no prompt, as the reference.  Models without
+ * the prompt_kernel.* tensors ignore it.  Applies to later encode_new calls;
+ * synchronous. */
+int sc_stream_encoder_set_prompts(sc_stream_encoder *e, const int32_t *prompt_ids);
+/* Number of prompts of the model's prompt MLP (0: none). */
+int64_t sc_stream_encoder_n_prompts(const sc_stream_encoder *e);
 /* Stage dumps of one layer, the device twin of the reference's
  * STEALCODE_DUMP_DIR block dumps (streaming.rs:426-434, 462-631): after
  * set_dump(layer) (-1 = off) every encode_new records, for that layer and
@@ -283,6 +292,55 @@ int sc_stream_encoder_set_dump(sc_stream_encoder *e, int32_t layer);
 int sc_stream_encoder_dump(const sc_stream_encoder *e, int32_t stage,
                            float *out_host, int64_t *rows);
 int sc_stream_encoder_destroy(sc_stream_encoder *e);
+
+/* ---- RNN-T greedy decoder --------------------------------------------------
+ * The streaming transcriber's decode loop (nemotron/live.rs:56-145,
+ * decode_frames) with the predictor LSTM and the joint network
+ * (nemotron/decoder.rs:75-235) for n_streams streams, each with its own
+ * carried StreamState (live.rs:24-50).  Tensors (GGUF names, as the
+ * reference loads them): decoder.prediction.embed.weight f32 [vocab x
+ * hidden]; decoder.prediction.dec_rnn.lstm.{ih,hh}_l<i>.weight Q8_0
+ * [hidden -> 4 hidden] with f32 .bias; joint.enc [d_enc -> joint],
+ * joint.pred [hidden -> joint], joint.joint_net.2 [joint -> vocab], Q8_0
+ * with optional f32 biases.  hidden, joint, d_enc: multiples of 32. */
+typedef struct {
+  int32_t d_enc, hidden, n_layers, joint;
+  int32_t vocab;        /* classes including blank (RnntConfig::vocab_size) */
+  int32_t blank;        /* blank_id */
+  int32_t max_symbols;  /* max_symbols_per_step; 0 = no per-frame cap */
+  int32_t max_frames;   /* largest n of one decode_frames call (1..256) */
+} sc_rnnt_config;
+
+typedef struct sc_rnnt_decoder sc_rnnt_decoder;
+
+/* GreedyDecoder::load (decoder.rs:238-247) plus StreamState::new for every
+ * stream; weights are repacked once for the device.  Synchronous. */
+int sc_rnnt_create(const sc_rnnt_config *cfg, const sc_tensor *tensors,
+                   int n_tensors, int64_t n_streams, sc_rnnt_decoder **out);
+/* decode_frames (live.rs:56-145) for every stream at once: frames (device)
+ * is [n_streams][n][d_enc], e.g. sc_stream_encoder_output's frames.  Each
+ * stream's state carries over to the next call.  Synchronises `stream`
+ * (the loop length depends on the tokens).  SC_ERR_STATE when a stream
+ * hits the iteration cap 16 n + 64 (the reference's bail). */
+int sc_rnnt_decode_frames(sc_rnnt_decoder *r, const float *frames, int64_t n,
+                          void *stream);
+/* Tokens the last decode_frames emitted for one stream: (id, frame step
+ * within that call) pairs, the reference's Token {id, step} with p = 1;
+ * up to cap of them are written, *count gets how many were emitted. */
+int sc_rnnt_tokens(const sc_rnnt_decoder *r, int64_t stream_idx, int32_t *ids,
+                   int32_t *steps, int32_t cap, int32_t *count);
+/* Device arrays of the last call's tokens: ids/steps [n_streams][*cap],
+ * counts [n_streams]; valid until the next decode_frames. */
+int sc_rnnt_tokens_device(const sc_rnnt_decoder *r, const int32_t **ids,
+                          const int32_t **steps, const int32_t **counts,
+                          int32_t *cap);
+/* StreamState::new for one stream (-1: all streams). */
+int sc_rnnt_reset(sc_rnnt_decoder *r, int64_t stream_idx);
+/* A stream's LSTM state h, c ([n_layers][hidden] each, host) and its last
+ * emitted token (-1 before the first). */
+int sc_rnnt_state(const sc_rnnt_decoder *r, int64_t stream_idx, float *h,
+                  float *c, int32_t *last_token);
+int sc_rnnt_destroy(sc_rnnt_decoder *r);
 
 #ifdef __cplusplus
 }

@@ -75,9 +75,19 @@ SIGNATURES = {
     "sc_stream_encoder_total": (c_int64, [_P]),
     "sc_stream_encoder_frames": (c_int, [_P, _I, _I, _I, _P]),
     "sc_stream_encoder_output": (c_int, [_P, POINTER(c_void_p), POINTER(c_int64), POINTER(c_int64)]),
+    "sc_stream_encoder_set_prompts": (c_int, [_P, _P]),
+    "sc_stream_encoder_n_prompts": (c_int64, [_P]),
     "sc_stream_encoder_set_dump": (c_int, [_P, c_int32]),
     "sc_stream_encoder_dump": (c_int, [_P, c_int32, _P, POINTER(c_int64)]),
     "sc_stream_encoder_destroy": (c_int, [_P]),
+    "sc_rnnt_create": (c_int, [_P, _P, c_int, _I, POINTER(c_void_p)]),
+    "sc_rnnt_decode_frames": (c_int, [_P, _P, _I, _P]),
+    "sc_rnnt_tokens": (c_int, [_P, _I, _P, _P, c_int32, POINTER(c_int32)]),
+    "sc_rnnt_tokens_device": (c_int, [_P, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p),
+                                      POINTER(c_int32)]),
+    "sc_rnnt_reset": (c_int, [_P, _I]),
+    "sc_rnnt_state": (c_int, [_P, _I, _P, _P, POINTER(c_int32)]),
+    "sc_rnnt_destroy": (c_int, [_P]),
     "sc_attn_stream": (c_int, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, c_float,
                                _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "sc_attn_stream_host": (c_int, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, c_float,

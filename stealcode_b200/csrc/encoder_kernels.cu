@@ -499,6 +499,35 @@ __global__ void flatten_kernel(const float *__restrict__ x, int t, int f, int C,
   }
 }
 
+// Input codes of the prompt MLP's first linear for every row: the row's d
+// features followed by the one-hot of its stream's prompt (streaming.rs:
+// 323-331, cat = [x ; onehot(prompt_id)]), quantised per 32-block as
+// quantize_col does.  One warp per block; rows whose stream has no prompt
+// get an all-zero one-hot (their MLP output is discarded).
+__global__ void prompt_cat_quant_kernel(const float *__restrict__ x, int64_t rows, int c, int d, int n_prompts,
+                                        const int32_t *__restrict__ pids, QOut qo) {
+  const int64_t row = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // whole warps of one block
+  const int k = d + n_prompts;
+  if (row >= rows || (i & ~31) >= k) return;
+  const int pid = pids[row / c];
+  const bool valid = i < k;
+  const float v = i < d ? x[row * d + i] : (valid && i - d == pid ? 1.0f : 0.0f);
+  float sblk;
+  const int8_t q = warp_quantize_block(v, valid, sblk);
+  qo.xq[qout_code_index(qo, row, i)] = q;
+  if ((threadIdx.x & 31) == 0) qo.dx[(i / 32) * qo.t_pad + row] = sblk;
+}
+
+// Rows of streams with a prompt take the prompt MLP's output
+// (streaming.rs:337-341: the block output frames are replaced).
+__global__ void prompt_select_kernel(float *__restrict__ x, const float *__restrict__ y, int c, int d,
+                                     const int32_t *__restrict__ pids) {
+  const int64_t row = blockIdx.x;
+  if (pids[row / c] < 0) return;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) x[row * d + i] = y[row * d + i];
+}
+
 // Output frames into the per-stream output ring (slot = frame % cap).
 __global__ void out_ring_kernel(const float *__restrict__ x, int c, int d, float *__restrict__ ring, int cap,
                                 int64_t s) {
@@ -583,6 +612,27 @@ int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int s
                    cudaStream_t st, QOut qo) {
   dim3 grid((unsigned)ceil_div((int64_t)C * f, 256), (unsigned)(n_streams * c));
   flatten_kernel<<<grid, 256, 0, st>>>(x, t, f, C, start_rel, c, out, qo);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+int launch_prompt_cat_quant(const float *x, int64_t rows, int c, int d, int n_prompts, const int32_t *pids,
+                            const QOut &qo, cudaStream_t st) {
+  if (!qo.xq || (d % 32)) {
+    set_error("prompt_cat_quant: codes output required and d a multiple of 32");
+    return kErrInvalid;
+  }
+  dim3 grid((unsigned)ceil_div((int64_t)d + n_prompts, 256), (unsigned)rows);
+  prompt_cat_quant_kernel<<<grid, 256, 0, st>>>(x, rows, c, d, n_prompts, pids, qo);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+int launch_prompt_select(float *x, const float *y, int64_t rows, int c, int d, const int32_t *pids,
+                         cudaStream_t st) {
+  prompt_select_kernel<<<(unsigned)rows, 256, 0, st>>>(x, y, c, d, pids);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;

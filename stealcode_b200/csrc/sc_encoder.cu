@@ -54,6 +54,10 @@ int launch_dwconv_ln_silu_quant(const float *ring, int cap, int64_t rows, int c,
                                 const float *wt, const float *lnw, const float *lnb, float eps, const QOut &qo,
                                 float *out, cudaStream_t st);
 int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st);
+int launch_prompt_cat_quant(const float *x, int64_t rows, int c, int d, int n_prompts, const int32_t *pids,
+                            const QOut &qo, cudaStream_t st);
+int launch_prompt_select(float *x, const float *y, int64_t rows, int c, int d, const int32_t *pids,
+                         cudaStream_t st);
 
 constexpr int kMelHistory = 24;  // mel frames of left context (streaming.rs:188)
 constexpr int kDumpStages = 8;
@@ -93,6 +97,12 @@ struct sc_stream_encoder {
   std::vector<Layer> layers;
   Conv c0{}, c2{}, c3{}, c5{}, c6{};
   Lin pre_out;
+  // multilingual prompt MLP (nemotron/encoder.rs:260-270), optional:
+  // prompt0 [d + n_prompts -> hidden], prompt2 [hidden -> d]
+  Lin prompt0, prompt2;
+  int64_t n_prompts = 0, prompt_hidden = 0;
+  int32_t *pids = nullptr;  // [n_streams] device: prompt of each stream, -1 none
+  bool any_prompt = false;
   std::vector<void *> allocs;
   // state
   int64_t total = 0;
@@ -122,8 +132,10 @@ struct sc_stream_encoder {
         cudaFree(q->w.qs);
         cudaFree(q->w.sc);
       }
-    cudaFree(pre_out.w.qs);
-    cudaFree(pre_out.w.sc);
+    for (Lin *q : {&pre_out, &prompt0, &prompt2}) {
+      cudaFree(q->w.qs);
+      cudaFree(q->w.sc);
+    }
     for (void *p : allocs) cudaFree(p);
   }
 };
@@ -357,6 +369,25 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
       ok = L.err.empty();
     }
   }
+  // optional prompt MLP: its input width d + n_prompts gives n_prompts
+  if (const sc_tensor *p0 = ok ? L.find("prompt_kernel.0.weight") : nullptr) {
+    if (p0->n_dims == 2 && p0->dims[0] > d && (p0->dims[0] - d) % 32 == 0 && p0->dims[1] % 128 == 0) {
+      e->n_prompts = p0->dims[0] - d;
+      e->prompt_hidden = p0->dims[1];
+      ok = L.lin({"prompt_kernel.0"}, d + e->n_prompts, e->prompt_hidden, &e->prompt0, true) &&
+           L.lin({"prompt_kernel.2"}, e->prompt_hidden, d, &e->prompt2, true);
+      if (ok) {
+        e->pids = (int32_t *)L.dev_alloc((size_t)n_streams * 4);
+        std::vector<int32_t> none((size_t)n_streams, -1);
+        ok = e->pids && cudaMemcpy(e->pids, none.data(), none.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+        if (!ok && L.err.empty()) L.err = "upload failed";
+      }
+    } else {
+      L.err = "prompt_kernel.0.weight: dims [d + n_prompts, hidden] with n_prompts and hidden multiples of 32 and "
+              "128 expected";
+      ok = false;
+    }
+  }
   const int64_t M = n_streams * c.max_frames;
   if (ok) {
     e->x = L.dev_alloc(M * d * 4);
@@ -377,7 +408,8 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     e->p2 = L.dev_alloc((size_t)(n_streams * t0 * f0 * C * 4));
     e->flat = L.dev_alloc((size_t)(M * f_final * C * 4));
     e->pos_in = L.dev_alloc((size_t)(e->n_pos * d * 4));
-    const int64_t kmax = std::max<int64_t>(std::max<int64_t>(dff, f_final * C), d);
+    const int64_t kmax = std::max<int64_t>(std::max<int64_t>(std::max<int64_t>(dff, f_final * C), d),
+                                           std::max<int64_t>(d + e->n_prompts, e->prompt_hidden));
     const int64_t tmax = std::max<int64_t>(M, e->n_pos);
     e->ws_bytes = gemm_ws_bytes(tmax, kmax);
     e->ws = L.dev_alloc(e->ws_bytes);
@@ -605,6 +637,14 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
     TRY(launch_ln_rows(e->y, d, ly.ln_out_w, ly.ln_out_b, eps, e->x, d, M, (int)d, st));
     TRY(dump(7, e->x, d));
   }
+  // ---- prompt MLP on the new frames (streaming.rs:320-342) ----
+  if (e->any_prompt) {
+    const QOut qcat = qbuf(0, d + e->n_prompts), qh = qbuf(1, e->prompt_hidden);
+    TRY(launch_prompt_cat_quant(e->x, M, (int)cf, (int)d, (int)e->n_prompts, e->pids, qcat, st));
+    TRY(gemm_q(e->prompt0, qcat, nullptr, e->prompt_hidden, Epilogue{kEpiRelu, nullptr, 1.0f}, qh));
+    TRY(gemm_q(e->prompt2, qh, e->y, d, Epilogue{}, QOut{}));
+    TRY(launch_prompt_select(e->x, e->y, M, (int)cf, (int)d, e->pids, st));
+  }
   TRY(launch_out_ring(e->x, M, (int)cf, (int)d, e->out_ring, (int)e->out_cap, s, st));
   e->hist_cur ^= 1;
   e->hist_frames = (int)std::min<int64_t>(kMelHistory, e->hist_frames + n_new);
@@ -612,6 +652,27 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
   e->last_c = cf;
   return kOk;
 }
+
+int sc_stream_encoder_set_prompts(sc_stream_encoder *e, const int32_t *prompt_ids) {
+  if (!e || !prompt_ids) {
+    set_error("stream_encoder_set_prompts: invalid argument");
+    return kErrInvalid;
+  }
+  if (!e->n_prompts) return kOk;  // no prompt MLP: the output is left unchanged
+  // an id out of range means no prompt, as the reference's `pid < num_prompts`
+  std::vector<int32_t> ids((size_t)e->n_streams);
+  bool any = false;
+  for (int64_t i = 0; i < e->n_streams; i++) {
+    const int32_t p = prompt_ids[i];
+    ids[(size_t)i] = p >= 0 && p < e->n_prompts ? p : -1;
+    any |= ids[(size_t)i] >= 0;
+  }
+  SC_CUDA(cudaMemcpy(e->pids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice));
+  e->any_prompt = any;
+  return kOk;
+}
+
+int64_t sc_stream_encoder_n_prompts(const sc_stream_encoder *e) { return e ? e->n_prompts : 0; }
 
 int sc_stream_encoder_set_dump(sc_stream_encoder *e, int32_t layer) {
   if (!e || layer >= (int32_t)e->layers.size()) {

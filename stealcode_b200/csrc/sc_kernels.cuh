@@ -12,7 +12,8 @@ namespace sc {
 //   kEpiSilu:     y = v * (1 / (1 + exp(-v)))        (simd_kernel.rs:817-839)
 //   kEpiResidual: y = res + alpha * v                 (res may alias y;
 //                 streaming.rs:458-460, 596-598, 643-645, 667-669)
-enum : int { kEpiNone = 0, kEpiSilu = 1, kEpiResidual = 2 };
+//   kEpiRelu:     y = max(v, 0), NaN -> 0             (simd_kernel.rs:843-861)
+enum : int { kEpiNone = 0, kEpiSilu = 1, kEpiResidual = 2, kEpiRelu = 3 };
 struct Epilogue {
   int op = kEpiNone;
   const float *res = nullptr;
@@ -22,6 +23,7 @@ struct Epilogue {
 __device__ __forceinline__ float apply_epilogue(const Epilogue &e, float v, int64_t idx) {
   if (e.op == kEpiSilu) return silu_ref(v);
   if (e.op == kEpiResidual) return __fadd_rn(e.res[idx], __fmul_rn(e.alpha, v));
+  if (e.op == kEpiRelu) return v > 0.0f ? v : 0.0f;
   return v;
 }
 

@@ -276,17 +276,23 @@ def encoder_config(g: GgufFile, max_frames: int = 8) -> "_model.EncoderConfig":
     if ctx != "causal":
         raise GgufError(f"GGUF metadata: conv_context {ctx} is not causal (streaming needs causal)")
     vals = {f: u32(k) for f, k in ENCODER_KEYS.items()}
-    return _model.EncoderConfig(att_right=6, max_frames=max_frames, **vals)
+    n_prompts = g.kv.get("asr.rnnt.num_prompts", 0) if "prompt_kernel.0.weight" in g._by_name else 0
+    return _model.EncoderConfig(att_right=6, max_frames=max_frames, n_prompts=int(n_prompts), **vals)
 
 
 def model_from_gguf(g: GgufFile, max_frames: int = 8) -> "_model.Model":
-    """The encoder's tensors (every `encoder.*` tensor of the file) as a
-    Model whose arrays are zero-copy views of the map (f32 tensors are
-    viewed as f32, Q8_0 tensors as their stored blocks)."""
+    """The encoder's tensors (every `encoder.*` tensor of the file and the
+    prompt MLP's `prompt_kernel.*`) as a Model whose arrays are zero-copy
+    views of the map (f32 tensors are viewed as f32, Q8_0 tensors as their
+    stored blocks)."""
     cfg = encoder_config(g, max_frames)
+    return _model.Model(cfg, _views(g, ("encoder.", "prompt_kernel.")))
+
+
+def _views(g: GgufFile, prefixes) -> list:
     out = []
     for t in g.tensors:
-        if not t.name.startswith("encoder."):
+        if not t.name.startswith(prefixes):
             continue
         raw = g.tensor_data(t)
         if t.dtype == F32:
@@ -294,9 +300,9 @@ def model_from_gguf(g: GgufFile, max_frames: int = 8) -> "_model.Model":
         elif t.dtype == Q8_0_F16:
             data = raw.reshape(-1, (int(t.dims[0]) + 31) // 32 * 34)
         else:
-            raise GgufError(f"tensor {t.name}: dtype {t.dtype} not supported by the device encoder")
+            raise GgufError(f"tensor {t.name}: dtype {t.dtype} not supported on the device path")
         out.append(_model.Tensor(t.name, t.dtype, tuple(int(d) for d in t.dims), data))
-    return _model.Model(cfg, out)
+    return out
 
 
 def save_model(m: "_model.Model", path: str, extra_kv: dict | None = None) -> None:
@@ -305,6 +311,7 @@ def save_model(m: "_model.Model", path: str, extra_kv: dict | None = None) -> No
     c = m.config
     kv = {k: int(getattr(c, f)) for f, k in ENCODER_KEYS.items()}
     kv.update({"asr.encoder.conv_context": "causal", "asr.encoder.xscaling": False, "asr.encoder.use_bias": True,
-               "asr.encoder.subsampling_factor": 8, "asr.encoder.pos_emb_max_len": 5000})
+               "asr.encoder.subsampling_factor": 8, "asr.encoder.pos_emb_max_len": 5000,
+               "asr.rnnt.num_prompts": int(c.n_prompts)})
     kv.update(extra_kv or {})
     write_gguf(path, kv, m.tensors)

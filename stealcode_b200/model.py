@@ -183,7 +183,17 @@ class RnntConfig:
     max_symbols: int = 10
 
 
-def random_decoder(cfg: RnntConfig, seed: int = synth.SEED_BASE + 5, blank_bias: float = 0.8,
+class ScRnntConfig(ctypes.Structure):
+    _fields_ = [("d_enc", ctypes.c_int32), ("hidden", ctypes.c_int32), ("n_layers", ctypes.c_int32),
+                ("joint", ctypes.c_int32), ("vocab", ctypes.c_int32), ("blank", ctypes.c_int32),
+                ("max_symbols", ctypes.c_int32), ("max_frames", ctypes.c_int32)]
+
+    @classmethod
+    def of(cls, c: "RnntConfig", max_frames: int) -> "ScRnntConfig":
+        return cls(c.d_enc, c.hidden, c.n_layers, c.joint, c.vocab, c.blank, c.max_symbols, max_frames)
+
+
+def random_decoder(cfg: RnntConfig, seed: int = synth.SEED_BASE + 5, blank_bias: float = 1.3,
                    lstm_std: float = 0.08, pred_std: float = 0.1) -> Model:
     """Random-init RNN-T decoder with the reference's tensor names
     (nemotron/decoder.rs:75-235): embedding ~N(0, 1) (f32), LSTM linears

@@ -269,6 +269,18 @@ class StreamEncoder:
         check(lib.sc_stream_encoder_output(self._h, ctypes.byref(ptr), ctypes.byref(rows), ctypes.byref(d)))
         return ptr.value, rows.value, d.value
 
+    def set_prompts(self, prompt_ids) -> None:
+        """Prompt of each stream for the prompt MLP (the prompt_id argument of
+        encode_new, streaming.rs:687-699); None / < 0 / out of range: none."""
+        ids = np.array([-1 if p is None else int(p) for p in prompt_ids], dtype=np.int32)
+        if ids.shape != (self.n_streams,):
+            raise ValueError(f"set_prompts: {ids.shape[0]} ids for {self.n_streams} streams")
+        check(lib.sc_stream_encoder_set_prompts(self._h, _hp(ids)))
+
+    @property
+    def n_prompts(self) -> int:
+        return int(lib.sc_stream_encoder_n_prompts(self._h))
+
     def set_dump(self, layer: int) -> None:
         check(lib.sc_stream_encoder_set_dump(self._h, layer))
 
@@ -290,5 +302,71 @@ class StreamEncoder:
             pass
 
 
-__all__ = ["StreamEncoder", "q8_gemm", "Q8Mat", "Lin", "quantize", "AttnStreamKernel", "attn_stream_ring",
+class RnntDecoder:
+    """Device greedy RNN-T decoder for n_streams streams, each with its own
+    carried state: decode_frames (live.rs:56-145) over the predictor LSTM
+    and joint network (nemotron/decoder.rs:75-235)."""
+
+    def __init__(self, model, n_streams: int, max_frames: int = 16):
+        from .model import ScRnntConfig
+
+        self.model = model
+        self.config = model.config
+        self._table = model.table()
+        self._cfg = ScRnntConfig.of(model.config, max_frames)
+        h = ctypes.c_void_p()
+        check(lib.sc_rnnt_create(ctypes.byref(self._cfg), self._table, len(model.tensors), n_streams,
+                                 ctypes.byref(h)))
+        self._h = h
+        self.n_streams = n_streams
+        self.cap = 16 * max_frames + 64
+
+    def decode_frames(self, frames, stream=None) -> None:
+        """frames: CUDA tensor [n_streams, n, d_enc] (f32) or a raw device
+        pointer with n given as (ptr, n).  Synchronises the stream."""
+        if isinstance(frames, tuple):
+            ptr, n = frames
+        else:
+            if frames.dim() != 3 or frames.shape[0] != self.n_streams or frames.shape[2] != self.config.d_enc:
+                raise ValueError(f"frames must be [{self.n_streams}, n, {self.config.d_enc}]")
+            import torch
+
+            if not frames.is_contiguous() or frames.dtype != torch.float32:
+                raise ValueError("frames must be contiguous f32")
+            ptr, n = frames.data_ptr(), frames.shape[1]
+        check(lib.sc_rnnt_decode_frames(self._h, ptr, n, _stream_ptr(stream)))
+
+    def tokens(self, stream_idx: int):
+        """(ids, steps) the last decode_frames emitted for one stream."""
+        ids = np.empty(self.cap, dtype=np.int32)
+        steps = np.empty(self.cap, dtype=np.int32)
+        cnt = ctypes.c_int32()
+        check(lib.sc_rnnt_tokens(self._h, stream_idx, _hp(ids), _hp(steps), self.cap, ctypes.byref(cnt)))
+        return ids[: cnt.value].copy(), steps[: cnt.value].copy()
+
+    def state(self, stream_idx: int):
+        """(h, c, last_token) of one stream; h, c: [n_layers, hidden]."""
+        c = self.config
+        h = np.empty((c.n_layers, c.hidden), dtype=np.float32)
+        cc = np.empty_like(h)
+        last = ctypes.c_int32()
+        check(lib.sc_rnnt_state(self._h, stream_idx, _hp(h), _hp(cc), ctypes.byref(last)))
+        return h, cc, last.value
+
+    def reset(self, stream_idx: int = -1) -> None:
+        check(lib.sc_rnnt_reset(self._h, stream_idx))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib.sc_rnnt_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+__all__ = ["StreamEncoder", "RnntDecoder", "q8_gemm", "Q8Mat", "Lin", "quantize", "AttnStreamKernel", "attn_stream_ring",
            "SC_LAYOUT_FEATURE_MAJOR", "SC_LAYOUT_TIME_MAJOR", "_lib"]

@@ -41,7 +41,7 @@ def _err(got, ref):
 TOL = 1e-4  # max |d| / RMS(reference), f32 outputs
 
 
-def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11, simd_too=False):
+def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11, simd_too=False, prompts=None):
     """Runs the device encoder and per-stream oracles side by side; returns
     (t0, stream, max/RMS, mean/RMS, exact fraction[, oracle scalar-vs-SIMD
     max/RMS, device-vs-SIMD max/RMS]) per step and stream."""
@@ -54,6 +54,10 @@ def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11, simd_too=False):
     refs = [oracle.StreamingEncoder(m) for _ in range(n_streams)]
     for r in refs:
         r.set_device_rounding()
+    if prompts is not None:
+        dev.set_prompts(prompts)
+        for r, p in zip(refs, prompts):  # out of range: no prompt, as the reference
+            r.set_prompt(p if p is not None and 0 <= p < cfg.n_prompts else None)
     simd = [oracle.StreamingEncoder(m) for _ in range(n_streams)] if simd_too else []
     stats = []
     batches = [(56 * i, 56 * (i + 1), False) for i in range(n_steps)]
@@ -116,6 +120,16 @@ def test_encoder_24_layers_matches_oracle(torch):
     # against the reference's own dispatch: within its scalar path's spread
     for s in stats:
         assert s[6] <= s[5] + TOL
+
+
+def test_encoder_prompt_mlp_matches_oracle(torch):
+    """The multilingual prompt MLP on the new frames (streaming.rs:320-342):
+    per-stream prompts, none, the last id and an out-of-range id (no prompt,
+    as the reference), 2 blocks at full width, 128 prompts."""
+    cfg = model.EncoderConfig(n_layers=2, n_prompts=128)
+    stats = run_steps(torch, cfg, 4, 3, tail=24, seed=17, prompts=[None, 3, 127, 500])
+    _report("encoder + prompt MLP", stats)
+    assert max(s[2] for s in stats) <= TOL
 
 
 def test_encoder_out_of_sync_is_rejected(torch):
