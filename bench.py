@@ -22,6 +22,12 @@ Also in the line:
   e2e           the same metric through the C ABI with host mel buffers:
                 pinned host -> device copy of each step's mel, encode_new,
                 device -> pinned host copy of the step's output frames;
+  transcriber   the streaming transcriber's whole step (LiveTranscriber::
+                process): encode_new, then the RNN-T greedy decode of each
+                stream's 7 new frames (random-init 2 x 640 LSTM predictor,
+                joint 640, 1025 classes) straight from the encoder's device
+                output; CUDA-event time per step, the decoder's share, and
+                the tokens emitted per frame;
   cpu_baseline  the reference CPU path (the oracle's restatement: AVX2 +
                 threads GEMMs, one StreamingEncoder per stream) on a bounded
                 sample of the same workload.
@@ -58,6 +64,7 @@ PRIME_STEPS = 11           # band reaches its steady 77 frames
 N_LAYERS = 24
 MODEL_SEED = 0x5EED0000 + 3
 MEL_POOL = 8               # distinct mel chunks cycled through the steps
+DECODER_BLANK_BIAS = 0.9   # random decoder's blank bias: ~0.5 tokens / frame on the encoder's output
 
 SHAPES = [("qkv", 1024, 3072), ("out", 1024, 1024), ("ffn_up", 1024, 4096), ("ffn_down", 4096, 1024)]
 MS = [1, 8, 32, 128]
@@ -74,6 +81,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the GEMM shape sweep block")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-decoder", action="store_true", help="skip the transcriber (encoder + decoder) block")
     ap.add_argument("--profile", default=None, choices=["gemm", "attn", "tc", "encoder", "breakdown"],
                     help="small eager case for ncu captures (no timing, no JSON line); breakdown: per-kernel "
                          "device time of 3 steady headline steps (CUPTI through torch.profiler)")
@@ -498,6 +506,7 @@ def run_ours(args, rank, world, local_rank):
            "h2d_bytes_per_step": Z * MEL_PER_STEP * cfg.feat_in * 4, "d2h_bytes_per_step": rows * cfg.d_model * 4,
            "api": "sc_stream_encoder_encode_new + sc_stream_encoder_output, pinned host mel in / frames out, "
                   "synchronised every step"}
+    trans = None if args.no_decoder else transcriber_leg(args, enc, pool, state, Z, world, dev, stream)
     enc.close()
     del pool, enc
     torch.cuda.empty_cache()
@@ -527,10 +536,59 @@ def run_ours(args, rank, world, local_rank):
                            "frames_per_gemm": Z * 7, "parallelism": f"streams sharded, {world} independent ranks",
                            "l2": "inputs larger than L2: each step streams 587 MB of Q8_0 weights (L2 126 MB)"},
                 "realtime_streams_per_gpu": value / world,
-                "roofline": roof, "gemm_sweep": sweep, "cpu_baseline": cpu, "e2e": e2e,
+                "roofline": roof, "gemm_sweep": sweep, "cpu_baseline": cpu, "e2e": e2e, "transcriber": trans,
                 "gpu_launches": launches_timed, "launches_per_step": launches / (args.steps + args.warmup),
                 "clocks": clk, "peaks_file": {k: p.get(k) for k in ("hbm_gbs", "bf16_tflops")}}
         print(json.dumps(line), flush=True)
+
+
+def transcriber_leg(args, enc, pool, state, Z, world, dev, stream):
+    """LiveTranscriber::process for every stream (live.rs:336-375):
+    encode_new of the step's 56 mel frames, then decode_frames over the 7 new
+    encoder frames of each stream, read from the encoder's device output."""
+    import torch
+
+    from stealcode_b200 import model
+    from stealcode_b200.ops import RnntDecoder
+
+    dcfg = model.RnntConfig()
+    # blank bias 0.9: about 0.5 tokens per frame on this encoder's output
+    # frames (a speech-like rate; 80 ms frames)
+    dec = RnntDecoder(model.random_decoder(dcfg, blank_bias=DECODER_BLANK_BIAS), Z, max_frames=8)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    emitted = torch.zeros(Z, dtype=torch.int64)
+
+    def one(e=None):
+        i = state["i"]
+        if e:
+            e[0].record(stream)
+        enc.encode_new(pool[i % MEL_POOL], MEL_PER_STEP * i, MEL_PER_STEP * (i + 1), stream=stream)
+        if e:
+            e[1].record(stream)
+        ptr, r, _ = enc.output()
+        dec.decode_frames((ptr, r // Z), stream=stream)
+        if e:
+            e[2].record(stream)
+        state["i"] = i + 1
+
+    for _ in range(args.warmup):
+        one()
+    frames = 0
+    for k in range(args.steps):
+        one(ev[k])
+        emitted += torch.as_tensor(dec.emitted())
+        frames += 7 * Z
+    torch.cuda.synchronize()
+    enc_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    dec_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    step_ms = reduce_max(enc_ms + dec_ms, dev)
+    dec.close()
+    return {"value": world * Z * AUDIO_S_PER_STEP / (step_ms * 1e-3), "unit": UNIT, "ms_per_step": step_ms,
+            "encoder_ms_per_step": enc_ms, "decoder_ms_per_step": dec_ms,
+            "tokens_per_frame": float(emitted.sum()) / frames, "steps": args.steps,
+            "decoder": f"random-init RNN-T: {dcfg.n_layers} x {dcfg.hidden} LSTM, joint {dcfg.joint}, "
+                       f"{dcfg.vocab} classes, greedy, max_symbols {dcfg.max_symbols}; per-stream state carried",
+            "api": "sc_stream_encoder_encode_new, then sc_rnnt_decode_frames on sc_stream_encoder_output"}
 
 
 def run_profile(args):

@@ -329,6 +329,8 @@ int sc_rnnt_decode_frames(sc_rnnt_decoder *r, const float *frames, int64_t n,
  * up to cap of them are written, *count gets how many were emitted. */
 int sc_rnnt_tokens(const sc_rnnt_decoder *r, int64_t stream_idx, int32_t *ids,
                    int32_t *steps, int32_t cap, int32_t *count);
+/* How many tokens each stream emitted in the last call, [n_streams] (host). */
+int sc_rnnt_emitted(const sc_rnnt_decoder *r, int32_t *counts);
 /* Device arrays of the last call's tokens: ids/steps [n_streams][*cap],
  * counts [n_streams]; valid until the next decode_frames. */
 int sc_rnnt_tokens_device(const sc_rnnt_decoder *r, const int32_t **ids,

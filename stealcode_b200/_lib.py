@@ -85,6 +85,7 @@ SIGNATURES = {
     "sc_rnnt_tokens": (c_int, [_P, _I, _P, _P, c_int32, POINTER(c_int32)]),
     "sc_rnnt_tokens_device": (c_int, [_P, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p),
                                       POINTER(c_int32)]),
+    "sc_rnnt_emitted": (c_int, [_P, _P]),
     "sc_rnnt_reset": (c_int, [_P, _I]),
     "sc_rnnt_state": (c_int, [_P, _I, _P, _P, POINTER(c_int32)]),
     "sc_rnnt_destroy": (c_int, [_P]),

@@ -730,6 +730,16 @@ int sc_rnnt_tokens(const sc_rnnt_decoder *r, int64_t stream_idx, int32_t *ids, i
   return kOk;
 }
 
+int sc_rnnt_emitted(const sc_rnnt_decoder *r, int32_t *counts) {
+  if (!r || !counts) {
+    set_error("rnnt_emitted: invalid argument");
+    return kErrInvalid;
+  }
+  SC_CUDA(cudaDeviceSynchronize());
+  SC_CUDA(cudaMemcpy(counts, r->st.emitted, (size_t)r->S * 4, cudaMemcpyDeviceToHost));
+  return kOk;
+}
+
 int sc_rnnt_tokens_device(const sc_rnnt_decoder *r, const int32_t **ids, const int32_t **steps,
                           const int32_t **counts, int32_t *cap) {
   if (!r || !ids || !steps || !counts || !cap) {

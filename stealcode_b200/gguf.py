@@ -305,13 +305,48 @@ def _views(g: GgufFile, prefixes) -> list:
     return out
 
 
-def save_model(m: "_model.Model", path: str, extra_kv: dict | None = None) -> None:
+# ------------------------------------------------------- RNN-T decoder ---
+RNNT_KEYS = {
+    "vocab": "asr.rnnt.vocab_size", "blank": "asr.rnnt.blank_id", "hidden": "asr.rnnt.pred_hidden",
+    "n_layers": "asr.rnnt.pred_num_layers", "joint": "asr.rnnt.joint_dim",
+    "max_symbols": "asr.rnnt.max_symbols_per_step",
+}
+
+
+def rnnt_config(g: GgufFile) -> "_model.RnntConfig":
+    """RnntConfig from the metadata (nemotron/config.rs:171-186); the joint's
+    encoder width is the encoder's d_model (joint.enc, decoder.rs:219-221)."""
+    vals = {}
+    for f, k in RNNT_KEYS.items():
+        v = g.kv.get(k)
+        if not isinstance(v, int):
+            raise GgufError(f"GGUF metadata: missing u32 {k}")
+        vals[f] = v
+    d_enc = g.kv.get("asr.encoder.d_model", 1024)
+    return _model.RnntConfig(d_enc=int(d_enc), **vals)
+
+
+def decoder_from_gguf(g: GgufFile) -> "_model.Model":
+    """The RNN-T decoder's tensors (`decoder.*`, `joint.*`) as a Model of
+    zero-copy views of the map."""
+    return _model.Model(rnnt_config(g), _views(g, ("decoder.", "joint.")))
+
+
+def save_model(m: "_model.Model", path: str, extra_kv: dict | None = None,
+               decoder: "_model.Model | None" = None) -> None:
     """Write a Model (e.g. a seeded random-init one) as a GGUF checkpoint
-    with the encoder metadata the reference reads."""
+    with the encoder metadata the reference reads, and optionally the RNN-T
+    decoder's tensors and metadata in the same file."""
     c = m.config
     kv = {k: int(getattr(c, f)) for f, k in ENCODER_KEYS.items()}
     kv.update({"asr.encoder.conv_context": "causal", "asr.encoder.xscaling": False, "asr.encoder.use_bias": True,
                "asr.encoder.subsampling_factor": 8, "asr.encoder.pos_emb_max_len": 5000,
                "asr.rnnt.num_prompts": int(c.n_prompts)})
+    tensors = list(m.tensors)
+    if decoder is not None:
+        dc = decoder.config
+        kv.update({k: int(getattr(dc, f)) for f, k in RNNT_KEYS.items()})
+        kv.update({"asr.rnnt.pred_embed_dim": int(dc.hidden)})
+        tensors += decoder.tensors
     kv.update(extra_kv or {})
-    write_gguf(path, kv, m.tensors)
+    write_gguf(path, kv, tensors)

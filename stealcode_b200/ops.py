@@ -321,6 +321,17 @@ class RnntDecoder:
         self.n_streams = n_streams
         self.cap = 16 * max_frames + 64
 
+    @classmethod
+    def from_gguf(cls, path: str, n_streams: int, max_frames: int = 16) -> "RnntDecoder":
+        """Build from a GGUF checkpoint in the reference's layout
+        (GreedyDecoder::load, nemotron/decoder.rs:238-247), memory-mapped."""
+        from . import gguf
+
+        g = gguf.open_gguf(path)
+        dec = cls(gguf.decoder_from_gguf(g), n_streams, max_frames)
+        dec._gguf = g  # the mapping backs the model's arrays
+        return dec
+
     def decode_frames(self, frames, stream=None) -> None:
         """frames: CUDA tensor [n_streams, n, d_enc] (f32) or a raw device
         pointer with n given as (ptr, n).  Synchronises the stream."""
@@ -343,6 +354,12 @@ class RnntDecoder:
         cnt = ctypes.c_int32()
         check(lib.sc_rnnt_tokens(self._h, stream_idx, _hp(ids), _hp(steps), self.cap, ctypes.byref(cnt)))
         return ids[: cnt.value].copy(), steps[: cnt.value].copy()
+
+    def emitted(self) -> np.ndarray:
+        """Tokens each stream emitted in the last decode_frames, [n_streams]."""
+        out = np.empty(self.n_streams, dtype=np.int32)
+        check(lib.sc_rnnt_emitted(self._h, _hp(out)))
+        return out
 
     def state(self, stream_idx: int):
         """(h, c, last_token) of one stream; h, c: [n_layers, hidden]."""

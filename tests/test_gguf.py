@@ -121,3 +121,25 @@ def test_oracle_encoder_from_file_matches_memory(tmp_path, small_model):
             assert a.encode_new(mel[:t1], t0, t1) == 0 and b.encode_new(mel[:t1], t0, t1) == 0
         assert np.array_equal(a.frames(0, a.total()), b.frames(0, b.total()))
         del a, b, m2
+
+
+def test_encoder_decoder_checkpoint(tmp_path):
+    """One file with the encoder (prompt MLP included) and the RNN-T decoder:
+    configs from the metadata, and the oracle decoder built from the file
+    emits what the in-memory one does."""
+    enc = model.random_model(model.EncoderConfig(**SMALL, n_prompts=32), seed=22)
+    dcfg = model.RnntConfig(d_enc=256, hidden=128, n_layers=2, joint=128, vocab=65, blank=64, max_symbols=4)
+    dec = model.random_decoder(dcfg, blank_bias=0.21)
+    path = str(tmp_path / "asr.gguf")
+    gguf.save_model(enc, path, decoder=dec)
+    with gguf.open_gguf(path) as g:
+        e2, d2 = gguf.model_from_gguf(g), gguf.decoder_from_gguf(g)
+        assert e2.config == enc.config and e2.config.n_prompts == 32
+        assert d2.config == dcfg
+        assert {t.name for t in e2.tensors} == {t.name for t in enc.tensors}
+        assert {t.name for t in d2.tensors} == {t.name for t in dec.tensors}
+        fr = synth.normal(23, (12, 256))
+        a, b = oracle.RnntDecoder(dec), oracle.RnntDecoder(d2)
+        ra, rb = a.decode_frames(fr, a.new_state()), b.decode_frames(fr, b.new_state())
+        assert ra[0].tolist() == rb[0].tolist() and ra[1].tolist() == rb[1].tolist()
+        del a, b, e2, d2

@@ -168,3 +168,25 @@ def test_encoder_to_decoder_on_device(torch):
             assert dec.tokens(z)[0].tolist() == odec.decode_frames(fr, ost[z])[0].tolist()
     enc.close()
     dec.close()
+
+
+def test_decoder_from_gguf_matches_memory(torch, tmp_path):
+    """A device decoder built from a GGUF checkpoint emits what one built in
+    memory does."""
+    from stealcode_b200 import gguf
+    from stealcode_b200.ops import RnntDecoder
+
+    em = model.random_model(model.EncoderConfig(n_layers=0), seed=41)
+    dm = model.random_decoder(FULL)
+    path = str(tmp_path / "asr.gguf")
+    gguf.save_model(em, path, decoder=dm)
+    a, b = RnntDecoder(dm, 2, max_frames=8), RnntDecoder.from_gguf(path, 2, max_frames=8)
+    for ci in range(3):
+        fr = torch.from_numpy(synth.normal(700 + ci, (2, 7, FULL.d_enc))).cuda()
+        a.decode_frames(fr)
+        b.decode_frames(fr)
+        assert a.emitted().tolist() == b.emitted().tolist()
+        for z in range(2):
+            assert a.tokens(z)[0].tolist() == b.tokens(z)[0].tolist()
+    a.close()
+    b.close()
