@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
           float sblk;
           const int8_t q = warp_quantize_block(acc[j], true, sblk);
           p.qout.xq[qout_code_index(p.qout, z * c + j, hoff + t)] = q;
-          if (lane == 0) p.qout.dx[((hoff + t) >> 5) * p.qout.t_pad + z * c + j] = sblk;
+          if (lane == 0) p.qout.dx[qout_dx_index(p.qout, z * c + j, (hoff + t) >> 5)] = sblk;
         }
       }
   }

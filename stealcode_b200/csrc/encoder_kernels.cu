@@ -194,7 +194,7 @@ __device__ __forceinline__ void quant_lane(const float (&v)[E], const QOut &qo, 
     int8_t *dst = qo.xq + qout_code_index(qo, f, i);
     *reinterpret_cast<uint4 *>(dst) = make_uint4(words[0], words[1], words[2], words[3]);
     *reinterpret_cast<uint4 *>(dst + (int64_t)qo.ft * 16) = make_uint4(words[4], words[5], words[6], words[7]);
-    qo.dx[(i / 32) * qo.t_pad + f] = sc;
+    qo.dx[qout_dx_index(qo, f, i / 32)] = sc;
   }
 }
 
@@ -494,7 +494,7 @@ __global__ void flatten_kernel(const float *__restrict__ x, int t, int f, int C,
     const int8_t q = warp_quantize_block(v, valid, sblk);
     if (i < (C * f + 31) / 32 * 32) {
       qo.xq[qout_code_index(qo, row, i)] = q;
-      if ((threadIdx.x & 31) == 0) qo.dx[(i / 32) * qo.t_pad + row] = sblk;
+      if ((threadIdx.x & 31) == 0) qo.dx[qout_dx_index(qo, row, i / 32)] = sblk;
     }
   }
 }
@@ -516,7 +516,7 @@ __global__ void prompt_cat_quant_kernel(const float *__restrict__ x, int64_t row
   float sblk;
   const int8_t q = warp_quantize_block(v, valid, sblk);
   qo.xq[qout_code_index(qo, row, i)] = q;
-  if ((threadIdx.x & 31) == 0) qo.dx[(i / 32) * qo.t_pad + row] = sblk;
+  if ((threadIdx.x & 31) == 0) qo.dx[qout_dx_index(qo, row, i / 32)] = sblk;
 }
 
 // Rows of streams with a prompt take the prompt MLP's output

@@ -11,19 +11,20 @@
 // tensor core already computes the next block into the other buffer.
 //
 // CTA roles (warp-specialised, one CTA per 128-row group x FT-frame tile):
-//   warp 0       producer: 1-D bulk copies (TMA engine, no multicast) of the
-//                block's weight tile (the row-group tile layout is already the
-//                no-swizzle K-major UMMA operand layout), the activation tile,
-//                and the block's weight and activation scales, into a ring of
-//                shared-memory stages;
+//   warp 0       producer: 1-D bulk copies (TMA engine, no multicast) into a
+//                ring of shared-memory stages of kTcKb K blocks each: the
+//                blocks' weight tiles (the row-group tile layout is already
+//                the no-swizzle K-major UMMA operand layout), activation
+//                tiles, weight scales and activation scales, one copy each;
 //   warp 1       allocates TMEM and issues one tcgen05.mma per block (single
-//                thread), committing to the stage's "empty" barrier and the
-//                TMEM buffer's "full" barrier;
+//                thread) into a rotating TMEM accumulator, committing to the
+//                accumulator's "full" barrier, and to the stage's "empty"
+//                barrier after the stage's last block;
 //   warps 2..    drain warpgroups: each thread owns one weight row (TMEM lane)
-//                and 32 frame columns; the scales multiply in packed f32x2,
-//                the accumulation runs in the reference scalar oracle's
-//                order with unfused scalar multiply + add, and the int32 ->
-//                f32 conversion is an exact integer add.
+//                and 32 frame columns; per block it reads the accumulator
+//                (tcgen05.ld), releases it, and applies the block's scales in
+//                packed f32x2 arithmetic in the reference scalar oracle's
+//                order; the int32 -> f32 conversion is an exact integer add.
 // Every mbarrier wait is bounded; a wait that gives up sets a status bit and
 // the kernel runs to its end without waiting again, so it cannot hang.
 #include "sc_device.cuh"
@@ -31,25 +32,28 @@
 
 namespace sc {
 
+// K blocks per shared-memory stage: one bulk copy per operand moves
+// kTcKb consecutive blocks (weight tiles, activation tiles and both scale
+// rows are contiguous in their layouts), so a stage costs four copies for
+// kTcKb blocks.  Bulk copies issued by one thread complete one after
+// another, so each (copy kind, stage phase) pair has its own producer lane.
+#ifndef SC_TC_KB
+#define SC_TC_KB 4
+#endif
 #ifndef SC_TC_STAGES
-#define SC_TC_STAGES 8
+#define SC_TC_STAGES 4
 #endif
 #ifndef SC_TC_PHASES
-#define SC_TC_PHASES 4
+#define SC_TC_PHASES 2
 #endif
+constexpr int kTcKb = SC_TC_KB;
 constexpr int kTcStages = SC_TC_STAGES;
-// Bulk copies issued by one thread complete one after another (about half
-// a microsecond each, whatever their size), so the producer spreads them:
-// 4 lanes per block (one per copy), and kTcPhases block phases, lane
-// (phase, copy) handling blocks b = phase (mod kTcPhases).
 constexpr int kTcPhases = SC_TC_PHASES;
 static_assert(kTcStages >= kTcPhases, "every producer phase needs a stage in flight");
-#ifndef SC_TC_ACC_BUFS
-#define SC_TC_ACC_BUFS 2
-#endif
-// TMEM accumulator buffers (FT columns each, at most 512 columns in all):
-// a block's MMA may start once the drain has emptied the buffer it reuses.
-constexpr int kTcAccBufs = SC_TC_ACC_BUFS;
+// TMEM accumulators (FT columns each, 512 columns in all): the MMA of a
+// block may start once the drain has read the accumulator it reuses.
+template <int FT>
+constexpr int tc_acc_bufs() { return 512 / FT < 8 ? 512 / FT : 8; }
 
 static __device__ unsigned g_tc_status;
 
@@ -67,6 +71,7 @@ struct TcParams {
   unsigned *status;
   Epilogue epi;
   QOut qout;
+  float neg_zero;  // -0.0f, opaque to the compiler (see the drain)
 };
 
 // ---- tcgen05 wrappers -----------------------------------------------------
@@ -123,12 +128,13 @@ __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sy
 
 template <int FT, int DWG>
 struct TcSmem {
-  static constexpr int kA = SC_TILE_BYTES;          // 128 x 32 int8
-  static constexpr int kB = FT * 32;                // FT x 32 int8
-  static constexpr int kS = SC_GROUP_ROWS * 2;      // 128 f16 weight scales
-  static constexpr int kD = FT * 4;                 // FT f32 activation scales
-  static constexpr int kStage = kA + kB + kS + kD;  // all multiples of 16
-  static constexpr int kBars = 8 * (2 * kTcStages + 2 * kTcAccBufs) + 16;
+  static constexpr int kA = SC_TILE_BYTES * kTcKb;      // kTcKb tiles of 128 x 32 int8
+  static constexpr int kB = FT * 32 * kTcKb;            // kTcKb tiles of FT x 32 int8
+  static constexpr int kS = SC_GROUP_ROWS * 2 * kTcKb;  // f16 weight scales [kTcKb][128]
+  static constexpr int kD = FT * 4 * kTcKb;             // f32 activation scales [kTcKb][FT]
+  static constexpr int kStage = kA + kB + kS + kD;      // all multiples of 16
+  static constexpr int kAcc = tc_acc_bufs<FT>();
+  static constexpr int kBars = 8 * (2 * kTcStages + 2 * kAcc) + 16;
   static constexpr int kBytes = kTcStages * kStage + kBars;
 };
 
@@ -138,9 +144,6 @@ __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
 }
 __device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
 __device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
-#ifndef SC_TC_DRAIN
-#define SC_TC_DRAIN 0
-#endif
 __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
@@ -161,17 +164,19 @@ template <int FT, int DWG>
 __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __grid_constant__ TcParams p) {
   using L = TcSmem<FT, DWG>;
   static_assert(FT == 32 * DWG, "each drain warpgroup owns 32 frame columns");
+  constexpr int kAcc = L::kAcc;
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t *full = (uint64_t *)(smem + kTcStages * L::kStage);
   uint64_t *empty = full + kTcStages;
   uint64_t *tfull = empty + kTcStages;
-  uint64_t *tempty = tfull + kTcAccBufs;
-  uint32_t *tmem_slot = (uint32_t *)(tempty + kTcAccBufs);
+  uint64_t *tempty = tfull + kAcc;
+  uint32_t *tmem_slot = (uint32_t *)(tempty + kAcc);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t g = blockIdx.x, ft = blockIdx.y;
   const int nb = (int)p.nb;
-  constexpr uint32_t kTmemCols = FT * kTcAccBufs < 32 ? 32 : FT * kTcAccBufs;
+  const int n_stages = (nb + kTcKb - 1) / kTcKb;
+  constexpr uint32_t kTmemCols = FT * kAcc < 32 ? 32 : FT * kAcc;
 
   // All inputs are read after the previous kernel on the stream completes;
   // TMEM is allocated after that too, so a CTA never holds tensor memory
@@ -184,7 +189,7 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
       mbar_init(&full[s], 4);             // one arrive.expect_tx per copy lane
       mbar_init(&empty[s], 1 + 4 * DWG);  // MMA commit + one arrival per drain warp
     }
-    for (int b = 0; b < kTcAccBufs; b++) {
+    for (int b = 0; b < kAcc; b++) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4 * DWG);
     }
@@ -204,26 +209,26 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
   bool ok = true;
   if (warp == 0) {
     if (lane < 4 * kTcPhases) {
-      const int cp = lane & 3, phase = lane >> 2;  // copy kind, block phase
-      for (int b = phase; b < nb && ok; b += kTcPhases) {
-        const int s = b % kTcStages;
-        const uint32_t ph = (uint32_t)(b / kTcStages) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u)) { ok = false; break; }
+      const int cp = lane & 3, phase = lane >> 2;  // copy kind, stage phase
+      for (int si = phase; si < n_stages && ok; si += kTcPhases) {
+        const int s = si % kTcStages;
+        if (!mbar_wait(&empty[s], ((uint32_t)(si / kTcStages) & 1u) ^ 1u)) { ok = false; break; }
+        const int b0 = si * kTcKb, nblk = nb - b0 < kTcKb ? nb - b0 : kTcKb;
         unsigned char *st = smem + s * L::kStage;
         // each copy lane arrives with its own byte count before its copy, so
         // the stage completes only when all four have arrived and landed
         if (cp == 0) {
-          mbar_arrive_expect_tx(&full[s], L::kA);
-          bulk_g2s(st, p.qs + (g * p.nb + b) * SC_TILE_BYTES, L::kA, &full[s]);
+          mbar_arrive_expect_tx(&full[s], nblk * SC_TILE_BYTES);
+          bulk_g2s(st, p.qs + (g * p.nb + b0) * SC_TILE_BYTES, nblk * SC_TILE_BYTES, &full[s]);
         } else if (cp == 1) {
-          mbar_arrive_expect_tx(&full[s], L::kB);
-          bulk_g2s(st + L::kA, p.xq + (ft * p.nb + b) * (int64_t)(FT * 32), L::kB, &full[s]);
+          mbar_arrive_expect_tx(&full[s], nblk * FT * 32);
+          bulk_g2s(st + L::kA, p.xq + (ft * p.nb + b0) * (int64_t)(FT * 32), nblk * FT * 32, &full[s]);
         } else if (cp == 2) {
-          mbar_arrive_expect_tx(&full[s], L::kS);
-          bulk_g2s(st + L::kA + L::kB, p.sc + (g * p.nb + b) * SC_GROUP_ROWS, L::kS, &full[s]);
+          mbar_arrive_expect_tx(&full[s], nblk * SC_GROUP_ROWS * 2);
+          bulk_g2s(st + L::kA + L::kB, p.sc + (g * p.nb + b0) * SC_GROUP_ROWS, nblk * SC_GROUP_ROWS * 2, &full[s]);
         } else {
-          mbar_arrive_expect_tx(&full[s], L::kD);
-          bulk_g2s(st + L::kA + L::kB + L::kS, p.dx + (int64_t)b * p.t_pad + ft * FT, L::kD, &full[s]);
+          mbar_arrive_expect_tx(&full[s], nblk * FT * 4);
+          bulk_g2s(st + L::kA + L::kB + L::kS, p.dx + (ft * p.nb + b0) * (int64_t)FT, nblk * FT * 4, &full[s]);
         }
       }
     }
@@ -231,17 +236,22 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_i8(FT);
-      for (int b = 0; b < nb && ok; b++) {
-        const int s = b % kTcStages, buf = b % kTcAccBufs;
-        if (!mbar_wait(&full[s], (uint32_t)(b / kTcStages) & 1u)) { ok = false; break; }
-        if (!mbar_wait(&tempty[buf], ((uint32_t)(b / kTcAccBufs) & 1u) ^ 1u)) { ok = false; break; }
-        tc_fence_after();
+      int b = 0;
+      for (int si = 0; si < n_stages && ok; si++) {
+        const int s = si % kTcStages;
+        if (!mbar_wait(&full[s], (uint32_t)(si / kTcStages) & 1u)) { ok = false; break; }
+        const int nblk = nb - si * kTcKb < kTcKb ? nb - si * kTcKb : kTcKb;
         const unsigned char *st = smem + s * L::kStage;
-        const uint64_t ad = umma_desc(st, 2048, 128);
-        const uint64_t bd = umma_desc(st + L::kA, FT * 16, 128);
-        tc_mma_i8(tmem_base + (uint32_t)(buf * FT), ad, bd, idesc, 0u);
-        tc_commit(&empty[s]);
-        tc_commit(&tfull[buf]);
+        for (int i = 0; i < nblk; i++, b++) {
+          const int buf = b % kAcc;
+          if (!mbar_wait(&tempty[buf], ((uint32_t)(b / kAcc) & 1u) ^ 1u)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = umma_desc(st + i * SC_TILE_BYTES, 2048, 128);
+          const uint64_t bd = umma_desc(st + L::kA + i * FT * 32, FT * 16, 128);
+          tc_mma_i8(tmem_base + (uint32_t)(buf * FT), ad, bd, idesc, 0u);
+          tc_commit(&tfull[buf]);
+        }
+        tc_commit(&empty[s]);  // the stage's tiles are free once its MMAs complete
       }
     }
     __syncwarp();
@@ -255,56 +265,45 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
     // int32 -> f32 without I2F: for |d| < 2^22, the float with bit pattern
     // d + 0x4B400000 is exactly 1.5 * 2^23 + d (block dots are below 2^20).
     const uint64_t neg_magic = pack2(-12582912.0f, -12582912.0f);
-    const uint64_t neg_zero = pack2(-0.0f, -0.0f), one2 = pack2(1.0f, 1.0f);
-    (void)neg_zero;
-    (void)one2;
+    // fma(s, dot, -0) is the rounded product s * dot (an exact zero keeps its
+    // sign: +0 + -0 = +0, -0 + -0 = -0); -0 arrives as a kernel parameter so
+    // the code generator cannot turn the fma back into a multiply and fuse
+    // it into the following add.
+    const uint64_t nz2 = pack2(p.neg_zero, p.neg_zero);
     uint64_t acc[16];
 #pragma unroll
     for (int j = 0; j < 16; j++) acc[j] = 0ull;
-    for (int b = 0; b < nb && ok; b++) {
-      const int s = b % kTcStages, buf = b % kTcAccBufs;
-      // warp-uniform waits: tcgen05.ld below needs the whole warp
-      bool got = mbar_wait(&full[s], (uint32_t)(b / kTcStages) & 1u);
-      got = got && mbar_wait(&tfull[buf], (uint32_t)(b / kTcAccBufs) & 1u);
-      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t r[32];
-      tc_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * FT + col_base), r);
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
+    int b = 0;
+    for (int si = 0; si < n_stages && ok; si++) {
+      const int s = si % kTcStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(si / kTcStages) & 1u))) { ok = false; break; }
+      const int nblk = nb - si * kTcKb < kTcKb ? nb - si * kTcKb : kTcKb;
       const unsigned char *st = smem + s * L::kStage;
-      const float dwv = __half2float(((const __half *)(st + L::kA + L::kB))[row]);
-      const uint64_t dw2 = pack2(dwv, dwv);
-      const uint64_t *dx2 = (const uint64_t *)(st + L::kA + L::kB + L::kS) + col_base / 2;
-      // acc += (dw * dx) * dot with the three roundings of the reference's
-      // scalar oracle (sgemm_kernel.rs:185-196), so each output is bit-equal
-      // to q8_gemm_scalar's.  The product and the sum are scalar __fmul_rn /
-      // __fadd_rn, which are never fused into an FMA (a packed f32x2 multiply
-      // followed by a packed add was, measurably).
+      for (int i = 0; i < nblk; i++, b++) {
+        const int buf = b % kAcc;
+        // warp-uniform wait: tcgen05.ld below needs the whole warp
+        if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (uint32_t)(b / kAcc) & 1u))) { ok = false; break; }
+        tc_fence_after();
+        uint32_t r[32];
+        tc_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * FT + col_base), r);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        const float dwv = __half2float(((const __half *)(st + L::kA + L::kB))[i * SC_GROUP_ROWS + row]);
+        const uint64_t dw2 = pack2(dwv, dwv);
+        const uint64_t *dx2 = (const uint64_t *)(st + L::kA + L::kB + L::kS) + (i * FT + col_base) / 2;
+        // acc += (dw * dx) * dot with the three roundings of the reference's
+        // scalar oracle (sgemm_kernel.rs:185-196), so each output is bit-equal
+        // to q8_gemm_scalar's, in packed f32x2 arithmetic.
 #pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const uint64_t s2 = fmul2(dw2, dx2[j]);  // dw * dx per column
-        const uint64_t f2 = fadd2(pack2(__uint_as_float(r[2 * j] + 0x4B400000u),
-                                        __uint_as_float(r[2 * j + 1] + 0x4B400000u)),
-                                  neg_magic);   // exact block dots as f32
-#if SC_TC_DRAIN == 0
-        acc[j] = pack2(__fadd_rn(lo_of(acc[j]), __fmul_rn(lo_of(s2), lo_of(f2))),
-                       __fadd_rn(hi_of(acc[j]), __fmul_rn(hi_of(s2), hi_of(f2))));
-#elif SC_TC_DRAIN == 1
-        acc[j] = fadd2(acc[j], ffma2(s2, f2, neg_zero));
-#elif SC_TC_DRAIN == 2
-        acc[j] = ffma2(fmul2(s2, f2), one2, acc[j]);
-#elif SC_TC_DRAIN == 4
-        acc[j] = ffma2(s2, f2, acc[j]);
-#else
-        {
-          uint64_t p2 = fmul2(s2, f2);
-          asm volatile("" : "+l"(p2));
-          acc[j] = fadd2(acc[j], p2);
+        for (int j = 0; j < 16; j++) {
+          const uint64_t s2 = fmul2(dw2, dx2[j]);  // dw * dx per column
+          const uint64_t f2 = fadd2(pack2(__uint_as_float(r[2 * j] + 0x4B400000u),
+                                          __uint_as_float(r[2 * j + 1] + 0x4B400000u)),
+                                    neg_magic);   // exact block dots as f32
+          acc[j] = fadd2(acc[j], ffma2(s2, f2, nz2));
         }
-#endif
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -341,7 +340,7 @@ __global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __g
       const float sblk = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
       const float inv = __fdiv_rn(1.0f, sblk);
       const int64_t fbase = ft * FT + col_base;  // frames of this thread's columns (< t_pad)
-      p.qout.dx[(n >> 5) * p.qout.t_pad + fbase + mycol] = sblk;
+      p.qout.dx[qout_dx_index(p.qout, fbase + mycol, n >> 5)] = sblk;
       // codes: row n is element n % 32 of block n / 32 of the next GEMM's K
       int8_t *dst = p.qout.xq + ((int64_t)ft * p.qout.nb + (n >> 5)) * (FT * 32) + ((n & 31) >> 4) * (FT * 16) +
                     (int64_t)col_base * 16 + (n & 15);
@@ -445,6 +444,7 @@ int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
   p.status = tc_status_ptr();
   p.epi = a.epi;
   p.qout = a.qout;
+  p.neg_zero = -0.0f;
   if (p.qout.xq && (w->rows % SC_GROUP_ROWS || p.epi.op == kEpiResidual || p.qout.t_pad != a.t_pad ||
                     p.qout.ft != tc_frame_tile(a.t) || p.qout.nb * 32 != w->rows)) {
     set_error("q8_gemm_tc: quantised output needs rows %% 128 == 0, no residual and the same frame tiling");

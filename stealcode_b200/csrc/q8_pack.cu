@@ -113,7 +113,7 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t m,
        (lane & 15)] = q;
   else
     xq[col * k_pad + kk] = q;
-  if (lane == 0) dx[b * m_pad + col] = s;
+  if (lane == 0) dx[tile_ft ? ((col / tile_ft) * nb + b) * tile_ft + col % tile_ft : b * m_pad + col] = s;
 }
 
 // Time-major variant with 16-byte loads: one warp per (frame, 4 blocks); the
@@ -168,7 +168,7 @@ __global__ void quantize_act_v4_kernel(const float *__restrict__ x, int64_t m, i
                   (col % tile_ft) * 16 + (sub & 3) * 4) = packed;
   else
     *(uint32_t *)(xq + col * k_pad + kk) = packed;
-  if (sub == 0) dx[b * m_pad + col] = s;
+  if (sub == 0) dx[tile_ft ? ((col / tile_ft) * nb + b) * tile_ft + col % tile_ft : b * m_pad + col] = s;
 }
 
 int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx,

@@ -30,9 +30,10 @@ __device__ __forceinline__ float apply_epilogue(const Epilogue &e, float v, int6
 // q8_pack.cu
 int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k, int64_t block_bytes,
                      int64_t qoff, Q8Weights *w, cudaStream_t st);
-// tile_ft == 0: xq is [m_pad][k_pad]; tile_ft > 0: xq is the tensor-core
-// operand layout [m_pad/tile_ft][nb][2][tile_ft][16] (frame tiles of
-// tile_ft rows, one no-swizzle K-major tile per 32-wide block).
+// tile_ft == 0: xq is [m_pad][k_pad], dx [nb][m_pad]; tile_ft > 0: xq is the
+// tensor-core operand layout [m_pad/tile_ft][nb][2][tile_ft][16] (frame tiles
+// of tile_ft rows, one no-swizzle K-major tile per 32-wide block) and dx
+// [m_pad/tile_ft][nb][tile_ft] (the QOut layout).
 int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx, bool feature_major,
                  int64_t m_pad, int8_t *xq, float *dx, cudaStream_t st, int tile_ft = 0);
 
@@ -60,13 +61,17 @@ int small_gemm_status(unsigned *out);  // read and clear the kernels' status wor
 // the tensor-core GEMM's tiled operand layout (ft = tc_frame_tile(t)): the
 // code of frame f, feature i at
 //   ((f / ft) * nb + i / 32) * ft * 32 + ((i % 32) / 16) * ft * 16 + (f % ft) * 16 + i % 16
-// and the block scale at dx[(i / 32) * t_pad + f].  xq == nullptr: unused.
+// and the block scale at dx[((f / ft) * nb + i / 32) * ft + f % ft] (a frame
+// tile's scales for consecutive blocks are contiguous).  xq == nullptr: unused.
 struct QOut {
   int8_t *xq;
   float *dx;
   int64_t nb, t_pad;
   int ft;
 };
+__host__ __device__ inline int64_t qout_dx_index(const QOut &q, int64_t f, int64_t blk) {
+  return ((f / q.ft) * q.nb + blk) * (int64_t)q.ft + f % q.ft;
+}
 __host__ __device__ inline int64_t qout_code_index(const QOut &q, int64_t f, int64_t i) {
   return ((f / q.ft) * q.nb + i / 32) * (int64_t)q.ft * 32 + ((i & 31) >> 4) * (int64_t)q.ft * 16 +
          (f % q.ft) * 16 + (i & 15);
