@@ -331,6 +331,9 @@ int sc_rnnt_tokens(const sc_rnnt_decoder *r, int64_t stream_idx, int32_t *ids,
                    int32_t *steps, int32_t cap, int32_t *count);
 /* How many tokens each stream emitted in the last call, [n_streams] (host). */
 int sc_rnnt_emitted(const sc_rnnt_decoder *r, int32_t *counts);
+/* Loop rounds the last decode_frames ran (each round is one iteration of
+ * every still-active stream; no reference counterpart, for diagnostics). */
+int64_t sc_rnnt_last_rounds(const sc_rnnt_decoder *r);
 /* Device arrays of the last call's tokens: ids/steps [n_streams][*cap],
  * counts [n_streams]; valid until the next decode_frames. */
 int sc_rnnt_tokens_device(const sc_rnnt_decoder *r, const int32_t **ids,

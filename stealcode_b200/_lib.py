@@ -86,6 +86,7 @@ SIGNATURES = {
     "sc_rnnt_tokens_device": (c_int, [_P, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p),
                                       POINTER(c_int32)]),
     "sc_rnnt_emitted": (c_int, [_P, _P]),
+    "sc_rnnt_last_rounds": (c_int64, [_P]),
     "sc_rnnt_reset": (c_int, [_P, _I]),
     "sc_rnnt_state": (c_int, [_P, _I, _P, _P, POINTER(c_int32)]),
     "sc_rnnt_destroy": (c_int, [_P]),

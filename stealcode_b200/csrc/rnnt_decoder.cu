@@ -5,15 +5,22 @@
 //
 // Every stream runs the reference's loop; the device runs the loops of all
 // streams in lockstep rounds.  One round is one loop iteration of every
-// stream that is still decoding:
-//   1. predictor step (one launch per LSTM layer) for the streams that
+// stream that is still decoding, five kernels:
+//   1. predictor step, one launch per LSTM layer, for the streams that
 //      emitted in the previous round (the reference's `predictor_dirty`);
 //   2. joint.pred over the new predictor output, for the same streams;
 //   3. joint.out over relu(enc_proj[step] + pred) for every active stream;
 //   4. per stream: greedy argmax, token append, the step / max_symbols
 //      bookkeeping, and the stream lists of the next round.
-// The host stops launching rounds once no stream is active (it reads the
-// count one round behind, so the GPU never idles on the check).
+// Every linear reads its input as int8 codes that the producer of the input
+// quantised once (quantize_col per 32-block): the embedding rows at load,
+// each LSTM layer's new h in that layer's epilogue (it is both the next
+// layer's input and, after an emission, the layer's h input), relu(enc +
+// pred) in joint.pred's epilogue or, for streams whose predictor output did
+// not change, in the update.  The round's kernels are captured once into a
+// CUDA graph (two rounds, one per list parity); the host replays it and
+// stops once no stream is active, reading the count one replay behind so the
+// GPU never idles on the check.
 //
 // Arithmetic follows the reference's CPU path to the bit.  Every linear is a
 // q8_gemm call with n = 1 (n = frames for joint.enc) and the reference
@@ -42,10 +49,10 @@
 namespace sc {
 namespace {
 
-constexpr int kRows = 128;    // output rows of a tile: one per thread
-constexpr int kCols = 8;      // input vectors (columns) of a tile
-constexpr int kThreads = 128;
-constexpr int kCtasPerSm = 4;
+constexpr int kLsRows = 128;  // rows of a lane-split tile: 8 threads per row, one per SIMD lane
+constexpr int kLsLanes = 8;
+constexpr int kLsThreads = kLsRows * kLsLanes;
+constexpr int kLsCols = 4;    // columns of a lane-split tile
 
 // A Q8_0 matrix in the decoder's lane order: int8 [rows_pad][k] with the
 // element l + 8j of every 32-block at byte 4l + j, f32 block scales
@@ -58,28 +65,76 @@ struct LaneMat {
   bool simd = false;      // the reference's SIMD order for an n <= 16 GEMM
 };
 
+// Per-call parameters, in device memory so that the captured round graph
+// serves every call.
+struct CallParams {
+  int n, max_iters;
+};
+
 // Device state of all streams (StreamState, live.rs:24-50, plus the loop
-// variables of decode_frames).
+// variables of decode_frames).  Codes are in lane order, one f32 scale per
+// 32-block (dx arrays hold k / 32 scales per vector).
 struct DecState {
-  const float *embed;  // [vocab][H]
-  float *hc;           // [S][2 bufs][h, c][L][H]; buf cur[z] is (h, c), the other (nh, nc)
+  const int8_t *emb_q;  // [vocab][H] codes of the embedding rows
+  const float *emb_dx;  // [vocab][H / 32]
+  const int8_t *zq;     // [H] zero codes (the zero input before the first token)
+  const float *zdx;     // [H / 32] ones (quantize_col's scale of a zero block)
+  float *hc;            // [S][2 bufs][h, c][L][H]; buf cur[z] is (h, c), the other (nh, nc)
+  int8_t *qh;           // [S][2 bufs][L][H] codes of each buffer's h
+  float *qh_dx;         // [S][2 bufs][L][H / 32]
   int32_t *cur, *last_tok, *pred_valid;  // [S]
-  float *pred;         // [S][J] joint.pred of the current predictor output
-  float *enc;          // [S][n][J] joint.enc of this call's frames
-  float *logits;       // [S][V]
-  const float *frames; // [S][n][d_enc]
+  float *pred;          // [S][J] joint.pred of the current predictor output
+  float *enc;           // [S][max_frames][J] joint.enc of this call's frames
+  float *logits;        // [S][V]
+  int8_t *qo;           // [S][J] codes of relu(enc[step] + pred), joint.out's input
+  float *qo_dx;         // [S][J / 32]
+  int8_t *qf;           // [S * max_frames][d_enc] codes of this call's frames
+  float *qf_dx;         // [S * max_frames][d_enc / 32]
+  const float *frames;  // this call's frames (set per call; used outside the graph)
   int32_t *step, *nsym, *iter, *emitted, *status;  // [S]
   int32_t *ids, *steps;                            // [S][cap]
-  int32_t *lists;      // [2 parities][dirty, active][S]
-  int32_t *counts;     // [2 parities][dirty, active]
-  int S, H, L, J, V, n, cap, blank, max_symbols, max_iters, d_enc;
+  int32_t *lists;       // [2 parities][dirty, active][S]
+  int32_t *counts;      // [2 parities][dirty, active]
+  const CallParams *call;
+  int S, H, L, J, V, cap, blank, max_symbols, d_enc;
 };
 
 __device__ __forceinline__ float *hc_at(const DecState &s, int z, int buf, int which, int l) {
   return s.hc + ((((int64_t)z * 2 + buf) * 2 + which) * s.L + l) * s.H;
 }
+__device__ __forceinline__ int8_t *qh_at(const DecState &s, int z, int buf, int l) {
+  return s.qh + (((int64_t)z * 2 + buf) * s.L + l) * s.H;
+}
+__device__ __forceinline__ float *qhdx_at(const DecState &s, int z, int buf, int l) {
+  return s.qh_dx + (((int64_t)z * 2 + buf) * s.L + l) * (s.H / 32);
+}
 __device__ __forceinline__ int32_t *list_at(const DecState &s, int parity, int which) {
   return s.lists + (int64_t)(parity * 2 + which) * s.S;
+}
+
+// Lane-order position of element e within its 32-block.
+__device__ __forceinline__ int lane_pos(int e) { return (e & 7) * 4 + (e >> 3); }
+
+// quantize_col of one 32-block, one warp, lane e holding element e: codes
+// (lane order) and the block's scale.
+__device__ __forceinline__ void warp_store_block(float v, int8_t *codes, float *dx, int blk) {
+  const int lane = threadIdx.x & 31;
+  float sc;
+  const int8_t q = warp_quantize_block(v, true, sc);
+  codes[blk * 32 + lane_pos(lane)] = q;
+  if (lane == 0) dx[blk] = sc;
+}
+
+// joint.out's input for stream z at its current step, all J/32 blocks, by
+// one warp: relu(enc_proj[step] + pred) (live.rs:102-105).
+__device__ void warp_store_out_codes(const DecState &s, int z) {
+  const int lane = threadIdx.x & 31;
+  const float *e = s.enc + ((int64_t)z * s.call->n + s.step[z]) * s.J;
+  const float *p = s.pred + (int64_t)z * s.J;
+  for (int b = 0; b < s.J / 32; b++) {
+    const float v = __fadd_rn(e[b * 32 + lane], p[b * 32 + lane]);
+    warp_store_block(v > 0.0f ? v : 0.0f, s.qo + (int64_t)z * s.J, s.qo_dx + (int64_t)z * (s.J / 32), b);
+  }
 }
 
 // sigmoid and tanh as decoder.rs:431-433 and f32::tanh write them, with
@@ -89,162 +144,340 @@ __device__ __forceinline__ float sigmoid_ref(float x) {
 }
 __device__ __forceinline__ float tanh_rn(float x) { return (float)tanh((double)x); }
 
-// ---- the column sources and sinks of each linear -------------------------
-// LSTM layer l of the predictor step (decoder.rs:158-190): input [x ; h_l]
-// with x the embedding of the last token (zeros before the first) or the new
-// h of layer l-1; rows in gate-interleaved order 4k + g (g = i, f, g, o), so
-// the 4 gates of a cell sit in 4 adjacent lanes.
+// ---- lane-split GEMV ------------------------------------------------------
+// Thread (row, l) of a tile of 128 rows handles SIMD lane l of its row (the
+// products of elements l, l+8, l+16, l+24 of every block: one dp4a) for
+// kLsCols input vectors.  kSimd: the reference's 8-lane order, per block
+// fma(dp4a, dw * dx, acc) and at the end the row's 8 lane sums added in lane
+// order (reduce_sum); otherwise q8_gemm_scalar's order, the 8 lanes' exact
+// integer parts summed per block and acc += (dw * dx) * dot.  The tile's
+// weight rows stream through shared memory in double-buffered chunks of
+// kChunk blocks (cp.async), its input codes are staged once, so the loop
+// never waits on a dependent global load.  Op supplies the column list, the
+// input codes (in up to two parts along K) and the epilogue.
+constexpr int kChunk = 8;                 // K blocks per staged weight chunk
+constexpr int kRing = 4;                  // chunks in flight (a ring of shared-memory buffers)
+constexpr int kWRow = kChunk * 32 + 32;   // staged bytes per row (padded: conflict-free reads)
+
+__device__ __forceinline__ void dec_cp16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void dec_cp4(void *smem, const void *gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void dec_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void dec_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__host__ __device__ inline size_t lane_split_smem(int k, int nb) {
+  return (size_t)kRing * kLsRows * kWRow + (size_t)kRing * kLsRows * kChunk * 4 + (size_t)kLsCols * k +
+         (size_t)kLsCols * nb * 4 + (size_t)kLsCols * kLsRows * 4 + 2 * kLsCols * 2 * sizeof(void *);
+}
+
+template <class Op, bool kSimd>
+__global__ void __launch_bounds__(kLsThreads, 1) lane_split_kernel(LaneMat w, DecState s, Op op) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  int8_t *wsm = reinterpret_cast<int8_t *>(smem);                            // [kRing][128][kWRow]
+  float *ssm = reinterpret_cast<float *>(smem + kRing * kLsRows * kWRow);    // [kRing][128][kChunk]
+  int8_t *xs = reinterpret_cast<int8_t *>(ssm + kRing * kLsRows * kChunk);   // [kLsCols][k]
+  float *xds = reinterpret_cast<float *>(xs + kLsCols * w.k);                // [kLsCols][nb]
+  float(&vals)[kLsCols][kLsRows] = *reinterpret_cast<float(*)[kLsCols][kLsRows]>(xds + kLsCols * w.nb);
+  const int8_t **srcx = reinterpret_cast<const int8_t **>(&vals[kLsCols][0]);  // [kLsCols][2]
+  const float **srcd = reinterpret_cast<const float **>(srcx + 2 * kLsCols);
+  const int t = threadIdx.x, rloc = t >> 3, l = t & 7;
+  op.prologue(s);
+  const int ncols = op.n_cols(s);
+  const int row_tiles = w.rows_pad / kLsRows, col_tiles = (ncols + kLsCols - 1) / kLsCols;
+  const int nbx = Op::kParts == 2 ? op.nbx(s) : w.nb;  // blocks of part 0
+  const int nch = (w.nb + kChunk - 1) / kChunk;
+  for (int tile = blockIdx.x; tile < row_tiles * col_tiles; tile += gridDim.x) {
+    const int rt = tile % row_tiles, ct = tile / row_tiles;
+    int id[kLsCols];
+#pragma unroll
+    for (int c = 0; c < kLsCols; c++) {
+      const int j = ct * kLsCols + c;
+      id[c] = j < ncols ? op.col_id(s, j) : -1;
+    }
+    __syncthreads();  // the previous tile's shared-memory reads are done
+    if (t < kLsCols * Op::kParts && id[t / Op::kParts] >= 0)
+      op.src(s, id[t / Op::kParts], t % Op::kParts, srcx[t / Op::kParts * 2 + t % Op::kParts],
+             srcd[t / Op::kParts * 2 + t % Op::kParts]);
+    __syncthreads();
+    // group 0: the input codes and scales of the tile's columns, and chunk 0
+    for (int i = t; i < kLsCols * (w.k / 16); i += kLsThreads) {
+      const int c = i / (w.k / 16), off = (i % (w.k / 16)) * 16, b = off / 32;
+      if (id[c] < 0) continue;
+      const int part = b >= nbx;
+      dec_cp16(xs + c * w.k + off, srcx[c * 2 + part] + off - (part ? nbx * 32 : 0));
+    }
+    for (int i = t; i < kLsCols * w.nb; i += kLsThreads) {
+      const int c = i / w.nb, b = i % w.nb;
+      if (id[c] < 0) continue;
+      const int part = b >= nbx;
+      dec_cp4(xds + c * w.nb + b, srcd[c * 2 + part] + b - (part ? nbx : 0));
+    }
+    // each iteration commits one group (empty past the last chunk), so
+    // waiting for all but the kRing - 1 newest groups lands chunk ch
+    auto stage = [&](int ch) {
+      if (ch < nch) {
+        const int buf = ch % kRing, b0 = ch * kChunk, nbk = w.nb - b0 < kChunk ? w.nb - b0 : kChunk;
+        const int per_row = nbk * 2;
+        for (int i = t; i < kLsRows * per_row; i += kLsThreads) {
+          const int r = i / per_row, q = i % per_row;
+          dec_cp16(wsm + (buf * kLsRows + r) * kWRow + q * 16,
+                   w.qs + (int64_t)(rt * kLsRows + r) * w.k + b0 * 32 + q * 16);
+        }
+        for (int i = t; i < kLsRows * nbk; i += kLsThreads) {
+          const int r = i / nbk, q = i % nbk;
+          dec_cp4(ssm + (buf * kLsRows + r) * kChunk + q, w.sc + (int64_t)(rt * kLsRows + r) * w.nb + b0 + q);
+        }
+      }
+      dec_cp_commit();
+    };
+#pragma unroll
+    for (int ch = 0; ch < kRing - 1; ch++) stage(ch);
+    float acc[kLsCols];
+#pragma unroll
+    for (int c = 0; c < kLsCols; c++) acc[c] = 0.0f;
+    for (int ch = 0; ch < nch; ch++) {
+      stage(ch + kRing - 1);
+      dec_cp_wait<kRing - 1>();
+      __syncthreads();
+      const int buf = ch % kRing, b0 = ch * kChunk, nbk = w.nb - b0 < kChunk ? w.nb - b0 : kChunk;
+      const int8_t *wr = wsm + (buf * kLsRows + rloc) * kWRow + 4 * l;
+      const float *sr = ssm + (buf * kLsRows + rloc) * kChunk;
+      for (int q = 0; q < nbk; q++) {
+        const int b = b0 + q;
+        const int wv = *reinterpret_cast<const int *>(wr + q * 32);
+        const float dw = sr[q];
+#pragma unroll
+        for (int c = 0; c < kLsCols; c++) {
+          if (id[c] < 0) continue;
+          const int xw = *reinterpret_cast<const int *>(xs + c * w.k + b * 32 + 4 * l);
+          const float scale = __fmul_rn(dw, xds[c * w.nb + b]);
+          if (kSimd) {
+            acc[c] = __fmaf_rn((float)__dp4a(wv, xw, 0), scale, acc[c]);
+          } else {  // the block's exact dot: the 8 lanes' integer parts
+            int d = __dp4a(wv, xw, 0);
+            d += __shfl_xor_sync(0xffffffffu, d, 1);
+            d += __shfl_xor_sync(0xffffffffu, d, 2);
+            d += __shfl_xor_sync(0xffffffffu, d, 4);
+            acc[c] = __fadd_rn(acc[c], __fmul_rn(scale, (float)d));
+          }
+        }
+      }
+      __syncthreads();  // the chunk's buffer may be restaged
+    }
+    dec_cp_wait<0>();  // no copy of this tile still in flight (the trailing groups are empty)
+    if (kSimd) {
+      // reduce_sum over the row's 8 lanes, in lane order (every lane of the
+      // row computes the same sum from the same values)
+      const int base = (threadIdx.x & 31) & ~7;
+#pragma unroll
+      for (int c = 0; c < kLsCols; c++) {
+        float y = __shfl_sync(0xffffffffu, acc[c], base);
+#pragma unroll
+        for (int q = 1; q < kLsLanes; q++) y = __fadd_rn(y, __shfl_sync(0xffffffffu, acc[c], base + q));
+        acc[c] = y;
+      }
+    }
+    op.epilogue(s, w, id, rt, rloc, l, acc, vals);
+  }
+}
+
+// LSTM layer l of the predictor step (decoder.rs:158-195) for the streams
+// that emitted: input [x ; h_l], x the embedding of the last token (zeros
+// before the first) or layer l-1's new h; rows in gate-interleaved order
+// 4k + g (g = i, f, g, o), so a warp (4 rows) holds one cell's gates.  The
+// epilogue adds the merged bias, runs the cell, stores nc/nh, and quantises
+// the tile's 32 new h values (one 32-block) for the next layer and for the
+// next step's h input.
 struct LstmOp {
-  int l, parity;
+  static constexpr int kParts = 2;
+  int l_, parity;  // layer, list parity
+  __device__ void prologue(const DecState &) const {}
   __device__ int n_cols(const DecState &s) const { return s.counts[parity * 2]; }
   __device__ int col_id(const DecState &s, int j) const { return list_at(s, parity, 0)[j]; }
-  __device__ float input(const DecState &s, int z, int i) const {
-    const int H = s.H;
-    if (i >= H) return hc_at(s, z, s.cur[z], 0, l)[i - H];
-    if (l > 0) return hc_at(s, z, s.cur[z] ^ 1, 0, l - 1)[i];
-    const int tok = s.last_tok[z];
-    return tok >= 0 ? s.embed[(int64_t)tok * H + i] : 0.0f;
+  __device__ int nbx(const DecState &s) const { return s.H / 32; }
+  __device__ void src(const DecState &s, int z, int part, const int8_t *&x, const float *&dx) const {
+    if (part) {
+      x = qh_at(s, z, s.cur[z], l_);
+      dx = qhdx_at(s, z, s.cur[z], l_);
+    } else if (l_ > 0) {
+      x = qh_at(s, z, s.cur[z] ^ 1, l_ - 1);
+      dx = qhdx_at(s, z, s.cur[z] ^ 1, l_ - 1);
+    } else {
+      const int tok = s.last_tok[z];
+      x = tok >= 0 ? s.emb_q + (int64_t)tok * s.H : s.zq;
+      dx = tok >= 0 ? s.emb_dx + (int64_t)tok * (s.H / 32) : s.zdx;
+    }
   }
-  __device__ void output(const DecState &s, const LaneMat &w, int z, int row, float y) const {
-    // gates[k] += bias[k] (decoder.rs:176-178), then the cell (:185-194)
-    const float g = __fadd_rn(y, w.bias[row < w.rows ? row : 0]);
-    const int lane = threadIdx.x & 31, base = lane & ~3;
-    const float gi = __shfl_sync(0xffffffffu, g, base), gf = __shfl_sync(0xffffffffu, g, base + 1);
-    const float gg = __shfl_sync(0xffffffffu, g, base + 2), go = __shfl_sync(0xffffffffu, g, base + 3);
-    const int k = row >> 2;
-    if (z < 0 || (lane & 3) || k >= s.H) return;
-    const int nb = s.cur[z] ^ 1;
-    const float ig = sigmoid_ref(gi), fg = sigmoid_ref(gf), gt = tanh_rn(gg), og = sigmoid_ref(go);
-    const float cold = hc_at(s, z, nb ^ 1, 1, l)[k];
-    const float cn = __fadd_rn(__fmul_rn(fg, cold), __fmul_rn(ig, gt));
-    hc_at(s, z, nb, 1, l)[k] = cn;
-    hc_at(s, z, nb, 0, l)[k] = __fmul_rn(og, tanh_rn(cn));
+  __device__ void epilogue(const DecState &s, const LaneMat &w, const int (&id)[kLsCols], int rt, int rloc, int l,
+                           const float (&y)[kLsCols], float (&vals)[kLsCols][kLsRows]) const {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = rt * kLsRows + rloc, k = rt * 32 + warp;  // warp = cell of the tile
+    const int gate = lane >> 3;                               // this thread's row = gate `gate` of the cell
+    // gates[k] += bias[k] (decoder.rs:176-178); lane (gate, l < kLsCols)
+    // applies its gate's activation for column l
+    float a = 0.0f;
+    {
+      const float bias = w.bias[row];
+      float g = 0.0f;
+#pragma unroll
+      for (int c = 0; c < kLsCols; c++)
+        if (c == l) g = __fadd_rn(y[c], bias);
+      if (l < kLsCols) a = gate == 2 ? tanh_rn(g) : sigmoid_ref(g);
+    }
+    const float ig = __shfl_sync(0xffffffffu, a, l & 7), fg = __shfl_sync(0xffffffffu, a, 8 + (l & 7));
+    const float gt = __shfl_sync(0xffffffffu, a, 16 + (l & 7)), og = __shfl_sync(0xffffffffu, a, 24 + (l & 7));
+    // the cell (decoder.rs:185-194), lane l < kLsCols of row group 0 for column l
+    int z = -1;
+#pragma unroll
+    for (int c = 0; c < kLsCols; c++)
+      if (c == l) z = id[c];
+    if (gate == 0 && l < kLsCols && z >= 0) {
+      const int nb = s.cur[z] ^ 1;
+      const float cn = __fadd_rn(__fmul_rn(fg, hc_at(s, z, nb ^ 1, 1, l_)[k]), __fmul_rn(ig, gt));
+      const float hn = __fmul_rn(og, tanh_rn(cn));
+      hc_at(s, z, nb, 1, l_)[k] = cn;
+      hc_at(s, z, nb, 0, l_)[k] = hn;
+      vals[l][warp] = hn;
+    }
+    __syncthreads();
+    if (warp < kLsCols && id[warp] >= 0) {
+      const int zz = id[warp], nb = s.cur[zz] ^ 1;
+      warp_store_block(vals[warp][lane], qh_at(s, zz, nb, l_), qhdx_at(s, zz, nb, l_), rt);
+    }
+    __syncthreads();
   }
 };
 
-// joint.pred over the last layer's new h (live.rs:100-101, Lin::matvec).
+// joint.pred over the last layer's new h (live.rs:100-101, Lin::matvec) for
+// the streams whose predictor ran; the epilogue stores pred and quantises
+// joint.out's input relu(enc_proj[step] + pred) for them.  Block 0 also
+// clears the next round's list counts (their last readers, the previous
+// round's kernels, have finished).
 struct PredOp {
+  static constexpr int kParts = 1;
   int parity;
+  __device__ void prologue(const DecState &s) const {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      s.counts[(parity ^ 1) * 2] = 0;
+      s.counts[(parity ^ 1) * 2 + 1] = 0;
+    }
+  }
   __device__ int n_cols(const DecState &s) const { return s.counts[parity * 2]; }
   __device__ int col_id(const DecState &s, int j) const { return list_at(s, parity, 0)[j]; }
-  __device__ float input(const DecState &s, int z, int i) const {
-    return hc_at(s, z, s.cur[z] ^ 1, 0, s.L - 1)[i];
+  __device__ int nbx(const DecState &s) const { return 0; }
+  __device__ void src(const DecState &s, int z, int, const int8_t *&x, const float *&dx) const {
+    x = qh_at(s, z, s.cur[z] ^ 1, s.L - 1);
+    dx = qhdx_at(s, z, s.cur[z] ^ 1, s.L - 1);
   }
-  __device__ void output(const DecState &s, const LaneMat &w, int z, int row, float y) const {
-    if (z < 0 || row >= w.rows) return;
-    s.pred[(int64_t)z * s.J + row] = w.bias ? __fadd_rn(y, w.bias[row]) : y;
-    if (row == 0) s.pred_valid[z] = 1;
+  __device__ void epilogue(const DecState &s, const LaneMat &w, const int (&id)[kLsCols], int rt, int rloc, int l,
+                           const float (&y)[kLsCols], float (&vals)[kLsCols][kLsRows]) const {
+    const int row = rt * kLsRows + rloc;
+#pragma unroll
+    for (int c = 0; c < kLsCols; c++) {
+      const int z = id[c];
+      if (l == 0 && z >= 0) {
+        float v = 0.0f;
+        if (row < w.rows) {
+          const float p = w.bias ? __fadd_rn(y[c], w.bias[row]) : y[c];
+          s.pred[(int64_t)z * s.J + row] = p;
+          v = __fadd_rn(s.enc[((int64_t)z * s.call->n + s.step[z]) * s.J + row], p);
+          v = v > 0.0f ? v : 0.0f;  // (e + p).max(0.0): NaN -> 0
+          if (row == 0) s.pred_valid[z] = 1;
+        }
+        vals[c][rloc] = v;
+      }
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < kLsCols * (kLsRows / 32)) {
+      const int c = warp / (kLsRows / 32), blk = warp % (kLsRows / 32), gb = rt * (kLsRows / 32) + blk;
+      const int z = id[c];
+      if (z >= 0 && gb < s.J / 32)
+        warp_store_block(vals[c][blk * 32 + lane], s.qo + (int64_t)z * s.J, s.qo_dx + (int64_t)z * (s.J / 32),
+                         gb);
+    }
+    __syncthreads();
   }
 };
 
-// joint.out over relu(enc_proj[step] + pred) (live.rs:102-106), every
-// active stream.
+// joint.out (live.rs:106, Lin::matvec) for every active stream: logits.
 struct OutOp {
+  static constexpr int kParts = 1;
   int parity;
+  __device__ void prologue(const DecState &) const {}
   __device__ int n_cols(const DecState &s) const { return s.counts[parity * 2 + 1]; }
   __device__ int col_id(const DecState &s, int j) const { return list_at(s, parity, 1)[j]; }
-  __device__ float input(const DecState &s, int z, int i) const {
-    const float v = __fadd_rn(s.enc[((int64_t)z * s.n + s.step[z]) * s.J + i], s.pred[(int64_t)z * s.J + i]);
-    return v > 0.0f ? v : 0.0f;  // (e + p).max(0.0): NaN -> 0
+  __device__ int nbx(const DecState &) const { return 0; }
+  __device__ void src(const DecState &s, int z, int, const int8_t *&x, const float *&dx) const {
+    x = s.qo + (int64_t)z * s.J;
+    dx = s.qo_dx + (int64_t)z * (s.J / 32);
   }
-  __device__ void output(const DecState &s, const LaneMat &w, int z, int row, float y) const {
-    if (z < 0 || row >= w.rows) return;
-    s.logits[(int64_t)z * s.V + row] = w.bias ? __fadd_rn(y, w.bias[row]) : y;
+  __device__ void epilogue(const DecState &s, const LaneMat &w, const int (&id)[kLsCols], int rt, int rloc, int l,
+                           const float (&y)[kLsCols], float (&)[kLsCols][kLsRows]) const {
+    const int row = rt * kLsRows + rloc;
+    if (l || row >= w.rows) return;
+#pragma unroll
+    for (int c = 0; c < kLsCols; c++)
+      if (id[c] >= 0) s.logits[(int64_t)id[c] * s.V + row] = w.bias ? __fadd_rn(y[c], w.bias[row]) : y[c];
   }
 };
 
 // joint.enc over the call's frames (live.rs:71-81, Lin::forward_t with n
-// frames): column z * n + t.
+// frames, bias added after): column z * n + t.
 struct EncOp {
-  __device__ int n_cols(const DecState &s) const { return s.S * s.n; }
+  static constexpr int kParts = 1;
+  __device__ void prologue(const DecState &) const {}
+  __device__ int n_cols(const DecState &s) const { return s.S * s.call->n; }
   __device__ int col_id(const DecState &, int j) const { return j; }
-  __device__ float input(const DecState &s, int col, int i) const {
-    return s.frames[(int64_t)col * s.d_enc + i];
+  __device__ int nbx(const DecState &) const { return 0; }
+  __device__ void src(const DecState &s, int col, int, const int8_t *&x, const float *&dx) const {
+    x = s.qf + (int64_t)col * s.d_enc;
+    dx = s.qf_dx + (int64_t)col * (s.d_enc / 32);
   }
-  __device__ void output(const DecState &s, const LaneMat &w, int col, int row, float y) const {
-    if (col < 0 || row >= w.rows) return;
-    s.enc[(int64_t)col * s.J + row] = w.bias ? __fadd_rn(y, w.bias[row]) : y;
+  __device__ void epilogue(const DecState &s, const LaneMat &w, const int (&id)[kLsCols], int rt, int rloc, int l,
+                           const float (&y)[kLsCols], float (&)[kLsCols][kLsRows]) const {
+    const int row = rt * kLsRows + rloc;
+    if (l || row >= w.rows) return;
+#pragma unroll
+    for (int c = 0; c < kLsCols; c++)
+      if (id[c] >= 0) s.enc[(int64_t)id[c] * s.J + row] = w.bias ? __fadd_rn(y[c], w.bias[row]) : y[c];
   }
 };
 
-// y = W x for tiles of 128 rows x 8 columns, grid-stride over the tiles
-// the column count (read on the device) needs.  The columns' codes are
-// quantised per 32-block in the prologue (quantize_col, one warp per block)
-// into shared memory in lane order; every thread owns one row.
-template <bool kSimd, class Op>
-__global__ void __launch_bounds__(kThreads) lane_gemv_kernel(LaneMat w, DecState s, Op op) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  int8_t *xs = reinterpret_cast<int8_t *>(smem);                // [kCols][k]
-  float *dxs = reinterpret_cast<float *>(smem + kCols * w.k);   // [kCols][nb]
-  int *ids = reinterpret_cast<int *>(dxs + kCols * w.nb);       // [kCols]
-  const int ncols = op.n_cols(s);
-  const int row_tiles = w.rows_pad / kRows, col_tiles = (ncols + kCols - 1) / kCols;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int tile = blockIdx.x; tile < row_tiles * col_tiles; tile += gridDim.x) {
-    const int rt = tile % row_tiles, ct = tile / row_tiles;
-    __syncthreads();  // the previous tile's reads of xs/dxs/ids are done
-    for (int c = warp; c < kCols; c += kThreads / 32) {
-      const int j = ct * kCols + c;
-      const int id = j < ncols ? op.col_id(s, j) : -1;
-      if (lane == 0) ids[c] = id;
-      for (int b = 0; b < w.nb; b++) {
-        const float v = id >= 0 ? op.input(s, id, b * 32 + lane) : 0.0f;
-        float sc;
-        const int8_t q = warp_quantize_block(v, true, sc);
-        xs[c * w.k + b * 32 + (lane & 7) * 4 + (lane >> 3)] = q;
-        if (lane == 0) dxs[c * w.nb + b] = sc;
-      }
-    }
-    __syncthreads();
-    const int row = rt * kRows + threadIdx.x;
-    const int4 *wq = reinterpret_cast<const int4 *>(w.qs + (int64_t)row * w.k);
-    const float *wsc = w.sc + (int64_t)row * w.nb;
-    float acc[kCols][kSimd ? 8 : 1];
-#pragma unroll
-    for (int c = 0; c < kCols; c++)
-#pragma unroll
-      for (int l = 0; l < (kSimd ? 8 : 1); l++) acc[c][l] = 0.0f;
-    for (int b = 0; b < w.nb; b++) {
-      const int4 lo = __ldg(wq + 2 * b), hi = __ldg(wq + 2 * b + 1);
-      const int wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-      const float dw = __ldg(wsc + b);
-#pragma unroll
-      for (int c = 0; c < kCols; c++) {
-        const int4 *xb = reinterpret_cast<const int4 *>(xs + c * w.k + b * 32);
-        const int4 xlo = xb[0], xhi = xb[1];
-        const int xv[8] = {xlo.x, xlo.y, xlo.z, xlo.w, xhi.x, xhi.y, xhi.z, xhi.w};
-        const float scale = __fmul_rn(dw, dxs[c * w.nb + b]);
-        if (kSimd) {
-#pragma unroll
-          for (int l = 0; l < 8; l++) acc[c][l] = __fmaf_rn((float)__dp4a(wv[l], xv[l], 0), scale, acc[c][l]);
-        } else {
-          int dot = 0;
-#pragma unroll
-          for (int l = 0; l < 8; l++) dot = __dp4a(wv[l], xv[l], dot);
-          acc[c][0] = __fadd_rn(acc[c][0], __fmul_rn(scale, (float)dot));
-        }
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < kCols; c++) {
-      float y = acc[c][0];
-      if (kSimd) {
-#pragma unroll
-        for (int l = 1; l < 8; l++) y = __fadd_rn(y, acc[c][l]);  // reduce_sum: lanes in order
-      }
-      op.output(s, w, ids[c], row, y);
-    }
-  }
+// quantize_col of every frame of the call (one warp per frame and block).
+__global__ void rnnt_quant_frames_kernel(DecState s, int64_t cols) {
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nbk = s.d_enc / 32;
+  if (wid >= cols * nbk) return;
+  const int64_t col = wid / nbk;
+  const int b = (int)(wid % nbk);
+  warp_store_block(s.frames[col * s.d_enc + b * 32 + (threadIdx.x & 31)], s.qf + col * s.d_enc,
+                   s.qf_dx + col * nbk, b);
+}
+
+// Embedding rows -> codes, once at load (one warp per row and block).
+__global__ void rnnt_quant_embed_kernel(const float *emb, int64_t rows, int H, int8_t *q, float *dx) {
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nbk = H / 32;
+  if (wid >= rows * nbk) return;
+  const int64_t r = wid / nbk;
+  const int b = (int)(wid % nbk);
+  warp_store_block(emb[r * H + b * 32 + (threadIdx.x & 31)], q + r * H, dx + r * nbk, b);
 }
 
 // Start of a decode_frames call: the loop variables of every stream, the
 // first round's lists (every stream active; the predictor runs where its
-// output is not already current).  One CTA.
+// output is not already current) and joint.out's input for the streams
+// whose predictor output is current.  One warp per stream; the list counts
+// were cleared before.
 __global__ void rnnt_init_kernel(DecState s) {
-  if (threadIdx.x == 0)
-    for (int i = 0; i < 4; i++) s.counts[i] = 0;
-  __syncthreads();
-  for (int z = threadIdx.x; z < s.S; z += blockDim.x) {
+  const int z = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (z >= s.S) return;
+  if (lane == 0) {
     s.step[z] = 0;
     s.nsym[z] = 0;
     s.iter[z] = 0;
@@ -253,33 +486,35 @@ __global__ void rnnt_init_kernel(DecState s) {
     list_at(s, 0, 1)[atomicAdd(&s.counts[1], 1)] = z;
     if (!s.pred_valid[z]) list_at(s, 0, 0)[atomicAdd(&s.counts[0], 1)] = z;
   }
-}
-
-// Clears the next round's list counts (their last readers, the previous
-// round's kernels, have finished).
-__global__ void rnnt_clear_kernel(DecState s, int parity) {
-  s.counts[(parity ^ 1) * 2] = 0;
-  s.counts[(parity ^ 1) * 2 + 1] = 0;
+  __syncwarp();
+  if (s.pred_valid[z]) warp_store_out_codes(s, z);
 }
 
 // One loop iteration's decision per active stream (live.rs:107-140): the
 // first index of the largest logit (NaNs never win; a NaN logit 0 keeps
 // index 0), then blank -> next frame, else emit, swap the LSTM state and
-// count symbols against max_symbols.  One warp per stream.
-__global__ void rnnt_update_kernel(DecState s, int parity) {
-  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (wid >= s.counts[parity * 2 + 1]) return;
-  const int z = list_at(s, parity, 1)[wid];
+// count symbols against max_symbols.  A stream that stays active without
+// emitting gets joint.out's input for its new step here.  One CTA per
+// stream: the argmax over the whole CTA, the input codes one warp per block.
+constexpr int kUpdThreads = 512;
+__global__ void __launch_bounds__(kUpdThreads) rnnt_update_kernel(DecState s, int parity) {
+  __shared__ float sv[kUpdThreads / 32];
+  __shared__ int si[kUpdThreads / 32];
+  __shared__ int keep_s;
+  if ((int)blockIdx.x >= s.counts[parity * 2 + 1]) return;
+  const int z = list_at(s, parity, 1)[blockIdx.x];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float *lg = s.logits + (int64_t)z * s.V;
   float bv = 0.0f;
   int bi = INT_MAX;
-  for (int i = lane; i < s.V; i += 32) {
+  for (int i = threadIdx.x; i < s.V; i += kUpdThreads) {
     const float v = lg[i];
     if (v == v && (bi == INT_MAX || v > bv)) {
       bv = v;
       bi = i;
     }
   }
+  // (value, index) order: larger value first, then the smaller index
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -289,41 +524,64 @@ __global__ void rnnt_update_kernel(DecState s, int parity) {
       bi = oi;
     }
   }
-  if (lane) return;
-  const float v0 = lg[0];
-  const int best = (v0 != v0 || bi == INT_MAX) ? 0 : bi;
-  int step = s.step[z], ns = s.nsym[z], em = s.emitted[z];
-  const int it = s.iter[z] + 1;
-  bool dirty = false;
-  if (best == s.blank) {
-    step++;
-    ns = 0;
-  } else {
-    if (em < s.cap) {
-      s.ids[(int64_t)z * s.cap + em] = best;
-      s.steps[(int64_t)z * s.cap + em] = step;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int q = 1; q < kUpdThreads / 32; q++) {
+      const float ov = sv[q];
+      const int oi = si[q];
+      if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) {
+        bv = ov;
+        bi = oi;
+      }
     }
-    em++;
-    s.last_tok[z] = best;
-    s.cur[z] ^= 1;  // std::mem::swap(h, nh), (c, nc)
-    s.pred_valid[z] = 0;
-    dirty = true;
-    ns++;
-    if (s.max_symbols > 0 && ns >= s.max_symbols) {
+    const float v0 = lg[0];
+    const int best = (v0 != v0 || bi == INT_MAX) ? 0 : bi;
+    int step = s.step[z], ns = s.nsym[z], em = s.emitted[z];
+    const int it = s.iter[z] + 1;
+    bool dirty = false;
+    if (best == s.blank) {
       step++;
       ns = 0;
+    } else {
+      if (em < s.cap) {
+        s.ids[(int64_t)z * s.cap + em] = best;
+        s.steps[(int64_t)z * s.cap + em] = step;
+      }
+      em++;
+      s.last_tok[z] = best;
+      s.cur[z] ^= 1;  // std::mem::swap(h, nh), (c, nc)
+      s.pred_valid[z] = 0;
+      dirty = true;
+      ns++;
+      if (s.max_symbols > 0 && ns >= s.max_symbols) {
+        step++;
+        ns = 0;
+      }
     }
+    s.step[z] = step;
+    s.nsym[z] = ns;
+    s.iter[z] = it;
+    s.emitted[z] = em;
+    const bool active = step < s.call->n && it < s.call->max_iters;
+    if (!active && it >= s.call->max_iters) s.status[z] = 1;  // "rnnt decode: iteration cap hit"
+    if (active) {
+      const int np = parity ^ 1;
+      list_at(s, np, 1)[atomicAdd(&s.counts[np * 2 + 1], 1)] = z;
+      if (dirty) list_at(s, np, 0)[atomicAdd(&s.counts[np * 2], 1)] = z;
+    }
+    keep_s = active && !dirty;
   }
-  s.step[z] = step;
-  s.nsym[z] = ns;
-  s.iter[z] = it;
-  s.emitted[z] = em;
-  const bool active = step < s.n && it < s.max_iters;
-  if (!active && it >= s.max_iters) s.status[z] = 1;  // "rnnt decode: iteration cap hit"
-  if (active) {
-    const int np = parity ^ 1;
-    list_at(s, np, 1)[atomicAdd(&s.counts[np * 2 + 1], 1)] = z;
-    if (dirty) list_at(s, np, 0)[atomicAdd(&s.counts[np * 2], 1)] = z;
+  __syncthreads();  // thread 0's stores of the loop variables are visible to the CTA
+  if (!keep_s) return;
+  const float *e = s.enc + ((int64_t)z * s.call->n + s.step[z]) * s.J;
+  const float *p = s.pred + (int64_t)z * s.J;
+  for (int b = warp; b < s.J / 32; b += kUpdThreads / 32) {
+    const float v = __fadd_rn(e[b * 32 + lane], p[b * 32 + lane]);
+    warp_store_block(v > 0.0f ? v : 0.0f, s.qo + (int64_t)z * s.J, s.qo_dx + (int64_t)z * (s.J / 32), b);
   }
 }
 
@@ -365,11 +623,15 @@ struct sc_rnnt_decoder {
   std::vector<LaneMat> lstm;
   LaneMat jenc, jpred, jout;
   DecState st{};
-  int32_t *pinned = nullptr;  // [2] active counts read back
+  CallParams *call = nullptr;     // device
+  int32_t *pinned = nullptr;      // [2] active counts read back; [2..3] call parameters staging
   cudaEvent_t ev[2] = {nullptr, nullptr};
-  int64_t last_n = 0;
+  cudaGraphExec_t rounds = nullptr;  // two rounds (list parities 0, 1)
+  int round_launches = 0;
+  int64_t last_n = 0, last_rounds = 0;
   std::vector<void *> allocs;
   ~sc_rnnt_decoder() {
+    if (rounds) cudaGraphExecDestroy(rounds);
     for (void *p : allocs) cudaFree(p);
     if (pinned) cudaFreeHost(pinned);
     for (cudaEvent_t e : ev)
@@ -439,7 +701,7 @@ struct RLoader {
   bool lane_mat(const std::vector<const uint8_t *> &parts, int64_t k_each, int64_t rows, F src_row,
                 const std::vector<float> *bias, LaneMat *m) {
     const int64_t nb_each = k_each / 32, k = k_each * (int64_t)parts.size(), nb = k / 32;
-    const int64_t rows_pad = (rows + kRows - 1) / kRows * kRows;
+    const int64_t rows_pad = (rows + kLsRows - 1) / kLsRows * kLsRows;
     std::vector<int8_t> qs((size_t)(rows_pad * k), 0);
     std::vector<float> sc((size_t)(rows_pad * nb), 0.0f);
     for (int64_t p = 0; p < rows; p++) {
@@ -479,45 +741,83 @@ struct RLoader {
   }
 };
 
-int launch_gemv(const sc_rnnt_decoder *r, const LaneMat &w, int64_t max_cols, bool simd, int kind, int arg,
-                cudaStream_t st) {
-  const int64_t tiles = (w.rows_pad / kRows) * ((max_cols + kCols - 1) / kCols);
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)r->sm_count * kCtasPerSm));
-  const size_t smem = (size_t)kCols * w.k + (size_t)kCols * w.nb * 4 + kCols * 4;
-  const DecState &s = r->st;
-#define SC_GEMV(OP)                                                                        \
-  do {                                                                                     \
-    if (simd)                                                                              \
-      lane_gemv_kernel<true, OP><<<grid, kThreads, smem, st>>>(w, s, op);                  \
-    else                                                                                   \
-      lane_gemv_kernel<false, OP><<<grid, kThreads, smem, st>>>(w, s, op);                 \
-  } while (0)
-  switch (kind) {
-    case 0: {
-      LstmOp op{arg >> 1, arg & 1};
-      SC_GEMV(LstmOp);
-      break;
-    }
-    case 1: {
-      PredOp op{arg};
-      SC_GEMV(PredOp);
-      break;
-    }
-    case 2: {
-      OutOp op{arg};
-      SC_GEMV(OutOp);
-      break;
-    }
-    default: {
-      EncOp op{};
-      SC_GEMV(EncOp);
-      break;
-    }
-  }
-#undef SC_GEMV
+template <class Op, bool kSimd>
+int launch_lane_split_t(const sc_rnnt_decoder *r, const LaneMat &w, Op op, int64_t max_cols, cudaStream_t st) {
+  const int64_t tiles = (w.rows_pad / kLsRows) * ceil_div(max_cols, kLsCols);
+  // one wave at most: CTAs past the live columns' tiles exit at once, and
+  // a second wave of them would only add scheduling time
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)r->sm_count));
+  const size_t smem = lane_split_smem(w.k, w.nb);
+  lane_split_kernel<Op, kSimd><<<grid, kLsThreads, smem, st>>>(w, r->st, op);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
+}
+
+template <class Op>
+int launch_lane_split(const sc_rnnt_decoder *r, const LaneMat &w, Op op, int64_t max_cols, bool simd,
+                      cudaStream_t st) {
+  return simd ? launch_lane_split_t<Op, true>(r, w, op, max_cols, st)
+              : launch_lane_split_t<Op, false>(r, w, op, max_cols, st);
+}
+
+// Shared-memory limit of every lane-split instantiation, set once before the
+// round graph is captured.
+int configure_lane_split(size_t smem) {
+  const int b = (int)smem;
+  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<LstmOp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<LstmOp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<PredOp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<PredOp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<OutOp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<OutOp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<EncOp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<EncOp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  return kOk;
+}
+
+// One round of the decode loop for list parity `parity` (its launches are
+// captured into the round graph).
+int launch_round(const sc_rnnt_decoder *r, int parity, cudaStream_t st) {
+  for (int l = 0; l < (int)r->lstm.size(); l++) {
+    int rc = launch_lane_split(r, r->lstm[(size_t)l], LstmOp{l, parity}, r->S, true, st);
+    if (rc) return rc;
+  }
+  int rc = launch_lane_split(r, r->jpred, PredOp{parity}, r->S, r->jpred.simd, st);
+  if (rc) return rc;
+  rc = launch_lane_split(r, r->jout, OutOp{parity}, r->S, r->jout.simd, st);
+  if (rc) return rc;
+  rnnt_update_kernel<<<(unsigned)r->S, kUpdThreads, 0, st>>>(r->st, parity);  // one CTA per stream
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+// Captures two rounds (parities 0 and 1) into a graph on a private stream.
+int build_round_graph(sc_rnnt_decoder *r) {
+  cudaStream_t cs;
+  SC_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+  cudaGraph_t g = nullptr;
+  int rc = kOk;
+  if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    cudaGetLastError();
+    cudaStreamDestroy(cs);
+    set_error("rnnt_create: stream capture failed");
+    return kErrCuda;
+  }
+  rc = launch_round(r, 0, cs);
+  if (!rc) rc = launch_round(r, 1, cs);
+  const cudaError_t e = cudaStreamEndCapture(cs, &g);
+  if (!rc && e != cudaSuccess) rc = cuda_fail(e, "cudaStreamEndCapture");
+  if (!rc && cudaGraphInstantiate(&r->rounds, g, 0) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("rnnt_create: graph instantiation failed");
+    rc = kErrCuda;
+  }
+  if (g) cudaGraphDestroy(g);
+  cudaStreamDestroy(cs);
+  r->round_launches = 2 * ((int)r->lstm.size() + 3);
+  return rc;
 }
 
 #define TRY(call)         \
@@ -584,15 +884,26 @@ int sc_rnnt_create(const sc_rnnt_config *cfg, const sc_tensor *tensors, int n_te
   if (ld.err.empty()) ld.linear("joint.pred", H, J, &r->jpred);
   if (ld.err.empty()) ld.linear("joint.joint_net.2", J, V, &r->jout);
   DecState &s = r->st;
+  float *emb_dev = nullptr;
   if (ld.err.empty()) {
-    s.embed = ld.upload(std::vector<float>(embed, embed + V * H));
+    emb_dev = ld.upload(std::vector<float>(embed, embed + V * H));
+    s.emb_q = (int8_t *)ld.dev((size_t)(V * H));
+    s.emb_dx = (float *)ld.dev((size_t)(V * H / 32 * 4));
+    s.zq = (int8_t *)ld.dev((size_t)H);
+    s.zdx = ld.upload(std::vector<float>((size_t)(H / 32), 1.0f));
     s.hc = (float *)ld.dev((size_t)(S * 4 * L * H * 4));
+    s.qh = (int8_t *)ld.dev((size_t)(S * 2 * L * H));
+    s.qh_dx = (float *)ld.dev((size_t)(S * 2 * L * H / 32 * 4));
     s.cur = (int32_t *)ld.dev((size_t)S * 4);
     s.last_tok = (int32_t *)ld.dev((size_t)S * 4);
     s.pred_valid = (int32_t *)ld.dev((size_t)S * 4);
     s.pred = (float *)ld.dev((size_t)(S * J * 4));
     s.enc = (float *)ld.dev((size_t)(S * c.max_frames * J * 4));
     s.logits = (float *)ld.dev((size_t)(S * V * 4));
+    s.qo = (int8_t *)ld.dev((size_t)(S * J));
+    s.qo_dx = (float *)ld.dev((size_t)(S * J / 32 * 4));
+    s.qf = (int8_t *)ld.dev((size_t)(S * c.max_frames * c.d_enc));
+    s.qf_dx = (float *)ld.dev((size_t)(S * c.max_frames * c.d_enc / 32 * 4));
     s.step = (int32_t *)ld.dev((size_t)S * 4);
     s.nsym = (int32_t *)ld.dev((size_t)S * 4);
     s.iter = (int32_t *)ld.dev((size_t)S * 4);
@@ -602,8 +913,10 @@ int sc_rnnt_create(const sc_rnnt_config *cfg, const sc_tensor *tensors, int n_te
     s.steps = (int32_t *)ld.dev((size_t)(S * r->cap * 4));
     s.lists = (int32_t *)ld.dev((size_t)(S * 4 * 4));
     s.counts = (int32_t *)ld.dev(16);
+    r->call = (CallParams *)ld.dev(sizeof(CallParams));
+    s.call = r->call;
   }
-  if (ld.err.empty() && (cudaHostAlloc(&r->pinned, 8, cudaHostAllocDefault) != cudaSuccess ||
+  if (ld.err.empty() && (cudaHostAlloc(&r->pinned, 16, cudaHostAllocDefault) != cudaSuccess ||
                          cudaEventCreateWithFlags(&r->ev[0], cudaEventDisableTiming) != cudaSuccess ||
                          cudaEventCreateWithFlags(&r->ev[1], cudaEventDisableTiming) != cudaSuccess)) {
     cudaGetLastError();
@@ -624,13 +937,28 @@ int sc_rnnt_create(const sc_rnnt_config *cfg, const sc_tensor *tensors, int n_te
   s.blank = c.blank;
   s.max_symbols = c.max_symbols;
   s.d_enc = c.d_enc;
-  *out = r;
-  rc = sc_rnnt_reset(r, -1);
-  if (rc) {
-    *out = nullptr;
-    delete r;
+  // the embedding rows' codes (the predictor's layer-0 input), once
+  SC_CUDA(cudaMemset((void *)s.zq, 0, (size_t)H));
+  rnnt_quant_embed_kernel<<<(unsigned)ceil_div(V * (H / 32) * 32, 256), 256>>>(emb_dev, V, (int)H,
+                                                                                 (int8_t *)s.emb_q,
+                                                                                 (float *)s.emb_dx);
+  note_launch();
+  const cudaError_t ce = cudaDeviceSynchronize();
+  rc = ce == cudaSuccess ? kOk : cuda_fail(ce, "rnnt_create: embedding codes");
+  if (rc == kOk) {
+    size_t smem = 0;
+    for (const LaneMat *m : {&r->jenc, &r->jpred, &r->jout}) smem = std::max(smem, lane_split_smem(m->k, m->nb));
+    for (const LaneMat &m : r->lstm) smem = std::max(smem, lane_split_smem(m.k, m.nb));
+    rc = configure_lane_split(smem);
   }
-  return rc;
+  if (rc == kOk) rc = build_round_graph(r);
+  if (rc == kOk) rc = sc_rnnt_reset(r, -1);
+  if (rc) {
+    delete r;
+    return rc;
+  }
+  *out = r;
+  return kOk;
 }
 
 int sc_rnnt_reset(sc_rnnt_decoder *r, int64_t stream_idx) {
@@ -640,9 +968,13 @@ int sc_rnnt_reset(sc_rnnt_decoder *r, int64_t stream_idx) {
   }
   const DecState &s = r->st;
   const int64_t lo = stream_idx < 0 ? 0 : stream_idx, cnt = stream_idx < 0 ? r->S : 1;
-  const size_t per = (size_t)4 * s.L * s.H * 4;
+  const int64_t lh = (int64_t)s.L * s.H;
   SC_CUDA(cudaDeviceSynchronize());
-  SC_CUDA(cudaMemset(s.hc + lo * 4 * s.L * s.H, 0, per * cnt));
+  SC_CUDA(cudaMemset(s.hc + lo * 4 * lh, 0, (size_t)(cnt * 4 * lh * 4)));
+  // h = 0 in both buffers: zero codes with quantize_col's scale 1 for a zero block
+  SC_CUDA(cudaMemset(s.qh + lo * 2 * lh, 0, (size_t)(cnt * 2 * lh)));
+  std::vector<float> ones((size_t)(cnt * 2 * lh / 32), 1.0f);
+  SC_CUDA(cudaMemcpy(s.qh_dx + lo * 2 * lh / 32, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice));
   SC_CUDA(cudaMemset(s.cur + lo, 0, cnt * 4));
   SC_CUDA(cudaMemset(s.pred_valid + lo, 0, cnt * 4));
   SC_CUDA(cudaMemset(s.emitted + lo, 0, cnt * 4));
@@ -665,38 +997,38 @@ int sc_rnnt_decode_frames(sc_rnnt_decoder *r, const float *frames, int64_t n, vo
     SC_CUDA(cudaStreamSynchronize(st));
     return kOk;
   }
-  s.n = (int)n;
   s.frames = frames;
-  s.max_iters = (int)(16 * n + 64);
-  rnnt_init_kernel<<<1, 1024, 0, st>>>(s);
+  const int max_iters = (int)(16 * n + 64);
+  r->pinned[2] = (int32_t)n;
+  r->pinned[3] = max_iters;
+  SC_CUDA(cudaMemcpyAsync(r->call, r->pinned + 2, sizeof(CallParams), cudaMemcpyHostToDevice, st));
+  // joint.enc over every stream's frames (the SIMD order for n <= 16), then
+  // the first round's lists and inputs
+  const int64_t cols = r->S * n;
+  rnnt_quant_frames_kernel<<<(unsigned)ceil_div(cols * (s.d_enc / 32) * 32, 256), 256, 0, st>>>(s, cols);
   note_launch();
   SC_CUDA(cudaGetLastError());
-  // joint.enc over every stream's frames: the SIMD order for n <= 16
-  TRY(launch_gemv(r, r->jenc, r->S * n, r->jenc.simd && n <= 16, 3, 0, st));
-  const int L = (int)r->lstm.size();
-  const unsigned upd_blocks = (unsigned)ceil_div(r->S, 8);  // 8 warps per CTA
-  int64_t rounds = 0;
-  bool done = false;
-  for (int64_t it = 0; it < s.max_iters && !done; it++) {
-    const int parity = (int)(it & 1);
-    for (int l = 0; l < L; l++)
-      TRY(launch_gemv(r, r->lstm[(size_t)l], r->S, true, 0, (l << 1) | parity, st));
-    TRY(launch_gemv(r, r->jpred, r->S, r->jpred.simd, 1, parity, st));
-    TRY(launch_gemv(r, r->jout, r->S, r->jout.simd, 2, parity, st));
-    rnnt_clear_kernel<<<1, 1, 0, st>>>(s, parity);
-    note_launch();
-    rnnt_update_kernel<<<upd_blocks, 256, 0, st>>>(s, parity);
-    note_launch();
-    SC_CUDA(cudaGetLastError());
-    rounds++;
-    // every stream needs n iterations; from then on read the active count
-    // of the round before (the GPU keeps working on this one meanwhile)
-    if (it >= n - 1) {
-      SC_CUDA(cudaMemcpyAsync(r->pinned + parity, s.counts + (parity ^ 1) * 2 + 1, 4, cudaMemcpyDeviceToHost, st));
-      SC_CUDA(cudaEventRecord(r->ev[parity], st));
-      if (it >= n) {
-        SC_CUDA(cudaEventSynchronize(r->ev[parity ^ 1]));
-        done = r->pinned[parity ^ 1] == 0;
+  TRY(launch_lane_split(r, r->jenc, EncOp{}, cols, r->jenc.simd && n <= 16, st));
+  SC_CUDA(cudaMemsetAsync(s.counts, 0, 16, st));
+  rnnt_init_kernel<<<(unsigned)ceil_div(r->S, 8), 256, 0, st>>>(s);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  // two rounds per replay; every stream needs n iterations, so from then on
+  // the host reads the active count left by the replay before (the GPU is
+  // busy with the current one meanwhile)
+  const int64_t pairs = (max_iters + 1) / 2;
+  r->last_rounds = 0;
+  for (int64_t pr = 0; pr < pairs; pr++) {
+    SC_CUDA(cudaGraphLaunch(r->rounds, st));
+    r->last_rounds += 2;
+    for (int i = 0; i < r->round_launches; i++) note_launch();
+    const int slot = (int)(pr & 1);
+    if (2 * (pr + 1) >= n) {
+      SC_CUDA(cudaMemcpyAsync(r->pinned + slot, s.counts + 1, 4, cudaMemcpyDeviceToHost, st));
+      SC_CUDA(cudaEventRecord(r->ev[slot], st));
+      if (2 * pr >= n) {
+        SC_CUDA(cudaEventSynchronize(r->ev[slot ^ 1]));
+        if (r->pinned[slot ^ 1] == 0) break;
       }
     }
   }
@@ -708,7 +1040,6 @@ int sc_rnnt_decode_frames(sc_rnnt_decoder *r, const float *frames, int64_t n, vo
       set_error("rnnt decode: iteration cap hit (stream %lld)", (long long)z);
       return kErrState;
     }
-  (void)rounds;
   return kOk;
 }
 
@@ -739,6 +1070,8 @@ int sc_rnnt_emitted(const sc_rnnt_decoder *r, int32_t *counts) {
   SC_CUDA(cudaMemcpy(counts, r->st.emitted, (size_t)r->S * 4, cudaMemcpyDeviceToHost));
   return kOk;
 }
+
+int64_t sc_rnnt_last_rounds(const sc_rnnt_decoder *r) { return r ? r->last_rounds : 0; }
 
 int sc_rnnt_tokens_device(const sc_rnnt_decoder *r, const int32_t **ids, const int32_t **steps,
                           const int32_t **counts, int32_t *cap) {

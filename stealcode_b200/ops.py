@@ -355,6 +355,10 @@ class RnntDecoder:
         check(lib.sc_rnnt_tokens(self._h, stream_idx, _hp(ids), _hp(steps), self.cap, ctypes.byref(cnt)))
         return ids[: cnt.value].copy(), steps[: cnt.value].copy()
 
+    def last_rounds(self) -> int:
+        """Loop rounds the last decode_frames ran (diagnostic)."""
+        return int(lib.sc_rnnt_last_rounds(self._h))
+
     def emitted(self) -> np.ndarray:
         """Tokens each stream emitted in the last decode_frames, [n_streams]."""
         out = np.empty(self.n_streams, dtype=np.int32)
