@@ -97,9 +97,11 @@ static int default_ws(size_t bytes, void **out) {
 
 static bool layout_ok(int32_t l) { return l == SC_LAYOUT_FEATURE_MAJOR || l == SC_LAYOUT_TIME_MAJOR; }
 
-// Frames up to which the weight-streaming kernel runs; above it the
-// tensor-core kernel takes over.
+// Frames up to which the weight-streaming kernel runs (the reference's SIMD
+// dispatch covers up to 16 frames); up to kMidMaxFrames the mid-size dp4a
+// kernel in q8_gemm_scalar's order; above it the tensor-core kernel.
 constexpr int64_t kSmallMaxFrames = 16;
+constexpr int64_t kMidMaxFrames = 128;
 
 // Quantise + GEMM on device pointers.
 int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
@@ -128,6 +130,20 @@ int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, i
   if (ws && (ws_bytes < need || ((uintptr_t)ws & 255))) {
     set_error("q8_gemm: workspace needs %zu bytes at 256-byte alignment", need);
     return kErrInvalid;
+  }
+  if (t > kSmallMaxFrames && t <= kMidMaxFrames && !force_tc && !dots) {
+    // Mid-size path: plain [m_pad][k_pad] codes, then the dp4a kernel.
+    if (!ws) {
+      rc = default_ws(need, &ws);
+      if (rc) return rc;
+    }
+    const int64_t m_pad = ceil_div(t, 128) * 128, k_pad = w->nb * 32;
+    int8_t *xq = (int8_t *)ws;
+    float *dx = (float *)((char *)ws + ((size_t)m_pad * k_pad + 255) / 256 * 256);
+    rc = quantize_act(x, t, w->k, ldx, x_layout == SC_LAYOUT_FEATURE_MAJOR, m_pad, xq, dx, st, 0);
+    if (rc) return rc;
+    MidGemmArgs ma{w, xq, dx, t, m_pad, k_pad, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy, epi};
+    return gemm_mid(ma, st);
   }
   if ((t > kSmallMaxFrames || force_tc) && !dots) {
     // Tensor-core path: quantise into the tiled operand layout, then tcgen05.

@@ -56,6 +56,20 @@ struct SmallGemmArgs {
 int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st);
 int small_gemm_status(unsigned *out);  // read and clear the kernels' status word
 
+// q8_gemm_mid.cu: 16 < m <= 128 frames, q8_gemm_scalar's order (bit-exact)
+struct MidGemmArgs {
+  const Q8Weights *w;
+  const int8_t *xq;   // [m_pad][k_pad] codes (quantize_act, tile_ft 0)
+  const float *dx;    // [nb][m_pad]
+  int64_t m, m_pad, k_pad;
+  const float *bias;  // [rows] or nullptr
+  float *y;
+  int y_time_major;   // 1: y[col*ldy + n]; 0: y[n*ldy + col]
+  int64_t ldy;
+  Epilogue epi;
+};
+int gemm_mid(const MidGemmArgs &a, cudaStream_t st);
+
 // q8_gemm_tc.cu
 // Activation codes quantised by the kernel that produces them, written in
 // the tensor-core GEMM's tiled operand layout (ft = tc_frame_tile(t)): the

@@ -226,9 +226,32 @@ def test_no_device_wait_timed_out(torch):
     assert _lib.device_status() == 0
 
 
+# ---- mid-size path (17..128 frames): q8_gemm_scalar's order, bit-exact ----
+@pytest.mark.parametrize("t,k,n", [(17, 1024, 256), (40, 1000, 37), (100, 4096, 128), (128, 1024, 384),
+                                   (33, 4352, 1024)])
+@pytest.mark.parametrize("layout", [SC_LAYOUT_TIME_MAJOR, SC_LAYOUT_FEATURE_MAJOR])
+def test_mid_path_bit_exact_scalar_order(torch, t, k, n, layout):
+    """More than 16 frames is where the reference runs q8_gemm_scalar
+    (simd_kernel.rs:111-125); the mid-size kernel reproduces it bit for bit,
+    bias added after."""
+    w = synth.q8_weights(4000 + t + k, n, k)
+    x_tk = edge_activations(k, t, 5000 + t)
+    x_tk = np.nan_to_num(x_tk, nan=0.0, posinf=0.0, neginf=0.0)
+    bias = synth.normal(6000 + n, (n,), std=0.02)
+    ref = oracle.q8_gemm_scalar(n, k, t, w, ((k + 31) // 32) * 34, 34, 2, np.ascontiguousarray(x_tk.T))
+    ref = (ref + bias[:, None]).astype(np.float32)
+    mat = Q8Mat(w, n, k)
+    xd = torch.from_numpy(x_tk if layout == SC_LAYOUT_TIME_MAJOR else np.ascontiguousarray(x_tk.T)).cuda()
+    y = mat.gemm(xd, x_layout=layout, bias=torch.from_numpy(bias).cuda(), y_layout=layout)
+    torch.cuda.synchronize()
+    y = y.cpu().numpy()
+    got = y.T if layout == SC_LAYOUT_TIME_MAJOR else y
+    assert np.array_equal(got, ref)
+
+
 # ---- tensor-core path (tcgen05 kind::i8), t > 16 frames -------------------
 @pytest.mark.parametrize("t,k,n", [(17, 1024, 256), (33, 1000, 37), (64, 1024, 384), (100, 4096, 128),
-                                   (129, 1024, 256), (300, 4352, 128)])
+                                   (129, 1024, 256), (300, 4352, 128), (1000, 1024, 640)])
 @pytest.mark.parametrize("layout", [SC_LAYOUT_TIME_MAJOR, SC_LAYOUT_FEATURE_MAJOR])
 def test_tensor_core_path_matches_oracle(torch, t, k, n, layout):
     w = synth.q8_weights(1000 + t + k, n, k)
