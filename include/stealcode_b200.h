@@ -229,7 +229,9 @@ typedef struct {
 } sc_tensor;
 
 /* EncoderConfig (nemotron/config.rs:19-39) plus max_frames, the largest
- * number of encoder frames one encode_new call may add (1..16).
+ * number of encoder frames one encode_new call may add (1..64): 7 for
+ * streaming chunks, more to encode a longer stretch of audio per call (a
+ * prefill); the output is the same either way.
  * att_right is the chunk's right context: chunk = att_right + 1 (the
  * reference fixes it to 6, nemotron/config.rs:164). */
 typedef struct {

@@ -295,6 +295,7 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int hoff = h * HD;
   const int c = p.c;
+  const int64_t zq = p.zrows > 0 ? p.zrows : c, zn = p.zrows > 0 ? p.zrows : p.rows_new;
   const int kk_new = (int)(p.new_lo - p.k_lo);
   const int slot0 = p.cap > 0 ? (int)(p.k_lo % p.cap) : 0;
   const int cap = (int)p.cap;
@@ -304,7 +305,7 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
     return ring + (z * cap + slot) * (int64_t)p.d + hoff;
   };
   auto key_row = [&](float *ring, const float *nw, int kk) -> const float * {
-    if (kk >= kk_new) return nw + (z * p.rows_new + (kk - kk_new)) * p.ld_new + hoff;
+    if (kk >= kk_new) return nw + (z * zn + p.r0 + (kk - kk_new)) * p.ld_new + hoff;
     return ring_row(ring, kk);
   };
   const int kk_s = (int)(p.s - p.k_lo);
@@ -335,7 +336,7 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
   {
     const int dt = LM ? t : lane_major(t);
     for (int j = 0; j < CQ; j++) {
-      const float qd = j < c ? p.q[(z * c + j) * p.ldq + hoff + t] : 0.0f;
+      const float qd = j < c ? p.q[(z * zq + p.r0 + j) * p.ldq + hoff + t] : 0.0f;
       s_qu[j * HD + dt] = j < c ? __fadd_rn(qd, p.u[hoff + t]) : 0.0f;
       s_qv[j * HD + dt] = j < c ? __fadd_rn(qd, p.v[hoff + t]) : 0.0f;
     }
@@ -469,12 +470,12 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
 #pragma unroll
     for (int j = 0; j < CQ; j++)
       if (j < c) {
-        if (p.out) p.out[(z * c + j) * p.ldo + hoff + t] = acc[j];
+        if (p.out) p.out[(z * zq + p.r0 + j) * p.ldo + hoff + t] = acc[j];
         if (p.qout.xq) {  // the warp's 32 dims are one block of the out-proj input
           float sblk;
           const int8_t q = warp_quantize_block(acc[j], true, sblk);
-          p.qout.xq[qout_code_index(p.qout, z * c + j, hoff + t)] = q;
-          if (lane == 0) p.qout.dx[qout_dx_index(p.qout, z * c + j, (hoff + t) >> 5)] = sblk;
+          p.qout.xq[qout_code_index(p.qout, z * zq + p.r0 + j, hoff + t)] = q;
+          if (lane == 0) p.qout.dx[qout_dx_index(p.qout, z * zq + p.r0 + j, (hoff + t) >> 5)] = sblk;
         }
       }
   }
@@ -568,8 +569,8 @@ static int launch_stage_t(const AttnParams &p, int64_t n_streams, cudaStream_t s
 template <int HD, int CQ>
 static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
   if (stage_fits<HD, CQ>(p)) return launch_stage_t<HD, CQ>(p, n_streams, st);
-  if (p.lane_major || p.qout.xq) {
-    set_error("attn_stream: lane-major rows / quantised output need the staged kernel (band %lld too large or "
+  if (p.lane_major || p.qout.xq || p.zrows) {
+    set_error("attn_stream: lane-major rows / quantised output / row sub-ranges need the staged kernel (band %lld too large or "
               "rows unaligned)",
               (long long)(p.k_hi - p.k_lo));
     return kErrUnsupported;

@@ -280,12 +280,12 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
   *out = nullptr;
   const sc_encoder_config &c = *cfg;
   if (c.d_model % 256 || c.d_model > 4096 || c.n_heads <= 0 || c.d_model % c.n_heads || c.att_right < 0 ||
-      c.conv_kernel < 1 || c.conv_left != c.conv_kernel - 1 || c.max_frames < 1 || c.max_frames > 16 ||
+      c.conv_kernel < 1 || c.conv_left != c.conv_kernel - 1 || c.max_frames < 1 || c.max_frames > 64 ||
       c.feat_in <= 0 || c.conv_channels <= 0 || c.n_layers < 0 ||
       (c.d_model / c.n_heads != 64 && c.d_model / c.n_heads != 128) || (c.d_model & (c.d_model - 1)) ||
       c.d_ff % 128) {
     set_error("stream_encoder_create: unsupported config (d_model %d (a power of two, 256..4096), heads %d "
-              "(head_dim 64 or 128), d_ff a multiple of 128, conv %d/%d, max_frames %d)",
+              "(head_dim 64 or 128), d_ff a multiple of 128, conv %d/%d, max_frames %d (1..64))",
               c.d_model, c.n_heads, c.conv_kernel, c.conv_left, c.max_frames);
     return kErrUnsupported;
   }
@@ -305,7 +305,7 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
   e->n_pos = (e->left_chunks + 2) * e->chunk - 1;
   e->kv_cap = e->left_chunks * e->chunk + (e->chunk - 1) + c.max_frames;
   e->glu_cap = c.conv_left + c.max_frames;
-  e->out_cap = 64;
+  e->out_cap = std::max<int64_t>(64, c.max_frames);
   e->t_mel_max = kMelHistory + 8 * (int64_t)c.max_frames + 8;
   const int64_t d = c.d_model, dff = c.d_ff, C = c.conv_channels, hd = d / c.n_heads;
   Loader L{tensors, n_tensors, e, {}};
@@ -541,8 +541,7 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
   TRY(launch_mel_hist(e->hist[e->hist_cur], kMelHistory, e->hist_frames, mel_new, (int)n_new, c.feat_in,
                       e->hist[e->hist_cur ^ 1], Z, st));
   // ---- band and pos rows (streaming.rs:226-261) ----
-  const int64_t k_lo = (s / e->chunk > e->left_chunks ? s / e->chunk - e->left_chunks : 0) * e->chunk;
-  const int64_t k_hi = t_new, pos_off = e->chunk - 1;
+  const int64_t pos_off = e->chunk - 1;
   if (!e->pos_ready) {
     // sinusoid rows computed on the host in f32 exactly as the reference does
     std::vector<float> pet((size_t)(e->n_pos * d));
@@ -585,15 +584,20 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
     TRY(launch_ln_quant(e->y, d, ly.ln_att_w, ly.ln_att_b, eps, (int)d, M, qa, dumping ? e->xn : nullptr, d, st));
     TRY(dump(1, e->xn, d));
     TRY(gemm_q(ly.qkv, qa, e->qkv, 3 * d, Epilogue{}, QOut{}));
-    {
+    // the call's frames [s, t_new) in sub-ranges that stay inside one
+    // attention chunk, in order: each launch writes its frames' K/V rows to
+    // the rings before the next one reads them, and every band stays within
+    // left context + one chunk however many frames the call brings
+    for (int64_t a = s; a < t_new;) {
+      const int64_t b = std::min<int64_t>(t_new, (a / e->chunk + 1) * e->chunk);
       AttnParams p{};
       p.q = e->qkv;
       p.ldq = 3 * d;
       p.k_new = e->qkv + d;
       p.v_new = e->qkv + 2 * d;
       p.ld_new = 3 * d;
-      p.rows_new = cf;
-      p.new_lo = s;
+      p.rows_new = b - a;
+      p.new_lo = a;
       p.k_ring = ly.k_ring;
       p.v_ring = ly.v_ring;
       p.cap = e->kv_cap;
@@ -603,19 +607,22 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
       p.out = dumping ? e->attn : nullptr;
       p.ldo = d;
       p.qout = qb_d;
-      p.c = (int)cf;
+      p.c = (int)(b - a);
       p.d = (int)d;
       p.n_heads = c.n_heads;
       p.scale = 1.0f / sqrtf((float)(d / c.n_heads));
-      p.s = s;
-      p.k_lo = k_lo;
-      p.k_hi = k_hi;
+      p.s = a;
+      p.k_lo = (a / e->chunk > e->left_chunks ? a / e->chunk - e->left_chunks : 0) * e->chunk;
+      p.k_hi = b;
       p.chunk = e->chunk;
       p.left_chunks = e->left_chunks;
       p.pos_off = pos_off;
       p.lane_major = 1;  // q, k, pos rows and biases in lane-major head order
+      p.zrows = cf;      // rows of stream z: z * cf + (frame - s)
+      p.r0 = a - s;
       TRY(attn_prepare(p, e->n_pos));
       TRY(launch_attn(p, Z, st));
+      a = b;
     }
     TRY(dump(2, e->attn, d));
     TRY(gemm_q(ly.out, qb_d, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}, QOut{}));

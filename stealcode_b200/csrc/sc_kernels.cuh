@@ -143,6 +143,10 @@ struct AttnParams {
   int lane_major;       // q, k (new and ring), u, v and pos rows are stored
                         // lane-major within each head (element 16*ch + l
                         // at (ch/4)*64 + 4l + ch%4); v_new / v_ring natural
+  // Sub-range of a longer call (staged kernel only): when zrows > 0 the
+  // q / out / qout rows of stream z, query j are z*zrows + r0 + j and its new
+  // K/V rows z*zrows + r0 + (fr - new_lo); 0 keeps the layouts above.
+  int64_t zrows = 0, r0 = 0;
 };
 int attn_prepare(AttnParams &p, int64_t n_pos);
 int launch_attn(const AttnParams &p, int64_t n_streams, cudaStream_t st);

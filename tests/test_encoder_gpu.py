@@ -132,6 +132,39 @@ def test_encoder_prompt_mlp_matches_oracle(torch):
     assert max(s[2] for s in stats) <= TOL
 
 
+def test_encoder_long_calls_match_streaming_steps(torch):
+    """One encode_new call may bring up to 64 frames (a prefill of a longer
+    stretch of audio): 56-frame calls, the attention run chunk by chunk
+    inside the call, give the same bits as 7-frame streaming steps over the
+    same audio, and match the oracle given the same calls."""
+    from stealcode_b200.ops import StreamEncoder
+
+    long_cfg = model.EncoderConfig(n_layers=2, max_frames=64)
+    m = model.random_model(long_cfg, seed=19)
+    short = StreamEncoder(model.Model(model.EncoderConfig(n_layers=2, max_frames=8), m.tensors), 2)
+    long_ = StreamEncoder(m, 2)
+    ref = oracle.StreamingEncoder(m)
+    ref.set_device_rounding()
+    mel = model.mel_stream(20, 2, 448 * 2 + 24, long_cfg.feat_in)
+    worst = 0.0
+    for t0, t1, fin in ((0, 448, False), (448, 896, False), (896, 920, True)):
+        s = long_.total()
+        long_.encode_new(torch.from_numpy(np.ascontiguousarray(mel[:, t0:t1])).cuda(), t0, t1, fin)
+        for a in range(t0, t1, 56):
+            b = min(a + 56, t1)
+            short.encode_new(torch.from_numpy(np.ascontiguousarray(mel[:, a:b])).cuda(), a, b, fin and b == t1)
+        torch.cuda.synchronize()
+        assert long_.total() == short.total()
+        for z in range(2):
+            assert np.array_equal(long_.frames(z, s, long_.total()), short.frames(z, s, short.total()))
+        assert ref.encode_new(mel[0, :t1], t0, t1, fin) == 0
+        worst = max(worst, _err(long_.frames(0, s, long_.total()), ref.frames(s, ref.total()))[0])
+    print("long calls vs oracle: worst max/RMS %.3g" % worst)
+    assert worst <= TOL
+    long_.close()
+    short.close()
+
+
 def test_encoder_out_of_sync_is_rejected(torch):
     from stealcode_b200.ops import StreamEncoder
 
