@@ -251,8 +251,9 @@ static int launch_stream(StreamParams &p, int64_t groups, int64_t mtiles, cudaSt
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = SC_STREAM_PDL ? 2 : 1;
+  // no cluster without a K split: the kernel then syncs only its own CTA
+  cfg.attrs = p.ks > 1 ? attr : attr + 1;
+  cfg.numAttrs = (p.ks > 1 ? 1 : 0) + (SC_STREAM_PDL ? 1 : 0);
   note_launch();
   SC_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
   return kOk;
@@ -285,9 +286,12 @@ int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st) {
   const int64_t groups = w->rows_pad / SC_GROUP_ROWS;
   // K split (a cluster dimension, at most 8): smallest power of two that
   // fills the GPU, keeps at least two blocks per CTA and fits shared memory.
+  // One or two frames with a K that fits one CTA: no split (measured: the
+  // cluster reduction costs more than the extra parallelism buys there).
   int ks = 1;
+  const bool no_split = a.m <= 2 && w->nb <= kNblCap;
   while (ks < SC_STREAM_KS_MAX && (ceil_div(w->nb, ks) > kNblCap ||
-                    (groups * mtiles * ks < sm_count && w->nb / (ks * 2) >= 2)))
+                    (!no_split && groups * mtiles * ks < sm_count && w->nb / (ks * 2) >= 2)))
     ks *= 2;
   if (ceil_div(w->nb, ks) > kNblCap || ks > 8) {
     set_error("q8_gemm: K=%lld too large for the streaming kernel", (long long)w->k);
