@@ -407,6 +407,84 @@ __global__ void conv2d_3x3s2_kernel(const float *__restrict__ x, int t_in, int x
   }
 }
 
+// conv0 (1 -> C channels, 3x3 stride 2, ReLU) feeding the depthwise conv2
+// (3x3 stride 2), fused: each conv2 output rebuilds the conv0 values it reads
+// from the 7 mel rows it depends on (staged in shared memory), with the same
+// taps in the same order as conv2d_3x3s2_kernel, so the result is the same
+// as running the two convs apart -- and conv0's output, the largest tensor
+// of the pre-encode stack, never goes to memory.  One CTA per conv2 output
+// row and stream, one thread per channel.
+__global__ void conv02_fused_kernel(const float *__restrict__ win, int t_mel, int f_mel,
+                                    const float *__restrict__ w0, const float *__restrict__ b0,
+                                    const float *__restrict__ w2, const float *__restrict__ b2, int C, int ta,
+                                    int fa, int out_row0, int out_rows, int fb, float *__restrict__ out) {
+  extern __shared__ float mel[];  // [7][f_mel]
+  const int r = blockIdx.x, z = blockIdx.y;
+  const int ot = out_row0 + r;    // conv2 output row
+  const int m0 = 4 * ot - 6;      // first mel row any of its conv0 inputs reads
+  for (int i = threadIdx.x; i < 7 * f_mel; i += blockDim.x) {
+    const int mt = m0 + i / f_mel;
+    mel[i] = (mt >= 0 && mt < t_mel) ? win[((size_t)z * t_mel + mt) * f_mel + i % f_mel] : 0.0f;
+  }
+  __syncthreads();
+  // conv0 at (row 2*ot + kt - 2, frequency f0) for this thread's channel,
+  // ReLU applied: mel rows 2 kt + kt0 of the tile
+  auto conv0 = [&](const float (&w0r)[9], float bias0, int kt, int f0) -> float {
+    float a0 = bias0;
+#pragma unroll
+    for (int kt0 = 0; kt0 < 3; kt0++) {
+      const int mt = m0 + 2 * kt + kt0;
+      if (mt < 0 || mt >= t_mel) continue;
+      const float *mr = mel + (2 * kt + kt0) * f_mel;
+#pragma unroll
+      for (int kf0 = 0; kf0 < 3; kf0++) {
+        const int mf = 2 * f0 + kf0 - 2;
+        if (mf < 0 || mf >= f_mel) continue;
+        a0 = __fadd_rn(a0, __fmul_rn(mr[mf], w0r[kt0 * 3 + kf0]));
+      }
+    }
+    return fmaxf(a0, 0.0f);
+  };
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float w0r[9], w2r[9];
+#pragma unroll
+    for (int tap = 0; tap < 9; tap++) {
+      w0r[tap] = w0[c * 9 + tap];
+      w2r[tap] = w2[c * 9 + tap];
+    }
+    const float bias0 = b0[c], bias2 = b2[c];
+    bool rv[3];
+#pragma unroll
+    for (int kt = 0; kt < 3; kt++) {
+      const int t0 = 2 * ot + kt - 2;
+      rv[kt] = t0 >= 0 && t0 < ta;
+    }
+    float *o = out + ((size_t)z * out_rows + r) * fb * C + c;
+    // conv0 columns 2 f2 - 2, 2 f2 - 1, 2 f2 of the 3 rows; the first is the
+    // previous output's last, so each column is computed once
+    float vl[3] = {0.0f, 0.0f, 0.0f};
+    for (int f2 = 0; f2 < fb; f2++) {
+      float vm[3], vr[3];
+#pragma unroll
+      for (int kt = 0; kt < 3; kt++) {
+        vm[kt] = rv[kt] && 2 * f2 - 1 >= 0 && 2 * f2 - 1 < fa ? conv0(w0r, bias0, kt, 2 * f2 - 1) : 0.0f;
+        vr[kt] = rv[kt] && 2 * f2 < fa ? conv0(w0r, bias0, kt, 2 * f2) : 0.0f;
+      }
+      float acc = bias2;
+#pragma unroll
+      for (int kt = 0; kt < 3; kt++) {
+        if (!rv[kt]) continue;
+        if (2 * f2 - 2 >= 0 && 2 * f2 - 2 < fa) acc = __fadd_rn(acc, __fmul_rn(vl[kt], w2r[kt * 3 + 0]));
+        if (2 * f2 - 1 >= 0 && 2 * f2 - 1 < fa) acc = __fadd_rn(acc, __fmul_rn(vm[kt], w2r[kt * 3 + 1]));
+        if (2 * f2 < fa) acc = __fadd_rn(acc, __fmul_rn(vr[kt], w2r[kt * 3 + 2]));
+      }
+      o[(size_t)f2 * C] = acc;
+#pragma unroll
+      for (int kt = 0; kt < 3; kt++) vl[kt] = vr[kt];
+    }
+  }
+}
+
 // Pointwise conv: Y[m][n] = max(sum_k W[n][k] X[m][k] + b[n], 0) over all
 // spatial positions m of all streams (X, Y channels-last).  Each output's
 // k-sum is one fused multiply-add chain from k = 0 upwards, then the bias
@@ -578,6 +656,21 @@ int launch_mel_hist(const float *old_hist, int hist_cap, int hist_frames, const 
                     int n_mels, float *new_hist, int64_t n_streams, cudaStream_t st) {
   dim3 grid((unsigned)ceil_div((int64_t)hist_cap * n_mels, 256), (unsigned)n_streams);
   mel_hist_kernel<<<grid, 256, 0, st>>>(old_hist, hist_cap, hist_frames, mel_new, n_new, n_mels, new_hist);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+int launch_conv02_fused(const float *win, int64_t n_streams, int t_mel, int f_mel, const float *w0, const float *b0,
+                        const float *w2, const float *b2, int C, int ta, int fa, int out_row0, int out_rows, int fb,
+                        float *out, cudaStream_t st) {
+  if (C > 1024 || f_mel > 1024) {
+    set_error("pre_encode conv: %d channels / %d mel bins unsupported (at most 1024)", C, f_mel);
+    return kErrUnsupported;
+  }
+  if (out_rows <= 0 || n_streams <= 0) return kOk;
+  conv02_fused_kernel<<<dim3((unsigned)out_rows, (unsigned)n_streams), (unsigned)C, 7 * f_mel * sizeof(float), st>>>(
+      win, t_mel, f_mel, w0, b0, w2, b2, C, ta, fa, out_row0, out_rows, fb, out);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;

@@ -44,6 +44,9 @@ int launch_mel_hist(const float *old_hist, int hist_cap, int hist_frames, const 
 int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int x_row0, int x_rows, int f_in, int c_in,
                         const float *w, const float *b, int c_out, int out_row0, int out_rows, int f_out, int relu,
                         float *out, cudaStream_t st);
+int launch_conv02_fused(const float *win, int64_t n_streams, int t_mel, int f_mel, const float *w0, const float *b0,
+                        const float *w2, const float *b2, int C, int ta, int fa, int out_row0, int out_rows, int fb,
+                        float *out, cudaStream_t st);
 int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t m_rows, int n, int k,
                         cudaStream_t st);
 int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int start_rel, int c, float *out,
@@ -518,10 +521,12 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
   int64_t r3, e3, r0, e0;
   need(r5, r5 + n5, tb, r3, e3);          // conv2 / conv3 rows
   need(r3, e3, ta, r0, e0);               // conv0 rows
-  TRY(launch_conv2d_3x3s2(e->win, Z, (int)t_mel, 0, (int)t_mel, c.feat_in, 1, e->c0.w, e->c0.b, (int)C, (int)r0,
-                          (int)(e0 - r0), (int)fa, 1, e->p0, st));
-  TRY(launch_conv2d_3x3s2(e->p0, Z, (int)ta, (int)r0, (int)(e0 - r0), (int)fa, (int)C, e->c2.w, e->c2.b, (int)C,
-                          (int)r3, (int)(e3 - r3), (int)fb, 0, e->p1, st));
+  // conv0 + ReLU and the depthwise conv2 in one kernel (conv0 rows [r0, e0)
+  // are rebuilt where conv2 reads them)
+  (void)r0;
+  (void)e0;
+  TRY(launch_conv02_fused(e->win, Z, (int)t_mel, c.feat_in, e->c0.w, e->c0.b, e->c2.w, e->c2.b, (int)C, (int)ta,
+                          (int)fa, (int)r3, (int)(e3 - r3), (int)fb, e->p1, st));
   TRY(launch_pw_conv_relu(e->p1, e->c3.w, e->c3.b, e->p2, Z * (e3 - r3) * fb, (int)C, (int)C, st));
   TRY(launch_conv2d_3x3s2(e->p2, Z, (int)tb, (int)r3, (int)(e3 - r3), (int)fb, (int)C, e->c5.w, e->c5.b, (int)C,
                           (int)r5, (int)n5, (int)fc, 0, e->p1, st));
