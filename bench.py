@@ -47,6 +47,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -265,11 +266,22 @@ def time_steps(fn, steps, warmup, world, dev, stream):
     return ms / steps
 
 
+def step_halves(streams, frames=7):
+    """Frames per GEMM of the encoder step's sub-batches: the encoder runs
+    two halves of the streams in flight, split where the 128-frame tiles of
+    its GEMM inputs split (sc_stream_encoder_set_concurrency)."""
+    unit = 128 // math.gcd(frames, 128)
+    z0 = (streams // 2) // unit * unit
+    return [z0 * frames, (streams - z0) * frames] if 0 < z0 < streams else [streams * frames]
+
+
 def tc_roofline(m, streams, dev, stream):
-    """The tcgen05 int8 GEMM at the encoder step's shapes (t = streams * 7
-    frames) over the 24 layers' own Q8_0 weights, in the step's order.  The
-    GEMM kernel's time is (quantise + GEMM) minus quantise, each timed with
-    CUDA events over the same sequence."""
+    """The tcgen05 int8 GEMM at the encoder step's shapes over the 24
+    layers' own Q8_0 weights, in the step's order, with the step's two
+    sub-batches (halves of the streams, 896 frames each at 256 streams) in
+    flight on two CUDA streams as the encoder runs them.  The GEMM kernel's
+    time is (quantise + GEMM) minus quantise, each timed with CUDA events
+    over the same sequence."""
     import torch
 
     from stealcode_b200 import _lib
@@ -282,7 +294,9 @@ def tc_roofline(m, streams, dev, stream):
     names = ["feed_forward1.linear1", "feed_forward1.linear2", ("self_attn.linear_q", "self_attn.linear_k",
              "self_attn.linear_v"), "self_attn.linear_out", "conv.pointwise_conv1", "conv.pointwise_conv2",
              "feed_forward2.linear1", "feed_forward2.linear2"]
-    t = streams * 7
+    halves = step_halves(streams)
+    side = torch.cuda.Stream(device=dev)
+    sts = [stream, side][:len(halves)]
     mats = []
     for li in range(m.config.n_layers):
         for nm in names:
@@ -291,50 +305,63 @@ def tc_roofline(m, streams, dev, stream):
             rows, k = blocks.shape[0], int(parts[0].dims[0])
             mats.append((Q8Mat(blocks, rows, k), rows, k))
     ks = sorted({k for _, _, k in mats})
-    xs = {k: torch.randn(t, k, device=dev) for k in ks}
-    ys = {r: torch.empty(t, r, device=dev) for r in sorted({r for _, r, _ in mats})}
-    ws_bytes = max(mt.workspace_bytes(t) for mt, _, _ in mats)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    qbuf = {k: (torch.empty(t, k, dtype=torch.int8, device=dev), torch.empty(k // 32, t, device=dev)) for k in ks}
-    sp = stream.cuda_stream
+    # per half its own inputs, outputs, workspace and codes (the halves run at once)
+    bufs = []
+    for t in halves:
+        ws_bytes = max(mt.workspace_bytes(t) for mt, _, _ in mats)
+        bufs.append({"x": {k: torch.randn(t, k, device=dev) for k in ks},
+                     "y": {r: torch.empty(t, r, device=dev) for r in sorted({r for _, r, _ in mats})},
+                     "ws": torch.empty(ws_bytes, dtype=torch.uint8, device=dev), "ws_bytes": ws_bytes,
+                     "q": {k: (torch.empty(t, k, dtype=torch.int8, device=dev), torch.empty(k // 32, t, device=dev))
+                           for k in ks}})
 
     def gemms():
         for mt, rows, k in mats:
-            check(lib.sc_q8_gemm(mt.handle, xs[k].data_ptr(), t, SC_LAYOUT_TIME_MAJOR, 0, None, ys[rows].data_ptr(),
-                                 SC_LAYOUT_TIME_MAJOR, 0, ws.data_ptr(), ws_bytes, sp))
+            for t, b, st in zip(halves, bufs, sts):
+                check(lib.sc_q8_gemm(mt.handle, b["x"][k].data_ptr(), t, SC_LAYOUT_TIME_MAJOR, 0, None,
+                                     b["y"][rows].data_ptr(), SC_LAYOUT_TIME_MAJOR, 0, b["ws"].data_ptr(),
+                                     b["ws_bytes"], st.cuda_stream))
 
     def quants():
         for mt, rows, k in mats:
-            q, d = qbuf[k]
-            check(lib.sc_q8_quantize(xs[k].data_ptr(), t, k, SC_LAYOUT_TIME_MAJOR, 0, q.data_ptr(), d.data_ptr(), sp))
+            for t, b, st in zip(halves, bufs, sts):
+                q, d = b["q"][k]
+                check(lib.sc_q8_quantize(b["x"][k].data_ptr(), t, k, SC_LAYOUT_TIME_MAJOR, 0, q.data_ptr(),
+                                         d.data_ptr(), st.cuda_stream))
 
     def timed(fn, reps=3):
         fn()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        for st in sts[1:]:
+            st.wait_event(e0)
         for _ in range(reps):
             fn()
+        for st in sts[1:]:
+            ev = torch.cuda.Event()
+            ev.record(st)
+            stream.wait_event(ev)
         e1.record(stream)
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps
 
-    with torch.cuda.stream(stream):
-        ms_all = timed(gemms)
-        ms_q = timed(quants)
+    ms_all = timed(gemms)
+    ms_q = timed(quants)
     ms_tc = ms_all - ms_q
-    ops = sum(2.0 * t * rows * k for _, rows, k in mats)
+    ops = sum(2.0 * t * rows * k for t in halves for _, rows, k in mats)
     p = peaks()
     bf16 = p.get("bf16_tflops")
     peak = 2.0 * bf16 if bf16 else 2.0 * 1590.0
     achieved = ops / (ms_tc * 1e-3) / 1e12
-    n = len(mats)
-    del mats
+    n = len(mats) * len(halves)
+    del mats, bufs
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
             "peak_source": ("2 x measured dense bf16 TFLOP/s (B200's dense int8 rate is twice its bf16 rate)"
                             if bf16 else "2 x fallback bf16"),
             "kernel": "q8_gemm_tc_kernel (tcgen05 kind::i8)", "traffic": None,
-            "frames": t, "launches": n, "us_per_launch": 1e3 * ms_tc / n, "ops_per_launch": ops / n,
+            "frames": halves, "launches": n, "us_per_launch": 1e3 * ms_tc / n, "ops_per_launch": ops / n,
+            "note": "the step's sub-batches in flight on two streams: us_per_launch is step GEMM time / launches",
             "linear_incl_quantize": {"tops": ops / (ms_all * 1e-3) / 1e12, "us_per_launch": 1e3 * ms_all / n}}
 
 
@@ -539,7 +566,8 @@ def run_ours(args, rank, world, local_rank):
                                                             "8 heads, FFN 4096, conv 9, Q8_0 linears",
                            "streams_per_gpu": Z, "global_streams": Z * world, "chunk_ms": 560,
                            "frames_per_step": 7, "left_context_frames": 70, "prime_steps": PRIME_STEPS,
-                           "frames_per_gemm": Z * 7, "parallelism": f"streams sharded, {world} independent ranks",
+                           "frames_per_gemm": step_halves(Z), "sub_batches": len(step_halves(Z)),
+                           "parallelism": f"streams sharded, {world} independent ranks",
                            "l2": "inputs larger than L2: each step streams 587 MB of Q8_0 weights (L2 126 MB)"},
                 "realtime_streams_per_gpu": value / world,
                 "roofline": roof, "gemm_sweep": sweep, "cpu_baseline": cpu, "e2e": e2e, "transcriber": trans, "prefill": prefill,
@@ -596,7 +624,7 @@ def prefill_leg(m, world, dev, stream):
     audio = Z * PREFILL_MEL * 0.01
     return {"value": world * audio / (ms * 1e-3), "unit": UNIT, "ms": ms, "streams_per_gpu": Z,
             "frames_per_stream": frames, "calls": len(calls), "frames_per_call": PREFILL_CALL_MEL // 8,
-            "frames_per_gemm": Z * PREFILL_CALL_MEL // 8,
+            "frames_per_gemm": step_halves(Z, PREFILL_CALL_MEL // 8),
             "note": "same encoder and bits as streaming; long calls, attention run chunk by chunk inside a call"}
 
 
@@ -684,6 +712,7 @@ def run_profile(args):
 
         m = encoder_model()
         enc = StreamEncoder(m, args.streams)
+        enc.set_concurrency(1)  # kernels one after another: durations add up to the step
         mel = torch.randn((args.streams, MEL_PER_STEP, m.config.feat_in), device=dev)
         for i in range(PRIME_STEPS + 2):
             enc.encode_new(mel, MEL_PER_STEP * i, MEL_PER_STEP * (i + 1))

@@ -293,6 +293,16 @@ int64_t sc_stream_encoder_n_prompts(const sc_stream_encoder *e);
 int sc_stream_encoder_set_dump(sc_stream_encoder *e, int32_t layer);
 int sc_stream_encoder_dump(const sc_stream_encoder *e, int32_t stage,
                            float *out_host, int64_t *rows);
+/* How many sub-batches of streams one encode_new keeps in flight: 2 (the
+ * default) splits the streams into two halves at a 128-frame boundary of
+ * the GEMM inputs and runs the second half on a stream the encoder owns,
+ * forked from and joined back to the caller's stream, so one half's kernels
+ * fill the SMs the other half's last GEMM wave leaves idle; 1 runs every
+ * kernel on the caller's stream.  Both give the same bits.  Steps whose
+ * stream count has no such boundary, and steps with stage dumps on, run as
+ * one batch.  No counterpart in the reference, which encodes one stream at
+ * a time. */
+int sc_stream_encoder_set_concurrency(sc_stream_encoder *e, int32_t n_batches);
 int sc_stream_encoder_destroy(sc_stream_encoder *e);
 
 /* ---- RNN-T greedy decoder --------------------------------------------------

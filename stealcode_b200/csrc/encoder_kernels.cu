@@ -210,11 +210,31 @@ __global__ void __launch_bounds__(128) ln_quant_kernel(const float *__restrict__
   const bool live = row < rows;
   const int i0 = l * E;
   float v[E];
-  const float *xr = x + (live ? row : 0) * ldx + i0;
+  if constexpr (E == 32 && L == 32) {
+    // d = 1024, one row per warp: coalesced 512-byte loads, then through
+    // shared memory (element i at i + 4 * (i / 32), conflict-free both
+    // ways) to the lane-contiguous split
+    __shared__ __align__(16) float s_row[4][1024 + 128];
+    float *sr = s_row[threadIdx.x >> 5];
+    const float *xr = x + (live ? row : 0) * ldx + 4 * lane;
 #pragma unroll
-  for (int e4 = 0; e4 < E / 4; e4++) {
-    const float4 t = *reinterpret_cast<const float4 *>(xr + 4 * e4);
-    v[4 * e4] = t.x, v[4 * e4 + 1] = t.y, v[4 * e4 + 2] = t.z, v[4 * e4 + 3] = t.w;
+    for (int k = 0; k < 8; k++) {
+      const int i = 4 * lane + 128 * k;
+      *reinterpret_cast<float4 *>(sr + i + 4 * (i >> 5)) = *reinterpret_cast<const float4 *>(xr + 128 * k);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int e4 = 0; e4 < 8; e4++) {
+      const float4 t = *reinterpret_cast<const float4 *>(sr + 36 * lane + 4 * e4);
+      v[4 * e4] = t.x, v[4 * e4 + 1] = t.y, v[4 * e4 + 2] = t.z, v[4 * e4 + 3] = t.w;
+    }
+  } else {
+    const float *xr = x + (live ? row : 0) * ldx + i0;
+#pragma unroll
+    for (int e4 = 0; e4 < E / 4; e4++) {
+      const float4 t = *reinterpret_cast<const float4 *>(xr + 4 * e4);
+      v[4 * e4] = t.x, v[4 * e4 + 1] = t.y, v[4 * e4 + 2] = t.z, v[4 * e4 + 3] = t.w;
+    }
   }
   ln_lane<E, L>(v, lead, w, b, eps, i0);  // all lanes take part in the shuffles
   if (!live) return;
@@ -245,23 +265,66 @@ __global__ void __launch_bounds__(128)
   const int64_t z = rr / c, fr = s + rr % c;
   const int i0 = l * E;
   float v[E];
+  if constexpr (E == 32 && L == 32) {
+    // d = 1024, one row per warp: the taps are read coalesced (lane l owns
+    // elements 4l + 128k, one 512-byte run per warp load), then the row
+    // passes through shared memory to the LayerNorm's split (lane l owns
+    // [32l, 32l + 32)).  Element i sits at i + 4 * (i / 32) there, so both
+    // the scattered float4 writes and the lane-contiguous reads are free of
+    // bank conflicts.  Per element the same ordered chain of fused
+    // multiply-adds over the taps.
+    __shared__ __align__(16) float s_row[4][1024 + 128];
+    float *sr = s_row[threadIdx.x >> 5];
+    float4 a4[8];
 #pragma unroll
-  for (int e = 0; e < E; e++) v[e] = 0.0f;
+    for (int k = 0; k < 8; k++) a4[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-  for (int t = 0; t < (KH > 0 ? KH : 64); t++) {
-    if (KH == 0 && t >= kh) break;
-    const int64_t ti = fr - (kh - 1) + t;
-    if (ti < 0) continue;
-    const float *rw = ring + (z * cap + ti % cap) * (int64_t)d + i0;
-    const float *ww = wt + (int64_t)t * d + i0;
+    for (int t = 0; t < (KH > 0 ? KH : 64); t++) {
+      if (KH == 0 && t >= kh) break;
+      const int64_t ti = fr - (kh - 1) + t;
+      if (ti < 0) continue;
+      const float *rw = ring + (z * cap + ti % cap) * (int64_t)d + 4 * lane;
+      const float *ww = wt + (int64_t)t * d + 4 * lane;
 #pragma unroll
-    for (int e4 = 0; e4 < E / 4; e4++) {
-      const float4 a = *reinterpret_cast<const float4 *>(rw + 4 * e4);
-      const float4 k = *reinterpret_cast<const float4 *>(ww + 4 * e4);
-      v[4 * e4] = __fmaf_rn(a.x, k.x, v[4 * e4]);
-      v[4 * e4 + 1] = __fmaf_rn(a.y, k.y, v[4 * e4 + 1]);
-      v[4 * e4 + 2] = __fmaf_rn(a.z, k.z, v[4 * e4 + 2]);
-      v[4 * e4 + 3] = __fmaf_rn(a.w, k.w, v[4 * e4 + 3]);
+      for (int k = 0; k < 8; k++) {
+        const float4 a = *reinterpret_cast<const float4 *>(rw + 128 * k);
+        const float4 w = *reinterpret_cast<const float4 *>(ww + 128 * k);
+        a4[k].x = __fmaf_rn(a.x, w.x, a4[k].x);
+        a4[k].y = __fmaf_rn(a.y, w.y, a4[k].y);
+        a4[k].z = __fmaf_rn(a.z, w.z, a4[k].z);
+        a4[k].w = __fmaf_rn(a.w, w.w, a4[k].w);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int i = 4 * lane + 128 * k;
+      *reinterpret_cast<float4 *>(sr + i + 4 * (i >> 5)) = a4[k];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int e4 = 0; e4 < 8; e4++) {
+      const float4 t4 = *reinterpret_cast<const float4 *>(sr + 36 * lane + 4 * e4);
+      v[4 * e4] = t4.x, v[4 * e4 + 1] = t4.y, v[4 * e4 + 2] = t4.z, v[4 * e4 + 3] = t4.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; e++) v[e] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < (KH > 0 ? KH : 64); t++) {
+      if (KH == 0 && t >= kh) break;
+      const int64_t ti = fr - (kh - 1) + t;
+      if (ti < 0) continue;
+      const float *rw = ring + (z * cap + ti % cap) * (int64_t)d + i0;
+      const float *ww = wt + (int64_t)t * d + i0;
+#pragma unroll
+      for (int e4 = 0; e4 < E / 4; e4++) {
+        const float4 a = *reinterpret_cast<const float4 *>(rw + 4 * e4);
+        const float4 k = *reinterpret_cast<const float4 *>(ww + 4 * e4);
+        v[4 * e4] = __fmaf_rn(a.x, k.x, v[4 * e4]);
+        v[4 * e4 + 1] = __fmaf_rn(a.y, k.y, v[4 * e4 + 1]);
+        v[4 * e4 + 2] = __fmaf_rn(a.z, k.z, v[4 * e4 + 2]);
+        v[4 * e4 + 3] = __fmaf_rn(a.w, k.w, v[4 * e4 + 3]);
+      }
     }
   }
   ln_lane<E, L>(v, lead, lnw, lnb, eps, i0);

@@ -123,6 +123,13 @@ struct sc_stream_encoder {
   float *qd[2] = {nullptr, nullptr};
   void *ws = nullptr;
   size_t ws_bytes = 0;
+  // second sub-batch's stream and the fork / join events
+  cudaStream_t side = nullptr;
+  // per-stream sizes of the pre-encode buffers and the code buffers' widest
+  // row (features), as allocated
+  int64_t win_stride = 0, conv_stride = 0, code_k = 0;
+  int max_batches = 2;  // sub-batches of streams in flight (1 or 2)
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   // stage dumps of one layer (the reference's STEALCODE_DUMP_DIR senc_b*_*
   // files, streaming.rs:426-434): -1 = off
   int dump_layer = -1;
@@ -140,6 +147,9 @@ struct sc_stream_encoder {
       cudaFree(q->w.sc);
     }
     for (void *p : allocs) cudaFree(p);
+    if (ev_fork) cudaEventDestroy(ev_fork);
+    if (ev_join) cudaEventDestroy(ev_join);
+    if (side) cudaStreamDestroy(side);
   }
 };
 
@@ -417,11 +427,20 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     e->ws_bytes = gemm_ws_bytes(tmax, kmax);
     e->ws = L.dev_alloc(e->ws_bytes);
     const int64_t tp = std::max<int64_t>(ceil_div(M, 128) * 128, 64), kp = ceil_div(kmax, 32) * 32;
+    e->win_stride = e->t_mel_max * c.feat_in;
+    e->conv_stride = t0 * f0 * C;
+    e->code_k = kp;
     for (int i = 0; i < 2; i++) {
       e->qx[i] = (int8_t *)L.dev_alloc((size_t)(tp * kp));
       e->qd[i] = L.dev_alloc((size_t)(kp / 32 * tp * 4));
     }
     ok = L.err.empty();
+  }
+  if (ok && (cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking) != cudaSuccess ||
+             cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+             cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming) != cudaSuccess)) {
+    L.err = "side stream / event creation failed";
+    ok = false;
   }
   if (!ok) {
     set_error("stream_encoder_create: %s", L.err.c_str());
@@ -465,112 +484,71 @@ int sc_stream_encoder_frames(const sc_stream_encoder *e, int64_t stream_idx, int
   return kOk;
 }
 
-int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int64_t t0, int64_t t1, int32_t fin,
-                                 void *stream) {
-  if (!e || (!mel_new && t1 > t0) || t0 < 0 || t1 < t0 || t0 % 8) {
-    set_error("stream_encoder_encode_new: invalid argument (t0 must be a multiple of 8)");
-    return kErrInvalid;
-  }
-  cudaStream_t st = (cudaStream_t)stream;
+// Sizes of one encode_new step, shared by its sub-batches.
+struct StepGeom {
+  int64_t s, n_new, t_new, cf, t_mel, start_rel;
+  int64_t ta, fa, tb, fb, fc, r3, e3, r5, n5;
+};
+
+// One step for streams [z0, z0 + nz) on stream st.  Every buffer is indexed
+// by stream (or by row = stream * cf + frame) with per-stream strides that
+// depend only on the step's sizes, so a sub-batch is the same launches over
+// offset base pointers.  Its GEMM-input codes start at frame z0 * cf of the
+// code buffers, which is a whole number of 128-frame tiles (or 0).
+static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *mel_new, int64_t z0, int64_t nz,
+                          cudaStream_t st) {
   const sc_encoder_config &c = e->cfg;
-  const int64_t d = c.d_model, dff = c.d_ff, C = c.conv_channels, Z = e->n_streams;
+  const int64_t d = c.d_model, dff = c.d_ff, C = c.conv_channels, Z = nz;
   const float eps = c.ln_eps;
-  // ---- frames of this step (streaming.rs:160-180) ----
-  const int64_t s = t0 / 8, n_new = t1 - t0, ecount = s + (n_new + 7) / 8;
-  if (s != e->total) {
-    set_error("streaming encoder out of sync: expected frame %lld, cache has %lld", (long long)s,
-              (long long)e->total);
-    return kErrState;
-  }
-  const int64_t t_new = fin ? s + (((n_new / 2 + 1) / 2 + 1) / 2 + 1) : ecount;
-  if (t_new <= s) return kOk;
-  const int64_t cf = t_new - s;
-  if (cf > c.max_frames) {
-    set_error("stream_encoder_encode_new: %lld new frames exceed max_frames %d", (long long)cf, c.max_frames);
-    return kErrUnsupported;
-  }
-  const int64_t M = Z * cf;
-  // ---- pre-encode window (streaming.rs:182-218) ----
-  const int64_t mel_lo = s * 8, win_start = mel_lo > kMelHistory ? mel_lo - kMelHistory : 0;
-  const int64_t start_rel = (mel_lo - win_start) / 8, rel_max = start_rel + cf - 1;
-  const int64_t avail = t1 - win_start;
-  const int64_t want = std::max<int64_t>(8 * rel_max + 1, t_new * 8 - win_start);
-  const int64_t t_mel = std::min<int64_t>(avail, want);
-  if (mel_lo - win_start != e->hist_frames || t_mel > e->t_mel_max) {
-    set_error("stream_encoder_encode_new: window of %lld mel frames unsupported", (long long)t_mel);
-    return kErrUnsupported;
-  }
-  TRY(launch_mel_window(e->hist[e->hist_cur], kMelHistory, e->hist_frames, mel_new, (int)n_new, c.feat_in,
-                        (int)t_mel, e->win, Z, st));
+  const int64_t s = g.s, cf = g.cf, t_new = g.t_new, t_mel = g.t_mel;
+  const int64_t M = Z * cf, f0 = z0 * cf;
+  const int64_t fin_ = c.feat_in;
+  // Per-stream regions of the pre-encode buffers start at z0 times the
+  // allocated per-stream size: the kernels index each buffer with this
+  // step's (smaller) strides, so a half stays inside its own streams'
+  // regions whichever stage the other half is at.
+  float *win = e->win + z0 * e->win_stride;
+  float *hist_cur = e->hist[e->hist_cur] + z0 * kMelHistory * fin_;
+  float *hist_nxt = e->hist[e->hist_cur ^ 1] + z0 * kMelHistory * fin_;
+  const float *mel = mel_new ? mel_new + z0 * g.n_new * fin_ : nullptr;
+  float *p0 = e->p0 + z0 * e->conv_stride, *p1 = e->p1 + z0 * e->conv_stride, *p2 = e->p2 + z0 * e->conv_stride;
+  float *x = e->x + f0 * d, *y = e->y + f0 * d, *qkv = e->qkv + f0 * 3 * d, *h2 = e->h2 + f0 * 2 * d;
+  float *xn = e->xn + f0 * d, *attn = e->attn + f0 * d, *o2 = e->o2 + f0 * d;
+  TRY(launch_mel_window(hist_cur, kMelHistory, e->hist_frames, mel, (int)g.n_new, c.feat_in, (int)t_mel, win, Z,
+                        st));
   // ---- pre-encode stack (nemotron/encoder.rs:400-482) ----
-  const int64_t ta = conv_out(t_mel), fa = conv_out(c.feat_in);
-  const int64_t tb = conv_out(ta), fb = conv_out(fa);
-  const int64_t tc = conv_out(tb), fc = conv_out(fb);
-  if (tc < start_rel + cf) {
-    set_error("pre_encode produced too few frames: %lld < %lld", (long long)tc, (long long)(start_rel + cf));
-    return kErrInvalid;
-  }
-  // Rows each stage must produce for output frames [start_rel, start_rel + cf)
-  // (a 3x3 stride-2 conv with top pad 2 maps output row r to input rows
-  // 2r - 2 .. 2r); the convs compute only those rows.
-  auto need = [](int64_t lo, int64_t hi, int64_t t_in, int64_t &in_lo, int64_t &in_hi) {
-    in_lo = std::max<int64_t>(2 * lo - 2, 0);
-    in_hi = std::min<int64_t>(2 * (hi - 1) + 1, t_in);
-  };
-  const int64_t r5 = start_rel, n5 = cf;  // conv5 / conv6 rows
-  int64_t r3, e3, r0, e0;
-  need(r5, r5 + n5, tb, r3, e3);          // conv2 / conv3 rows
-  need(r3, e3, ta, r0, e0);               // conv0 rows
-  // conv0 + ReLU and the depthwise conv2 in one kernel (conv0 rows [r0, e0)
-  // are rebuilt where conv2 reads them)
-  (void)r0;
-  (void)e0;
-  TRY(launch_conv02_fused(e->win, Z, (int)t_mel, c.feat_in, e->c0.w, e->c0.b, e->c2.w, e->c2.b, (int)C, (int)ta,
-                          (int)fa, (int)r3, (int)(e3 - r3), (int)fb, e->p1, st));
-  TRY(launch_pw_conv_relu(e->p1, e->c3.w, e->c3.b, e->p2, Z * (e3 - r3) * fb, (int)C, (int)C, st));
-  TRY(launch_conv2d_3x3s2(e->p2, Z, (int)tb, (int)r3, (int)(e3 - r3), (int)fb, (int)C, e->c5.w, e->c5.b, (int)C,
-                          (int)r5, (int)n5, (int)fc, 0, e->p1, st));
-  TRY(launch_pw_conv_relu(e->p1, e->c6.w, e->c6.b, e->p0, Z * n5 * fc, (int)C, (int)C, st));
+  // conv0 + ReLU and the depthwise conv2 in one kernel (the conv0 rows that
+  // conv2 reads are rebuilt where it reads them)
+  TRY(launch_conv02_fused(win, Z, (int)t_mel, c.feat_in, e->c0.w, e->c0.b, e->c2.w, e->c2.b, (int)C, (int)g.ta,
+                          (int)g.fa, (int)g.r3, (int)(g.e3 - g.r3), (int)g.fb, p1, st));
+  TRY(launch_pw_conv_relu(p1, e->c3.w, e->c3.b, p2, Z * (g.e3 - g.r3) * g.fb, (int)C, (int)C, st));
+  TRY(launch_conv2d_3x3s2(p2, Z, (int)g.tb, (int)g.r3, (int)(g.e3 - g.r3), (int)g.fb, (int)C, e->c5.w, e->c5.b,
+                          (int)C, (int)g.r5, (int)g.n5, (int)g.fc, 0, p1, st));
+  TRY(launch_pw_conv_relu(p1, e->c6.w, e->c6.b, p0, Z * g.n5 * g.fc, (int)C, (int)C, st));
   // GEMM inputs are quantised by their producers straight into the
   // tensor-core operand layout (code buffers qx/qd, ping-pong)
   const int ft = tc_frame_tile(M);
   const int64_t t_pad = ceil_div(M, ft) * ft;
-  auto qbuf = [&](int i, int64_t k) { return QOut{e->qx[i], e->qd[i], ceil_div(k, 32), t_pad, ft}; };
+  // a half's codes start at frame f0 times the buffers' widest row, so the
+  // halves' regions stay apart for every feature width
+  auto qbuf = [&](int i, int64_t k) {
+    return QOut{e->qx[i] + f0 * e->code_k, e->qd[i] + f0 * (e->code_k / 32), ceil_div(k, 32), t_pad, ft};
+  };
   auto gemm_q = [&](const Lin &l, const QOut &in, float *out, int64_t ldo, Epilogue epi, QOut next) {
     TcGemmArgs ta{&l.w, in.xq, in.dx, M, t_pad, l.bias, out, 1, ldo, epi, next};
     return gemm_tc(ta, st);
   };
-  TRY(launch_flatten(e->p0, Z, (int)n5, (int)fc, (int)C, 0, (int)cf, nullptr, st, qbuf(0, C * fc)));
-  TRY(gemm_q(e->pre_out, qbuf(0, C * fc), e->x, d, Epilogue{}, QOut{}));
+  TRY(launch_flatten(p0, Z, (int)g.n5, (int)g.fc, (int)C, 0, (int)cf, nullptr, st, qbuf(0, C * g.fc)));
+  TRY(gemm_q(e->pre_out, qbuf(0, C * g.fc), x, d, Epilogue{}, QOut{}));
   // history for the next window
-  TRY(launch_mel_hist(e->hist[e->hist_cur], kMelHistory, e->hist_frames, mel_new, (int)n_new, c.feat_in,
-                      e->hist[e->hist_cur ^ 1], Z, st));
-  // ---- band and pos rows (streaming.rs:226-261) ----
-  const int64_t pos_off = e->chunk - 1;
-  if (!e->pos_ready) {
-    // sinusoid rows computed on the host in f32 exactly as the reference does
-    std::vector<float> pet((size_t)(e->n_pos * d));
-    const float ln10000 = logf(10000.0f);
-    for (int64_t i = 0; i < e->n_pos; i++) {
-      const float pos = (float)i + (float)(1 - e->chunk);
-      for (int64_t k = 0; k < d / 2; k++) {
-        const float div = expf(-2.0f * (float)k * ln10000 / (float)d);
-        pet[i * d + 2 * k] = sinf(pos * div);
-        pet[i * d + 2 * k + 1] = cosf(pos * div);
-      }
-    }
-    SC_CUDA(cudaMemcpyAsync(e->pos_in, pet.data(), pet.size() * 4, cudaMemcpyHostToDevice, st));
-    for (auto &ly : e->layers)
-      TRY(gemm_impl(&ly.pos.w, e->pos_in, e->n_pos, SC_LAYOUT_TIME_MAJOR, 0, ly.pos.bias, ly.pos_p,
-                    SC_LAYOUT_TIME_MAJOR, d, e->ws, e->ws_bytes, nullptr, st, Epilogue{}, true));
-    SC_CUDA(cudaStreamSynchronize(st));  // pet must outlive the copy
-    e->pos_ready = true;
-  }
+  TRY(launch_mel_hist(hist_cur, kMelHistory, e->hist_frames, mel, (int)g.n_new, c.feat_in, hist_nxt, Z, st));
   // ---- conformer blocks (streaming.rs:279-318, block_new :395-680) ----
+  const int64_t pos_off = e->chunk - 1;
   Epilogue silu{kEpiSilu, nullptr, 1.0f};
-  e->dump_rows = M;
   for (size_t li = 0; li < e->layers.size(); li++) {
     Layer &ly = e->layers[li];
+    float *k_ring = ly.k_ring + z0 * e->kv_cap * d, *v_ring = ly.v_ring + z0 * e->kv_cap * d;
+    float *glu_ring = ly.glu_ring + z0 * e->glu_cap * d;
     auto dump = [&](int stage, const float *src, int64_t width) -> int {
       if ((int)li != e->dump_layer || !e->dump) return kOk;
       SC_CUDA(cudaMemcpy2DAsync(e->dump + (size_t)stage * M * 2 * d, 2 * d * 4, src, width * 4, d * 4, M,
@@ -580,15 +558,15 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
     const bool dumping = (int)li == e->dump_layer && e->dump;
     const QOut qa = qbuf(0, d), qb_ff = qbuf(1, dff), qb_d = qbuf(1, d);
     // macaron FF1: y = x + 0.5 * FF(LN(x)); the SiLU output goes to ff1_2 as codes
-    TRY(launch_ln_quant(e->x, d, ly.ln_ff1_w, ly.ln_ff1_b, eps, (int)d, M, qa, nullptr, d, st));
+    TRY(launch_ln_quant(x, d, ly.ln_ff1_w, ly.ln_ff1_b, eps, (int)d, M, qa, nullptr, d, st));
     TRY(gemm_q(ly.ff1_1, qa, nullptr, dff, silu, qb_ff));
-    TRY(gemm_q(ly.ff1_2, qb_ff, e->y, d, Epilogue{kEpiResidual, e->x, 0.5f}, QOut{}));
-    TRY(dump(0, e->y, d));
+    TRY(gemm_q(ly.ff1_2, qb_ff, y, d, Epilogue{kEpiResidual, x, 0.5f}, QOut{}));
+    TRY(dump(0, y, d));
     // rel-pos MHSA over the band, K/V from the rings; its output goes to
     // the out projection as codes
-    TRY(launch_ln_quant(e->y, d, ly.ln_att_w, ly.ln_att_b, eps, (int)d, M, qa, dumping ? e->xn : nullptr, d, st));
-    TRY(dump(1, e->xn, d));
-    TRY(gemm_q(ly.qkv, qa, e->qkv, 3 * d, Epilogue{}, QOut{}));
+    TRY(launch_ln_quant(y, d, ly.ln_att_w, ly.ln_att_b, eps, (int)d, M, qa, dumping ? xn : nullptr, d, st));
+    TRY(dump(1, xn, d));
+    TRY(gemm_q(ly.qkv, qa, qkv, 3 * d, Epilogue{}, QOut{}));
     // the call's frames [s, t_new) in sub-ranges that stay inside one
     // attention chunk, in order: each launch writes its frames' K/V rows to
     // the rings before the next one reads them, and every band stays within
@@ -596,20 +574,20 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
     for (int64_t a = s; a < t_new;) {
       const int64_t b = std::min<int64_t>(t_new, (a / e->chunk + 1) * e->chunk);
       AttnParams p{};
-      p.q = e->qkv;
+      p.q = qkv;
       p.ldq = 3 * d;
-      p.k_new = e->qkv + d;
-      p.v_new = e->qkv + 2 * d;
+      p.k_new = qkv + d;
+      p.v_new = qkv + 2 * d;
       p.ld_new = 3 * d;
       p.rows_new = b - a;
       p.new_lo = a;
-      p.k_ring = ly.k_ring;
-      p.v_ring = ly.v_ring;
+      p.k_ring = k_ring;
+      p.v_ring = v_ring;
       p.cap = e->kv_cap;
       p.pos_p = ly.pos_p;
       p.u = ly.pos_u;
       p.v = ly.pos_v;
-      p.out = dumping ? e->attn : nullptr;
+      p.out = dumping ? attn : nullptr;
       p.ldo = d;
       p.qout = qb_d;
       p.c = (int)(b - a);
@@ -629,39 +607,167 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
       TRY(launch_attn(p, Z, st));
       a = b;
     }
-    TRY(dump(2, e->attn, d));
-    TRY(gemm_q(ly.out, qb_d, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}, QOut{}));
-    TRY(dump(3, e->y, d));
+    TRY(dump(2, attn, d));
+    TRY(gemm_q(ly.out, qb_d, y, d, Epilogue{kEpiResidual, y, 1.0f}, QOut{}));
+    TRY(dump(3, y, d));
     // conv module: LN, pw1, GLU (ring), causal dw conv + LN + SiLU (codes), pw2
-    TRY(launch_ln_quant(e->y, d, ly.ln_conv_w, ly.ln_conv_b, eps, (int)d, M, qa, nullptr, d, st));
-    TRY(gemm_q(ly.pw1, qa, e->h2, 2 * d, Epilogue{}, QOut{}));
-    TRY(launch_glu_ring(e->h2, M, (int)cf, (int)d, ly.glu_ring, (int)e->glu_cap, s, st));
-    TRY(launch_dwconv_ln_silu_quant(ly.glu_ring, (int)e->glu_cap, M, (int)cf, (int)d, c.conv_kernel, s, ly.dw_t,
-                                    ly.conv_ln_w, ly.conv_ln_b, eps, qb_d, dumping ? e->o2 : nullptr, st));
-    TRY(dump(4, e->qkv, 3 * d));  // q of the new frames
-    TRY(dump(5, e->o2, d));
-    TRY(gemm_q(ly.pw2, qb_d, e->y, d, Epilogue{kEpiResidual, e->y, 1.0f}, QOut{}));
-    TRY(dump(6, e->y, d));
+    TRY(launch_ln_quant(y, d, ly.ln_conv_w, ly.ln_conv_b, eps, (int)d, M, qa, nullptr, d, st));
+    TRY(gemm_q(ly.pw1, qa, h2, 2 * d, Epilogue{}, QOut{}));
+    TRY(launch_glu_ring(h2, M, (int)cf, (int)d, glu_ring, (int)e->glu_cap, s, st));
+    TRY(launch_dwconv_ln_silu_quant(glu_ring, (int)e->glu_cap, M, (int)cf, (int)d, c.conv_kernel, s, ly.dw_t,
+                                    ly.conv_ln_w, ly.conv_ln_b, eps, qb_d, dumping ? o2 : nullptr, st));
+    TRY(dump(4, qkv, 3 * d));  // q of the new frames
+    TRY(dump(5, o2, d));
+    TRY(gemm_q(ly.pw2, qb_d, y, d, Epilogue{kEpiResidual, y, 1.0f}, QOut{}));
+    TRY(dump(6, y, d));
     // macaron FF2 and the block's final LN
-    TRY(launch_ln_quant(e->y, d, ly.ln_ff2_w, ly.ln_ff2_b, eps, (int)d, M, qa, nullptr, d, st));
+    TRY(launch_ln_quant(y, d, ly.ln_ff2_w, ly.ln_ff2_b, eps, (int)d, M, qa, nullptr, d, st));
     TRY(gemm_q(ly.ff2_1, qa, nullptr, dff, silu, qb_ff));
-    TRY(gemm_q(ly.ff2_2, qb_ff, e->y, d, Epilogue{kEpiResidual, e->y, 0.5f}, QOut{}));
-    TRY(launch_ln_rows(e->y, d, ly.ln_out_w, ly.ln_out_b, eps, e->x, d, M, (int)d, st));
-    TRY(dump(7, e->x, d));
+    TRY(gemm_q(ly.ff2_2, qb_ff, y, d, Epilogue{kEpiResidual, y, 0.5f}, QOut{}));
+    TRY(launch_ln_rows(y, d, ly.ln_out_w, ly.ln_out_b, eps, x, d, M, (int)d, st));
+    TRY(dump(7, x, d));
   }
   // ---- prompt MLP on the new frames (streaming.rs:320-342) ----
   if (e->any_prompt) {
     const QOut qcat = qbuf(0, d + e->n_prompts), qh = qbuf(1, e->prompt_hidden);
-    TRY(launch_prompt_cat_quant(e->x, M, (int)cf, (int)d, (int)e->n_prompts, e->pids, qcat, st));
+    TRY(launch_prompt_cat_quant(x, M, (int)cf, (int)d, (int)e->n_prompts, e->pids + z0, qcat, st));
     TRY(gemm_q(e->prompt0, qcat, nullptr, e->prompt_hidden, Epilogue{kEpiRelu, nullptr, 1.0f}, qh));
-    TRY(gemm_q(e->prompt2, qh, e->y, d, Epilogue{}, QOut{}));
-    TRY(launch_prompt_select(e->x, e->y, M, (int)cf, (int)d, e->pids, st));
+    TRY(gemm_q(e->prompt2, qh, y, d, Epilogue{}, QOut{}));
+    TRY(launch_prompt_select(x, y, M, (int)cf, (int)d, e->pids + z0, st));
   }
-  TRY(launch_out_ring(e->x, M, (int)cf, (int)d, e->out_ring, (int)e->out_cap, s, st));
+  TRY(launch_out_ring(x, M, (int)cf, (int)d, e->out_ring + z0 * e->out_cap * d, (int)e->out_cap, s, st));
+  return kOk;
+}
+
+// First stream of the second sub-batch, or 0 for one batch: the halves are
+// split where the code buffers' 128-frame tiles split (z0 * cf a multiple of
+// 128), so the two halves' GEMM inputs never share a tile.  Stage dumps keep
+// one batch (their buffer holds the whole step).
+static int64_t split_point(const sc_stream_encoder *e, int64_t cf) {
+  const int64_t Z = e->n_streams;
+  if (!e->side || e->max_batches < 2 || e->dump_layer >= 0 || Z < 2) return 0;
+  int64_t gcd = 128, v = cf;
+  while (v) {
+    const int64_t r = gcd % v;
+    gcd = v;
+    v = r;
+  }
+  const int64_t unit = 128 / gcd;  // streams per 128-frame tile boundary
+  const int64_t z0 = (Z / 2) / unit * unit;
+  return z0 > 0 && z0 < Z ? z0 : 0;
+}
+
+int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int64_t t0, int64_t t1, int32_t fin,
+                                 void *stream) {
+  if (!e || (!mel_new && t1 > t0) || t0 < 0 || t1 < t0 || t0 % 8) {
+    set_error("stream_encoder_encode_new: invalid argument (t0 must be a multiple of 8)");
+    return kErrInvalid;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const sc_encoder_config &c = e->cfg;
+  const int64_t d = c.d_model, Z = e->n_streams;
+  StepGeom g{};
+  // ---- frames of this step (streaming.rs:160-180) ----
+  const int64_t s = t0 / 8, n_new = t1 - t0, ecount = s + (n_new + 7) / 8;
+  if (s != e->total) {
+    set_error("streaming encoder out of sync: expected frame %lld, cache has %lld", (long long)s,
+              (long long)e->total);
+    return kErrState;
+  }
+  const int64_t t_new = fin ? s + (((n_new / 2 + 1) / 2 + 1) / 2 + 1) : ecount;
+  if (t_new <= s) return kOk;
+  const int64_t cf = t_new - s;
+  if (cf > c.max_frames) {
+    set_error("stream_encoder_encode_new: %lld new frames exceed max_frames %d", (long long)cf, c.max_frames);
+    return kErrUnsupported;
+  }
+  // ---- pre-encode window (streaming.rs:182-218) ----
+  const int64_t mel_lo = s * 8, win_start = mel_lo > kMelHistory ? mel_lo - kMelHistory : 0;
+  const int64_t start_rel = (mel_lo - win_start) / 8, rel_max = start_rel + cf - 1;
+  const int64_t avail = t1 - win_start;
+  const int64_t want = std::max<int64_t>(8 * rel_max + 1, t_new * 8 - win_start);
+  const int64_t t_mel = std::min<int64_t>(avail, want);
+  if (mel_lo - win_start != e->hist_frames || t_mel > e->t_mel_max) {
+    set_error("stream_encoder_encode_new: window of %lld mel frames unsupported", (long long)t_mel);
+    return kErrUnsupported;
+  }
+  g.s = s;
+  g.n_new = n_new;
+  g.t_new = t_new;
+  g.cf = cf;
+  g.t_mel = t_mel;
+  g.start_rel = start_rel;
+  g.ta = conv_out(t_mel);
+  g.fa = conv_out(c.feat_in);
+  g.tb = conv_out(g.ta);
+  g.fb = conv_out(g.fa);
+  const int64_t tc = conv_out(g.tb);
+  g.fc = conv_out(g.fb);
+  if (tc < start_rel + cf) {
+    set_error("pre_encode produced too few frames: %lld < %lld", (long long)tc, (long long)(start_rel + cf));
+    return kErrInvalid;
+  }
+  // Rows each pre-encode stage must produce for output frames
+  // [start_rel, start_rel + cf) (a 3x3 stride-2 conv with top pad 2 maps
+  // output row r to input rows 2r - 2 .. 2r); the convs compute only those.
+  g.r5 = start_rel;
+  g.n5 = cf;
+  g.r3 = std::max<int64_t>(2 * g.r5 - 2, 0);
+  g.e3 = std::min<int64_t>(2 * (g.r5 + g.n5 - 1) + 1, g.tb);
+  // ---- pos rows, once (streaming.rs:236-261) ----
+  if (!e->pos_ready) {
+    // sinusoid rows computed on the host in f32 exactly as the reference does
+    std::vector<float> pet((size_t)(e->n_pos * d));
+    const float ln10000 = logf(10000.0f);
+    for (int64_t i = 0; i < e->n_pos; i++) {
+      const float pos = (float)i + (float)(1 - e->chunk);
+      for (int64_t k = 0; k < d / 2; k++) {
+        const float div = expf(-2.0f * (float)k * ln10000 / (float)d);
+        pet[i * d + 2 * k] = sinf(pos * div);
+        pet[i * d + 2 * k + 1] = cosf(pos * div);
+      }
+    }
+    SC_CUDA(cudaMemcpyAsync(e->pos_in, pet.data(), pet.size() * 4, cudaMemcpyHostToDevice, st));
+    for (auto &ly : e->layers)
+      TRY(gemm_impl(&ly.pos.w, e->pos_in, e->n_pos, SC_LAYOUT_TIME_MAJOR, 0, ly.pos.bias, ly.pos_p,
+                    SC_LAYOUT_TIME_MAJOR, d, e->ws, e->ws_bytes, nullptr, st, Epilogue{}, true));
+    SC_CUDA(cudaStreamSynchronize(st));  // pet must outlive the copy
+    e->pos_ready = true;
+  }
+  e->dump_rows = Z * cf;
+  // ---- the streams, as one batch or as two halves in flight at once on the
+  // caller's stream and the encoder's side stream (each half's GEMMs are
+  // under two waves of CTAs, so the other half's kernels fill the SMs their
+  // last wave leaves idle) ----
+  const int64_t z0 = split_point(e, cf);
+  int rc;
+  if (z0 == 0) {
+    rc = encode_streams(e, g, mel_new, 0, Z, st);
+  } else {
+    SC_CUDA(cudaEventRecord(e->ev_fork, st));
+    SC_CUDA(cudaStreamWaitEvent(e->side, e->ev_fork, 0));
+    rc = encode_streams(e, g, mel_new, 0, z0, st);
+    const int rc1 = encode_streams(e, g, mel_new, z0, Z - z0, e->side);
+    if (!rc) rc = rc1;
+    // join even after an error, so the caller's stream never runs ahead of
+    // work left on the side stream
+    SC_CUDA(cudaEventRecord(e->ev_join, e->side));
+    SC_CUDA(cudaStreamWaitEvent(st, e->ev_join, 0));
+  }
+  if (rc) return rc;
   e->hist_cur ^= 1;
   e->hist_frames = (int)std::min<int64_t>(kMelHistory, e->hist_frames + n_new);
   e->total = t_new;
   e->last_c = cf;
+  return kOk;
+}
+
+int sc_stream_encoder_set_concurrency(sc_stream_encoder *e, int32_t n_batches) {
+  if (!e || n_batches < 1 || n_batches > 2) {
+    set_error("stream_encoder_set_concurrency: n_batches must be 1 or 2");
+    return kErrInvalid;
+  }
+  e->max_batches = n_batches;
   return kOk;
 }
 

@@ -281,6 +281,10 @@ class StreamEncoder:
     def n_prompts(self) -> int:
         return int(lib.sc_stream_encoder_n_prompts(self._h))
 
+    def set_concurrency(self, n_batches: int) -> None:
+        """Sub-batches of streams in flight per encode_new (1 or 2; same bits)."""
+        check(lib.sc_stream_encoder_set_concurrency(self._h, n_batches))
+
     def set_dump(self, layer: int) -> None:
         check(lib.sc_stream_encoder_set_dump(self._h, layer))
 

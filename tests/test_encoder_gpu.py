@@ -165,6 +165,55 @@ def test_encoder_long_calls_match_streaming_steps(torch):
     short.close()
 
 
+class _DevRows:
+    """A device pointer [rows, d] f32 viewed as a torch tensor (no copy)."""
+
+    def __init__(self, ptr, rows, d):
+        self.__cuda_array_interface__ = {"shape": (rows, d), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def test_encoder_two_sub_batches_match_one_batch(torch):
+    """encode_new over many streams runs two halves of the streams in flight
+    on two CUDA streams (the caller's and the encoder's own): 256 streams of
+    7-frame steps (halves of 128 streams) and 32 streams of 56-frame calls
+    (halves of 16) give the same bits as one batch on the caller's stream,
+    and the streams at both edges of both halves match the oracle."""
+    from stealcode_b200.ops import StreamEncoder
+
+    for n_streams, frames, max_frames, n_calls in ((256, 7, 8, 3), (32, 56, 64, 2)):
+        cfg = model.EncoderConfig(n_layers=2, max_frames=max_frames)
+        m = model.random_model(cfg, seed=23)
+        mel_per = 8 * frames
+        mel = model.mel_stream(24, n_streams, mel_per * n_calls, cfg.feat_in)
+        two, one = StreamEncoder(m, n_streams), StreamEncoder(m, n_streams)
+        one.set_concurrency(1)
+        edges = (0, n_streams // 2 - 1, n_streams // 2, n_streams - 1)
+        refs = {z: oracle.StreamingEncoder(m) for z in edges}
+        for r in refs.values():
+            r.set_device_rounding()
+        worst = 0.0
+        for i in range(n_calls):
+            t0, t1 = mel_per * i, mel_per * (i + 1)
+            x = torch.from_numpy(np.ascontiguousarray(mel[:, t0:t1])).cuda()
+            s = two.total()
+            two.encode_new(x, t0, t1)
+            a = torch.as_tensor(_DevRows(*two.output()), device="cuda").cpu().numpy()
+            one.encode_new(x, t0, t1)
+            b = torch.as_tensor(_DevRows(*one.output()), device="cuda").cpu().numpy()
+            assert a.shape == (n_streams * frames, cfg.d_model)
+            assert np.array_equal(a, b), "two sub-batches differ from one batch"
+            for z, r in refs.items():
+                assert r.encode_new(mel[z, :t1], t0, t1, False) == 0
+                got = a[z * frames:(z + 1) * frames]
+                worst = max(worst, _err(got, r.frames(s, r.total()))[0])
+        print("%d streams x %d frames: two halves == one batch; edge streams vs oracle worst max/RMS %.3g"
+              % (n_streams, frames, worst))
+        assert worst <= TOL
+        two.close()
+        one.close()
+
+
 def test_encoder_out_of_sync_is_rejected(torch):
     from stealcode_b200.ops import StreamEncoder
 
