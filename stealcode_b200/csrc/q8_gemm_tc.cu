@@ -50,10 +50,15 @@ constexpr int kTcKb = SC_TC_KB;
 constexpr int kTcStages = SC_TC_STAGES;
 constexpr int kTcPhases = SC_TC_PHASES;
 static_assert(kTcStages >= kTcPhases, "every producer phase needs a stage in flight");
-// TMEM accumulators (FT columns each, 512 columns in all): the MMA of a
-// block may start once the drain has read the accumulator it reuses.
+// TMEM accumulators (FT columns each): the MMA of a block may start once
+// the drain has read the accumulator it reuses.  128-frame tiles take all
+// 512 columns (one CTA per SM); 64-frame tiles take 256, so two CTAs share
+// an SM (their drains run independently, and twice as many tiles per wave
+// even out the last wave of a grid of a few hundred tiles).
 template <int FT>
-constexpr int tc_acc_bufs() { return 512 / FT < 8 ? 512 / FT : 8; }
+constexpr int tc_acc_bufs() { return FT == 64 ? 4 : (512 / FT < 8 ? 512 / FT : 8); }
+template <int FT>
+constexpr int tc_ctas_per_sm() { return FT == 64 ? 2 : 1; }
 
 static __device__ unsigned g_tc_status;
 
@@ -161,7 +166,7 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
 }
 
 template <int FT, int DWG>
-__global__ void __launch_bounds__(64 + 128 * DWG, 1) q8_gemm_tc_kernel(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(64 + 128 * DWG, tc_ctas_per_sm<FT>()) q8_gemm_tc_kernel(const __grid_constant__ TcParams p) {
   using L = TcSmem<FT, DWG>;
   static_assert(FT == 32 * DWG, "each drain warpgroup owns 32 frame columns");
   constexpr int kAcc = L::kAcc;
@@ -424,7 +429,11 @@ static int launch_tc(const TcParams &p, int64_t groups, cudaStream_t st) {
   return kOk;
 }
 
-int tc_frame_tile(int64_t t) { return t <= 32 ? 32 : t <= 64 ? 64 : 128; }
+// Frame tile of a GEMM over t frames: 64-frame tiles (two CTAs per SM) up
+// to 1024 frames, where a grid of 128-frame tiles would leave most of its
+// last wave idle; 128 above (measured at 896 / 1792 frames over the four
+// layer shapes: 193 vs 227 us / 305 vs 308 us).
+int tc_frame_tile(int64_t t) { return t <= 32 ? 32 : t <= 1024 ? 64 : 128; }
 
 int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
   const Q8Weights *w = a.w;
