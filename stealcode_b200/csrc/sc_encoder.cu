@@ -747,8 +747,7 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
     SC_CUDA(cudaEventRecord(e->ev_fork, st));
     SC_CUDA(cudaStreamWaitEvent(e->side, e->ev_fork, 0));
     rc = encode_streams(e, g, mel_new, 0, z0, st);
-    const int rc1 = encode_streams(e, g, mel_new, z0, Z - z0, e->side);
-    if (!rc) rc = rc1;
+    if (!rc) rc = encode_streams(e, g, mel_new, z0, Z - z0, e->side);
     // join even after an error, so the caller's stream never runs ahead of
     // work left on the side stream
     SC_CUDA(cudaEventRecord(e->ev_join, e->side));
