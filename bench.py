@@ -14,8 +14,10 @@ step streams are larger than L2 (126 MB).
 
 Also in the line:
   roofline      the tcgen05 int8 GEMM (the step's dominant kernel) at the
-                step's shapes (M = streams * 7 frames), over the 24 layers'
-                own weights, timed with CUDA events (tensor-bound);
+                step's shapes (the encoder's two halves of the streams, 896
+                frames each at 256 streams, in flight on two CUDA streams),
+                over the 24 layers' own weights, timed with CUDA events
+                (tensor-bound);
   gemm_sweep    the Q8_0 GEMM shape sweep of one layer (M = 1, 8, 32, 128;
                 QKV, out-proj, FFN-up, FFN-down; 24 weight copies, 321 MB)
                 as HBM GB/s, and its weight-streaming kernel's roofline;
@@ -34,7 +36,9 @@ Also in the line:
                 the tokens emitted per frame;
   cpu_baseline  the reference CPU path (the oracle's restatement: AVX2 +
                 threads GEMMs, one StreamingEncoder per stream) on a bounded
-                sample of the same workload.
+                sample of the same workload, and the reference CPU GEMM on
+                one streaming chunk (M 8, K 1024, N 4096) with all host
+                threads and with one.
 
 Multi-GPU: one process per GPU (torchrun); every rank encodes its own 256
 streams with its own weight copy (streams are independent: no collective on
@@ -198,6 +202,35 @@ def cpu_encoder_sample(m, n_streams, n_steps, budget_s=None):
     dt = time.perf_counter() - t0
     audio = n_streams * done * AUDIO_S_PER_STEP
     return audio / dt, dt, audio, done
+
+
+def cpu_gemm_sample(budget_s=2.0):
+    """The reference CPU GEMM on the single streaming-chunk workload (8
+    frames x K 1024 through a 4096-row Q8_0 matrix, weights ~N(0, 0.02)
+    quantised to Q8_0, activations ~N(0, 1), seeded): the oracle's AVX2
+    restatement of q8_gemm's SIMD dispatch (simd_kernel.rs:96-394), with all
+    host threads and with one.  Returns µs per GEMM and GEMM GB/s for each."""
+    import oracle
+    from stealcode_b200 import synth
+
+    m, k, n = 4096, 1024, 8
+    w = synth.q8_weights(synth.SEED_BASE, m, k)
+    x = synth.normal(synth.SEED_BASE + 1, (k, n))
+    y = np.zeros((m, n), dtype=np.float32)
+    nbytes = m * (k // 32) * 34 + 4 * k * n + 4 * m * n
+    out = {"workload": "q8_gemm M=8 K=1024 N=4096 (one streaming chunk)", "bytes_per_gemm": nbytes}
+    for label, threads in (("all_threads", 0), ("one_thread", 1)):
+        oracle.q8_gemm(m, k, n, w, (k // 32) * 34, 34, 2, x, nthreads=threads, y=y)
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            oracle.q8_gemm(m, k, n, w, (k // 32) * 34, 34, 2, x, nthreads=threads, y=y)
+            reps += 1
+            dt = time.perf_counter() - t0
+            if dt > budget_s:
+                break
+        out[label] = {"us_per_gemm": 1e6 * dt / reps, "gbs": nbytes * reps / dt / 1e9,
+                      "threads": oracle.num_cpus() if threads == 0 else 1}
+    return out
 
 
 def run_reference(args, rank):
@@ -556,7 +589,8 @@ def run_ours(args, rank, world, local_rank):
         v, dt, audio, steps = cpu_encoder_sample(m, 4, 8, budget_s=15.0)
         cpu = {"value": v, "unit": UNIT, "cores": oracle.num_cpus(), "kind": "port",
                "sample": f"4 streams x {steps} chunks from t=0 ({audio:.2f} audio s in {dt:.1f} s), oracle "
-                         "StreamingEncoder with the reference's GEMM dispatch"}
+                         "StreamingEncoder with the reference's GEMM dispatch",
+               "gemm": cpu_gemm_sample()}
     if rank == 0:
         p = peaks()
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
