@@ -259,7 +259,12 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg,
  * [t0, t1) as [n_streams][t1 - t0][feat_in]; the encoder keeps the mel left
  * context itself, so the whole mel history is not passed.  t0 must equal 8 *
  * the frames encoded so far (else SC_ERR_STATE, as the reference's "out of
- * sync" bail); fin marks a stream's last batch.  Async on stream. */
+ * sync" bail); fin marks a stream's last batch.  Async on stream, except
+ * the first call, which also computes every layer's positional rows
+ * (streaming.rs:236-261) from host sinusoids and synchronises the stream.
+ * With enough streams the call runs half of them on the encoder's own CUDA
+ * stream, joined back into `stream` before it returns
+ * (sc_stream_encoder_set_concurrency). */
 int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new,
                                  int64_t t0, int64_t t1, int32_t fin,
                                  void *stream);

@@ -547,13 +547,9 @@ static int launch_stage_lm(const AttnParams &p, int64_t n_streams, cudaStream_t 
   const int band = (int)(p.k_hi - p.k_lo);
   const size_t smem = attn_stage_smem_floats<HD, CQ>(band, LM ? 0 : p.np) * sizeof(float);
   auto kern = attn_stage_kernel<HD, CQ, LM>;
-  static size_t smem_set[64] = {};
-  int dev = 0;
-  SC_CUDA(cudaGetDevice(&dev));
-  if (smem > 48 * 1024 && dev < 64 && smem_set[dev] < smem) {
-    SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    smem_set[dev] = smem;
-  }
+  static std::atomic<size_t> smem_limit[64];
+  const int rc = raise_smem_limit((const void *)kern, smem, smem_limit);
+  if (rc) return rc;
   kern<<<dim3((unsigned)p.n_heads, (unsigned)n_streams), HD, smem, st>>>(p);
   note_launch();
   SC_CUDA(cudaGetLastError());
@@ -578,13 +574,9 @@ static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st
   int band = (int)(p.k_hi - p.k_lo);
   size_t smem = attn_smem_floats<HD, CQ>(band) * sizeof(float);
   auto kern = attn_stream_kernel<HD, CQ>;
-  static size_t smem_set[64] = {};
-  int dev = 0;
-  SC_CUDA(cudaGetDevice(&dev));
-  if (smem > 48 * 1024 && dev < 64 && smem_set[dev] < smem) {
-    SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    smem_set[dev] = smem;
-  }
+  static std::atomic<size_t> smem_limit[64];
+  const int rc = raise_smem_limit((const void *)kern, smem, smem_limit);
+  if (rc) return rc;
   kern<<<dim3((unsigned)p.n_heads, (unsigned)n_streams), HD, smem, st>>>(p);
   note_launch();
   SC_CUDA(cudaGetLastError());

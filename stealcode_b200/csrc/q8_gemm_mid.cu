@@ -168,13 +168,9 @@ int gemm_mid(const MidGemmArgs &a, cudaStream_t st) {
     set_error("q8_gemm_mid: codes must be [m_pad][k_pad] with m_pad a multiple of %d", kMidCols);
     return kErrInvalid;
   }
-  static bool configured[64] = {};
-  int dev = 0;
-  SC_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !configured[dev]) {
-    SC_CUDA(cudaFuncSetAttribute(q8_gemm_mid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MidSmem::kBytes));
-    configured[dev] = true;
-  }
+  static std::atomic<size_t> smem_limit[64];
+  const int rc = raise_smem_limit((const void *)q8_gemm_mid_kernel, MidSmem::kBytes, smem_limit);
+  if (rc) return rc;
   MidParams p{a.w->qs, a.w->sc, a.w->nb, a.w->rows, a.xq, a.dx, a.m, a.m_pad, a.k_pad, a.bias, a.y,
               a.y_time_major, a.ldy, a.epi};
   const dim3 grid((unsigned)(a.w->rows_pad / kMidRows), (unsigned)ceil_div(a.m, kMidCols));  // (group, slice) x frames

@@ -232,13 +232,9 @@ template <int MT, bool kDump>
 static int launch_stream(StreamParams &p, int64_t groups, int64_t mtiles, cudaStream_t st) {
   auto kern = q8_gemm_stream_kernel<MT, kDump>;
   const size_t smem = stream_smem(MT, p.nbl_max);
-  static size_t smem_set[64] = {};
-  int dev = 0;
-  SC_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && smem_set[dev] < smem) {
-    SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    smem_set[dev] = smem;
-  }
+  static std::atomic<size_t> smem_limit[64];
+  const int rc = raise_smem_limit((const void *)kern, smem, smem_limit);
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)groups, (unsigned)p.ks, (unsigned)mtiles);
   cfg.blockDim = dim3(kStreamThreads, 1, 1);
@@ -260,15 +256,17 @@ static int launch_stream(StreamParams &p, int64_t groups, int64_t mtiles, cudaSt
 }
 
 static unsigned *small_status_ptr() {
-  static unsigned *ptr[64] = {};
+  static std::atomic<unsigned *> ptr[64];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return nullptr;
-  if (!ptr[dev]) {
-    void *q = nullptr;
-    if (cudaGetSymbolAddress(&q, g_small_status) != cudaSuccess) return nullptr;
-    ptr[dev] = (unsigned *)q;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  unsigned *q = ptr[dev].load(std::memory_order_acquire);
+  if (!q) {
+    void *a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_small_status) != cudaSuccess) return nullptr;
+    q = (unsigned *)a;
+    ptr[dev].store(q, std::memory_order_release);  // every caller stores the same address
   }
-  return ptr[dev];
+  return q;
 }
 
 int small_gemm_status(unsigned *out) {

@@ -384,15 +384,17 @@ __global__ void __launch_bounds__(64 + 128 * DWG, tc_ctas_per_sm<FT>()) q8_gemm_
 }
 
 static unsigned *tc_status_ptr() {
-  static unsigned *ptr[64] = {};
+  static std::atomic<unsigned *> ptr[64];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return nullptr;
-  if (!ptr[dev]) {
-    void *q = nullptr;
-    if (cudaGetSymbolAddress(&q, g_tc_status) != cudaSuccess) return nullptr;
-    ptr[dev] = (unsigned *)q;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  unsigned *q = ptr[dev].load(std::memory_order_acquire);
+  if (!q) {
+    void *a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_tc_status) != cudaSuccess) return nullptr;
+    q = (unsigned *)a;
+    ptr[dev].store(q, std::memory_order_release);  // every caller stores the same address
   }
-  return ptr[dev];
+  return q;
 }
 
 int tc_gemm_status(unsigned *out) {
@@ -407,13 +409,9 @@ template <int FT, int DWG>
 static int launch_tc(const TcParams &p, int64_t groups, cudaStream_t st) {
   using L = TcSmem<FT, DWG>;
   auto kern = q8_gemm_tc_kernel<FT, DWG>;
-  static bool configured[64] = {};
-  int dev = 0;
-  SC_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !configured[dev]) {
-    SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-    configured[dev] = true;
-  }
+  static std::atomic<size_t> smem_limit[64];
+  const int rc = raise_smem_limit((const void *)kern, L::kBytes, smem_limit);
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)groups, (unsigned)(p.t_pad / FT), 1);
   cfg.blockDim = dim3(64 + 128 * DWG, 1, 1);

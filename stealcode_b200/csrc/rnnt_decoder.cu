@@ -761,19 +761,25 @@ int launch_lane_split(const sc_rnnt_decoder *r, const LaneMat &w, Op op, int64_t
               : launch_lane_split_t<Op, false>(r, w, op, max_cols, st);
 }
 
-// Shared-memory limit of every lane-split instantiation, set once before the
-// round graph is captured.
+// Shared-memory limit of every lane-split instantiation, raised before the
+// round graph is captured.  The limits only grow, so a decoder built later
+// with smaller matrices never lowers them under an earlier decoder.
+template <class Op, bool SIMD>
+static int raise_lane_split(size_t smem) {
+  static std::atomic<size_t> smem_limit[64];
+  return raise_smem_limit((const void *)lane_split_kernel<Op, SIMD>, smem, smem_limit);
+}
+
 int configure_lane_split(size_t smem) {
-  const int b = (int)smem;
-  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<LstmOp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<LstmOp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<PredOp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<PredOp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<OutOp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<OutOp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<EncOp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  SC_CUDA(cudaFuncSetAttribute(lane_split_kernel<EncOp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  return kOk;
+  int rc = raise_lane_split<LstmOp, true>(smem);
+  if (!rc) rc = raise_lane_split<LstmOp, false>(smem);
+  if (!rc) rc = raise_lane_split<PredOp, true>(smem);
+  if (!rc) rc = raise_lane_split<PredOp, false>(smem);
+  if (!rc) rc = raise_lane_split<OutOp, true>(smem);
+  if (!rc) rc = raise_lane_split<OutOp, false>(smem);
+  if (!rc) rc = raise_lane_split<EncOp, true>(smem);
+  if (!rc) rc = raise_lane_split<EncOp, false>(smem);
+  return rc;
 }
 
 // One round of the decode loop for list parity `parity` (its launches are

@@ -30,7 +30,7 @@ int cuda_fail(cudaError_t e, const char *what) {
 
 // ---- per-device state: SM count and a default workspace ----------------
 struct DeviceState {
-  int sm_count = 0;
+  std::atomic<int> sm_count{0};
   void *ws = nullptr;
   size_t ws_bytes = 0;
   void *stage = nullptr;  // host-twin staging for x and y (grow-only)
@@ -50,12 +50,29 @@ int current_device(int *dev, int *sm_count) {
     return kErrInvalid;
   }
   DeviceState &ds = g_dev[*dev];
-  if (ds.sm_count == 0) {
-    int n = 0;
+  int n = ds.sm_count.load(std::memory_order_relaxed);
+  if (n == 0) {
     SC_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, *dev));
-    ds.sm_count = n;
+    ds.sm_count.store(n, std::memory_order_relaxed);
   }
-  if (sm_count) *sm_count = ds.sm_count;
+  if (sm_count) *sm_count = n;
+  return kOk;
+}
+
+int raise_smem_limit(const void *kern, size_t bytes, std::atomic<size_t> *limit) {
+  if (bytes <= 48 * 1024) return kOk;
+  int dev = 0;
+  SC_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    set_error("device ordinal %d out of range", dev);
+    return kErrInvalid;
+  }
+  if (limit[dev].load(std::memory_order_acquire) >= bytes) return kOk;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (limit[dev].load(std::memory_order_relaxed) >= bytes) return kOk;
+  SC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  limit[dev].store(bytes, std::memory_order_release);
   return kOk;
 }
 

@@ -2,6 +2,8 @@
 // translation units and the C ABI (sc_api.cu).
 #pragma once
 
+#include <atomic>
+
 #include "sc_common.cuh"
 
 namespace sc {
@@ -115,6 +117,11 @@ int tc_gemm_status(unsigned *out);
 // force_tc so that every output is rounded the same way at any frame count.
 size_t gemm_ws_bytes(int64_t m, int64_t k);
 int current_device(int *dev, int *sm_count);
+// Raises kernel `kern`'s dynamic shared-memory limit on the current device to
+// at least `bytes` (a no-op up to the 48 KB default).  `limit` is the
+// kernel's per-device record [64]: it only grows and changes under a lock,
+// so no caller lowers the limit under another's launch.
+int raise_smem_limit(const void *kern, size_t bytes, std::atomic<size_t> *limit);
 int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, int64_t ldx,
               const float *bias, float *y, int32_t y_layout, int64_t ldy, void *ws, size_t ws_bytes,
               int32_t *dots, cudaStream_t st, Epilogue epi, bool force_tc = false);
