@@ -390,6 +390,7 @@ def tc_roofline(m, streams, dev, stream):
     n = len(mats) * len(halves)
     del mats, bufs
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
+            "frac_of_nominal_4500_tops": achieved / 4500.0,
             "peak_source": ("2 x measured dense bf16 TFLOP/s (B200's dense int8 rate is twice its bf16 rate)"
                             if bf16 else "2 x fallback bf16"),
             "kernel": "q8_gemm_tc_kernel (tcgen05 kind::i8)", "traffic": None,
@@ -498,6 +499,7 @@ def gemm_sweep(args, dev, world, stream):
             "launches_per_sweep": n_launch,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": "measured" if "hbm_gbs" in p else "fallback",
+                         "frac_of_spec_8000_gbs": achieved / 8000.0,
                          "kernel": "q8_gemm_stream_kernel", "bytes_per_launch_avg": kb / n_k,
                          "us_per_launch_avg": 1e3 * ms_k / n_k, "traffic": None, "by_m": by_m}}
 
