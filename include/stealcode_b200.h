@@ -268,6 +268,20 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg,
 int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new,
                                  int64_t t0, int64_t t1, int32_t fin,
                                  void *stream);
+/* StreamEncoder::encode_new with host buffers, the twin of the reference's
+ * call (which takes the mel frames in host memory): mel_host holds
+ * [n_streams][t1 - t0][feat_in] floats (at most 8 * max_frames frames); the
+ * call's output frames, [n_streams * c][d_model] stream-major as
+ * sc_stream_encoder_output gives them, go to out_host (if not NULL; room for
+ * n_streams * max_frames rows) and *rows (if not NULL) receives
+ * n_streams * c.  Each half of the streams is copied in, encoded and copied
+ * out on its own CUDA stream, so one half's copies overlap the other half's
+ * kernels (page-locked host buffers let the copies run asynchronously).
+ * Synchronous: out_host is filled when the call returns. */
+int sc_stream_encoder_encode_new_host(sc_stream_encoder *e,
+                                      const float *mel_host, int64_t t0,
+                                      int64_t t1, int32_t fin, float *out_host,
+                                      int64_t *rows, void *stream);
 /* StreamEncoder::total (streaming.rs:702-703). */
 int64_t sc_stream_encoder_total(const sc_stream_encoder *e);
 /* StreamEncoder::frames (streaming.rs:700-701, 111-127) for one stream,

@@ -79,6 +79,7 @@ SIGNATURES = {
     "sc_stream_encoder_n_prompts": (c_int64, [_P]),
     "sc_stream_encoder_set_dump": (c_int, [_P, c_int32]),
     "sc_stream_encoder_set_concurrency": (c_int, [_P, c_int32]),
+    "sc_stream_encoder_encode_new_host": (c_int, [_P, _P, c_int64, c_int64, c_int32, _P, _P, _P]),
     "sc_stream_encoder_dump": (c_int, [_P, c_int32, _P, POINTER(c_int64)]),
     "sc_stream_encoder_destroy": (c_int, [_P]),
     "sc_rnnt_create": (c_int, [_P, _P, c_int, _I, POINTER(c_void_p)]),

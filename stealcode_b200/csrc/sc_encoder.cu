@@ -128,6 +128,8 @@ struct sc_stream_encoder {
   // per-stream sizes of the pre-encode buffers and the code buffers' widest
   // row (features), as allocated
   int64_t win_stride = 0, conv_stride = 0, code_k = 0;
+  float *mel_stage = nullptr;   // [n_streams][mel_stage_frames][feat_in]: host-entry mel
+  int64_t mel_stage_frames = 0;
   int max_batches = 2;  // sub-batches of streams in flight (1 or 2)
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   // stage dumps of one layer (the reference's STEALCODE_DUMP_DIR senc_b*_*
@@ -427,6 +429,8 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     e->ws_bytes = gemm_ws_bytes(tmax, kmax);
     e->ws = L.dev_alloc(e->ws_bytes);
     const int64_t tp = std::max<int64_t>(ceil_div(M, 128) * 128, 64), kp = ceil_div(kmax, 32) * 32;
+    e->mel_stage_frames = 8 * (int64_t)c.max_frames;
+    e->mel_stage = L.dev_alloc((size_t)(n_streams * e->mel_stage_frames * c.feat_in * 4));
     e->win_stride = e->t_mel_max * c.feat_in;
     e->conv_stride = t0 * f0 * C;
     e->code_k = kp;
@@ -657,13 +661,17 @@ static int64_t split_point(const sc_stream_encoder *e, int64_t cf) {
   return z0 > 0 && z0 < Z ? z0 : 0;
 }
 
-int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int64_t t0, int64_t t1, int32_t fin,
-                                 void *stream) {
+// One encode_new step.  host_io: mel_new is host memory, copied per half
+// into the encoder's staging buffer on that half's stream, and each half's
+// output frames are copied to out_host (if given) on its stream, so one
+// half's copies overlap the other half's kernels; the call then waits for
+// the caller's stream.
+static int encode_call(sc_stream_encoder *e, const float *mel_new, int64_t t0, int64_t t1, int32_t fin,
+                       cudaStream_t st, bool host_io, float *out_host, int64_t *rows_out) {
   if (!e || (!mel_new && t1 > t0) || t0 < 0 || t1 < t0 || t0 % 8) {
     set_error("stream_encoder_encode_new: invalid argument (t0 must be a multiple of 8)");
     return kErrInvalid;
   }
-  cudaStream_t st = (cudaStream_t)stream;
   const sc_encoder_config &c = e->cfg;
   const int64_t d = c.d_model, Z = e->n_streams;
   StepGeom g{};
@@ -675,7 +683,13 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
     return kErrState;
   }
   const int64_t t_new = fin ? s + (((n_new / 2 + 1) / 2 + 1) / 2 + 1) : ecount;
+  if (rows_out) *rows_out = 0;
   if (t_new <= s) return kOk;
+  if (host_io && n_new > e->mel_stage_frames) {
+    set_error("stream_encoder_encode_new_host: %lld mel frames exceed the staging buffer's %lld",
+              (long long)n_new, (long long)e->mel_stage_frames);
+    return kErrUnsupported;
+  }
   const int64_t cf = t_new - s;
   if (cf > c.max_frames) {
     set_error("stream_encoder_encode_new: %lld new frames exceed max_frames %d", (long long)cf, c.max_frames);
@@ -739,26 +753,52 @@ int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int
   // caller's stream and the encoder's side stream (each half's GEMMs are
   // under two waves of CTAs, so the other half's kernels fill the SMs their
   // last wave leaves idle) ----
+  const int64_t fi = c.feat_in;
+  auto run = [&](int64_t za, int64_t nz, cudaStream_t sa) -> int {
+    const float *mel = mel_new;
+    if (host_io && n_new > 0) {
+      SC_CUDA(cudaMemcpyAsync(e->mel_stage + za * n_new * fi, mel_new + za * n_new * fi,
+                              (size_t)(nz * n_new * fi) * 4, cudaMemcpyHostToDevice, sa));
+      mel = e->mel_stage;
+    }
+    TRY(encode_streams(e, g, mel, za, nz, sa));
+    if (host_io && out_host)
+      SC_CUDA(cudaMemcpyAsync(out_host + za * cf * d, e->x + za * cf * d, (size_t)(nz * cf * d) * 4,
+                              cudaMemcpyDeviceToHost, sa));
+    return kOk;
+  };
   const int64_t z0 = split_point(e, cf);
   int rc;
   if (z0 == 0) {
-    rc = encode_streams(e, g, mel_new, 0, Z, st);
+    rc = run(0, Z, st);
   } else {
     SC_CUDA(cudaEventRecord(e->ev_fork, st));
     SC_CUDA(cudaStreamWaitEvent(e->side, e->ev_fork, 0));
-    rc = encode_streams(e, g, mel_new, 0, z0, st);
-    if (!rc) rc = encode_streams(e, g, mel_new, z0, Z - z0, e->side);
+    rc = run(0, z0, st);
+    if (!rc) rc = run(z0, Z - z0, e->side);
     // join even after an error, so the caller's stream never runs ahead of
     // work left on the side stream
     SC_CUDA(cudaEventRecord(e->ev_join, e->side));
     SC_CUDA(cudaStreamWaitEvent(st, e->ev_join, 0));
   }
+  if (!rc && host_io) SC_CUDA(cudaStreamSynchronize(st));
   if (rc) return rc;
+  if (rows_out) *rows_out = Z * cf;
   e->hist_cur ^= 1;
   e->hist_frames = (int)std::min<int64_t>(kMelHistory, e->hist_frames + n_new);
   e->total = t_new;
   e->last_c = cf;
   return kOk;
+}
+
+int sc_stream_encoder_encode_new(sc_stream_encoder *e, const float *mel_new, int64_t t0, int64_t t1, int32_t fin,
+                                 void *stream) {
+  return encode_call(e, mel_new, t0, t1, fin, (cudaStream_t)stream, false, nullptr, nullptr);
+}
+
+int sc_stream_encoder_encode_new_host(sc_stream_encoder *e, const float *mel_host, int64_t t0, int64_t t1,
+                                      int32_t fin, float *out_host, int64_t *rows, void *stream) {
+  return encode_call(e, mel_host, t0, t1, fin, (cudaStream_t)stream, true, out_host, rows);
 }
 
 int sc_stream_encoder_set_concurrency(sc_stream_encoder *e, int32_t n_batches) {

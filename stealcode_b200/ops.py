@@ -243,6 +243,40 @@ class StreamEncoder:
         check(lib.sc_stream_encoder_encode_new(self._h, mel_new.data_ptr() if mel_new is not None else None, t0, t1,
                                                int(fin), _stream_ptr(stream)))
 
+    def encode_new_host(self, mel_new: np.ndarray, t0: int, t1: int, fin: bool = False, out=None,
+                        stream=None):
+        """encode_new with host buffers (the reference's call shape): mel_new
+        is a host float32 array [n_streams, t1 - t0, feat_in]; returns the
+        call's output frames [n_streams * c, d] in `out` (a host float32
+        array of at least n_streams * max_frames rows, page-locked for
+        overlapped copies) or a new array.  Synchronous."""
+        mel = np.ascontiguousarray(mel_new, dtype=np.float32)
+        if mel.shape[0] != self.n_streams or (mel.ndim == 3 and mel.shape[1] != t1 - t0):
+            raise ValueError(f"encode_new_host: mel shape {mel.shape} for {self.n_streams} streams x {t1 - t0}")
+        cap = self.n_streams * self.model.config.max_frames
+        if out is None:
+            out = np.empty((cap, self.d), dtype=np.float32)
+        if isinstance(out, np.ndarray):
+            if out.dtype != np.float32 or not out.flags.c_contiguous or out.size < cap * self.d:
+                raise ValueError("encode_new_host: out must be C-contiguous float32 with n_streams * max_frames rows")
+            optr = _hp(out)
+        else:  # a page-locked torch CPU tensor
+            if out.numel() < cap * self.d:
+                raise ValueError("encode_new_host: out too small")
+            optr = out.data_ptr()
+        rows = ctypes.c_int64()
+        check(lib.sc_stream_encoder_encode_new_host(self._h, _hp(mel) if mel.size else None, t0, t1, int(fin),
+                                                    optr, ctypes.byref(rows), _stream_ptr(stream)))
+        return out[: rows.value]
+
+    def encode_new_host_ptr(self, mel_ptr: int, t0: int, t1: int, fin: bool, out_ptr: int, stream=None) -> int:
+        """encode_new_host on raw host pointers (page-locked buffers the caller
+        owns); returns the rows written."""
+        rows = ctypes.c_int64()
+        check(lib.sc_stream_encoder_encode_new_host(self._h, mel_ptr, t0, t1, int(fin), out_ptr,
+                                                    ctypes.byref(rows), _stream_ptr(stream)))
+        return rows.value
+
     @classmethod
     def from_gguf(cls, path: str, n_streams: int, max_frames: int = 8) -> "StreamEncoder":
         """Build from a GGUF checkpoint in the reference's layout

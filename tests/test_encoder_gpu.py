@@ -214,6 +214,31 @@ def test_encoder_two_sub_batches_match_one_batch(torch):
         one.close()
 
 
+def test_encoder_host_entry_matches_device_entry(torch):
+    """sc_stream_encoder_encode_new_host (host mel in, output frames out, each
+    half of the streams copied in, encoded and copied out on its own CUDA
+    stream) gives the bits of encode_new + output, at 256 streams (two
+    halves) and 3 streams (one batch), steady steps and a short final batch."""
+    from stealcode_b200.ops import StreamEncoder
+
+    for n_streams in (256, 3):
+        cfg = model.EncoderConfig(n_layers=2)
+        m = model.random_model(cfg, seed=29)
+        mel = model.mel_stream(30, n_streams, 56 * 3 + 24, cfg.feat_in)
+        a, b = StreamEncoder(m, n_streams), StreamEncoder(m, n_streams)
+        out = torch.empty((n_streams * cfg.max_frames, cfg.d_model), dtype=torch.float32).pin_memory()
+        for t0, t1, fin in ((0, 56, False), (56, 112, False), (112, 168, False), (168, 192, True)):
+            x = np.ascontiguousarray(mel[:, t0:t1])
+            a.encode_new(torch.from_numpy(x).cuda(), t0, t1, fin)
+            ref = torch.as_tensor(_DevRows(*a.output()), device="cuda").cpu().numpy()
+            got = b.encode_new_host(x, t0, t1, fin, out=out)
+            assert b.total() == a.total()
+            assert got.shape == ref.shape
+            assert np.array_equal(got.numpy(), ref)
+        a.close()
+        b.close()
+
+
 def test_encoder_out_of_sync_is_rejected(torch):
     from stealcode_b200.ops import StreamEncoder
 
