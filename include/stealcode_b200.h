@@ -132,8 +132,11 @@ int sc_q8_gemm_q(const sc_q8w *w, const int8_t *xq, const float *dx,
  * loads the library holds until the process exits.  Calls whose scratch need
  * (sc_q8_gemm_workspace_bytes(t, k)) exceeds it return SC_ERR_INVALID; split
  * the frames over several calls.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture.  All calls share the one
+ * array's device address (cudaGetSymbolAddress) with that device current,
+ * and does the one-time set-up of every GEMM kernel this entry point can
+ * run (their status words' addresses and shared-memory limits), so later
+ * calls of any frame count make no such host calls; make that first call
+ * before any stream capture.  All calls share the one
  * array, so calls that overlap on the GPU (different streams, or different
  * host threads) race and corrupt each other's results; serialise them.  The
  * array keeps the previous call's contents, but every byte a call reads is
@@ -247,6 +250,25 @@ typedef struct {
 } sc_encoder_config;
 
 typedef struct sc_stream_encoder sc_stream_encoder;
+
+/* relu(Conv2d::forward(x)) for the pre-encode's pointwise convs conv.3 and
+ * conv.6 (1x1, stride 1; nemotron/weights.rs:399-443, the ReLU that follows
+ * each of them in pre_encode_forward, nemotron/encoder.rs:400-482), over
+ * n_streams windows at once, device pointers.  x is [n_streams *
+ * rows_per_stream][c_in] (channels last), y the same rows x c_out; w is
+ * [c_out][c_in], bias [c_out].  Row r of stream z is position sp_base + r
+ * of a window of `spatial` (time x frequency) positions: the reference runs
+ * the conv as one f32 GEMM per window (sgemm_kernel::gemm_into, with
+ * spatial as its column count), and its rounding depends on the position's
+ * column (one fused chain per output for whole 16-column blocks, 16 lane
+ * sums for the last spatial % 16 columns; simd_kernel.rs:560-727), which
+ * this call reproduces bit for bit.  c_in a multiple of 16 (<= 4096), c_out
+ * a multiple of 8, else SC_ERR_UNSUPPORTED.  Async on stream. */
+int sc_pre_encode_pointwise_relu(const float *x, const float *w,
+                                 const float *bias, float *y,
+                                 int64_t n_streams, int64_t rows_per_stream,
+                                 int64_t sp_base, int64_t spatial,
+                                 int64_t c_out, int64_t c_in, void *stream);
 
 /* Build a device streaming encoder for n_streams streams from the model's
  * tensors (Encoder::load, nemotron/encoder.rs:249-282, then the weights'

@@ -72,6 +72,7 @@ for _name, _res, _args in [
     ("orc_dwconv_forward", None, [_P, _S, _S, _S, _S, _S, _P, _P]),
     ("orc_glu_from", None, [_P, _S, _S, _P]),
     ("orc_silu_inplace", None, [_P, _S]),
+    ("orc_gemm_simd_into", None, [_S, _S, _S, _P, _P, _P, _P]),
 ]:
     _f = getattr(lib, _name)
     _f.restype = _res
@@ -138,6 +139,20 @@ def q8_block_dots(m, k, n, w, padded_row, block_bytes, qoff, x_km):
     dots = np.zeros((m, n, nb), dtype=np.int32)
     lib.orc_q8_block_dots(m, k, n, _p(w), padded_row, block_bytes, qoff, _p(x), _p(dots))
     return dots
+
+
+def gemm_simd_into(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """The reference's f32 GEMM c[m, n] = a[m, k] @ b[k, n] with its rounding
+    (simd_kernel.rs:448-727 gemm_simd_into)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    k2, n = b.shape
+    assert k == k2
+    c = np.zeros((m, n), np.float32)
+    bt = np.zeros((max(n * k, 1),), np.float32)
+    lib.orc_gemm_simd_into(m, k, n, _p(a), _p(b), _p(c), _p(bt))
+    return c
 
 
 def score_dot(qu, uh, qv, vh, kk, p, scale):

@@ -122,6 +122,14 @@ void orc_attn_stream_testloop(const float *q, const float *kv,
                               size_t left_chunks, size_t k_hi, size_t pos_off,
                               float *out);
 
+/* The reference's f32 GEMM (sgemm_kernel.rs:17-33 -> simd_kernel.rs:448-727,
+ * gemm_simd_into): c[m, n] = a[m, k] @ b[k, n] row-major with its rounding
+ * (fused chains for whole 8-row x 16-column tiles, 16-lane partial sums
+ * and an ordered lane sum for the remaining columns and rows). bt: n * k
+ * floats of scratch. */
+void orc_gemm_simd_into(size_t m, size_t k, size_t n, const float *a, const float *b, float *c,
+                        float *bt);
+
 /* Online CPU count used by nthreads <= 0. */
 int orc_num_cpus(void);
 

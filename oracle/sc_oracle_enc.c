@@ -255,7 +255,8 @@ static void lin_tm(const orc_enc *e, const lin_t *l, const float *x, size_t t, f
 }
 
 /* ------------------------------------------------------------------ */
-/* pre-encode: nemotron/weights.rs:386-524 (Conv2d::forward),           */
+/* pre-encode: nemotron/weights.rs:386-524 (Conv2d::forward; pointwise  */
+/* convs through simd_kernel.rs:448-727 gemm_simd_into),               */
 /* nemotron/encoder.rs:400-482 (pre_encode_forward)                     */
 /* ------------------------------------------------------------------ */
 static size_t conv_dim(size_t in, size_t pad0, size_t pad1, size_t k, size_t stride) {
@@ -269,15 +270,24 @@ static float *conv2d_forward(const conv2d_t *cv, const float *x, size_t t_in, si
     size_t c_out = cv->out, c_in = cv->inp;
     float *out = calloc(t_out * f_out * c_out, sizeof(float));
     if (cv->kh == 1 && cv->kw == 1 && stride == 1) {
-        /* pointwise: the f32 GEMM W [c_out, c_in] x [c_in, spatial], then bias */
+        /* pointwise (weights.rs:399-443): x [spatial, c_in] transposed to
+         * [c_in, spatial], the f32 GEMM W [c_out, c_in] x [c_in, spatial]
+         * (gemm_simd_into's rounding, sc_oracle_sgemm.c), bias added row by
+         * row, transposed back */
         size_t spatial = t_in * f_in;
+        float *xt = calloc(c_in * spatial + 1, sizeof(float));
+        float *yt = malloc(c_out * spatial * sizeof(float));
+        float *bt = malloc(c_in * spatial * sizeof(float));
         for (size_t sp = 0; sp < spatial; sp++)
-            for (size_t oc = 0; oc < c_out; oc++) {
-                float acc = 0.0f;
-                for (size_t ic = 0; ic < c_in; ic++)
-                    acc = fmaf(cv->w[oc * c_in + ic], x[sp * c_in + ic], acc);
-                out[sp * c_out + oc] = acc + cv->b[oc];
-            }
+            for (size_t ic = 0; ic < c_in; ic++) xt[ic * spatial + sp] = x[sp * c_in + ic];
+        orc_gemm_simd_into(c_out, c_in, spatial, cv->w, xt, yt, bt);
+        for (size_t oc = 0; oc < c_out; oc++)
+            for (size_t sp = 0; sp < spatial; sp++) yt[oc * spatial + sp] += cv->b[oc];
+        for (size_t sp = 0; sp < spatial; sp++)
+            for (size_t oc = 0; oc < c_out; oc++) out[sp * c_out + oc] = yt[oc * spatial + sp];
+        free(xt);
+        free(yt);
+        free(bt);
     } else {
         size_t in_groups = c_in / cv->groups;
         for (size_t ot = 0; ot < t_out; ot++)

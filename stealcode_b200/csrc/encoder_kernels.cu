@@ -619,6 +619,64 @@ __global__ void __launch_bounds__(kPwThreads)
   }
 }
 
+// The pointwise conv's positions that the reference's f32 GEMM sums in its
+// column-tail order.  The reference runs a 1x1 conv as W [c_out, c_in] x
+// X^T [c_in, spatial] per stream (nemotron/weights.rs:399-443); its GEMM
+// (simd_kernel.rs:448-727) gives each output of a whole 16-column block one
+// fused chain over k (pw_conv_relu_kernel above), but each of the last
+// spatial % 16 columns (gemm_cols_tail, :688-727) 16 lane accumulators --
+// lane l a fused chain over k = l, l + 16, ... -- summed in lane order from
+// -0.0, then + the k tail (k % 16 == 0 here, so + 0.0), then the bias.
+// One CTA per stream rewrites those positions' outputs (at most 15, all in
+// the window's last time row, which the step computes): the stream's tail
+// input rows are staged in shared memory, thread = output channel, four
+// positions at a time.  Row r of a stream is window position sp_base + r.
+__global__ void __launch_bounds__(256)
+    pw_conv_tail_kernel(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
+                        float *__restrict__ y, int rows_per_stream, int tail_row0, int n, int k) {
+  extern __shared__ __align__(16) float xs[];  // [rows_per_stream - tail_row0][k]
+  const int nt = rows_per_stream - tail_row0;
+  const int64_t row0 = (int64_t)blockIdx.x * rows_per_stream + tail_row0;
+  for (int i = threadIdx.x; i < nt * k; i += blockDim.x) xs[i] = x[row0 * k + i];
+  __syncthreads();
+  for (int oc = threadIdx.x; oc < n; oc += blockDim.x) {
+    const float *wr = w + (int64_t)oc * k;
+    const float bias = b[oc];
+    for (int p0 = 0; p0 < nt; p0 += 4) {
+      const int np = min(4, nt - p0);
+      float lane[4][16];
+#pragma unroll
+      for (int p = 0; p < 4; p++)
+#pragma unroll
+        for (int l = 0; l < 16; l++) lane[p][l] = 0.0f;
+      for (int kk = 0; kk < k; kk += 16) {
+        float wv[16];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float4 v = *reinterpret_cast<const float4 *>(wr + kk + 4 * q);
+          wv[4 * q] = v.x, wv[4 * q + 1] = v.y, wv[4 * q + 2] = v.z, wv[4 * q + 3] = v.w;
+        }
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+          if (p >= np) break;
+          const float *xr = xs + (p0 + p) * k + kk;
+#pragma unroll
+          for (int l = 0; l < 16; l++) lane[p][l] = __fmaf_rn(wv[l], xr[l], lane[p][l]);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < 4; p++) {
+        if (p >= np) break;
+        float r = -0.0f;
+#pragma unroll
+        for (int l = 0; l < 16; l++) r = __fadd_rn(r, lane[p][l]);
+        r = __fadd_rn(r, 0.0f);  // + the (empty) k tail
+        y[(row0 + p0 + p) * n + oc] = fmaxf(__fadd_rn(r, bias), 0.0f);
+      }
+    }
+  }
+}
+
 // [z][t][f][C] -> rows (z, j) of [C*f] (channel-major, frequency fastest)
 // for frames start_rel .. start_rel + c - 1.
 __global__ void flatten_kernel(const float *__restrict__ x, int t, int f, int C, int start_rel, int c,
@@ -754,13 +812,35 @@ int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int x_row0,
   return kOk;
 }
 
-int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t m_rows, int n, int k,
-                        cudaStream_t st) {
+int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t n_streams,
+                        int rows_per_stream, int64_t sp_base, int64_t spatial, int n, int k, cudaStream_t st) {
+  const int64_t m_rows = n_streams * rows_per_stream;
   if (m_rows <= 0) return kOk;
+  // the reference's f32 GEMM order is restated for k a multiple of 16 (no k
+  // tail) and whole 8-row tiles of output channels
+  if (k % 16 || n % 8 || k > 4096 || sp_base < 0 || sp_base + rows_per_stream > spatial) {
+    set_error("pw_conv: c_in %d (multiple of 16, <= 4096), c_out %d (multiple of 8), rows [%lld, %lld) of %lld",
+              k, n, (long long)sp_base, (long long)(sp_base + rows_per_stream), (long long)spatial);
+    return kErrUnsupported;
+  }
   dim3 grid((unsigned)ceil_div(m_rows, kPwBM), (unsigned)ceil_div(n, kPwBN));
   pw_conv_relu_kernel<<<grid, kPwThreads, 0, st>>>(x, w, b, y, m_rows, n, k);
   note_launch();
   SC_CUDA(cudaGetLastError());
+  const int64_t sp_tail = spatial / 16 * 16;
+  const int64_t tail_row0 = std::max<int64_t>(sp_tail - sp_base, 0);
+  if (tail_row0 < rows_per_stream) {
+    const size_t smem = (size_t)(rows_per_stream - tail_row0) * k * 4;
+    if (smem > 48 * 1024) {
+      set_error("pw_conv: %lld tail rows x %d channels exceed the staging buffer",
+                (long long)(rows_per_stream - tail_row0), k);
+      return kErrUnsupported;
+    }
+    pw_conv_tail_kernel<<<(unsigned)n_streams, 256, smem, st>>>(x, w, b, y, rows_per_stream, (int)tail_row0, n,
+                                                                 k);
+    note_launch();
+    SC_CUDA(cudaGetLastError());
+  }
   return kOk;
 }
 

@@ -162,14 +162,19 @@ __global__ void __launch_bounds__(kMidThreads, 1) q8_gemm_mid_kernel(const __gri
   }
 }
 
+static std::atomic<size_t> g_mid_smem_limit[64];  // per device
+
+int mid_gemm_prime() {
+  return raise_smem_limit((const void *)q8_gemm_mid_kernel, MidSmem::kBytes, g_mid_smem_limit);
+}
+
 int gemm_mid(const MidGemmArgs &a, cudaStream_t st) {
   if (a.m <= 0) return kOk;
   if (a.m_pad % kMidCols || a.m_pad < a.m || a.k_pad != a.w->nb * 32) {
     set_error("q8_gemm_mid: codes must be [m_pad][k_pad] with m_pad a multiple of %d", kMidCols);
     return kErrInvalid;
   }
-  static std::atomic<size_t> smem_limit[64];
-  const int rc = raise_smem_limit((const void *)q8_gemm_mid_kernel, MidSmem::kBytes, smem_limit);
+  const int rc = mid_gemm_prime();
   if (rc) return rc;
   MidParams p{a.w->qs, a.w->sc, a.w->nb, a.w->rows, a.xq, a.dx, a.m, a.m_pad, a.k_pad, a.bias, a.y,
               a.y_time_major, a.ldy, a.epi};

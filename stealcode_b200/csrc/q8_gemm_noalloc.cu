@@ -32,12 +32,19 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[SC_Q8_GEMM_NOAL
 static void *g_noalloc_ptr[64];
 static std::mutex g_noalloc_mu;
 
+// The first call on a device also does every GEMM path's own one-time set-up
+// (status words, shared-memory limits), so later calls of any frame count
+// make no such host calls.
 static int noalloc_scratch(int dev, void **out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void *p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    int rc = small_gemm_prime();
+    if (!rc) rc = mid_gemm_prime();
+    if (!rc) rc = tc_gemm_prime();
+    if (rc) return rc;
     g_noalloc_ptr[dev] = p;
   }
   *out = g_noalloc_ptr[dev];

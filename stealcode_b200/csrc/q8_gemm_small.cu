@@ -228,12 +228,18 @@ static size_t stream_smem(int mt, int nbl_max) {
          (size_t)nbl_max * mt * 4 + (size_t)8 * mt * 32 * 4 + 16;
 }
 
+// Shared-memory limit raised so far per device, per kernel instance.
+template <int MT, bool kDump>
+static std::atomic<size_t> *stream_smem_limit() {
+  static std::atomic<size_t> limit[64];
+  return limit;
+}
+
 template <int MT, bool kDump>
 static int launch_stream(StreamParams &p, int64_t groups, int64_t mtiles, cudaStream_t st) {
   auto kern = q8_gemm_stream_kernel<MT, kDump>;
   const size_t smem = stream_smem(MT, p.nbl_max);
-  static std::atomic<size_t> smem_limit[64];
-  const int rc = raise_smem_limit((const void *)kern, smem, smem_limit);
+  const int rc = raise_smem_limit((const void *)kern, smem, stream_smem_limit<MT, kDump>());
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)groups, (unsigned)p.ks, (unsigned)mtiles);
@@ -267,6 +273,25 @@ static unsigned *small_status_ptr() {
     ptr[dev].store(q, std::memory_order_release);  // every caller stores the same address
   }
   return q;
+}
+
+template <int MT>
+static int prime_stream() {
+  return raise_smem_limit((const void *)q8_gemm_stream_kernel<MT, false>, stream_smem(MT, kNblCap),
+                          stream_smem_limit<MT, false>());
+}
+
+int small_gemm_prime() {
+  if (!small_status_ptr()) {
+    set_error("q8_gemm: status word lookup failed");
+    return kErrCuda;
+  }
+  int rc = prime_stream<1>();
+  if (!rc) rc = prime_stream<2>();
+  if (!rc) rc = prime_stream<4>();
+  if (!rc) rc = prime_stream<8>();
+  if (!rc) rc = prime_stream<16>();
+  return rc;
 }
 
 int small_gemm_status(unsigned *out) {

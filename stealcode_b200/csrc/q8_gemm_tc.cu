@@ -405,12 +405,35 @@ int tc_gemm_status(unsigned *out) {
   return kOk;
 }
 
+// Shared-memory limit raised so far per device, per kernel instance.
+template <int FT, int DWG>
+static std::atomic<size_t> *tc_smem_limit() {
+  static std::atomic<size_t> limit[64];
+  return limit;
+}
+
+template <int FT, int DWG>
+static int prime_tc() {
+  return raise_smem_limit((const void *)q8_gemm_tc_kernel<FT, DWG>, TcSmem<FT, DWG>::kBytes,
+                          tc_smem_limit<FT, DWG>());
+}
+
+int tc_gemm_prime() {
+  if (!tc_status_ptr()) {
+    set_error("q8_gemm_tc: status word lookup failed");
+    return kErrCuda;
+  }
+  int rc = prime_tc<32, 1>();
+  if (!rc) rc = prime_tc<64, 2>();
+  if (!rc) rc = prime_tc<128, 4>();
+  return rc;
+}
+
 template <int FT, int DWG>
 static int launch_tc(const TcParams &p, int64_t groups, cudaStream_t st) {
   using L = TcSmem<FT, DWG>;
   auto kern = q8_gemm_tc_kernel<FT, DWG>;
-  static std::atomic<size_t> smem_limit[64];
-  const int rc = raise_smem_limit((const void *)kern, L::kBytes, smem_limit);
+  const int rc = raise_smem_limit((const void *)kern, L::kBytes, tc_smem_limit<FT, DWG>());
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)groups, (unsigned)(p.t_pad / FT), 1);

@@ -47,8 +47,10 @@ int launch_conv2d_3x3s2(const float *x, int64_t n_streams, int t_in, int x_row0,
 int launch_conv02_fused(const float *win, int64_t n_streams, int t_mel, int f_mel, const float *w0, const float *b0,
                         const float *w2, const float *b2, int C, int ta, int fa, int out_row0, int out_rows, int fb,
                         float *out, cudaStream_t st);
-int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t m_rows, int n, int k,
-                        cudaStream_t st);
+// Rows of stream z are window positions sp_base .. sp_base + rows_per_stream
+// - 1 of a conv input with `spatial` positions (time x frequency).
+int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y, int64_t n_streams,
+                        int rows_per_stream, int64_t sp_base, int64_t spatial, int n, int k, cudaStream_t st);
 int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int start_rel, int c, float *out,
                    cudaStream_t st, QOut qo);
 int launch_ln_quant(const float *x, int64_t ldx, const float *w, const float *b, float eps, int d, int64_t rows,
@@ -525,10 +527,12 @@ static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *
   // conv2 reads are rebuilt where it reads them)
   TRY(launch_conv02_fused(win, Z, (int)t_mel, c.feat_in, e->c0.w, e->c0.b, e->c2.w, e->c2.b, (int)C, (int)g.ta,
                           (int)g.fa, (int)g.r3, (int)(g.e3 - g.r3), (int)g.fb, p1, st));
-  TRY(launch_pw_conv_relu(p1, e->c3.w, e->c3.b, p2, Z * (g.e3 - g.r3) * g.fb, (int)C, (int)C, st));
+  TRY(launch_pw_conv_relu(p1, e->c3.w, e->c3.b, p2, Z, (int)((g.e3 - g.r3) * g.fb), g.r3 * g.fb, g.tb * g.fb,
+                          (int)C, (int)C, st));
   TRY(launch_conv2d_3x3s2(p2, Z, (int)g.tb, (int)g.r3, (int)(g.e3 - g.r3), (int)g.fb, (int)C, e->c5.w, e->c5.b,
                           (int)C, (int)g.r5, (int)g.n5, (int)g.fc, 0, p1, st));
-  TRY(launch_pw_conv_relu(p1, e->c6.w, e->c6.b, p0, Z * g.n5 * g.fc, (int)C, (int)C, st));
+  TRY(launch_pw_conv_relu(p1, e->c6.w, e->c6.b, p0, Z, (int)(g.n5 * g.fc), g.r5 * g.fc,
+                          conv_out(g.tb) * g.fc, (int)C, (int)C, st));
   // GEMM inputs are quantised by their producers straight into the
   // tensor-core operand layout (code buffers qx/qd, ping-pong)
   const int ft = tc_frame_tile(M);
@@ -781,7 +785,12 @@ static int encode_call(sc_stream_encoder *e, const float *mel_new, int64_t t0, i
     SC_CUDA(cudaEventRecord(e->ev_join, e->side));
     SC_CUDA(cudaStreamWaitEvent(st, e->ev_join, 0));
   }
-  if (!rc && host_io) SC_CUDA(cudaStreamSynchronize(st));
+  if (host_io) {
+    // even after an error: copies already queued may still be reading the
+    // caller's mel buffer or writing its output buffer
+    const cudaError_t se = cudaStreamSynchronize(st);
+    if (!rc && se != cudaSuccess) return cuda_fail(se, "cudaStreamSynchronize");
+  }
   if (rc) return rc;
   if (rows_out) *rows_out = Z * cf;
   e->hist_cur ^= 1;
@@ -880,6 +889,19 @@ int sc_stream_encoder_output(const sc_stream_encoder *e, const float **frames, i
   if (rows) *rows = e->n_streams * e->last_c;
   if (d) *d = e->cfg.d_model;
   return kOk;
+}
+
+int sc_pre_encode_pointwise_relu(const float *x, const float *w, const float *bias, float *y, int64_t n_streams,
+                                 int64_t rows_per_stream, int64_t sp_base, int64_t spatial, int64_t c_out,
+                                 int64_t c_in, void *stream) {
+  if (!x || !w || !bias || !y || n_streams < 0 || rows_per_stream < 0 || c_out <= 0 || c_in <= 0 ||
+      c_out > (1 << 20) || rows_per_stream > (1 << 24)) {
+    set_error("pre_encode_pointwise_relu: invalid argument");
+    return kErrInvalid;
+  }
+  if (n_streams == 0 || rows_per_stream == 0) return kOk;
+  return launch_pw_conv_relu(x, w, bias, y, n_streams, (int)rows_per_stream, sp_base, spatial, (int)c_out,
+                             (int)c_in, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -57,6 +57,13 @@ struct SmallGemmArgs {
 };
 int gemm_small(const SmallGemmArgs &a, int sm_count, cudaStream_t st);
 int small_gemm_status(unsigned *out);  // read and clear the kernels' status word
+// One-time per-device set-up of each GEMM path, done ahead of its first
+// launch on the current device: the status word's device address and the
+// kernels' largest shared-memory limits (otherwise done by the first call
+// that needs them).
+int small_gemm_prime();
+int mid_gemm_prime();
+int tc_gemm_prime();
 
 // q8_gemm_mid.cu: 16 < m <= 128 frames, q8_gemm_scalar's order (bit-exact)
 struct MidGemmArgs {

@@ -90,6 +90,36 @@ def _report(name, stats):
               + ("  [oracle device-rounding vs reference dispatch %.3g, device vs reference dispatch %.3g]" % s[5:] if len(s) > 5 else ""))
 
 
+@pytest.mark.parametrize("t,f,r0,rows", [(21, 33, 14, 7), (21, 33, 0, 21), (11, 17, 4, 7), (11, 17, 0, 11),
+                                         (48, 17, 40, 8), (16, 33, 10, 5)])
+def test_pointwise_conv_matches_oracle_bit_exact(torch, t, f, r0, rows):
+    """The pre-encode's pointwise convs (conv.3, conv.6) through the C ABI:
+    rows r0 .. r0 + rows - 1 of a t x f window for 3 streams, against the
+    oracle's relu(f32 GEMM + bias) over each stream's whole window, bit for
+    bit.  21 x 33 and 11 x 17 are the steady-state conv.3 / conv.6 windows
+    (5 and 11 positions in the GEMM's column-tail order, all in the last
+    time row); 48 x 17 has none (768 = 48 x 16)."""
+    Z, C = 3, 256
+    rng = np.random.default_rng(t * 1000 + r0)
+    w = (rng.standard_normal((C, C)) * 0.06).astype(np.float32)
+    b = (rng.standard_normal(C) * 0.02).astype(np.float32)
+    x = np.maximum(rng.standard_normal((Z, t * f, C)), 0).astype(np.float32)
+    want = np.stack([np.maximum(oracle.gemm_simd_into(w, x[z].T) + b[:, None], 0).T for z in range(Z)])
+    xs = np.ascontiguousarray(x[:, r0 * f:(r0 + rows) * f])
+    xd = torch.from_numpy(xs).cuda()
+    wd, bd = torch.from_numpy(w).cuda(), torch.from_numpy(b).cuda()
+    yd = torch.full((Z, rows * f, C), float("nan"), device="cuda")
+    _lib.check(_lib.lib.sc_pre_encode_pointwise_relu(xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), yd.data_ptr(),
+                                                    Z, rows * f, r0 * f, t * f, C, C, None))
+    torch.cuda.synchronize()
+    got = yd.cpu().numpy()
+    ref = np.ascontiguousarray(want[:, r0 * f:(r0 + rows) * f])
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    # the unsupported shapes are rejected, not mis-summed
+    assert _lib.lib.sc_pre_encode_pointwise_relu(xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), yd.data_ptr(),
+                                                 Z, rows * f, r0 * f, t * f, C, C - 8, None) == _lib.SC_ERR_UNSUPPORTED
+
+
 def test_pre_encode_matches_oracle(torch):
     """0 conformer blocks: the output frames are the pre-encode stack's
     (convs, flatten, the 4352 -> 1024 Q8_0 linear), first window, steady
@@ -276,3 +306,41 @@ def test_encoder_from_gguf_file_matches_memory(torch, tmp_path):
         assert np.array_equal(a.frames(z, 0, a.total()), b.frames(z, 0, b.total()))
     a.close()
     b.close()
+
+
+def test_benched_workload_matches_oracle(torch):
+    """The headline workload as bench.py runs it: the 24-layer model with
+    the bench's seed, 256 streams in two halves of 128 streams in flight (896
+    frames per GEMM: the tensor-core kernel's 64-frame tiles, two CTAs per
+    SM), 13 steps so the attention band reaches its steady 77 frames (steps
+    10-12); the streams at both edges of both halves match the oracle
+    (device rounding) every step."""
+    import bench
+    from stealcode_b200.ops import StreamEncoder
+
+    Z, n_steps = 256, 13
+    m = bench.encoder_model()
+    cfg = m.config
+    assert cfg.n_layers == 24 and bench.step_halves(Z) == [896, 896]
+    mel = model.mel_stream(bench.MODEL_SEED + 1, Z, bench.MEL_PER_STEP * n_steps, cfg.feat_in)
+    dev = StreamEncoder(m, Z)
+    edges = (0, 127, 128, 255)
+    refs = {z: oracle.StreamingEncoder(m) for z in edges}
+    for r in refs.values():
+        r.set_device_rounding()
+    worst, exact = 0.0, 1.0
+    for i in range(n_steps):
+        t0, t1 = bench.MEL_PER_STEP * i, bench.MEL_PER_STEP * (i + 1)
+        s = dev.total()
+        dev.encode_new(torch.from_numpy(np.ascontiguousarray(mel[:, t0:t1])).cuda(), t0, t1)
+        out = torch.as_tensor(_DevRows(*dev.output()), device="cuda").cpu().numpy()
+        assert out.shape == (Z * 7, cfg.d_model)
+        for z, r in refs.items():
+            assert r.encode_new(mel[z, :t1], t0, t1, False) == 0
+            got, ref = out[z * 7:(z + 1) * 7], r.frames(s, r.total())
+            worst = max(worst, _err(got, ref)[0])
+            exact = min(exact, float(np.mean(got == ref)))
+    print("bench workload (24 layers, 256 streams, 13 steps): edge streams worst max/RMS %.3g, "
+          "min exact fraction %.6f" % (worst, exact))
+    assert worst <= TOL
+    dev.close()

@@ -203,3 +203,107 @@ def test_exp_modes():
             differ += 1
     assert differ < 0.005 * len(xs)
     assert oracle.lib.orc_get_exp_mode() == 0
+
+
+# ---- the pointwise convs' f32 GEMM (simd_kernel.rs:448-727) ----------------
+def _fma32(a, b, c):
+    """Correctly rounded f32 fused multiply-add of float32 arrays: the
+    product is exact in float64, the sum's rounding error comes from
+    TwoSum, and it decides the one case where rounding the float64 sum to
+    f32 differs from rounding the exact sum (an exact f32 halfway point)."""
+    a64, b64, c64 = (np.asarray(v, np.float32).astype(np.float64) for v in (a, b, c))
+    p = a64 * b64
+    s = p + c64
+    bb = s - p
+    err = (p - (s - bb)) + (c64 - bb)
+    r = s.astype(np.float32)
+    r64 = r.astype(np.float64)
+    up = np.nextafter(r, np.float32(np.inf))
+    dn = np.nextafter(r, np.float32(-np.inf))
+    half_up = (up.astype(np.float64) - r64) / 2
+    half_dn = (r64 - dn.astype(np.float64)) / 2
+    d = s - r64
+    above = (d == half_up) & (err != 0)   # s is the midpoint between r and up
+    below = (d == -half_dn) & (err != 0)  # s is the midpoint between dn and r
+    r = np.where(above & (err > 0), up, np.where(above & (err < 0), r, r))
+    r = np.where(below & (err < 0), dn, r)
+    return r.astype(np.float32)
+
+
+def _gemm_tile8_cols_tail(a, b):
+    """gemm_tile8 (simd_kernel.rs:560-627) for m % 8 == 0, k % 16 == 0, m <=
+    256, with gemm_cols_tail (:688-727) for the last n % 16 columns, written
+    out loop by loop in numpy."""
+    m, k = a.shape
+    n = b.shape[1]
+    assert m % 8 == 0 and k % 16 == 0 and m <= 256
+    n_main = n // 16 * 16
+    c = np.zeros((m, n), np.float32)
+    acc = np.zeros((m, n_main), np.float32)
+    for kk in range(k):  # acc[r] = splat(a[r][kk]).mul_add(b row kk, acc[r])
+        acc = _fma32(a[:, kk:kk + 1], b[kk:kk + 1, :n_main], acc)
+    c[:, :n_main] = acc + np.float32(0.0)  # + ktail (empty: k % 16 == 0)
+    if n > n_main:
+        bt = b[:, n_main:].T  # [tail columns, k]
+        lanes = np.zeros((m, n - n_main, 16), np.float32)
+        for kk in range(0, k, 16):  # acc = av.mul_add(bv, acc), 16 lanes
+            lanes = _fma32(a[:, None, kk:kk + 16], bt[None, :, kk:kk + 16], lanes)
+        r = np.full((m, n - n_main), -0.0, np.float32)
+        for l in range(16):  # reduce_sum: ordered lane sum
+            r = (r + lanes[:, :, l]).astype(np.float32)
+        c[:, n_main:] = r + np.float32(0.0)
+    return c
+
+
+def test_fma32_emulation_known_answers():
+    one = np.float32(1.0)
+    eps = np.float32(2.0 ** -23)
+    # (1 + 2^-23)(1 - 2^-23) = 1 - 2^-46: a separately rounded product gives 1
+    assert _fma32(one + eps, one - eps, np.float32(-1.0)) == np.float32(-(2.0 ** -46))
+    # 1 + 2^-23 + (2^-24 - 2^-70): float64 rounds the sum onto the f32
+    # halfway point 1 + 2^-23 + 2^-24 (where ties-to-even goes up); the exact
+    # sum is below it, so the fused result is 1 + 2^-23
+    a = np.float32(2.0 ** -24) * (one + eps)
+    b = one - eps
+    assert _fma32(a, b, one + eps) == one + eps
+    x = np.float32(1.0) + np.float32(2.0 ** -22)
+    got = _fma32(np.float32(2.0 ** -24), np.float32(1.0 + 2.0 ** -20), x)
+    assert got == np.nextafter(x, np.float32(2))
+
+
+@pytest.mark.parametrize("t,f", [(21, 33), (11, 17)])
+def test_pointwise_conv_gemm_matches_restatement(t, f):
+    """The oracle's f32 GEMM, through which its pointwise convs run, equals
+    the reference's gemm_tile8 + gemm_cols_tail written out in numpy, bit
+    for bit, at the pre-encode's conv.3 / conv.6 window shapes (spatial =
+    693 = 21 x 33, 187 = 11 x 17: 5 and 11 tail columns), 256 -> 256
+    channels; and the tail columns' lane order is not the one-chain order."""
+    rng = np.random.default_rng(t * 100 + f)
+    spatial = t * f
+    w = (rng.standard_normal((256, 256)) * 0.06).astype(np.float32)
+    x = np.maximum(rng.standard_normal((256, spatial)), 0).astype(np.float32)
+    got = oracle.gemm_simd_into(w, x)
+    want = _gemm_tile8_cols_tail(w, x)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    n_main = spatial // 16 * 16
+    chain = np.zeros((256, spatial - n_main), np.float32)
+    for kk in range(256):
+        chain = _fma32(w[:, kk:kk + 1], x[kk:kk + 1, n_main:], chain)
+    assert not np.array_equal(chain, want[:, n_main:])
+
+
+def test_gemm_simd_into_rows_and_k_tails():
+    """Shapes off the fast tile: m % 8 != 0 (gemm_row), k % 16 != 0 (the
+    separately rounded k tail), n < 16: against float64 within the f32
+    error bound, and the tiled part against the numpy restatement."""
+    rng = np.random.default_rng(3)
+    for m, k, n in [(13, 40, 7), (264, 48, 35), (8, 16, 16), (300, 19, 3)]:
+        a = rng.standard_normal((m, k)).astype(np.float32)
+        b = rng.standard_normal((k, n)).astype(np.float32)
+        got = oracle.gemm_simd_into(a, b)
+        ref = a.astype(np.float64) @ b.astype(np.float64)
+        bound = 2 * k * 2.0 ** -24 * (np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64))
+        assert np.all(np.abs(got - ref) <= bound + 1e-30)
+        if m % 8 == 0 and k % 16 == 0 and m <= 256:
+            want = _gemm_tile8_cols_tail(a, b)
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32))

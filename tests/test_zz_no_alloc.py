@@ -5,12 +5,18 @@ all device memory).  Its scratch is a fixed device array inside the library.
 
 Checked through the C ABI against sc_q8_gemm (the entry point that takes a
 workspace) on two calls in a row, so the second call runs over the first
-call's leftovers in the shared array.  This file is collected last, and it
-passes both on its own in a fresh process and after the other tests.
+call's leftovers in the shared array, and against the oracle's
+q8_gemm_scalar (the reference's arithmetic for more than 16 frames, which
+the mid-size and tensor-core kernels reproduce bit for bit) for every frame
+count class: the streaming kernel (8 frames), the mid-size kernel (64) and
+the tensor-core kernel (256, and 896 frames at k = 4096, the largest batch
+the fixed array holds).  This file is collected last, and it passes both on
+its own in a fresh process and after the other tests.
 """
 import numpy as np
 import pytest
 
+import oracle
 from stealcode_b200 import _lib, synth
 from stealcode_b200.ops import SC_LAYOUT_FEATURE_MAJOR, SC_LAYOUT_TIME_MAJOR, Q8Mat
 
@@ -72,3 +78,31 @@ def test_noalloc_rejects_frames_beyond_the_scratch():
     assert rc == _lib.SC_ERR_INVALID
     assert "scratch" in _lib.last_error()
     assert _lib.lib.sc_q8_gemm_noalloc(None, None, 1, 0, 0, None, None, 0, 0, None) == _lib.SC_ERR_INVALID
+
+
+def _oracle_scalar(w_blocks, rows, k, x_tk):
+    """q8_gemm_scalar (sgemm_kernel.rs:132-202) on host: y [t, rows]."""
+    t = x_tk.shape[0]
+    y = oracle.q8_gemm_scalar(rows, k, t, w_blocks, (k // 32) * 34, 34, 2, np.ascontiguousarray(x_tk.T))
+    return np.ascontiguousarray(y.T)
+
+
+@pytest.mark.parametrize("t,rows,k", [(8, 1024, 1024), (64, 1024, 1024), (256, 512, 4096), (896, 256, 4096)])
+def test_noalloc_matches_oracle_in_every_frame_class(t, rows, k):
+    import torch
+
+    assert _lib.lib.sc_q8_gemm_workspace_bytes(t, k) <= SCRATCH
+    wb = synth.q8_weights(910 + t, rows, k)
+    mat = Q8Mat(wb, rows, k)
+    x = synth.normal(911 + t, (t, k))
+    xd = torch.from_numpy(x).cuda()
+    outs = [_no_alloc(torch, mat, xd, t, SC_LAYOUT_TIME_MAJOR) for _ in range(2)]  # two calls in a row
+    torch.cuda.synchronize()
+    ref = _oracle_scalar(wb, rows, k, x)
+    for y in outs:
+        got = y.cpu().numpy()
+        assert np.isfinite(got).all()
+        if t > 16:  # the reference's scalar order: bit for bit
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        else:       # the SIMD dispatch's order differs in the last bits
+            assert _rms_err(got, ref) <= TOL_RMS
