@@ -64,6 +64,13 @@ int sc_device_status(uint32_t *flags);
  * reference. */
 long long sc_launch_count(void);
 
+/* Test hook for the allocation-failure paths: after this call the library's
+ * device allocations fail (the entry point that needed one returns
+ * SC_ERR_ALLOC and frees what it had allocated) once their total since the
+ * call would exceed `bytes`; bytes < 0 removes the cap.  No counterpart in
+ * the reference. */
+int sc_debug_set_device_alloc_cap(int64_t bytes);
+
 /* ---- weights --------------------------------------------------------- */
 
 /* Repack a GGUF Q8_0 tensor once into the device layout: int8 quants in

@@ -82,6 +82,7 @@ SIGNATURES = {
     "sc_stream_encoder_encode_new_host": (c_int, [_P, _P, c_int64, c_int64, c_int32, _P, _P, _P]),
     "sc_stream_encoder_dump": (c_int, [_P, c_int32, _P, POINTER(c_int64)]),
     "sc_stream_encoder_destroy": (c_int, [_P]),
+    "sc_debug_set_device_alloc_cap": (c_int, [_I]),
     "sc_pre_encode_pointwise_relu": (c_int, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
     "sc_rnnt_create": (c_int, [_P, _P, c_int, _I, POINTER(c_void_p)]),
     "sc_rnnt_decode_frames": (c_int, [_P, _P, _I, _P]),

@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
         if (p.qout.xq) {  // the warp's 32 dims are one block of the out-proj input
           float sblk;
           const int8_t q = warp_quantize_block(acc[j], true, sblk);
-          p.qout.xq[qout_code_index(p.qout, z * zq + p.r0 + j, hoff + t)] = q;
+          p.qout.xq[qout_code_index(p.qout, z * zq + p.r0 + j, hoff + t)] = code_half(q);
           if (lane == 0) p.qout.dx[qout_dx_index(p.qout, z * zq + p.r0 + j, (hoff + t) >> 5)] = sblk;
         }
       }

@@ -179,21 +179,18 @@ __device__ __forceinline__ void quant_lane(const float (&v)[E], const QOut &qo, 
     for (int e = 0; e < 32; e++) amax = fmaxf(amax, fabsf(v[32 * blk + e]));
     const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
     const float inv = __fdiv_rn(1.0f, sc);
-    uint32_t words[8];
-#pragma unroll
-    for (int w4 = 0; w4 < 8; w4++) {
-      uint32_t wd = 0;
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const int8_t code = amax != 0.0f ? rust_round_i8(__fmul_rn(v[32 * blk + 4 * w4 + q], inv)) : (int8_t)0;
-        wd |= (uint32_t)(uint8_t)code << (8 * q);
-      }
-      words[w4] = wd;
-    }
     const int i = i0 + 32 * blk;
-    int8_t *dst = qo.xq + qout_code_index(qo, f, i);
-    *reinterpret_cast<uint4 *>(dst) = make_uint4(words[0], words[1], words[2], words[3]);
-    *reinterpret_cast<uint4 *>(dst + (int64_t)qo.ft * 16) = make_uint4(words[4], words[5], words[6], words[7]);
+    __half *dst = qo.xq + qout_code_index(qo, f, i);
+#pragma unroll
+    for (int c8 = 0; c8 < 4; c8++) {  // four 8-feature chunks, 16 bytes each
+      __half h8[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+        h8[q] = code_half(amax != 0.0f ? rust_round_i8(__fmul_rn(v[32 * blk + 8 * c8 + q], inv)) : (int8_t)0);
+      uint4 u;
+      memcpy(&u, h8, 16);
+      *reinterpret_cast<uint4 *>(dst + (int64_t)c8 * qo.ft * 8) = u;
+    }
     qo.dx[qout_dx_index(qo, f, i / 32)] = sc;
   }
 }
@@ -692,7 +689,7 @@ __global__ void flatten_kernel(const float *__restrict__ x, int t, int f, int C,
     float sblk;
     const int8_t q = warp_quantize_block(v, valid, sblk);
     if (i < (C * f + 31) / 32 * 32) {
-      qo.xq[qout_code_index(qo, row, i)] = q;
+      qo.xq[qout_code_index(qo, row, i)] = code_half(q);
       if ((threadIdx.x & 31) == 0) qo.dx[qout_dx_index(qo, row, i / 32)] = sblk;
     }
   }
@@ -714,7 +711,7 @@ __global__ void prompt_cat_quant_kernel(const float *__restrict__ x, int64_t row
   const float v = i < d ? x[row * d + i] : (valid && i - d == pid ? 1.0f : 0.0f);
   float sblk;
   const int8_t q = warp_quantize_block(v, valid, sblk);
-  qo.xq[qout_code_index(qo, row, i)] = q;
+  qo.xq[qout_code_index(qo, row, i)] = code_half(q);
   if ((threadIdx.x & 31) == 0) qo.dx[qout_dx_index(qo, row, i / 32)] = sblk;
 }
 

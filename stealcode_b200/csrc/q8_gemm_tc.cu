@@ -1,74 +1,100 @@
 // q8_gemm_tc.cu -- large-M Q8_0 GEMM on the 5th-generation tensor cores
-// (tcgen05.mma kind::i8, int32 accumulators in tensor memory).
+// (tcgen05.mma kind::f16 with f32 accumulators in tensor memory), persistent.
 //
 // Same arithmetic as the reference (sgemm_kernel.rs:156-201): for every 32-wide
-// K block the exact int32 dot of int8 weights and int8 activation codes, scaled
-// by dw[n, b] * dx[col, b] and accumulated in f32.  Because each K block has
-// its own pair of scales, the int32 accumulator cannot run across blocks:
-// every tcgen05.mma covers exactly one block (M = 128 weight rows, N = FT
-// frames, K = 32) into a fresh TMEM buffer, and drain warps read it back
-// (tcgen05.ld), scale it and add it to f32 accumulators in registers while the
-// tensor core already computes the next block into the other buffer.
+// K block the exact dot of the int8 weight codes and int8 activation codes,
+// scaled by dw[n, b] * dx[col, b] and accumulated in f32 with three roundings
+// (acc + (dw * dx) * dot).  Because each K block has its own pair of scales,
+// the dot cannot be accumulated across blocks: every block is its own MMA
+// into a TMEM accumulator, and drain warps read it back (tcgen05.ld), scale it
+// and add it to f32 accumulators in registers while the tensor core computes
+// the next blocks into the other accumulators.
 //
-// CTA roles (warp-specialised, one CTA per 128-row group x FT-frame tile):
-//   warp 0       producer: 1-D bulk copies (TMA engine, no multicast) into a
-//                ring of shared-memory stages of kTcKb K blocks each: the
-//                blocks' weight tiles (the row-group tile layout is already
-//                the no-swizzle K-major UMMA operand layout), activation
-//                tiles, weight scales and activation scales, one copy each;
-//   warp 1       allocates TMEM and issues one tcgen05.mma per block (single
-//                thread) into a rotating TMEM accumulator, committing to the
-//                accumulator's "full" barrier, and to the stage's "empty"
-//                barrier after the stage's last block;
-//   warps 2..    drain warpgroups: each thread owns one weight row (TMEM lane)
-//                and 32 frame columns; per block it reads the accumulator
-//                (tcgen05.ld), releases it, and applies the block's scales in
-//                packed f32x2 arithmetic in the reference scalar oracle's
-//                order; the int32 -> f32 conversion is an exact integer add.
+// The codes are held as f16 (every int8 value is an f16 integer): a block's
+// dot is two K = 16 MMAs of kind::f16 into an f32 accumulator.  Every product
+// is an integer of magnitude <= 127^2 and every partial sum stays below 2^24,
+// so the f32 accumulator holds the exact integer dot, and the drain needs no
+// int -> f32 conversion: three f32 operations per output and block.
+//
+// Persistent CTAs (one per SM, all 512 TMEM columns): CTA c computes tiles
+// c, c + grid, ... of 128 weight rows x FT frames; the operand and scale
+// rings and the TMEM accumulator ring run on across tiles, so the next
+// tile's copies and MMAs overlap the current tile's epilogue.
+//
+// CTA roles (warp-specialised):
+//   warp 0       producer: one thread issues 1-D bulk copies (TMA engine, no
+//                multicast): per operand slot the f16 weight tiles and the
+//                f16 activation tiles of kTcKb blocks, per scale chunk the
+//                weight and activation scales of kTcScB blocks;
+//   warp 1       allocates TMEM; one thread issues two MMAs per block into a
+//                rotating accumulator and commits to its "full" barrier, and
+//                to the operand slot's "empty" barrier after its last block;
+//   warps 2..17  drain: 4 warpgroups, each thread one weight row (its TMEM
+//                lane) and FT/4 frame columns; then the tile's epilogue.
 // Every mbarrier wait is bounded; a wait that gives up sets a status bit and
-// the kernel runs to its end without waiting again, so it cannot hang.
+// that role stops waiting, so the kernel cannot hang.
 #include "sc_device.cuh"
 #include "sc_kernels.cuh"
 
 namespace sc {
 
-// K blocks per shared-memory stage: one bulk copy per operand moves
-// kTcKb consecutive blocks (weight tiles, activation tiles and both scale
-// rows are contiguous in their layouts), so a stage costs four copies for
-// kTcKb blocks.  Bulk copies issued by one thread complete one after
-// another, so each (copy kind, stage phase) pair has its own producer lane.
-#ifndef SC_TC_KB
-#define SC_TC_KB 4
+// Grid: one CTA per SM, each looping over tiles (0), or one CTA per tile (1).
+#ifndef SC_TC_GRID_TILES
+#define SC_TC_GRID_TILES 0
 #endif
-#ifndef SC_TC_STAGES
-#define SC_TC_STAGES 4
-#endif
-#ifndef SC_TC_PHASES
-#define SC_TC_PHASES 2
-#endif
-constexpr int kTcKb = SC_TC_KB;
-constexpr int kTcStages = SC_TC_STAGES;
-constexpr int kTcPhases = SC_TC_PHASES;
-static_assert(kTcStages >= kTcPhases, "every producer phase needs a stage in flight");
-// TMEM accumulators (FT columns each): the MMA of a block may start once
-// the drain has read the accumulator it reuses.  128-frame tiles take all
-// 512 columns (one CTA per SM); 64-frame tiles take 256, so two CTAs share
-// an SM (their drains run independently, and twice as many tiles per wave
-// even out the last wave of a grid of a few hundred tiles).
-template <int FT>
-constexpr int tc_acc_bufs() { return FT == 64 ? 4 : (512 / FT < 8 ? 512 / FT : 8); }
-template <int FT>
-constexpr int tc_ctas_per_sm() { return FT == 64 ? 2 : 1; }
+constexpr int kTcKb = 4;        // K blocks per operand copy (one ring slot)
+constexpr int kTcScB = 8;       // K blocks per scale chunk
+constexpr int kTcDrainWarps = 16;
+constexpr int kTcThreads = 64 + 32 * kTcDrainWarps;
 
 static __device__ unsigned g_tc_status;
 
+// Shared memory of one CTA:
+//   operand ring  kOps slots of kTcKb consecutive K blocks of one tile:
+//                 f16 weight tiles [kTcKb][4][128][8] and f16 activation
+//                 tiles [kTcKb][4][FT][8], one bulk copy each; a slot is
+//                 refilled as soon as the MMAs of its blocks complete;
+//   scale ring    kScs slots of kTcScB consecutive K blocks of one tile:
+//                 f16 weight scales [kTcScB][128] and f32 activation scales
+//                 [kTcScB][FT]; a slot is refilled once every drain warp has
+//                 scaled its blocks;
+//   transpose     per drain warp 8 frames x 32 rows of f32, through which the
+//                 epilogue turns a thread's row of outputs into 16-byte
+//                 stores of four rows.
+// The copy engine's time per bulk copy hardly depends on its size up to
+// 32 KB, so copies are few and large.
+template <int FT>
+struct TcCfg {
+  static constexpr int kCols = FT / 4;                  // frame columns per drain thread
+  static constexpr int kAcc = 512 / FT;                 // TMEM accumulators of FT columns
+  static constexpr int kA = kTcKb * 8192;               // f16 weight tiles of a slot
+  static constexpr int kOp = kA + kTcKb * FT * 64;      // + f16 activation tiles
+  static constexpr int kScW = kTcScB * SC_GROUP_ROWS * 2;
+  static constexpr int kSc = kScW + kTcScB * FT * 4;
+  static constexpr int kScs = 2;
+  static constexpr int kTr = kTcDrainWarps * 8 * 32 * 4;
+  static constexpr int kOps = (220 * 1024 - kScs * kSc - kTr) / kOp;
+  static constexpr int kBars = 8 * (2 * kOps + 2 * kScs + 2 * kAcc + 1);
+  static constexpr int kMisc = 16 + 4 * (kOps + kScs);  // TMEM slot, fail flag, last round per slot
+  static constexpr int kBytes = kOps * kOp + kScs * kSc + kTr + kBars + kMisc;
+  static_assert(kOps >= 2, "the operand ring needs two slots");
+  static_assert(kBytes <= 227 * 1024, "shared memory");
+  static_assert(2 * kBytes > 228 * 1024, "one CTA per SM: it takes all 512 TMEM columns");
+};
+
+// Epilogue store modes (uniform per launch).
+enum : int {
+  kStoreDirect = 0,  // each thread stores its outputs (any layout)
+  kStoreVec = 1,     // time-major y, 16-byte stores of four rows
+};
+
 struct TcParams {
-  const int8_t *qs;      // weight tiles
-  const __half *sc;      // weight scales [g][b][128]
+  const __half *qh;      // f16 weight tiles [G][nb][4][128][8]
+  const __half *sc;      // weight scales [G][nb][128]
   int64_t nb, n_rows;
-  const int8_t *xq;      // activation tiles [t_pad/FT][nb][2][FT][16]
-  const float *dx;       // activation scales [nb][t_pad]
-  int64_t t, t_pad;
+  const __half *xq;      // f16 activation tiles [t_pad/FT][nb][4][FT][8]
+  const float *dx;       // activation scales [t_pad/FT][nb][FT]
+  int64_t t, t_pad, n_ft, n_tiles;
   const float *bias;
   float *y;
   int y_time_major;
@@ -76,6 +102,7 @@ struct TcParams {
   unsigned *status;
   Epilogue epi;
   QOut qout;
+  int store;       // kStoreDirect / kStoreVec (y, no codes)
   float neg_zero;  // -0.0f, opaque to the compiler (see the drain)
 };
 
@@ -85,7 +112,7 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 // Shared-memory matrix descriptor, no swizzle, K-major canonical layout:
 // core matrices of 8 rows x 16 bytes, `lbo` bytes between the two 16-byte
-// K halves, `sbo` bytes between consecutive 8-row groups.
+// K chunks of a row's 32 bytes, `sbo` bytes between 8-row groups.
 __device__ __forceinline__ uint64_t umma_desc(const void *smem, uint32_t lbo, uint32_t sbo) {
   const uint32_t a = smem_u32(smem);
   uint64_t d = 0;
@@ -96,18 +123,18 @@ __device__ __forceinline__ uint64_t umma_desc(const void *smem, uint32_t lbo, ui
   return d;               // base offset 0, layout type 0 = no swizzle
 }
 
-// Instruction descriptor: kind::i8, D = s32, A = B = signed int8, both
-// K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t umma_idesc_i8(int n) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// Instruction descriptor: kind::f16, D = f32, A = B = f16, both K-major,
+// M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -117,7 +144,10 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+template <int N>
+__device__ __forceinline__ void tc_ld(uint32_t taddr, uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tc_ld<32>(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -128,20 +158,58 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+template <>
+__device__ __forceinline__ void tc_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+template <>
+__device__ __forceinline__ void tc_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Waits for this thread's tcgen05.ld results; the registers pass through the
+// statement, so no use of them can be scheduled before the wait.
+template <int N>
+__device__ __forceinline__ void tc_wait_ld(uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tc_wait_ld<32>(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])::"memory");
+}
+template <>
+__device__ __forceinline__ void tc_wait_ld<8>(uint32_t (&r)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7])::"memory");
+}
+template <>
+__device__ __forceinline__ void tc_wait_ld<16>(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])::"memory");
+}
 
-template <int FT, int DWG>
-struct TcSmem {
-  static constexpr int kA = SC_TILE_BYTES * kTcKb;      // kTcKb tiles of 128 x 32 int8
-  static constexpr int kB = FT * 32 * kTcKb;            // kTcKb tiles of FT x 32 int8
-  static constexpr int kS = SC_GROUP_ROWS * 2 * kTcKb;  // f16 weight scales [kTcKb][128]
-  static constexpr int kD = FT * 4 * kTcKb;             // f32 activation scales [kTcKb][FT]
-  static constexpr int kStage = kA + kB + kS + kD;      // all multiples of 16
-  static constexpr int kAcc = tc_acc_bufs<FT>();
-  static constexpr int kBars = 8 * (2 * kTcStages + 2 * kAcc) + 16;
-  static constexpr int kBytes = kTcStages * kStage + kBars;
-};
+// A barrier wait by lane 0 for the whole warp (one shared-memory poll
+// instead of 32); __syncwarp orders the lanes' later reads after it.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity) ? 1u : 0u;
+  __syncwarp();
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 
 // Packed f32x2 arithmetic (two lanes of f32 per 64-bit register pair).
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
@@ -165,23 +233,53 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   return d;
 }
 
-template <int FT, int DWG>
-__global__ void __launch_bounds__(64 + 128 * DWG, tc_ctas_per_sm<FT>()) q8_gemm_tc_kernel(const __grid_constant__ TcParams p) {
-  using L = TcSmem<FT, DWG>;
-  static_assert(FT == 32 * DWG, "each drain warpgroup owns 32 frame columns");
-  constexpr int kAcc = L::kAcc;
+// acc += (dw * dx) * dot over one block of the thread's C columns, with the
+// three roundings of the reference's scalar oracle (sgemm_kernel.rs:185-196);
+// r holds the block's exact integer dots as f32.  fma(s, dot, -0) is the
+// rounded product s * dot (an exact zero keeps its sign: +0 + -0 = +0,
+// -0 + -0 = -0); -0 arrives as a kernel parameter (nz2) so the code
+// generator cannot turn the fma back into a multiply and fuse it into the
+// following add.
+// The thread's columns are drained in two halves of H = C / 2 (acc pairs
+// OFF .. OFF + H/2 - 1), so one half's accumulator load is in flight while
+// the other half is scaled.
+template <int H, int OFF, int NACC>
+__device__ __forceinline__ void drain_half(uint64_t (&acc)[NACC], const uint32_t (&r)[H], uint64_t dw2,
+                                           const uint64_t *dx2, uint64_t nz2) {
+#pragma unroll
+  for (int jj = 0; jj < H / 2; jj++) {
+    const uint64_t s2 = fmul2(dw2, dx2[jj]);  // dw * dx per column
+    const uint64_t f2 = (uint64_t)r[2 * jj] | ((uint64_t)r[2 * jj + 1] << 32);
+    acc[OFF + jj] = fadd2(acc[OFF + jj], ffma2(s2, f2, nz2));
+  }
+}
+
+// Tile t of the work list is row group t / n_ft, frame tile t % n_ft: the
+// tiles in flight at once share their row groups' weights in L2.  A CTA's
+// blocks are numbered gb = 0, 1, ... over its tiles in order; operand slots
+// (go), scale chunks (gc) and accumulators (gb % kAcc) are numbered the same
+// way by every role.
+template <int FT>
+__global__ void __launch_bounds__(kTcThreads, 1) q8_gemm_tc_kernel(const __grid_constant__ TcParams p) {
+  using L = TcCfg<FT>;
+  constexpr int C = L::kCols, kAcc = L::kAcc, kOps = L::kOps, kScs = L::kScs;
   extern __shared__ __align__(1024) unsigned char smem[];
-  uint64_t *full = (uint64_t *)(smem + kTcStages * L::kStage);
-  uint64_t *empty = full + kTcStages;
-  uint64_t *tfull = empty + kTcStages;
+  unsigned char *ops = smem;                          // operand ring
+  unsigned char *scs = smem + kOps * L::kOp;          // scale ring
+  float *trs = (float *)(scs + kScs * L::kSc);        // transpose buffers
+  uint64_t *op_full = (uint64_t *)((unsigned char *)trs + L::kTr);
+  uint64_t *op_empty = op_full + kOps;
+  uint64_t *sc_full = op_empty + kOps;
+  uint64_t *sc_empty = sc_full + kScs;
+  uint64_t *tfull = sc_empty + kScs;
   uint64_t *tempty = tfull + kAcc;
-  uint32_t *tmem_slot = (uint32_t *)(tempty + kAcc);
+  uint64_t *mma_done = tempty + kAcc;
+  uint32_t *misc = (uint32_t *)(mma_done + 1);  // [0] TMEM base, [1] fail flag
+  int *last_round = (int *)(misc + 4);          // [kOps + kScs]: last fill of each slot
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t g = blockIdx.x, ft = blockIdx.y;
   const int nb = (int)p.nb;
-  const int n_stages = (nb + kTcKb - 1) / kTcKb;
-  constexpr uint32_t kTmemCols = FT * kAcc < 32 ? 32 : FT * kAcc;
+  const int opt = (nb + kTcKb - 1) / kTcKb;    // operand slots per tile
 
   // All inputs are read after the previous kernel on the stream completes;
   // TMEM is allocated after that too, so a CTA never holds tensor memory
@@ -190,196 +288,265 @@ __global__ void __launch_bounds__(64 + 128 * DWG, tc_ctas_per_sm<FT>()) q8_gemm_
   pdl_wait();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; s++) {
-      mbar_init(&full[s], 4);             // one arrive.expect_tx per copy lane
-      mbar_init(&empty[s], 1 + 4 * DWG);  // MMA commit + one arrival per drain warp
+    for (int s = 0; s < kOps; s++) {
+      mbar_init(&op_full[s], 1);   // the producer's arrival; the copies' bytes
+      mbar_init(&op_empty[s], 1);  // the commit after the slot's last MMA
     }
+    for (int s = 0; s < kScs; s++) {
+      mbar_init(&sc_full[s], 1);
+      mbar_init(&sc_empty[s], kTcDrainWarps);  // every drain warp
+    }
+    for (int s = 0; s < kOps + kScs; s++) last_round[s] = -1;
     for (int b = 0; b < kAcc; b++) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4 * DWG);
+      mbar_init(&tempty[b], kTcDrainWarps);
     }
+    mbar_init(mma_done, 1);
+    misc[1] = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(misc)),
+                 "r"(512)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_base = misc[0];
 
   bool ok = true;
   if (warp == 0) {
-    if (lane < 4 * kTcPhases) {
-      const int cp = lane & 3, phase = lane >> 2;  // copy kind, stage phase
-      for (int si = phase; si < n_stages && ok; si += kTcPhases) {
-        const int s = si % kTcStages;
-        if (!mbar_wait(&empty[s], ((uint32_t)(si / kTcStages) & 1u) ^ 1u)) { ok = false; break; }
-        const int b0 = si * kTcKb, nblk = nb - b0 < kTcKb ? nb - b0 : kTcKb;
-        unsigned char *st = smem + s * L::kStage;
-        // each copy lane arrives with its own byte count before its copy, so
-        // the stage completes only when all four have arrived and landed
-        if (cp == 0) {
-          mbar_arrive_expect_tx(&full[s], nblk * SC_TILE_BYTES);
-          bulk_g2s(st, p.qs + (g * p.nb + b0) * SC_TILE_BYTES, nblk * SC_TILE_BYTES, &full[s]);
-        } else if (cp == 1) {
-          mbar_arrive_expect_tx(&full[s], nblk * FT * 32);
-          bulk_g2s(st + L::kA, p.xq + (ft * p.nb + b0) * (int64_t)(FT * 32), nblk * FT * 32, &full[s]);
-        } else if (cp == 2) {
-          mbar_arrive_expect_tx(&full[s], nblk * SC_GROUP_ROWS * 2);
-          bulk_g2s(st + L::kA + L::kB, p.sc + (g * p.nb + b0) * SC_GROUP_ROWS, nblk * SC_GROUP_ROWS * 2, &full[s]);
-        } else {
-          mbar_arrive_expect_tx(&full[s], nblk * FT * 4);
-          bulk_g2s(st + L::kA + L::kB + L::kS, p.dx + (ft * p.nb + b0) * (int64_t)FT, nblk * FT * 4, &full[s]);
+    // ---- producer: one thread issues every copy (lanes of one warp that
+    // wait on different barriers would serialise) ----
+    if (lane == 0) {
+      int go = 0, gc = 0;
+      for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
+        const int64_t g = tile / p.n_ft, ft = tile % p.n_ft;
+        for (int j = 0; j < opt && ok; j++, go++) {
+          const int k0 = j * kTcKb;
+          if (k0 % kTcScB == 0) {  // the scale chunk that starts here
+            const int s = gc % kScs, nblk = nb - k0 < kTcScB ? nb - k0 : kTcScB;
+            if (!mbar_wait(&sc_empty[s], ((uint32_t)(gc / kScs) & 1u) ^ 1u)) { ok = false; break; }
+            unsigned char *dst = scs + s * L::kSc;
+            last_round[kOps + s] = gc / kScs;
+            mbar_arrive_expect_tx(&sc_full[s], nblk * (SC_GROUP_ROWS * 2 + FT * 4));
+            bulk_g2s(dst, p.sc + (g * p.nb + k0) * SC_GROUP_ROWS, nblk * SC_GROUP_ROWS * 2, &sc_full[s]);
+            bulk_g2s(dst + L::kScW, p.dx + (ft * p.nb + k0) * (int64_t)FT, nblk * FT * 4, &sc_full[s]);
+            gc++;
+          }
+          const int s = go % kOps, nblk = nb - k0 < kTcKb ? nb - k0 : kTcKb;
+          if (!mbar_wait(&op_empty[s], ((uint32_t)(go / kOps) & 1u) ^ 1u)) { ok = false; break; }
+          unsigned char *dst = ops + s * L::kOp;
+          last_round[s] = go / kOps;
+          mbar_arrive_expect_tx(&op_full[s], nblk * (8192 + FT * 64));
+          bulk_g2s(dst, p.qh + (g * p.nb + k0) * 4096, nblk * 8192, &op_full[s]);
+          bulk_g2s(dst + L::kA, p.xq + (ft * p.nb + k0) * (int64_t)(FT * 32), nblk * FT * 64, &op_full[s]);
         }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
+    // ---- MMA issuer ----
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_i8(FT);
-      int b = 0;
-      for (int si = 0; si < n_stages && ok; si++) {
-        const int s = si % kTcStages;
-        if (!mbar_wait(&full[s], (uint32_t)(si / kTcStages) & 1u)) { ok = false; break; }
-        const int nblk = nb - si * kTcKb < kTcKb ? nb - si * kTcKb : kTcKb;
-        const unsigned char *st = smem + s * L::kStage;
-        for (int i = 0; i < nblk; i++, b++) {
-          const int buf = b % kAcc;
-          if (!mbar_wait(&tempty[buf], ((uint32_t)(b / kAcc) & 1u) ^ 1u)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t ad = umma_desc(st + i * SC_TILE_BYTES, 2048, 128);
-          const uint64_t bd = umma_desc(st + L::kA + i * FT * 32, FT * 16, 128);
-          tc_mma_i8(tmem_base + (uint32_t)(buf * FT), ad, bd, idesc, 0u);
-          tc_commit(&tfull[buf]);
+      const uint32_t idesc = umma_idesc_f16(FT);
+      // descriptors of slot 0's first block; a block's and a K half's are
+      // these plus their byte offset / 16 (the start-address field, bits
+      // 0-13, holds shared-memory addresses below 256 KB without carrying)
+      const uint64_t a0 = umma_desc(ops, 2048, 128), b0 = umma_desc(ops + L::kA, FT * 16, 128);
+      int go = 0, gb = 0;
+      for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
+        for (int j = 0; j < opt && ok; j++, go++) {
+          const int s = go % kOps, nblk = nb - j * kTcKb < kTcKb ? nb - j * kTcKb : kTcKb;
+          if (!mbar_wait(&op_full[s], (uint32_t)(go / kOps) & 1u)) { ok = false; break; }
+          const uint64_t as = a0 + (uint64_t)((s * L::kOp) >> 4), bs = b0 + (uint64_t)((s * L::kOp) >> 4);
+          for (int i = 0; i < nblk; i++, gb++) {
+            const int buf = gb % kAcc;
+            if (!mbar_wait(&tempty[buf], ((uint32_t)(gb / kAcc) & 1u) ^ 1u)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d = tmem_base + (uint32_t)(buf * FT);
+            const uint64_t ai = as + (uint64_t)((i * 8192) >> 4), bi = bs + (uint64_t)((i * FT * 64) >> 4);
+            tc_mma_f16(d, ai, bi, idesc, 0u);                                            // K 0-15
+            tc_mma_f16(d, ai + (4096 >> 4), bi + (uint64_t)((FT * 32) >> 4), idesc, 1u);  // K 16-31
+            tc_commit(&tfull[buf]);
+          }
+          if (ok) tc_commit(&op_empty[s]);  // the slot is free once its MMAs complete
         }
-        tc_commit(&empty[s]);  // the stage's tiles are free once its MMAs complete
       }
+      // every MMA this thread issued completes before TMEM is released
+      tc_commit(mma_done);
+      if (!mbar_wait(mma_done, 0)) ok = false;
     }
     __syncwarp();
   } else {
-    // ---- drain warpgroups: 32 frame columns per thread ----
-    const int dw_idx = warp - 2;
-    const int wg = dw_idx >> 2;         // column slice
-    const int quarter = warp & 3;       // TMEM lane quarter this warp may access
+    // ---- drain: C frame columns per thread ----
+    const int dwi = warp - 2;
+    const int cg = dwi >> 2;       // column slice
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
-    const int col_base = wg * 32;
-    // int32 -> f32 without I2F: for |d| < 2^22, the float with bit pattern
-    // d + 0x4B400000 is exactly 1.5 * 2^23 + d (block dots are below 2^20).
-    const uint64_t neg_magic = pack2(-12582912.0f, -12582912.0f);
-    // fma(s, dot, -0) is the rounded product s * dot (an exact zero keeps its
-    // sign: +0 + -0 = +0, -0 + -0 = -0); -0 arrives as a kernel parameter so
-    // the code generator cannot turn the fma back into a multiply and fuse
-    // it into the following add.
+    const int col_base = cg * C;
+    const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col_base;
     const uint64_t nz2 = pack2(p.neg_zero, p.neg_zero);
-    uint64_t acc[16];
+    float *tr = trs + dwi * 8 * 32;  // this warp's transpose buffer [8 frames][32 rows]
+    int gb = 0, gc = 0;
+    for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
+      const int64_t g = tile / p.n_ft, ft = tile % p.n_ft;
+      uint64_t acc[C / 2];
 #pragma unroll
-    for (int j = 0; j < 16; j++) acc[j] = 0ull;
-    int b = 0;
-    for (int si = 0; si < n_stages && ok; si++) {
-      const int s = si % kTcStages;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(si / kTcStages) & 1u))) { ok = false; break; }
-      const int nblk = nb - si * kTcKb < kTcKb ? nb - si * kTcKb : kTcKb;
-      const unsigned char *st = smem + s * L::kStage;
-      for (int i = 0; i < nblk; i++, b++) {
-        const int buf = b % kAcc;
-        // warp-uniform wait: tcgen05.ld below needs the whole warp
-        if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (uint32_t)(b / kAcc) & 1u))) { ok = false; break; }
-        tc_fence_after();
-        uint32_t r[32];
-        tc_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * FT + col_base), r);
-        tc_wait_ld();
+      for (int j = 0; j < C / 2; j++) acc[j] = 0ull;
+      // The tile's blocks, each drained in two halves of the thread's
+      // columns: while one half is scaled the other half's accumulator load
+      // is in flight, and a block's TMEM accumulator is released as soon as
+      // both halves have landed.  rA holds the next block's first half.
+      constexpr int H = C / 2;
+      uint32_t rA[H], rB[H];
+      if (!warp_wait(&tfull[gb % kAcc], (uint32_t)(gb / kAcc) & 1u)) { ok = false; break; }
+      tc_fence_after();
+      tc_ld<H>(taddr + (uint32_t)((gb % kAcc) * FT), rA);
+      for (int k = 0; k < nb; k++, gb++) {
+        const int kc = k % kTcScB, ss = gc % kScs;  // block kc of scale chunk gc
+        if (kc == 0 && !warp_wait(&sc_full[ss], (uint32_t)(gc / kScs) & 1u)) { ok = false; break; }
+        const unsigned char *sc = scs + ss * L::kSc;
+        const float dwv = __half2float(((const __half *)sc)[kc * SC_GROUP_ROWS + row]);
+        const uint64_t dw2 = pack2(dwv, dwv);
+        const uint64_t *dx2 = (const uint64_t *)(sc + L::kScW) + (kc * FT + col_base) / 2;
+        const uint32_t tb = taddr + (uint32_t)((gb % kAcc) * FT);
+        tc_wait_ld<H>(rA);
+        tc_ld<H>(tb + H, rB);
+        drain_half<H, 0>(acc, rA, dw2, dx2, nz2);
+        tc_wait_ld<H>(rB);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
-        const float dwv = __half2float(((const __half *)(st + L::kA + L::kB))[i * SC_GROUP_ROWS + row]);
-        const uint64_t dw2 = pack2(dwv, dwv);
-        const uint64_t *dx2 = (const uint64_t *)(st + L::kA + L::kB + L::kS) + (i * FT + col_base) / 2;
-        // acc += (dw * dx) * dot with the three roundings of the reference's
-        // scalar oracle (sgemm_kernel.rs:185-196), so each output is bit-equal
-        // to q8_gemm_scalar's, in packed f32x2 arithmetic.
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const uint64_t s2 = fmul2(dw2, dx2[j]);  // dw * dx per column
-          const uint64_t f2 = fadd2(pack2(__uint_as_float(r[2 * j] + 0x4B400000u),
-                                          __uint_as_float(r[2 * j + 1] + 0x4B400000u)),
-                                    neg_magic);   // exact block dots as f32
-          acc[j] = fadd2(acc[j], ffma2(s2, f2, nz2));
+        if (lane == 0) mbar_arrive(&tempty[gb % kAcc]);
+        if (k + 1 < nb) {
+          if (!warp_wait(&tfull[(gb + 1) % kAcc], (uint32_t)((gb + 1) / kAcc) & 1u)) { ok = false; break; }
+          tc_fence_after();
+          tc_ld<H>(taddr + (uint32_t)(((gb + 1) % kAcc) * FT), rA);
+        }
+        drain_half<H, H / 2>(acc, rB, dw2, dx2 + H / 2, nz2);
+        if (kc == kTcScB - 1 || k + 1 == nb) {  // the chunk's scales are used
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sc_empty[ss]);
+          gc++;
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    // ---- epilogue: y (+ bias); or the next GEMM's codes, one block of 32
-    // output features per warp (the warp's lanes are 32 consecutive rows) ----
-    const int64_t n = g * SC_GROUP_ROWS + row;
-    if (p.qout.xq) {
-      const float bn = p.bias ? p.bias[n] : 0.0f;
-      float v[32], a[32];
-#pragma unroll
-      for (int j = 0; j < 32; j++) {
-        v[j] = apply_epilogue(p.epi, __fadd_rn((j & 1) ? hi_of(acc[j >> 1]) : lo_of(acc[j >> 1]), bn), 0);
-        a[j] = fabsf(v[j]);
-      }
-      // block amax of every column over the warp's 32 rows: a butterfly that
-      // leaves column col_of(lane) in a[0] of this lane (max ignores order;
-      // fmaxf skips NaN like quantize_col's amax)
-#pragma unroll
-      for (int cnt = 32, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
-        const bool up = (lane & off) != 0;
-#pragma unroll
-        for (int i = 0; i < cnt / 2; i++) {
-          const float send = up ? a[i] : a[i + cnt / 2];
-          const float keep = up ? a[i + cnt / 2] : a[i];
-          a[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, off));
-        }
-      }
-      int mycol = 0;  // column whose amax this lane holds
-#pragma unroll
-      for (int cnt = 32, off = 16; cnt > 1; cnt >>= 1, off >>= 1)
-        if (lane & off) mycol += cnt / 2;
-      const float amax = a[0];
-      const float sblk = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
-      const float inv = __fdiv_rn(1.0f, sblk);
+      if (!ok) break;
+      // ---- epilogue: u = acc + bias (then SiLU / ReLU) per row; then y,
+      // with the residual, or the next GEMM's codes ----
+      const int64_t n = g * SC_GROUP_ROWS + row;
       const int64_t fbase = ft * FT + col_base;  // frames of this thread's columns (< t_pad)
-      p.qout.dx[qout_dx_index(p.qout, fbase + mycol, n >> 5)] = sblk;
-      // codes: row n is element n % 32 of block n / 32 of the next GEMM's K
-      int8_t *dst = p.qout.xq + ((int64_t)ft * p.qout.nb + (n >> 5)) * (FT * 32) + ((n & 31) >> 4) * (FT * 16) +
-                    (int64_t)col_base * 16 + (n & 15);
+      const float bn = p.bias && n < p.n_rows ? p.bias[n] : 0.0f;
+      float v[C];
 #pragma unroll
-      for (int j = 0; j < 32; j++) {
-        int src = 0;  // lane holding column j: bit-reverse of the butterfly's split order
-#pragma unroll
-        for (int cnt = 32, off = 16, jj = j; cnt > 1; cnt >>= 1, off >>= 1)
-          if (jj >= cnt / 2) { src |= off; jj -= cnt / 2; }
-        const float ij = __shfl_sync(0xffffffffu, inv, src);
-        const float aj = __shfl_sync(0xffffffffu, amax, src);
-        dst[j * 16] = aj != 0.0f ? rust_round_i8(__fmul_rn(v[j], ij)) : (int8_t)0;
-        if (p.y && fbase + j < p.t) p.y[p.y_time_major ? (fbase + j) * p.ldy + n : n * p.ldy + fbase + j] = v[j];
+      for (int j = 0; j < C; j++) {
+        const float u = __fadd_rn((j & 1) ? hi_of(acc[j >> 1]) : lo_of(acc[j >> 1]), bn);
+        v[j] = p.epi.op == kEpiResidual ? u : apply_epilogue(p.epi, u, 0);
       }
-    } else if (n < p.n_rows) {
-      const float bn = p.bias ? p.bias[n] : 0.0f;
+      if (p.qout.xq) {
+        float a[C];
 #pragma unroll
-      for (int j = 0; j < 32; j++) {
-        const int64_t f = ft * FT + col_base + j;
-        const float v = (j & 1) ? hi_of(acc[j >> 1]) : lo_of(acc[j >> 1]);
-        if (f < p.t) {
-          const int64_t idx = p.y_time_major ? f * p.ldy + n : n * p.ldy + f;
-          p.y[idx] = apply_epilogue(p.epi, __fadd_rn(v, bn), idx);
+        for (int j = 0; j < C; j++) a[j] = fabsf(v[j]);
+        // block amax of every column over the warp's 32 rows: a butterfly
+        // that halves the columns a lane holds at each step (offsets 16, 8,
+        // ...), leaving column col_of(lane) in a[0]; with fewer than 32
+        // columns, the lanes that then share a column combine theirs.  max
+        // ignores order; fmaxf skips NaN like quantize_col's amax.
+#pragma unroll
+        for (int cnt = C, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
+          const bool up = (lane & off) != 0;
+#pragma unroll
+          for (int i = 0; i < cnt / 2; i++) {
+            const float send = up ? a[i] : a[i + cnt / 2];
+            const float keep = up ? a[i + cnt / 2] : a[i];
+            a[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, off));
+          }
+        }
+        constexpr int kShare = 32 / C;  // lanes per column after the butterfly
+#pragma unroll
+        for (int off = kShare / 2; off > 0; off >>= 1) a[0] = fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], off));
+        int mycol = 0;  // column whose amax this lane holds
+#pragma unroll
+        for (int cnt = C, off = 16; cnt > 1; cnt >>= 1, off >>= 1)
+          if (lane & off) mycol += cnt / 2;
+        const float amax = a[0];
+        const float sblk = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
+        const float inv = __fdiv_rn(1.0f, sblk);
+        if ((lane & (kShare - 1)) == 0) p.qout.dx[qout_dx_index(p.qout, fbase + mycol, n >> 5)] = sblk;
+        // codes: row n is element n % 32 of block n / 32 of the next GEMM's K
+        __half *dst = p.qout.xq + qout_code_index(p.qout, fbase, n);
+#pragma unroll
+        for (int j = 0; j < C; j++) {
+          int src = 0;  // a lane holding column j: the inverse of the butterfly's split order
+#pragma unroll
+          for (int cnt = C, off = 16, jj = j; cnt > 1; cnt >>= 1, off >>= 1)
+            if (jj >= cnt / 2) { src |= off; jj -= cnt / 2; }
+          const float ij = __shfl_sync(0xffffffffu, inv, src);
+          const float aj = __shfl_sync(0xffffffffu, amax, src);
+          dst[j * 8] = code_half(aj != 0.0f ? rust_round_i8(__fmul_rn(v[j], ij)) : (int8_t)0);
+          if (p.y && fbase + j < p.t) p.y[p.y_time_major ? (fbase + j) * p.ldy + n : n * p.ldy + fbase + j] = v[j];
+        }
+      } else if (p.store == kStoreVec) {
+        // time-major y in 16-byte stores of four rows: per 8 frames, the
+        // warp's 32 x 8 outputs pass through its transpose buffer; lane l
+        // then holds items l and l + 32 (frame item / 8, rows 4 (item % 8)
+        // .. + 3 of the warp)
+        const int64_t n0 = g * SC_GROUP_ROWS + quarter * 32;
+        const bool res = p.epi.op == kEpiResidual;
+#pragma unroll
+        for (int c8 = 0; c8 < C / 8; c8++) {
+#pragma unroll
+          for (int e = 0; e < 8; e++) tr[e * 32 + lane] = v[8 * c8 + e];
+          __syncwarp();
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const int item = lane + 32 * h, e = item >> 3, r4 = (item & 7) * 4;
+            const int64_t f = fbase + 8 * c8 + e, nn = n0 + r4;
+            float4 u4 = *reinterpret_cast<const float4 *>(tr + e * 32 + r4);
+            if (f < p.t && nn < p.n_rows) {
+              float *yp = p.y + f * p.ldy + nn;
+              if (res) {  // y = res + alpha * u, elementwise (res may be y itself)
+                const float4 r = *reinterpret_cast<const float4 *>(p.epi.res + f * p.ldy + nn);
+                const float al = p.epi.alpha;
+                u4 = make_float4(__fadd_rn(r.x, __fmul_rn(al, u4.x)), __fadd_rn(r.y, __fmul_rn(al, u4.y)),
+                                 __fadd_rn(r.z, __fmul_rn(al, u4.z)), __fadd_rn(r.w, __fmul_rn(al, u4.w)));
+              }
+              *reinterpret_cast<float4 *>(yp) = u4;
+            }
+          }
+          __syncwarp();
+        }
+      } else if (n < p.n_rows) {
+#pragma unroll
+        for (int j = 0; j < C; j++) {
+          const int64_t f = fbase + j;
+          if (f < p.t) {
+            const int64_t idx = p.y_time_major ? f * p.ldy + n : n * p.ldy + f;
+            p.y[idx] = p.epi.op == kEpiResidual ? __fadd_rn(p.epi.res[idx], __fmul_rn(p.epi.alpha, v[j])) : v[j];
+          }
         }
       }
     }
+    // no TMEM load of this thread is outstanding (a role that gave up may
+    // have left one) before the kernel ends
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
   }
-  if (!ok) atomicOr(p.status, kStatusWaitTimeout);
+  if (!ok) {
+    atomicOr(p.status, kStatusWaitTimeout);
+    atomicOr(&misc[1], 1u);
+  }
   tc_fence_before();
+  __syncthreads();
+  if (misc[1] && threadIdx.x == 0) {
+    // a role gave up: wait (bounded) for bulk copies that may still be
+    // landing in this CTA's shared memory before it exits
+    for (int s = 0; s < kOps + kScs; s++)
+      if (last_round[s] >= 0) mbar_wait(s < kOps ? &op_full[s] : &sc_full[s - kOps], (uint32_t)last_round[s] & 1u);
+  }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
-                 : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512) : "memory");
   }
 }
 
@@ -406,16 +573,15 @@ int tc_gemm_status(unsigned *out) {
 }
 
 // Shared-memory limit raised so far per device, per kernel instance.
-template <int FT, int DWG>
+template <int FT>
 static std::atomic<size_t> *tc_smem_limit() {
   static std::atomic<size_t> limit[64];
   return limit;
 }
 
-template <int FT, int DWG>
+template <int FT>
 static int prime_tc() {
-  return raise_smem_limit((const void *)q8_gemm_tc_kernel<FT, DWG>, TcSmem<FT, DWG>::kBytes,
-                          tc_smem_limit<FT, DWG>());
+  return raise_smem_limit((const void *)q8_gemm_tc_kernel<FT>, TcCfg<FT>::kBytes, tc_smem_limit<FT>());
 }
 
 int tc_gemm_prime() {
@@ -423,21 +589,20 @@ int tc_gemm_prime() {
     set_error("q8_gemm_tc: status word lookup failed");
     return kErrCuda;
   }
-  int rc = prime_tc<32, 1>();
-  if (!rc) rc = prime_tc<64, 2>();
-  if (!rc) rc = prime_tc<128, 4>();
+  int rc = prime_tc<64>();
+  if (!rc) rc = prime_tc<128>();
   return rc;
 }
 
-template <int FT, int DWG>
-static int launch_tc(const TcParams &p, int64_t groups, cudaStream_t st) {
-  using L = TcSmem<FT, DWG>;
-  auto kern = q8_gemm_tc_kernel<FT, DWG>;
-  const int rc = raise_smem_limit((const void *)kern, L::kBytes, tc_smem_limit<FT, DWG>());
+template <int FT>
+static int launch_tc(const TcParams &p, int sm_count, cudaStream_t st) {
+  using L = TcCfg<FT>;
+  auto kern = q8_gemm_tc_kernel<FT>;
+  const int rc = raise_smem_limit((const void *)kern, L::kBytes, tc_smem_limit<FT>());
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)groups, (unsigned)(p.t_pad / FT), 1);
-  cfg.blockDim = dim3(64 + 128 * DWG, 1, 1);
+  cfg.gridDim = dim3((unsigned)(SC_TC_GRID_TILES || p.n_tiles < sm_count ? p.n_tiles : sm_count), 1, 1);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -450,16 +615,23 @@ static int launch_tc(const TcParams &p, int64_t groups, cudaStream_t st) {
   return kOk;
 }
 
-// Frame tile of a GEMM over t frames: 64-frame tiles (two CTAs per SM) up
-// to 1024 frames, where a grid of 128-frame tiles would leave most of its
-// last wave idle; 128 above (measured at 896 / 1792 frames over the four
-// layer shapes: 193 vs 227 us / 305 vs 308 us).
-int tc_frame_tile(int64_t t) { return t <= 32 ? 32 : t <= 1024 ? 64 : 128; }
+// Frame tile of a GEMM over t frames (also the tile of its code layout):
+// 128-frame tiles, 64 for batches that a 128-frame tile would mostly pad
+// (measured in the 256-stream encoder step, two 896-frame halves in flight:
+// 19.6 ms per step with 128-frame tiles, 21.6 ms with 64).
+#ifndef SC_TC_FT64_MAX
+#define SC_TC_FT64_MAX 64
+#endif
+int tc_frame_tile(int64_t t) { return t <= SC_TC_FT64_MAX ? 64 : 128; }
 
 int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
   const Q8Weights *w = a.w;
+  if (!w->qh) {
+    set_error("q8_gemm_tc: weights have no f16 tiles");
+    return kErrInvalid;
+  }
   TcParams p{};
-  p.qs = w->qs;
+  p.qh = w->qh;
   p.sc = w->sc;
   p.nb = w->nb;
   p.n_rows = w->rows;
@@ -475,8 +647,14 @@ int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
   p.epi = a.epi;
   p.qout = a.qout;
   p.neg_zero = -0.0f;
+  // time-major y whose frame rows start 16-byte aligned: vector stores
+  p.store = !p.qout.xq && p.y && p.y_time_major && p.ldy % 4 == 0 && p.n_rows % 4 == 0 &&
+                    ((uintptr_t)p.y & 15) == 0 && (p.epi.op != kEpiResidual || ((uintptr_t)p.epi.res & 15) == 0)
+                ? kStoreVec
+                : kStoreDirect;
+  const int ft = tc_frame_tile(a.t);
   if (p.qout.xq && (w->rows % SC_GROUP_ROWS || p.epi.op == kEpiResidual || p.qout.t_pad != a.t_pad ||
-                    p.qout.ft != tc_frame_tile(a.t) || p.qout.nb * 32 != w->rows)) {
+                    p.qout.ft != ft || p.qout.nb * 32 != w->rows)) {
     set_error("q8_gemm_tc: quantised output needs rows %% 128 == 0, no residual and the same frame tiling");
     return kErrInvalid;
   }
@@ -484,17 +662,18 @@ int gemm_tc(const TcGemmArgs &a, cudaStream_t st) {
     set_error("q8_gemm_tc: status word lookup failed");
     return kErrCuda;
   }
-  const int ft = tc_frame_tile(a.t);
   if (a.t_pad % ft != 0) {
     set_error("q8_gemm_tc: t_pad %lld is not a multiple of the frame tile %d", (long long)a.t_pad, ft);
     return kErrInvalid;
   }
-  const int64_t groups = w->rows_pad / SC_GROUP_ROWS;
-  switch (ft) {
-    case 32: return launch_tc<32, 1>(p, groups, st);
-    case 64: return launch_tc<64, 2>(p, groups, st);
-    default: return launch_tc<128, 4>(p, groups, st);
-  }
+  p.n_ft = a.t_pad / ft;
+  p.n_tiles = (w->rows_pad / SC_GROUP_ROWS) * p.n_ft;
+  if (p.n_tiles == 0) return kOk;
+  int dev, sms;
+  const int rc = current_device(&dev, &sms);
+  if (rc) return rc;
+  return ft == 64 ? launch_tc<64>(p, sms, st) : launch_tc<128>(p, sms, st);
 }
 
 }  // namespace sc
+

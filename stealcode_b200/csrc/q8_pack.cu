@@ -10,7 +10,8 @@
 namespace sc {
 
 // One thread per (padded row, block): copy 32 quants into the tile layout and
-// the raw f16 scale bits into the scale array.  raw holds `rows` rows of
+// the raw f16 scale bits into the scale array; if qh is set, also write the
+// quants as f16 tiles (sc_common.cuh).  raw holds `rows` rows of
 // `padded_row` bytes; blocks are `block_bytes` long with the f16 scale at byte
 // 0 and the quants at byte `qoff`.
 __global__ void repack_q8f16_kernel(const uint8_t *__restrict__ raw, int64_t rows,
@@ -18,7 +19,8 @@ __global__ void repack_q8f16_kernel(const uint8_t *__restrict__ raw, int64_t row
                                     int64_t block_bytes, int64_t qoff,
                                     int64_t rows_pad, int64_t nb,
                                     int8_t *__restrict__ qs,
-                                    __half *__restrict__ sc) {
+                                    __half *__restrict__ sc,
+                                    __half *__restrict__ qh) {
   int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows_pad * nb) return;
   int64_t b = idx % nb;
@@ -43,6 +45,18 @@ __global__ void repack_q8f16_kernel(const uint8_t *__restrict__ raw, int64_t row
   *(uint4 *)(tile + r * 16) = lo;
   *(uint4 *)(tile + 2048 + r * 16) = hi;
   sc[(g * nb + b) * SC_GROUP_ROWS + r] = __ushort_as_half(s16);
+  if (qh) {  // the same quants as f16 tiles for the tensor-core path
+    __half *th = qh + (g * nb + b) * 4096;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      __half h8[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) h8[e] = __short2half_rn((short)(int8_t)q[8 * c + e]);
+      uint4 v;
+      memcpy(&v, h8, 16);
+      *(uint4 *)(th + c * 1024 + r * 8) = v;
+    }
+  }
 }
 
 int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k,
@@ -55,7 +69,7 @@ int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k,
   int threads = 256;
   repack_q8f16_kernel<<<(unsigned)ceil_div(n, threads), threads, 0, st>>>(
       raw_dev, rows, k, padded_row, block_bytes, qoff, rows_pad, nb, w->qs,
-      w->sc);
+      w->sc, w->qh);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
@@ -86,7 +100,7 @@ template <bool kFeatureMajor>
 __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t m,
                                     int64_t k, int64_t ldx, int64_t nb,
                                     int64_t m_pad, int64_t k_pad,
-                                    int8_t *__restrict__ xq,
+                                    void *__restrict__ xq,
                                     float *__restrict__ dx, int tile_ft) {
   int lane = threadIdx.x & 31;
   int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -109,10 +123,10 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t m,
     q = rust_round_i8(__fmul_rn(v, inv));
   }
   if (tile_ft)
-    xq[((col / tile_ft) * nb + b) * (int64_t)tile_ft * 32 + (lane >> 4) * tile_ft * 16 + (col % tile_ft) * 16 +
-       (lane & 15)] = q;
+    ((__half *)xq)[((col / tile_ft) * nb + b) * (int64_t)tile_ft * 32 + (lane >> 3) * tile_ft * 8 +
+                   (col % tile_ft) * 8 + (lane & 7)] = __short2half_rn((short)q);
   else
-    xq[col * k_pad + kk] = q;
+    ((int8_t *)xq)[col * k_pad + kk] = q;
   if (lane == 0) dx[tile_ft ? ((col / tile_ft) * nb + b) * tile_ft + col % tile_ft : b * m_pad + col] = s;
 }
 
@@ -121,7 +135,7 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t m,
 // 8-lane group and store their 4 codes with one 32-bit store.  Same
 // arithmetic per element as quantize_act_kernel.
 __global__ void quantize_act_v4_kernel(const float *__restrict__ x, int64_t m, int64_t k, int64_t ldx,
-                                       int64_t nb, int64_t m_pad, int64_t k_pad, int8_t *__restrict__ xq,
+                                       int64_t nb, int64_t m_pad, int64_t k_pad, void *__restrict__ xq,
                                        float *__restrict__ dx, int tile_ft) {
   const int lane = threadIdx.x & 31;
   const int64_t nq = ceil_div(nb, 4);
@@ -153,26 +167,32 @@ __global__ void quantize_act_v4_kernel(const float *__restrict__ x, int64_t m, i
   for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if (amax != amax) amax = 0.0f;
   const float s = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
-  uint32_t packed = 0;
+  int8_t q[4] = {0, 0, 0, 0};
   if (amax != 0.0f) {
     const float inv = __fdiv_rn(1.0f, s);
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const int8_t q = valid[e] ? rust_round_i8(__fmul_rn(v[e], inv)) : (int8_t)0;
-      packed |= (uint32_t)(uint8_t)q << (8 * e);
-    }
+    for (int e = 0; e < 4; e++) q[e] = valid[e] ? rust_round_i8(__fmul_rn(v[e], inv)) : (int8_t)0;
   }
   if (!blk_ok) return;
-  if (tile_ft)
-    *(uint32_t *)(xq + ((col / tile_ft) * nb + b) * (int64_t)tile_ft * 32 + (sub >> 2) * tile_ft * 16 +
-                  (col % tile_ft) * 16 + (sub & 3) * 4) = packed;
-  else
-    *(uint32_t *)(xq + col * k_pad + kk) = packed;
+  if (tile_ft) {  // 4 f16 codes: half of one 8-element chunk of the tile layout
+    __half h4[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) h4[e] = __short2half_rn((short)q[e]);
+    uint2 u;
+    memcpy(&u, h4, 8);
+    *(uint2 *)((__half *)xq + ((col / tile_ft) * nb + b) * (int64_t)tile_ft * 32 + (sub >> 1) * tile_ft * 8 +
+               (col % tile_ft) * 8 + (sub & 1) * 4) = u;
+  } else {
+    uint32_t packed = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) packed |= (uint32_t)(uint8_t)q[e] << (8 * e);
+    *(uint32_t *)((int8_t *)xq + col * k_pad + kk) = packed;
+  }
   if (sub == 0) dx[tile_ft ? ((col / tile_ft) * nb + b) * tile_ft + col % tile_ft : b * m_pad + col] = s;
 }
 
 int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx,
-                 bool feature_major, int64_t m_pad, int8_t *xq, float *dx,
+                 bool feature_major, int64_t m_pad, void *xq, float *dx,
                  cudaStream_t st, int tile_ft) {
   int64_t nb = ceil_div(k, 32);
   int64_t k_pad = nb * 32;

@@ -659,7 +659,7 @@ struct RLoader {
   }
   void *dev(size_t bytes) {
     void *p = nullptr;
-    if (cudaMalloc(&p, bytes < 16 ? 16 : bytes) != cudaSuccess) {
+    if (dev_malloc(&p, bytes < 16 ? 16 : bytes) != cudaSuccess) {
       cudaGetLastError();
       if (err.empty()) err = "cudaMalloc failed";
       return nullptr;

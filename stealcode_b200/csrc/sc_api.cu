@@ -43,6 +43,20 @@ static DeviceState g_dev[64];
 static std::atomic<long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+// Allocation cap for failure-path tests (sc_debug_set_device_alloc_cap):
+// -1 = none; else the bytes the library may still allocate.
+static std::atomic<long long> g_alloc_left{-1};
+
+cudaError_t dev_malloc(void **p, size_t bytes) {
+  *p = nullptr;
+  long long left = g_alloc_left.load(std::memory_order_relaxed);
+  while (left >= 0) {
+    if ((long long)bytes > left) return cudaErrorMemoryAllocation;
+    if (g_alloc_left.compare_exchange_weak(left, left - (long long)bytes, std::memory_order_relaxed)) break;
+  }
+  return cudaMalloc(p, bytes);
+}
+
 int current_device(int *dev, int *sm_count) {
   SC_CUDA(cudaGetDevice(dev));
   if (*dev < 0 || *dev >= 64) {
@@ -80,7 +94,7 @@ int raise_smem_limit(const void *kern, size_t bytes, std::atomic<size_t> *limit)
 // their scales [nb][m_pad] f32.
 size_t gemm_ws_bytes(int64_t m, int64_t k) {
   int64_t nb = ceil_div(k, 32), m_pad = ceil_div(m, 128) * 128;
-  size_t a = (size_t)m_pad * nb * 32;
+  size_t a = (size_t)m_pad * nb * 32 * 2;  // codes: int8, or f16 for the tensor-core path
   a = (a + 255) / 256 * 256;
   return a + (size_t)nb * m_pad * 4 + 256;
 }
@@ -100,7 +114,7 @@ static int default_ws(size_t bytes, void **out) {
       ds.ws_bytes = 0;
     }
     size_t nbytes = bytes < ((size_t)64 << 20) ? ((size_t)64 << 20) : bytes;
-    cudaError_t e = cudaMalloc(&ds.ws, nbytes);
+    cudaError_t e = dev_malloc(&ds.ws, nbytes);
     if (e != cudaSuccess) {
       cudaGetLastError();
       set_error("workspace cudaMalloc(%zu) failed: %s", nbytes, cudaGetErrorString(e));
@@ -170,8 +184,8 @@ int gemm_impl(const Q8Weights *w, const float *x, int64_t t, int32_t x_layout, i
     }
     const int ft = tc_frame_tile(t);
     const int64_t t_pad = ceil_div(t, ft) * ft, k_pad = w->nb * 32;
-    int8_t *xq = (int8_t *)ws;
-    float *dx = (float *)((char *)ws + ((size_t)t_pad * k_pad + 255) / 256 * 256);
+    __half *xq = (__half *)ws;
+    float *dx = (float *)((char *)ws + ((size_t)t_pad * k_pad * 2 + 255) / 256 * 256);
     rc = quantize_act(x, t, w->k, ldx, x_layout == SC_LAYOUT_FEATURE_MAJOR, t_pad, xq, dx, st, ft);
     if (rc) return rc;
     TcGemmArgs ta{w, xq, dx, t, t_pad, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy, epi};
@@ -198,6 +212,11 @@ const Q8Weights *q8w_weights(const sc_q8w *w) { return &w->w; }
 extern "C" {
 
 long long sc_launch_count(void) { return sc::g_launches.load(std::memory_order_relaxed); }
+
+int sc_debug_set_device_alloc_cap(int64_t bytes) {
+  sc::g_alloc_left.store(bytes < 0 ? -1 : bytes, std::memory_order_relaxed);
+  return kOk;
+}
 
 const char *sc_last_error(void) { return g_err; }
 
@@ -227,17 +246,20 @@ int sc_q8_repack_device(const uint8_t *blocks_dev, int64_t rows, int64_t k, int6
   w.rows_pad = ceil_div(rows, SC_GROUP_ROWS) * SC_GROUP_ROWS;
   w.device = dev;
   size_t qbytes = (size_t)w.rows_pad * w.nb * 32, sbytes = (size_t)w.rows_pad * w.nb * 2;
-  if (cudaMalloc(&w.qs, qbytes) != cudaSuccess || cudaMalloc(&w.sc, sbytes) != cudaSuccess) {
+  if (dev_malloc((void **)&w.qs, qbytes) != cudaSuccess || dev_malloc((void **)&w.sc, sbytes) != cudaSuccess ||
+      dev_malloc((void **)&w.qh, 2 * qbytes) != cudaSuccess) {
     cudaGetLastError();
-    if (w.qs) cudaFree(w.qs);
+    cudaFree(w.qs);
+    cudaFree(w.sc);
     delete h;
-    set_error("q8_repack: cudaMalloc of %zu bytes failed", qbytes + sbytes);
+    set_error("q8_repack: cudaMalloc of %zu bytes failed", 3 * qbytes + sbytes);
     return kErrAlloc;
   }
   rc = repack_q8_device(blocks_dev, rows, k, block_bytes, qoff, &w, (cudaStream_t)stream);
   if (rc) {
     cudaFree(w.qs);
     cudaFree(w.sc);
+    cudaFree(w.qh);
     delete h;
     return rc;
   }
@@ -259,7 +281,7 @@ int sc_q8_repack(const uint8_t *blocks, int64_t rows, int64_t k, int64_t block_b
   }
   size_t bytes = (size_t)rows * ceil_div(k, 32) * block_bytes;
   uint8_t *raw = nullptr;
-  if (cudaMalloc(&raw, bytes) != cudaSuccess) {
+  if (dev_malloc((void **)&raw, bytes) != cudaSuccess) {
     cudaGetLastError();
     set_error("q8_repack: staging cudaMalloc(%zu) failed", bytes);
     return kErrAlloc;
@@ -285,6 +307,7 @@ int sc_q8w_free(sc_q8w *w) {
   if (!w) return kOk;
   cudaFree(w->w.qs);
   cudaFree(w->w.sc);
+  cudaFree(w->w.qh);
   delete w;
   return kOk;
 }
@@ -365,7 +388,7 @@ int sc_q8mat_gemm_t(const sc_q8w *w, const float *x_host, int64_t t, float *y_ho
       ds.stage = nullptr;
       ds.stage_bytes = 0;
     }
-    if (cudaMalloc(&ds.stage, xb + yb) != cudaSuccess) {
+    if (dev_malloc((void **)&ds.stage, xb + yb) != cudaSuccess) {
       cudaGetLastError();
       set_error("q8mat_gemm_t: staging cudaMalloc(%zu) failed", xb + yb);
       return kErrAlloc;
@@ -457,7 +480,7 @@ int sc_attn_stream_host(const float *q, const float *kv, const float *vv, const 
   size_t qb = (size_t)c * d * 4, kb = (size_t)band * d * 4, pb = (size_t)n_pos * d * 4, db = (size_t)d * 4;
   size_t total = qb * 2 + kb * 2 + pb + db * 2;
   char *buf = nullptr;
-  if (cudaMalloc(&buf, total + 7 * 256) != cudaSuccess) {
+  if (dev_malloc((void **)&buf, total + 7 * 256) != cudaSuccess) {
     cudaGetLastError();
     set_error("attn_stream_host: cudaMalloc failed");
     return kErrAlloc;

@@ -13,6 +13,11 @@
 //   * scales: f16 [G][nb][128]: the scale of row g*128 + r, block b at
 //     (g * nb + b) * 128 + r (256 contiguous bytes per tile).
 // Padding rows and padding K positions hold zero quants and zero scales.
+//   * f16 quants for the tensor-core path (every int8 value is an f16
+//     integer): tile (g, b) of 128 rows x 32 k at element (g * nb + b) * 4096;
+//     inside it, element k of row r at ((k % 32) / 8) * 1024 + r * 8 + k % 8
+//     (four 8-wide K chunks, each the no-swizzle K-major core-matrix layout
+//     of 128 rows x 16 bytes).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -31,6 +36,7 @@ struct Q8Weights {
   int64_t nb;         // K blocks of 32
   int8_t *qs;         // device, rows_pad * nb * 32 bytes
   __half *sc;         // device, rows_pad * nb halves
+  __half *qh;         // device, the quants as f16 tiles for the tensor-core path (rows_pad * nb * 32 halves)
   int device;
 };
 
@@ -49,6 +55,10 @@ void set_error(const char *fmt, ...);
 int cuda_fail(cudaError_t e, const char *what);
 // Counts one kernel launch issued by this library (sc_launch_count).
 void note_launch();
+// cudaMalloc for every device allocation of this library; fails with
+// cudaErrorMemoryAllocation, without allocating, once the bytes allocated
+// since sc_debug_set_device_alloc_cap would exceed that cap.
+cudaError_t dev_malloc(void **p, size_t bytes);
 
 #define SC_CUDA(call)                                       \
   do {                                                      \

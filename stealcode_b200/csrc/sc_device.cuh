@@ -18,6 +18,9 @@ __device__ __forceinline__ int8_t rust_round_i8(float v) {
   return (int8_t)(int)r;
 }
 
+// An int8 code as the f16 operand of the tensor-core GEMM (exact).
+__device__ __forceinline__ __half code_half(int8_t q) { return __short2half_rn((short)q); }
+
 // One 32-wide block held one element per lane (valid = inside k).  Returns
 // the lane's code and the block scale s (same in every lane): amax ignores
 // NaN like `if v > maxv`, an all-zero block gets s = 1 and zero codes, s =

@@ -121,7 +121,7 @@ struct sc_stream_encoder {
   float *win, *p0, *p1, *p2, *flat, *pos_in;
   // GEMM inputs as codes in the tensor-core tiled layout (two, so that a
   // GEMM can write its successor's codes while reading its own)
-  int8_t *qx[2] = {nullptr, nullptr};
+  __half *qx[2] = {nullptr, nullptr};  // f16 codes of the GEMM inputs (QOut layout)
   float *qd[2] = {nullptr, nullptr};
   void *ws = nullptr;
   size_t ws_bytes = 0;
@@ -145,10 +145,12 @@ struct sc_stream_encoder {
       for (Lin *q : {&l.ff1_1, &l.ff1_2, &l.qkv, &l.pos, &l.out, &l.pw1, &l.pw2, &l.ff2_1, &l.ff2_2}) {
         cudaFree(q->w.qs);
         cudaFree(q->w.sc);
+        cudaFree(q->w.qh);
       }
     for (Lin *q : {&pre_out, &prompt0, &prompt2}) {
       cudaFree(q->w.qs);
       cudaFree(q->w.sc);
+      cudaFree(q->w.qh);
     }
     for (void *p : allocs) cudaFree(p);
     if (ev_fork) cudaEventDestroy(ev_fork);
@@ -177,7 +179,7 @@ struct Loader {
   }
   float *dev_alloc(size_t bytes) {
     void *p = nullptr;
-    if (cudaMalloc(&p, bytes < 16 ? 16 : bytes) != cudaSuccess) {
+    if (dev_malloc(&p, bytes < 16 ? 16 : bytes) != cudaSuccess) {
       cudaGetLastError();
       err = "cudaMalloc failed";
       return nullptr;
@@ -246,7 +248,7 @@ struct Loader {
     }
     (void)bias_optional;  // a linear without bias is allowed (Lin::bias is optional)
     uint8_t *draw = nullptr;
-    if (cudaMalloc(&draw, raw.size()) != cudaSuccess) {
+    if (dev_malloc((void **)&draw, raw.size()) != cudaSuccess) {
       cudaGetLastError();
       err = "cudaMalloc failed";
       return false;
@@ -258,8 +260,9 @@ struct Loader {
     w.rows_pad = (rows + SC_GROUP_ROWS - 1) / SC_GROUP_ROWS * SC_GROUP_ROWS;
     w.device = e->device;
     bool ok = cudaMemcpy(draw, raw.data(), raw.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
-              cudaMalloc(&w.qs, (size_t)w.rows_pad * nb * 32) == cudaSuccess &&
-              cudaMalloc(&w.sc, (size_t)w.rows_pad * nb * 2) == cudaSuccess &&
+              dev_malloc((void **)&w.qs, (size_t)w.rows_pad * nb * 32) == cudaSuccess &&
+              dev_malloc((void **)&w.sc, (size_t)w.rows_pad * nb * 2) == cudaSuccess &&
+              dev_malloc((void **)&w.qh, (size_t)w.rows_pad * nb * 64) == cudaSuccess &&
               repack_q8_device(draw, rows, inp, 34, 2, &w, 0) == kOk && cudaDeviceSynchronize() == cudaSuccess;
     cudaFree(draw);
     if (!ok) {
@@ -437,7 +440,7 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     e->conv_stride = t0 * f0 * C;
     e->code_k = kp;
     for (int i = 0; i < 2; i++) {
-      e->qx[i] = (int8_t *)L.dev_alloc((size_t)(tp * kp));
+      e->qx[i] = (__half *)L.dev_alloc((size_t)(tp * kp * 2));
       e->qd[i] = L.dev_alloc((size_t)(kp / 32 * tp * 4));
     }
     ok = L.err.empty();
@@ -847,7 +850,7 @@ int sc_stream_encoder_set_dump(sc_stream_encoder *e, int32_t layer) {
   }
   if (layer >= 0 && !e->dump) {
     const size_t bytes = (size_t)kDumpStages * e->n_streams * e->cfg.max_frames * 2 * e->cfg.d_model * 4;
-    if (cudaMalloc(&e->dump, bytes) != cudaSuccess) {
+    if (dev_malloc((void **)&e->dump, bytes) != cudaSuccess) {
       cudaGetLastError();
       set_error("stream_encoder_set_dump: cudaMalloc failed");
       return kErrAlloc;

@@ -32,12 +32,12 @@ __device__ __forceinline__ float apply_epilogue(const Epilogue &e, float v, int6
 // q8_pack.cu
 int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k, int64_t block_bytes,
                      int64_t qoff, Q8Weights *w, cudaStream_t st);
-// tile_ft == 0: xq is [m_pad][k_pad], dx [nb][m_pad]; tile_ft > 0: xq is the
-// tensor-core operand layout [m_pad/tile_ft][nb][2][tile_ft][16] (frame tiles
-// of tile_ft rows, one no-swizzle K-major tile per 32-wide block) and dx
-// [m_pad/tile_ft][nb][tile_ft] (the QOut layout).
+// tile_ft == 0: xq is int8 [m_pad][k_pad], dx [nb][m_pad]; tile_ft > 0: xq
+// holds f16 codes in the tensor-core operand layout (the QOut layout with ft
+// = tile_ft: [m_pad/tile_ft][nb][4][tile_ft][8]) and dx is
+// [m_pad/tile_ft][nb][tile_ft].
 int quantize_act(const float *x, int64_t m, int64_t k, int64_t ldx, bool feature_major,
-                 int64_t m_pad, int8_t *xq, float *dx, cudaStream_t st, int tile_ft = 0);
+                 int64_t m_pad, void *xq, float *dx, cudaStream_t st, int tile_ft = 0);
 
 // q8_gemm_small.cu
 struct SmallGemmArgs {
@@ -81,13 +81,16 @@ int gemm_mid(const MidGemmArgs &a, cudaStream_t st);
 
 // q8_gemm_tc.cu
 // Activation codes quantised by the kernel that produces them, written in
-// the tensor-core GEMM's tiled operand layout (ft = tc_frame_tile(t)): the
-// code of frame f, feature i at
-//   ((f / ft) * nb + i / 32) * ft * 32 + ((i % 32) / 16) * ft * 16 + (f % ft) * 16 + i % 16
-// and the block scale at dx[((f / ft) * nb + i / 32) * ft + f % ft] (a frame
-// tile's scales for consecutive blocks are contiguous).  xq == nullptr: unused.
+// the tensor-core GEMM's tiled operand layout (ft = tc_frame_tile(t)) as f16
+// values (every int8 code is an f16 integer): the code of frame f, feature i
+// at element
+//   ((f / ft) * nb + i / 32) * ft * 32 + ((i % 32) / 8) * ft * 8 + (f % ft) * 8 + i % 8
+// (per 32-wide block and frame tile: four 8-feature chunks, each the
+// no-swizzle K-major core-matrix layout of ft rows x 16 bytes), and the
+// block scale at dx[((f / ft) * nb + i / 32) * ft + f % ft] (a frame tile's
+// scales for consecutive blocks are contiguous).  xq == nullptr: unused.
 struct QOut {
-  int8_t *xq;
+  __half *xq;
   float *dx;
   int64_t nb, t_pad;
   int ft;
@@ -96,13 +99,13 @@ __host__ __device__ inline int64_t qout_dx_index(const QOut &q, int64_t f, int64
   return ((f / q.ft) * q.nb + blk) * (int64_t)q.ft + f % q.ft;
 }
 __host__ __device__ inline int64_t qout_code_index(const QOut &q, int64_t f, int64_t i) {
-  return ((f / q.ft) * q.nb + i / 32) * (int64_t)q.ft * 32 + ((i & 31) >> 4) * (int64_t)q.ft * 16 +
-         (f % q.ft) * 16 + (i & 15);
+  return ((f / q.ft) * q.nb + i / 32) * (int64_t)q.ft * 32 + ((i & 31) >> 3) * (int64_t)q.ft * 8 +
+         (f % q.ft) * 8 + (i & 7);
 }
 
 struct TcGemmArgs {
   const Q8Weights *w;
-  const int8_t *xq;   // tiled activation codes (quantize_act with tile_ft = tc_frame_tile(t))
+  const __half *xq;   // tiled f16 activation codes (quantize_act with tile_ft = tc_frame_tile(t))
   const float *dx;    // [nb][t_pad]
   int64_t t, t_pad;   // t_pad: multiple of tc_frame_tile(t)
   const float *bias;

@@ -311,10 +311,9 @@ def test_encoder_from_gguf_file_matches_memory(torch, tmp_path):
 def test_benched_workload_matches_oracle(torch):
     """The headline workload as bench.py runs it: the 24-layer model with
     the bench's seed, 256 streams in two halves of 128 streams in flight (896
-    frames per GEMM: the tensor-core kernel's 64-frame tiles, two CTAs per
-    SM), 13 steps so the attention band reaches its steady 77 frames (steps
-    10-12); the streams at both edges of both halves match the oracle
-    (device rounding) every step."""
+    frames per GEMM on the tensor-core kernel), 13 steps so the attention
+    band reaches its steady 77 frames (steps 10-12); the streams at both
+    edges of both halves match the oracle (device rounding) every step."""
     import bench
     from stealcode_b200.ops import StreamEncoder
 
