@@ -67,6 +67,7 @@ template <int FT>
 struct TcCfg {
   static constexpr int kCols = FT / 4;                  // frame columns per drain thread
   static constexpr int kAcc = 512 / FT;                 // TMEM accumulators of FT columns
+  static constexpr int kPairs = kAcc / 2;               // signalled in pairs (one commit per two blocks)
   static constexpr int kA = kTcKb * 8192;               // f16 weight tiles of a slot
   static constexpr int kOp = kA + kTcKb * FT * 64;      // + f16 activation tiles
   static constexpr int kScW = kTcScB * SC_GROUP_ROWS * 2;
@@ -74,7 +75,7 @@ struct TcCfg {
   static constexpr int kScs = 2;
   static constexpr int kTr = kTcDrainWarps * 8 * 32 * 4;
   static constexpr int kOps = (220 * 1024 - kScs * kSc - kTr) / kOp;
-  static constexpr int kBars = 8 * (2 * kOps + 2 * kScs + 2 * kAcc + 1);
+  static constexpr int kBars = 8 * (2 * kOps + 2 * kScs + 2 * kPairs + 1);
   static constexpr int kMisc = 16 + 4 * (kOps + kScs);  // TMEM slot, fail flag, last round per slot
   static constexpr int kBytes = kOps * kOp + kScs * kSc + kTr + kBars + kMisc;
   static_assert(kOps >= 2, "the operand ring needs two slots");
@@ -257,12 +258,15 @@ __device__ __forceinline__ void drain_half(uint64_t (&acc)[NACC], const uint32_t
 // Tile t of the work list is row group t / n_ft, frame tile t % n_ft: the
 // tiles in flight at once share their row groups' weights in L2.  A CTA's
 // blocks are numbered gb = 0, 1, ... over its tiles in order; operand slots
-// (go), scale chunks (gc) and accumulators (gb % kAcc) are numbered the same
-// way by every role.
+// (go), scale chunks (gc) and accumulator pairs (gp) are numbered the same
+// way by every role.  Accumulators are used in pairs: pair slot ps = gp %
+// kPairs holds a tile's blocks 2i and 2i + 1 in accumulators 2 ps and 2 ps +
+// 1, signalled by one commit (a tcgen05.commit costs the issuing thread
+// several times an MMA) and released by the drain once both are loaded.
 template <int FT>
 __global__ void __launch_bounds__(kTcThreads, 1) q8_gemm_tc_kernel(const __grid_constant__ TcParams p) {
   using L = TcCfg<FT>;
-  constexpr int C = L::kCols, kAcc = L::kAcc, kOps = L::kOps, kScs = L::kScs;
+  constexpr int C = L::kCols, kPairs = L::kPairs, kOps = L::kOps, kScs = L::kScs;
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char *ops = smem;                          // operand ring
   unsigned char *scs = smem + kOps * L::kOp;          // scale ring
@@ -272,8 +276,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) q8_gemm_tc_kernel(const __grid_
   uint64_t *sc_full = op_empty + kOps;
   uint64_t *sc_empty = sc_full + kScs;
   uint64_t *tfull = sc_empty + kScs;
-  uint64_t *tempty = tfull + kAcc;
-  uint64_t *mma_done = tempty + kAcc;
+  uint64_t *tempty = tfull + kPairs;
+  uint64_t *mma_done = tempty + kPairs;
   uint32_t *misc = (uint32_t *)(mma_done + 1);  // [0] TMEM base, [1] fail flag
   int *last_round = (int *)(misc + 4);          // [kOps + kScs]: last fill of each slot
 
@@ -297,7 +301,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q8_gemm_tc_kernel(const __grid_
       mbar_init(&sc_empty[s], kTcDrainWarps);  // every drain warp
     }
     for (int s = 0; s < kOps + kScs; s++) last_round[s] = -1;
-    for (int b = 0; b < kAcc; b++) {
+    for (int b = 0; b < kPairs; b++) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kTcDrainWarps);
     }
@@ -355,23 +359,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) q8_gemm_tc_kernel(const __grid_
       // these plus their byte offset / 16 (the start-address field, bits
       // 0-13, holds shared-memory addresses below 256 KB without carrying)
       const uint64_t a0 = umma_desc(ops, 2048, 128), b0 = umma_desc(ops + L::kA, FT * 16, 128);
-      int go = 0, gb = 0;
+      int go = 0, gp = 0;
       for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
-        for (int j = 0; j < opt && ok; j++, go++) {
-          const int s = go % kOps, nblk = nb - j * kTcKb < kTcKb ? nb - j * kTcKb : kTcKb;
-          if (!mbar_wait(&op_full[s], (uint32_t)(go / kOps) & 1u)) { ok = false; break; }
-          const uint64_t as = a0 + (uint64_t)((s * L::kOp) >> 4), bs = b0 + (uint64_t)((s * L::kOp) >> 4);
-          for (int i = 0; i < nblk; i++, gb++) {
-            const int buf = gb % kAcc;
-            if (!mbar_wait(&tempty[buf], ((uint32_t)(gb / kAcc) & 1u) ^ 1u)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t d = tmem_base + (uint32_t)(buf * FT);
-            const uint64_t ai = as + (uint64_t)((i * 8192) >> 4), bi = bs + (uint64_t)((i * FT * 64) >> 4);
-            tc_mma_f16(d, ai, bi, idesc, 0u);                                            // K 0-15
-            tc_mma_f16(d, ai + (4096 >> 4), bi + (uint64_t)((FT * 32) >> 4), idesc, 1u);  // K 16-31
-            tc_commit(&tfull[buf]);
+        uint64_t as = 0, bs = 0;
+        for (int k = 0; k < nb; k++) {
+          const int s = go % kOps, i = k % kTcKb, ps = gp % kPairs;
+          if (i == 0) {  // the operand slot of blocks k .. k + kTcKb - 1
+            if (!mbar_wait(&op_full[s], (uint32_t)(go / kOps) & 1u)) { ok = false; break; }
+            as = a0 + (uint64_t)((s * L::kOp) >> 4);
+            bs = b0 + (uint64_t)((s * L::kOp) >> 4);
           }
-          if (ok) tc_commit(&op_empty[s]);  // the slot is free once its MMAs complete
+          if ((k & 1) == 0) {  // a new accumulator pair
+            if (!mbar_wait(&tempty[ps], ((uint32_t)(gp / kPairs) & 1u) ^ 1u)) { ok = false; break; }
+            tc_fence_after();
+          }
+          const uint32_t d = tmem_base + (uint32_t)((2 * ps + (k & 1)) * FT);
+          const uint64_t ai = as + (uint64_t)((i * 8192) >> 4), bi = bs + (uint64_t)((i * FT * 64) >> 4);
+          tc_mma_f16(d, ai, bi, idesc, 0u);                                            // K 0-15
+          tc_mma_f16(d, ai + (4096 >> 4), bi + (uint64_t)((FT * 32) >> 4), idesc, 1u);  // K 16-31
+          if ((k & 1) || k + 1 == nb) {
+            tc_commit(&tfull[ps]);
+            gp++;
+          }
+          if (i == kTcKb - 1 || k + 1 == nb) {
+            tc_commit(&op_empty[s]);  // the slot is free once its MMAs complete
+            go++;
+          }
         }
       }
       // every MMA this thread issued completes before TMEM is released
@@ -389,7 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q8_gemm_tc_kernel(const __grid_
     const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col_base;
     const uint64_t nz2 = pack2(p.neg_zero, p.neg_zero);
     float *tr = trs + dwi * 8 * 32;  // this warp's transpose buffer [8 frames][32 rows]
-    int gb = 0, gc = 0;
+    int gp = 0, gc = 0;
     for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
       const int64_t g = tile / p.n_ft, ft = tile % p.n_ft;
       uint64_t acc[C / 2];
@@ -397,32 +410,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) q8_gemm_tc_kernel(const __grid_
       for (int j = 0; j < C / 2; j++) acc[j] = 0ull;
       // The tile's blocks, each drained in two halves of the thread's
       // columns: while one half is scaled the other half's accumulator load
-      // is in flight, and a block's TMEM accumulator is released as soon as
-      // both halves have landed.  rA holds the next block's first half.
+      // is in flight, and an accumulator pair is released as soon as both
+      // blocks' loads have landed.  rA holds the next block's first half.
       constexpr int H = C / 2;
       uint32_t rA[H], rB[H];
-      if (!warp_wait(&tfull[gb % kAcc], (uint32_t)(gb / kAcc) & 1u)) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[gp % kPairs], (uint32_t)(gp / kPairs) & 1u))) { ok = false; break; }
       tc_fence_after();
-      tc_ld<H>(taddr + (uint32_t)((gb % kAcc) * FT), rA);
-      for (int k = 0; k < nb; k++, gb++) {
+      tc_ld<H>(taddr + (uint32_t)(2 * (gp % kPairs) * FT), rA);
+      for (int k = 0; k < nb; k++) {
         const int kc = k % kTcScB, ss = gc % kScs;  // block kc of scale chunk gc
-        if (kc == 0 && !warp_wait(&sc_full[ss], (uint32_t)(gc / kScs) & 1u)) { ok = false; break; }
+        if (kc == 0 && !__all_sync(0xffffffffu, mbar_wait(&sc_full[ss], (uint32_t)(gc / kScs) & 1u))) { ok = false; break; }
         const unsigned char *sc = scs + ss * L::kSc;
         const float dwv = __half2float(((const __half *)sc)[kc * SC_GROUP_ROWS + row]);
         const uint64_t dw2 = pack2(dwv, dwv);
         const uint64_t *dx2 = (const uint64_t *)(sc + L::kScW) + (kc * FT + col_base) / 2;
-        const uint32_t tb = taddr + (uint32_t)((gb % kAcc) * FT);
+        const int ps = gp % kPairs;
+        const uint32_t tb = taddr + (uint32_t)((2 * ps + (k & 1)) * FT);
         tc_wait_ld<H>(rA);
         tc_ld<H>(tb + H, rB);
         drain_half<H, 0>(acc, rA, dw2, dx2, nz2);
         tc_wait_ld<H>(rB);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[gb % kAcc]);
+        const bool pair_end = (k & 1) || k + 1 == nb;
+        if (pair_end) {  // both of the pair's accumulators are loaded
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[ps]);
+          gp++;
+        }
         if (k + 1 < nb) {
-          if (!warp_wait(&tfull[(gb + 1) % kAcc], (uint32_t)((gb + 1) / kAcc) & 1u)) { ok = false; break; }
-          tc_fence_after();
-          tc_ld<H>(taddr + (uint32_t)(((gb + 1) % kAcc) * FT), rA);
+          if (pair_end) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[gp % kPairs], (uint32_t)(gp / kPairs) & 1u))) { ok = false; break; }
+            tc_fence_after();
+          }
+          tc_ld<H>(taddr + (uint32_t)((2 * (gp % kPairs) + ((k + 1) & 1)) * FT), rA);
         }
         drain_half<H, H / 2>(acc, rB, dw2, dx2 + H / 2, nz2);
         if (kc == kTcScB - 1 || k + 1 == nb) {  // the chunk's scales are used
