@@ -21,6 +21,8 @@ Also in the line:
   gemm_sweep    the Q8_0 GEMM shape sweep of one layer (M = 1, 8, 32, 128;
                 QKV, out-proj, FFN-up, FFN-down; 24 weight copies, 321 MB)
                 as HBM GB/s, and its weight-streaming kernel's roofline;
+                config0 is the single streaming chunk (M 8, K 1024, N 4096)
+                on its own;
   e2e           the same metric through the C ABI with host mel buffers:
                 pinned host -> device copy of each step's mel, encode_new,
                 device -> pinned host copy of the step's output frames;
@@ -28,6 +30,11 @@ Also in the line:
                 encoder given 56 encoder frames (448 mel) per encode_new call
                 (13 calls + a 22-frame tail), so every GEMM sees M = 64 * 56
                 frames; audio seconds per second of CUDA-event time;
+  box_scale     the box-scale streaming batch: 8192 concurrent streams
+                sharded by stream over the GPUs (8192 / N per GPU, each
+                rank's shard in one encoder; a shard that does not fit in
+                device memory is halved, and the streams actually resident
+                are reported), audio seconds per second over all ranks;
   transcriber   the streaming transcriber's whole step (LiveTranscriber::
                 process): encode_new, then the RNN-T greedy decode of each
                 stream's 7 new frames (random-init 2 x 640 LSTM predictor,
@@ -92,6 +99,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-decoder", action="store_true", help="skip the transcriber (encoder + decoder) block")
     ap.add_argument("--no-prefill", action="store_true", help="skip the 750-frame prefill block")
+    ap.add_argument("--box-streams", type=int, default=8192,
+                    help="global streams of the box-scale block (sharded over the GPUs); 0 skips it")
+    ap.add_argument("--box-steps", type=int, default=3)
     ap.add_argument("--profile", default=None, choices=["gemm", "attn", "tc", "encoder", "breakdown"],
                     help="small eager case for ncu captures (no timing, no JSON line); breakdown: per-kernel "
                          "device time of 3 steady headline steps (CUPTI through torch.profiler)")
@@ -158,9 +168,9 @@ def reduce_max(value: float, device) -> float:
 def stream_shard(global_streams: int, world: int, rank: int):
     """Contiguous streams [lo, hi) of `rank` when `global_streams` independent
     streams are spread over `world` GPUs (the first ranks take the remainder)."""
-    base, extra = divmod(global_streams, world)
-    lo = rank * base + min(rank, extra)
-    return lo, lo + base + (1 if rank < extra else 0)
+    from stealcode_b200 import shards
+
+    return shards.stream_shard(global_streams, world, rank)
 
 
 def peaks():
@@ -494,6 +504,34 @@ def gemm_sweep(args, dev, world, stream):
     kb = sum(kernel_bytes(m, k, n) for m in MS for _ in range(SWEEP_LAYERS) for _, k, n in SHAPES)
     del g_k
     achieved = kb / (ms_k * 1e-3) / 1e9
+    # the single streaming chunk (M 8, K 1024, N 4096) on its own, over 64
+    # weight copies (285 MB, larger than L2), through sc_q8_gemm (the
+    # streaming kernel quantises the activations itself)
+    c0 = [Q8Mat(wh["ffn_up"], 4096, 1024) for _ in range(64)]
+    x0, y0 = xs[(8, 1024)], ys[(8, 4096)]
+
+    def calls0(sp):
+        for mt in c0:
+            check(lib.sc_q8_gemm(mt.handle, x0.data_ptr(), 8, SC_LAYOUT_TIME_MAJOR, 0, None, y0.data_ptr(),
+                                 SC_LAYOUT_TIME_MAJOR, 0, ws.data_ptr(), ws_bytes, sp))
+        return len(c0)
+
+    s0 = torch.cuda.Stream(device=dev)
+    s0.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s0):
+        calls0(s0.cuda_stream)
+    torch.cuda.current_stream().wait_stream(s0)
+    torch.cuda.synchronize()
+    g0 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g0):
+        n0 = calls0(torch.cuda.current_stream().cuda_stream)
+    ms0 = time_graph(g0, reps)
+    del g0
+    b0 = gemm_bytes(8, 1024, 4096)
+    config0 = {"workload": "q8_gemm M=8 K=1024 N=4096 (one streaming chunk), 64 weight copies in a graph",
+               "us_per_gemm": 1e3 * ms0 / n0, "bytes_per_gemm": b0, "gbs": b0 * n0 / (ms0 * 1e-3) / 1e9,
+               "frac": b0 * n0 / (ms0 * 1e-3) / 1e9 / peak, "peak_source": "measured" if "hbm_gbs" in p else "fallback"}
+    del c0
     return {"metric": "Q8_0 GEMM HBM GB/s (FastConformer layer shape sweep)", "value": step_bytes / (ms * 1e-3) / 1e9,
             "unit": "GB/s", "shapes": SHAPES, "m": MS, "weight_copies": SWEEP_LAYERS, "ms_per_sweep": ms,
             "launches_per_sweep": n_launch,
@@ -501,7 +539,8 @@ def gemm_sweep(args, dev, world, stream):
                          "frac": achieved / peak, "peak_source": "measured" if "hbm_gbs" in p else "fallback",
                          "frac_of_spec_8000_gbs": achieved / 8000.0,
                          "kernel": "q8_gemm_stream_kernel", "bytes_per_launch_avg": kb / n_k,
-                         "us_per_launch_avg": 1e3 * ms_k / n_k, "traffic": None, "by_m": by_m}}
+                         "us_per_launch_avg": 1e3 * ms_k / n_k, "traffic": None, "by_m": by_m},
+            "config0": config0}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -597,6 +636,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.empty_cache()
 
     prefill = None if args.no_prefill else prefill_leg(m, world, dev, stream)
+    box = box_leg(args, m, world, rank, dev, stream) if args.box_streams > 0 else None
     roof = tc_roofline(m, Z, dev, stream)
     sweep = None if args.no_sweep else gemm_sweep(args, dev, world, stream)
     if world > 1:
@@ -624,7 +664,7 @@ def run_ours(args, rank, world, local_rank):
                            "parallelism": f"streams sharded, {world} independent ranks",
                            "l2": "inputs larger than L2: each step streams 587 MB of Q8_0 weights (L2 126 MB)"},
                 "realtime_streams_per_gpu": value / world,
-                "roofline": roof, "gemm_sweep": sweep, "cpu_baseline": cpu, "e2e": e2e, "transcriber": trans, "prefill": prefill,
+                "roofline": roof, "gemm_sweep": sweep, "cpu_baseline": cpu, "e2e": e2e, "transcriber": trans, "prefill": prefill, "box_scale": box,
                 "gpu_launches": launches_timed, "launches_per_step": launches / (args.steps + args.warmup),
                 "clocks": clk, "peaks_file": {k: p.get(k) for k in ("hbm_gbs", "bf16_tflops")}}
         print(json.dumps(line), flush=True)
@@ -680,6 +720,66 @@ def prefill_leg(m, world, dev, stream):
             "frames_per_stream": frames, "calls": len(calls), "frames_per_call": PREFILL_CALL_MEL // 8,
             "frames_per_gemm": step_halves(Z, PREFILL_CALL_MEL // 8),
             "note": "same encoder and bits as streaming; long calls, attention run chunk by chunk inside a call"}
+
+
+def box_leg(args, m, world, rank, dev, stream):
+    """The box-scale streaming batch: `--box-streams` concurrent streams (8192)
+    sharded by stream over the ranks, each rank's shard in one encoder (its
+    two halves in flight), no collective on the data path.  A rank whose
+    shard does not fit in device memory halves it until it does (the line
+    reports the streams actually resident).  Steady state after the priming
+    steps; value = resident streams x 0.56 s / max-over-ranks step time."""
+    import torch
+    import torch.distributed as dist
+
+    from stealcode_b200 import _lib
+    from stealcode_b200.ops import StreamEncoder
+
+    lo, hi = stream_shard(args.box_streams, world, rank)
+    want = hi - lo
+    Z, enc = want, None
+    free0, total = torch.cuda.mem_get_info(dev)
+    while Z > 0 and enc is None:
+        try:
+            enc = StreamEncoder(m, Z)
+        except _lib.ScError as exc:
+            if exc.code != _lib.SC_ERR_ALLOC:
+                raise
+            Z = Z // 2 // 128 * 128 if Z > 256 else Z // 2
+    used = free0 - torch.cuda.mem_get_info(dev)[0]
+    cfg = m.config
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(MODEL_SEED + 13 + rank)
+    pool = [torch.randn((Z, MEL_PER_STEP, cfg.feat_in), device=dev, generator=gen) for _ in range(2)]
+    state = {"i": 0}
+
+    def step():
+        i = state["i"]
+        enc.encode_new(pool[i % 2], MEL_PER_STEP * i, MEL_PER_STEP * (i + 1), stream=stream)
+        state["i"] = i + 1
+
+    with torch.cuda.stream(stream):
+        for _ in range(PRIME_STEPS):
+            step()
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    ms = time_steps(step, args.box_steps, 1, world, dev, stream)
+    launches = (_lib.launch_count() - n0) / (args.box_steps + 1)
+    enc.close()
+    del pool, enc
+    torch.cuda.empty_cache()
+    resident = Z
+    if world > 1:
+        t = torch.tensor([Z], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        resident = int(t.item())
+    return {"value": resident * AUDIO_S_PER_STEP / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
+            "global_streams_requested": args.box_streams, "global_streams_resident": resident,
+            "streams_per_gpu": Z, "requested_per_gpu": want, "frames_per_gemm": step_halves(Z),
+            "device_bytes_used": used, "device_bytes_total": total, "steps": args.box_steps,
+            "prime_steps": PRIME_STEPS, "launches_per_step": launches,
+            "realtime_streams_per_gpu": resident * AUDIO_S_PER_STEP / (ms * 1e-3) / world,
+            "note": "the headline encoder, 8192 streams sharded by stream over the GPUs (no collective)"}
 
 
 def transcriber_leg(args, enc, pool, state, Z, world, dev, stream):

@@ -259,10 +259,11 @@ struct Loader {
     w.nb = nb;
     w.rows_pad = (rows + SC_GROUP_ROWS - 1) / SC_GROUP_ROWS * SC_GROUP_ROWS;
     w.device = e->device;
-    bool ok = cudaMemcpy(draw, raw.data(), raw.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
-              dev_malloc((void **)&w.qs, (size_t)w.rows_pad * nb * 32) == cudaSuccess &&
-              dev_malloc((void **)&w.sc, (size_t)w.rows_pad * nb * 2) == cudaSuccess &&
-              dev_malloc((void **)&w.qh, (size_t)w.rows_pad * nb * 64) == cudaSuccess &&
+    const bool allocated = dev_malloc((void **)&w.qs, (size_t)w.rows_pad * nb * 32) == cudaSuccess &&
+                           dev_malloc((void **)&w.sc, (size_t)w.rows_pad * nb * 2) == cudaSuccess &&
+                           dev_malloc((void **)&w.qh, (size_t)w.rows_pad * nb * 64) == cudaSuccess;
+    if (!allocated) err = "cudaMalloc failed";
+    bool ok = allocated && cudaMemcpy(draw, raw.data(), raw.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
               repack_q8_device(draw, rows, inp, 34, 2, &w, 0) == kOk && cudaDeviceSynchronize() == cudaSuccess;
     cudaFree(draw);
     if (!ok) {
@@ -421,11 +422,14 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     e->out_ring = L.dev_alloc((size_t)(n_streams * e->out_cap * d * 4));
     e->hist[0] = L.dev_alloc((size_t)(n_streams * kMelHistory * c.feat_in * 4));
     e->hist[1] = L.dev_alloc((size_t)(n_streams * kMelHistory * c.feat_in * 4));
-    const int64_t t0 = conv_out(e->t_mel_max), f0 = conv_out(c.feat_in);
+    // the pre-encode buffers hold conv.2's (and conv.3's) output rows at
+    // most, [tb][fb][C] per stream (conv.0's output is never stored: the
+    // fused conv.0 + conv.2 kernel rebuilds the rows it reads)
+    const int64_t tb_max = conv_out(conv_out(e->t_mel_max)), fb = conv_out(conv_out(c.feat_in));
     e->win = L.dev_alloc((size_t)(n_streams * e->t_mel_max * c.feat_in * 4));
-    e->p0 = L.dev_alloc((size_t)(n_streams * t0 * f0 * C * 4));
-    e->p1 = L.dev_alloc((size_t)(n_streams * t0 * f0 * C * 4));
-    e->p2 = L.dev_alloc((size_t)(n_streams * t0 * f0 * C * 4));
+    e->p0 = L.dev_alloc((size_t)(n_streams * tb_max * fb * C * 4));
+    e->p1 = L.dev_alloc((size_t)(n_streams * tb_max * fb * C * 4));
+    e->p2 = L.dev_alloc((size_t)(n_streams * tb_max * fb * C * 4));
     e->flat = L.dev_alloc((size_t)(M * f_final * C * 4));
     e->pos_in = L.dev_alloc((size_t)(e->n_pos * d * 4));
     const int64_t kmax = std::max<int64_t>(std::max<int64_t>(std::max<int64_t>(dff, f_final * C), d),
@@ -437,7 +441,7 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     e->mel_stage_frames = 8 * (int64_t)c.max_frames;
     e->mel_stage = L.dev_alloc((size_t)(n_streams * e->mel_stage_frames * c.feat_in * 4));
     e->win_stride = e->t_mel_max * c.feat_in;
-    e->conv_stride = t0 * f0 * C;
+    e->conv_stride = tb_max * fb * C;
     e->code_k = kp;
     for (int i = 0; i < 2; i++) {
       e->qx[i] = (__half *)L.dev_alloc((size_t)(tp * kp * 2));
