@@ -126,6 +126,23 @@ int sc_q8_gemm_q(const sc_q8w *w, const int8_t *xq, const float *dx,
                  int64_t t, int64_t t_pad, const float *bias, float *y,
                  int32_t y_layout, int64_t ldy, void *stream);
 
+/* n independent GEMMs y[i] = W[i] x[i] (+ bias[i]) of the same frame count
+ * t (0..16) in one streaming pass over their weights (1 <= n <= 128; host
+ * arrays of handles and device pointers; bias may be NULL or hold NULLs):
+ * the batched form of q8_gemm (sgemm_kernel.rs:99-127) for the streaming
+ * chunk's small M, where one GEMM's weights take HBM well under a
+ * microsecond and a launch per GEMM would cost more than the weights.  Each
+ * output agrees with sc_q8_gemm's within the same f32 tolerance (both use
+ * the per-block fused multiply-add of the streaming kernel).  Packed leading
+ * dimensions.  workspace (256-byte aligned, sc_q8_gemm_batch_workspace_bytes)
+ * may be NULL for the per-device library workspace.  No counterpart in the
+ * reference, which calls q8_gemm once per matrix.  Async on stream. */
+int64_t sc_q8_gemm_batch_workspace_bytes(const sc_q8w *const *w, int32_t n);
+int sc_q8_gemm_batch(const sc_q8w *const *w, const float *const *x,
+                     const float *const *bias, float *const *y, int32_t n,
+                     int64_t t, int32_t x_layout, int32_t y_layout,
+                     void *workspace, int64_t workspace_bytes, void *stream);
+
 /* Size of the fixed device array behind sc_q8_gemm_noalloc (4 MiB). */
 #define SC_Q8_GEMM_NOALLOC_SCRATCH_BYTES (4u << 20)
 

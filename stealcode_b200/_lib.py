@@ -66,6 +66,8 @@ SIGNATURES = {
     "sc_q8_gemm": (c_int, [_P, _P, _I, c_int32, _I, _P, _P, c_int32, _I, _P, _I, _P]),
     "sc_q8_gemm_noalloc": (c_int, [_P, _P, _I, c_int32, _I, _P, _P, c_int32, _I, _P]),
     "sc_q8_gemm_q": (c_int, [_P, _P, _P, _I, _I, _P, _P, c_int32, _I, _P]),
+    "sc_q8_gemm_batch_workspace_bytes": (c_int64, [_P, c_int32]),
+    "sc_q8_gemm_batch": (c_int, [_P, _P, _P, _P, c_int32, _I, c_int32, c_int32, _P, _I, _P]),
     "sc_q8mat_gemm_t": (c_int, [_P, _P, _I, _P]),
     "sc_q8_gemm_host": (c_int, [c_size_t, c_size_t, c_size_t, _P, c_size_t, c_size_t, c_size_t, _P, _P]),
     "sc_q8_quantize": (c_int, [_P, _I, _I, c_int32, _I, _P, _P, _P]),

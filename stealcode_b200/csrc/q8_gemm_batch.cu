@@ -1,0 +1,279 @@
+// q8_gemm_batch.cu -- many independent small-M Q8_0 GEMMs in one streaming
+// pass: y_i = W_i x_i (+ bias_i) for i < n, every x_i with the same frame
+// count t <= 16.
+//
+// A single small-M GEMM moves a few MB of weights, which HBM delivers in well
+// under a microsecond; one launch's fixed costs (launch, first bytes' latency,
+// the K-split reduction, the tail) are several times that.  Independent
+// GEMMs -- the attention's Q, K, V and position projections, one projection
+// over many adapters, the layer-shape sweep of the benchmark -- need not pay
+// them one by one: here one persistent launch streams all their weights back
+// to back, so the HBM stream never stops between matrices.
+//
+// Arithmetic per output as the single-GEMM streaming kernel (q8_gemm_small.cu):
+// exact int8 x int8 block dots (dp4a), acc += (dw * dx) * dot with one fused
+// multiply-add per block, f32 accumulation (the reference's SIMD dispatch for
+// up to 16 frames sums in another f32 order, simd_kernel.rs:333-393; outputs
+// agree within the 1e-4 x RMS bar).  Activations are quantised exactly as
+// quantize_col (sgemm_kernel.rs:57-90) by a first launch.
+//
+// Stream kernel, persistent (one CTA per SM): work unit = (GEMM, 128-row
+// group), all of K; units are dealt round-robin.  Warp 0: one thread streams
+// the units' weight tiles and scales (4 K blocks per bulk copy, no multicast)
+// through a ring of shared-memory stages; warps 1-8: lane = weight row, 4 row
+// quarters x 2 block parities, dp4a from shared memory with the activation
+// codes read through L1 (all lanes the same address); the two parities'
+// partial sums are added in shared memory at the end of a unit.
+#include "sc_device.cuh"
+#include "sc_kernels.cuh"
+
+namespace sc {
+
+constexpr int kBatchKb = 4;      // K blocks per stage
+constexpr int kBatchStages = 12;  // 12 x 17 KB in flight per SM
+constexpr int kBatchComputeWarps = 8;
+constexpr int kBatchThreads = 32 + 32 * kBatchComputeWarps;
+constexpr int kBatchStage = kBatchKb * (SC_TILE_BYTES + SC_GROUP_ROWS * 2);
+
+static __device__ unsigned g_batch_status;
+
+struct BatchParams {
+  int n, t, y_time_major, total_units;
+  unsigned *status;
+  BatchItem items[kMaxBatch];
+};
+
+__device__ __forceinline__ int bdot32(const int4 w0, const int4 w1, const int4 x0, const int4 x1) {
+  int d = __dp4a(w0.x, x0.x, 0);
+  d = __dp4a(w0.y, x0.y, d);
+  d = __dp4a(w0.z, x0.z, d);
+  d = __dp4a(w0.w, x0.w, d);
+  d = __dp4a(w1.x, x1.x, d);
+  d = __dp4a(w1.y, x1.y, d);
+  d = __dp4a(w1.z, x1.z, d);
+  d = __dp4a(w1.w, x1.w, d);
+  return d;
+}
+
+// Item owning work unit u (the items' units are consecutive).
+__device__ __forceinline__ int batch_item(const BatchParams &p, int u) {
+  int lo = 0, hi = p.n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.items[mid].unit0 <= u) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Activation codes of every item: one warp per (item, frame < 16, block):
+// frames t .. 15 get zero codes, so the stream kernel may read all MT frames.
+__global__ void batch_quantize_kernel(const __grid_constant__ BatchParams p) {
+  const int i = blockIdx.y;
+  const BatchItem &it = p.items[i];
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (wid >= (int64_t)kBatchFrames * it.nb) return;
+  const int j = (int)(wid / it.nb), b = (int)(wid % it.nb);
+  const int64_t kk = (int64_t)b * 32 + lane;
+  const bool valid = j < p.t && kk < it.k;
+  const float v = valid ? (it.x_feature_major ? it.x[kk * it.ldx + j] : it.x[(int64_t)j * it.ldx + kk]) : 0.0f;
+  float s;
+  const int8_t q = warp_quantize_block(v, valid, s);
+  it.xq[(int64_t)j * it.nb * 32 + kk] = q;
+  if (lane == 0) it.dx[(int64_t)b * kBatchFrames + j] = s;
+  pdl_launch_dependents();
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kBatchThreads, 1) q8_gemm_batch_kernel(const __grid_constant__ BatchParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t *full = (uint64_t *)(smem + kBatchStages * kBatchStage);
+  uint64_t *empty = full + kBatchStages;
+  float *part = (float *)(empty + kBatchStages);  // [8 warps][MT][32]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBatchStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kBatchComputeWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  bool ok = true;
+  if (warp == 0) {
+    // ---- producer: weights never change, so they stream before the
+    // activation codes' kernel has finished ----
+    if (lane == 0) {
+      int gs = 0;
+      for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+        const BatchItem &it = p.items[batch_item(p, u)];
+        const int64_t g = u - it.unit0;
+        for (int b0 = 0; b0 < it.nb; b0 += kBatchKb, gs++) {
+          const int s = gs % kBatchStages, nblk = it.nb - b0 < kBatchKb ? it.nb - b0 : kBatchKb;
+          if (!mbar_wait(&empty[s], ((uint32_t)(gs / kBatchStages) & 1u) ^ 1u)) { ok = false; break; }
+          unsigned char *st = smem + s * kBatchStage;
+          mbar_arrive_expect_tx(&full[s], nblk * (SC_TILE_BYTES + SC_GROUP_ROWS * 2));
+          bulk_g2s(st, it.qs + (g * it.nb + b0) * SC_TILE_BYTES, nblk * SC_TILE_BYTES, &full[s]);
+          bulk_g2s(st + kBatchKb * SC_TILE_BYTES, it.sc + (g * it.nb + b0) * SC_GROUP_ROWS, nblk * SC_GROUP_ROWS * 2,
+                   &full[s]);
+        }
+      }
+      // the last copies have landed before the CTA can exit
+      for (int q = gs - kBatchStages; q < gs; q++)
+        if (q >= 0) mbar_wait(&full[q % kBatchStages], (uint32_t)(q / kBatchStages) & 1u);
+    }
+    __syncwarp();
+  } else {
+    pdl_wait();  // the activation codes
+    const int cw = warp - 1, rs = cw & 3, kp = cw >> 2;
+    const int r = rs * 32 + lane;
+    int gs = 0;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      const BatchItem &it = p.items[batch_item(p, u)];
+      const int64_t g = u - it.unit0;
+      float acc[MT];
+#pragma unroll
+      for (int j = 0; j < MT; j++) acc[j] = 0.0f;
+      for (int b0 = 0; b0 < it.nb; b0 += kBatchKb, gs++) {
+        const int s = gs % kBatchStages, nblk = it.nb - b0 < kBatchKb ? it.nb - b0 : kBatchKb;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(gs / kBatchStages) & 1u))) { ok = false; break; }
+        const unsigned char *st = smem + s * kBatchStage;
+        const __half *scs = (const __half *)(st + kBatchKb * SC_TILE_BYTES);
+        for (int bb = kp; bb < nblk; bb += 2) {
+          const unsigned char *tw = st + bb * SC_TILE_BYTES + r * 16;
+          const int4 w0 = *(const int4 *)tw, w1 = *(const int4 *)(tw + 2048);
+          const float dw = __half2float(scs[bb * SC_GROUP_ROWS + r]);
+          const int64_t b = b0 + bb;
+#pragma unroll
+          for (int j = 0; j < MT; j++) {
+            const int4 *xp = (const int4 *)(it.xq + ((int64_t)j * it.nb + b) * 32);
+            const int d = bdot32(w0, w1, __ldg(xp), __ldg(xp + 1));
+            acc[j] = fmaf(dw * __ldg(it.dx + b * kBatchFrames + j), (float)d, acc[j]);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      if (!ok) break;
+      // the two block parities' partial sums, then y (+ bias)
+#pragma unroll
+      for (int j = 0; j < MT; j++) part[(cw * MT + j) * 32 + lane] = acc[j];
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * kBatchComputeWarps) : "memory");
+      if (kp == 0) {
+        const int64_t n = g * SC_GROUP_ROWS + r;
+        if (n < it.rows) {
+          const float bn = it.bias ? it.bias[n] : 0.0f;
+#pragma unroll
+          for (int j = 0; j < MT; j++)
+            if (j < p.t) {
+              const float v = part[(cw * MT + j) * 32 + lane] + part[((cw + 4) * MT + j) * 32 + lane] + bn;
+              it.y[p.y_time_major ? (int64_t)j * it.ldy + n : n * it.ldy + j] = v;
+            }
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * kBatchComputeWarps) : "memory");
+    }
+  }
+  if (!ok) atomicOr(p.status, kStatusWaitTimeout);
+}
+
+static unsigned *batch_status_ptr() {
+  static std::atomic<unsigned *> ptr[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  unsigned *q = ptr[dev].load(std::memory_order_acquire);
+  if (!q) {
+    void *a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_batch_status) != cudaSuccess) return nullptr;
+    q = (unsigned *)a;
+    ptr[dev].store(q, std::memory_order_release);
+  }
+  return q;
+}
+
+template <int MT>
+static std::atomic<size_t> *batch_smem_limit() {
+  static std::atomic<size_t> limit[64];
+  return limit;
+}
+
+constexpr size_t kBatchSmem = (size_t)kBatchStages * kBatchStage + 16 * kBatchStages +
+                              (size_t)kBatchComputeWarps * 16 * 32 * 4;
+
+template <int MT>
+static int launch_batch(const BatchParams &p, int sm_count, cudaStream_t st) {
+  auto kern = q8_gemm_batch_kernel<MT>;
+  const int rc = raise_smem_limit((const void *)kern, kBatchSmem, batch_smem_limit<MT>());
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.total_units < sm_count ? p.total_units : sm_count), 1, 1);
+  cfg.blockDim = dim3(kBatchThreads, 1, 1);
+  cfg.dynamicSmemBytes = kBatchSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  note_launch();
+  SC_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
+  return kOk;
+}
+
+size_t batch_ws_bytes(const BatchItem *items, int n) {
+  size_t bytes = 0;
+  for (int i = 0; i < n; i++)
+    bytes += ((size_t)kBatchFrames * items[i].nb * 32 + 255) / 256 * 256 +
+             ((size_t)kBatchFrames * items[i].nb * 4 + 255) / 256 * 256;
+  return bytes;
+}
+
+int gemm_batch(BatchItem *items, int n, int t, int y_time_major, void *ws, size_t ws_bytes, int sm_count,
+               cudaStream_t st) {
+  if (n <= 0 || n > kMaxBatch || t <= 0 || t > kBatchFrames) {
+    set_error("q8_gemm_batch: 1..%d GEMMs of 1..%d frames", kMaxBatch, kBatchFrames);
+    return kErrInvalid;
+  }
+  if (ws_bytes < batch_ws_bytes(items, n) || ((uintptr_t)ws & 255)) {
+    set_error("q8_gemm_batch: workspace needs %zu bytes at 256-byte alignment", batch_ws_bytes(items, n));
+    return kErrInvalid;
+  }
+  BatchParams p{};
+  p.n = n;
+  p.t = t;
+  p.y_time_major = y_time_major;
+  p.status = batch_status_ptr();
+  if (!p.status) {
+    set_error("q8_gemm_batch: status word lookup failed");
+    return kErrCuda;
+  }
+  char *w = (char *)ws;
+  int units = 0, nb_max = 0;
+  for (int i = 0; i < n; i++) {
+    BatchItem it = items[i];
+    it.xq = (int8_t *)w;
+    w += ((size_t)kBatchFrames * it.nb * 32 + 255) / 256 * 256;
+    it.dx = (float *)w;
+    w += ((size_t)kBatchFrames * it.nb * 4 + 255) / 256 * 256;
+    it.unit0 = units;
+    units += it.groups;
+    nb_max = it.nb > nb_max ? it.nb : nb_max;
+    p.items[i] = it;
+  }
+  p.total_units = units;
+  dim3 qgrid((unsigned)ceil_div((int64_t)kBatchFrames * nb_max * 32, 256), (unsigned)n);
+  batch_quantize_kernel<<<qgrid, 256, 0, st>>>(p);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  const int mt = t <= 1 ? 1 : t <= 2 ? 2 : t <= 4 ? 4 : t <= 8 ? 8 : 16;
+  switch (mt) {
+    case 1: return launch_batch<1>(p, sm_count, st);
+    case 2: return launch_batch<2>(p, sm_count, st);
+    case 4: return launch_batch<4>(p, sm_count, st);
+    case 8: return launch_batch<8>(p, sm_count, st);
+    default: return launch_batch<16>(p, sm_count, st);
+  }
+}
+
+}  // namespace sc

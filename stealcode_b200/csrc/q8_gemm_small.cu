@@ -93,7 +93,9 @@ __global__ void __launch_bounds__(kStreamThreads)
   __half *sbuf = (__half *)(smem + (size_t)p.nbl_max * SC_TILE_BYTES);  // [nbl][128]
   int8_t *xs = (int8_t *)(sbuf + (size_t)p.nbl_max * SC_GROUP_ROWS);   // [MT][nbl*32]
   float *dxs = (float *)(xs + (size_t)MT * p.nbl_max * 32);      // [nbl][MT]
-  float *part = dxs + (size_t)p.nbl_max * MT;                    // [8][MT][32]
+  // partial sums (then the barrier) at the next 16-byte boundary: the scales
+  // before them take nbl_max * MT * 4 bytes, not always a multiple of 8
+  float *part = (float *)(((uintptr_t)(dxs + (size_t)p.nbl_max * MT) + 15) & ~(uintptr_t)15);  // [8][MT][32]
   uint64_t *bar = (uint64_t *)(part + 8 * MT * 32);
 
   if (tid == 0) {
@@ -225,7 +227,7 @@ __global__ void __launch_bounds__(kStreamThreads)
 
 static size_t stream_smem(int mt, int nbl_max) {
   return (size_t)nbl_max * (SC_TILE_BYTES + SC_GROUP_ROWS * 2) + (size_t)mt * nbl_max * 32 +
-         (size_t)nbl_max * mt * 4 + (size_t)8 * mt * 32 * 4 + 16;
+         (size_t)nbl_max * mt * 4 + 16 + (size_t)8 * mt * 32 * 4 + 16;  // + alignment pad, barrier
 }
 
 // Shared-memory limit raised so far per device, per kernel instance.

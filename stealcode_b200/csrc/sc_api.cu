@@ -9,6 +9,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <vector>
+
 #include "sc_kernels.cuh"
 #include "../../include/stealcode_b200.h"
 
@@ -428,6 +430,74 @@ int sc_q8_gemm_q(const sc_q8w *w, const int8_t *xq, const float *dx, int64_t t, 
   SmallGemmArgs a{&W, nullptr, 0, 0, xq, dx, W.nb * 32, t_pad, t, bias, y, y_layout == SC_LAYOUT_TIME_MAJOR, ldy,
                   nullptr, Epilogue{}};
   return gemm_small(a, sms, (cudaStream_t)stream);
+}
+
+static int batch_items(const sc_q8w *const *w, const float *const *x, const float *const *bias, float *const *y,
+                       int32_t n, int64_t t, int32_t x_layout, int32_t y_layout, std::vector<BatchItem> &items) {
+  if (!w || n <= 0 || n > kMaxBatch || t < 0 || t > kBatchFrames || !layout_ok(x_layout) || !layout_ok(y_layout)) {
+    set_error("q8_gemm_batch: 1..%d GEMMs of 0..%d frames and valid layouts", kMaxBatch, kBatchFrames);
+    return kErrInvalid;
+  }
+  int dev;
+  int rc = current_device(&dev, nullptr);
+  if (rc) return rc;
+  items.resize(n);
+  for (int i = 0; i < n; i++) {
+    if (!w[i] || (x && !x[i]) || (y && !y[i])) {
+      set_error("q8_gemm_batch: null weights, input or output %d", i);
+      return kErrInvalid;
+    }
+    const Q8Weights &W = w[i]->w;
+    if (W.device != dev) {
+      set_error("q8_gemm_batch: weights %d live on device %d, current device is %d", i, W.device, dev);
+      return kErrInvalid;
+    }
+    BatchItem it{};
+    it.qs = W.qs;
+    it.sc = W.sc;
+    it.x = x ? x[i] : nullptr;
+    it.bias = bias ? bias[i] : nullptr;
+    it.y = y ? y[i] : nullptr;
+    it.ldx = x_layout == SC_LAYOUT_TIME_MAJOR ? W.k : t;
+    it.ldy = y_layout == SC_LAYOUT_TIME_MAJOR ? W.rows : t;
+    it.nb = (int32_t)W.nb;
+    it.rows = (int32_t)W.rows;
+    it.groups = (int32_t)(W.rows_pad / SC_GROUP_ROWS);
+    it.k = (int32_t)W.k;
+    it.x_feature_major = x_layout == SC_LAYOUT_FEATURE_MAJOR;
+    items[i] = it;
+  }
+  return kOk;
+}
+
+int64_t sc_q8_gemm_batch_workspace_bytes(const sc_q8w *const *w, int32_t n) {
+  std::vector<BatchItem> items;
+  if (batch_items(w, nullptr, nullptr, nullptr, n, 1, SC_LAYOUT_TIME_MAJOR, SC_LAYOUT_TIME_MAJOR, items)) return -1;
+  return (int64_t)batch_ws_bytes(items.data(), n);
+}
+
+int sc_q8_gemm_batch(const sc_q8w *const *w, const float *const *x, const float *const *bias, float *const *y,
+                     int32_t n, int64_t t, int32_t x_layout, int32_t y_layout, void *workspace,
+                     int64_t workspace_bytes, void *stream) {
+  std::vector<BatchItem> items;
+  if (!x || !y) {
+    set_error("q8_gemm_batch: invalid argument");
+    return kErrInvalid;
+  }
+  int rc = batch_items(w, x, bias, y, n, t, x_layout, y_layout, items);
+  if (rc) return rc;
+  if (t == 0) return kOk;
+  const size_t need = batch_ws_bytes(items.data(), n);
+  if (!workspace) {
+    rc = default_ws(need, &workspace);
+    if (rc) return rc;
+    workspace_bytes = (int64_t)need;
+  }
+  int dev, sms;
+  rc = current_device(&dev, &sms);
+  if (rc) return rc;
+  return gemm_batch(items.data(), n, (int)t, y_layout == SC_LAYOUT_TIME_MAJOR, workspace, (size_t)workspace_bytes,
+                    sms, (cudaStream_t)stream);
 }
 
 int sc_q8_gemm_host(size_t m, size_t k, size_t n, const uint8_t *w, size_t padded_row, size_t block_bytes,

@@ -65,6 +65,25 @@ int small_gemm_prime();
 int mid_gemm_prime();
 int tc_gemm_prime();
 
+// q8_gemm_batch.cu: up to kMaxBatch independent GEMMs of the same t <=
+// kBatchFrames frames in one streaming pass.  The caller fills qs .. k,
+// x_feature_major; gemm_batch sets xq, dx (workspace) and unit0.
+constexpr int kMaxBatch = 128, kBatchFrames = 16;
+struct BatchItem {
+  const int8_t *qs;
+  const __half *sc;
+  const float *x;
+  const float *bias;
+  float *y;
+  int8_t *xq;   // [kBatchFrames][nb * 32] activation codes
+  float *dx;    // [nb][kBatchFrames] their block scales
+  int64_t ldx, ldy;
+  int32_t nb, rows, groups, unit0, k, x_feature_major;
+};
+size_t batch_ws_bytes(const BatchItem *items, int n);
+int gemm_batch(BatchItem *items, int n, int t, int y_time_major, void *ws, size_t ws_bytes, int sm_count,
+               cudaStream_t st);
+
 // q8_gemm_mid.cu: 16 < m <= 128 frames, q8_gemm_scalar's order (bit-exact)
 struct MidGemmArgs {
   const Q8Weights *w;

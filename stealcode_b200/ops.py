@@ -429,3 +429,26 @@ class RnntDecoder:
 
 __all__ = ["StreamEncoder", "RnntDecoder", "q8_gemm", "Q8Mat", "Lin", "quantize", "AttnStreamKernel", "attn_stream_ring",
            "SC_LAYOUT_FEATURE_MAJOR", "SC_LAYOUT_TIME_MAJOR", "_lib"]
+
+
+def q8_gemm_batch(mats, xs, *, biases=None, outs=None, x_layout: int = SC_LAYOUT_TIME_MAJOR,
+                  y_layout: int = SC_LAYOUT_TIME_MAJOR, workspace=None, stream=None):
+    """Independent GEMMs y[i] = mats[i] x[i] (+ biases[i]) of the same frame
+    count (<= 16) in one streaming pass (sc_q8_gemm_batch); torch CUDA
+    tensors; returns the outputs."""
+    import torch
+
+    n = len(mats)
+    t = xs[0].shape[0] if x_layout == SC_LAYOUT_TIME_MAJOR else xs[0].shape[1]
+    if outs is None:
+        outs = [torch.empty((t, m.rows) if y_layout == SC_LAYOUT_TIME_MAJOR else (m.rows, t), dtype=torch.float32,
+                            device=xs[0].device) for m in mats]
+    P = ctypes.c_void_p
+    hw = (P * n)(*[m.handle.value for m in mats])
+    hx = (P * n)(*[x.data_ptr() for x in xs])
+    hy = (P * n)(*[y.data_ptr() for y in outs])
+    hb = (P * n)(*[(b.data_ptr() if b is not None else None) for b in biases]) if biases is not None else None
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib.sc_q8_gemm_batch(hw, hx, hb, hy, n, t, x_layout, y_layout, _dp(workspace), ws_bytes,
+                               _stream_ptr(stream)))
+    return outs
