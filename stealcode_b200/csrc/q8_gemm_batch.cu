@@ -19,18 +19,23 @@
 //
 // Stream kernel, persistent (one CTA per SM): work unit = (GEMM, 128-row
 // group), all of K; units are dealt round-robin.  Warp 0: one thread streams
-// the units' weight tiles and scales (4 K blocks per bulk copy, no multicast)
-// through a ring of shared-memory stages; warps 1-8: lane = weight row, 4 row
-// quarters x 2 block parities, dp4a from shared memory with the activation
-// codes read through L1 (all lanes the same address); the two parities'
-// partial sums are added in shared memory at the end of a unit.
+// the units' weight tiles and scales (8 K blocks per bulk copy, no multicast)
+// through a ring of shared-memory stages; warps 1-8 compute:
+//   * 1-2 frames: lane = weight row, 4 row quarters x 2 block parities, dp4a
+//     from shared memory with the activation codes read through L1;
+//     the two parities' partial sums are added in shared memory at the end;
+//   * 4-16 frames: warp w owns 16 of the 128 rows and takes every block: one
+//     int8 tensor-core MMA (mma.sync m16n8k32, s32 accumulator cleared per
+//     block, so every block's dot is exact) per 8 frames, the weight
+//     fragments read straight from the row-group tile layout (conflict-free
+//     4-byte loads).
 #include "sc_device.cuh"
 #include "sc_kernels.cuh"
 
 namespace sc {
 
-constexpr int kBatchKb = 4;      // K blocks per stage
-constexpr int kBatchStages = 12;  // 12 x 17 KB in flight per SM
+constexpr int kBatchKb = 8;      // K blocks per stage
+constexpr int kBatchStages = 6;  // 6 x 34 KB in flight per SM
 constexpr int kBatchComputeWarps = 8;
 constexpr int kBatchThreads = 32 + 32 * kBatchComputeWarps;
 constexpr int kBatchStage = kBatchKb * (SC_TILE_BYTES + SC_GROUP_ROWS * 2);
@@ -85,6 +90,14 @@ __global__ void batch_quantize_kernel(const __grid_constant__ BatchParams p) {
   pdl_launch_dependents();
 }
 
+// One m16n8k32 int8 MMA: d = a (16 x 32, row) . b (32 x 8, col), from zero.
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0));
+}
+
 template <int MT>
 __global__ void __launch_bounds__(kBatchThreads, 1) q8_gemm_batch_kernel(const __grid_constant__ BatchParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -124,6 +137,73 @@ __global__ void __launch_bounds__(kBatchThreads, 1) q8_gemm_batch_kernel(const _
         if (q >= 0) mbar_wait(&full[q % kBatchStages], (uint32_t)(q / kBatchStages) & 1u);
     }
     __syncwarp();
+  } else if constexpr (MT >= 4) {
+    pdl_wait();  // the activation codes
+    // ---- tensor-core path: warp cw owns rows 16 cw .. 16 cw + 15 of the row
+    // group; thread (g = lane / 4, q = lane % 4) holds rows 16 cw + g and
+    // 16 cw + g + 8 at frames 2 q, 2 q + 1 (+ 8 per further 8-frame tile) ----
+    constexpr int NT = MT / 8 > 0 ? MT / 8 : 1;  // 8-frame tiles (MT 4 uses one, frames 4-7 zero codes)
+    const int cw = warp - 1, g = lane >> 2, q = lane & 3;
+    const int r0 = 16 * cw + g;
+    int gs = 0;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      const BatchItem &it = p.items[batch_item(p, u)];
+      const int64_t gr = u - it.unit0;
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[nt][e] = 0.0f;
+      for (int b0 = 0; b0 < it.nb; b0 += kBatchKb, gs++) {
+        const int s = gs % kBatchStages, nblk = it.nb - b0 < kBatchKb ? it.nb - b0 : kBatchKb;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(gs / kBatchStages) & 1u))) { ok = false; break; }
+        const unsigned char *st = smem + s * kBatchStage;
+        const __half *scs = (const __half *)(st + kBatchKb * SC_TILE_BYTES);
+        for (int bb = 0; bb < nblk; bb++) {
+          const int64_t b = b0 + bb;
+          uint32_t xb[NT][2];
+          float dxv[NT][2];
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++) {
+            const int8_t *xr = it.xq + ((int64_t)(8 * nt + g) * it.nb + b) * 32 + 4 * q;
+            xb[nt][0] = __ldg((const uint32_t *)xr);
+            xb[nt][1] = __ldg((const uint32_t *)(xr + 16));
+            dxv[nt][0] = __ldg(it.dx + b * kBatchFrames + 8 * nt + 2 * q);
+            dxv[nt][1] = __ldg(it.dx + b * kBatchFrames + 8 * nt + 2 * q + 1);
+          }
+          const unsigned char *tw = st + bb * SC_TILE_BYTES;
+          uint32_t a[4];
+          a[0] = *(const uint32_t *)(tw + r0 * 16 + 4 * q);
+          a[1] = *(const uint32_t *)(tw + (r0 + 8) * 16 + 4 * q);
+          a[2] = *(const uint32_t *)(tw + 2048 + r0 * 16 + 4 * q);
+          a[3] = *(const uint32_t *)(tw + 2048 + (r0 + 8) * 16 + 4 * q);
+          const float dw0 = __half2float(scs[bb * SC_GROUP_ROWS + r0]);
+          const float dw1 = __half2float(scs[bb * SC_GROUP_ROWS + r0 + 8]);
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++) {
+            int d[4];
+            mma_s8(d, a, xb[nt]);
+            acc[nt][0] = fmaf(dw0 * dxv[nt][0], (float)d[0], acc[nt][0]);
+            acc[nt][1] = fmaf(dw0 * dxv[nt][1], (float)d[1], acc[nt][1]);
+            acc[nt][2] = fmaf(dw1 * dxv[nt][0], (float)d[2], acc[nt][2]);
+            acc[nt][3] = fmaf(dw1 * dxv[nt][1], (float)d[3], acc[nt][3]);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      if (!ok) break;
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int64_t n = gr * SC_GROUP_ROWS + r0 + (e >> 1) * 8;
+          const int fr = 8 * nt + 2 * q + (e & 1);
+          if (fr < p.t && n < it.rows)
+            it.y[p.y_time_major ? (int64_t)fr * it.ldy + n : n * it.ldy + fr] =
+                acc[nt][e] + (it.bias ? it.bias[n] : 0.0f);
+        }
+    }
   } else {
     pdl_wait();  // the activation codes
     const int cw = warp - 1, rs = cw & 3, kp = cw >> 2;
@@ -199,7 +279,7 @@ static std::atomic<size_t> *batch_smem_limit() {
 }
 
 constexpr size_t kBatchSmem = (size_t)kBatchStages * kBatchStage + 16 * kBatchStages +
-                              (size_t)kBatchComputeWarps * 16 * 32 * 4;
+                              (size_t)kBatchComputeWarps * 2 * 32 * 4;
 
 template <int MT>
 static int launch_batch(const BatchParams &p, int sm_count, cudaStream_t st) {
