@@ -73,6 +73,10 @@ for _name, _res, _args in [
     ("orc_glu_from", None, [_P, _S, _S, _P]),
     ("orc_silu_inplace", None, [_P, _S]),
     ("orc_gemm_simd_into", None, [_S, _S, _S, _P, _P, _P, _P]),
+    ("orc_set_fast", None, [c_int]),
+    ("orc_get_fast", c_int, []),
+    ("orc_have_avx2", c_int, []),
+    ("orc_enc_phase_times", None, [_P, _P]),
 ]:
     _f = getattr(lib, _name)
     _f.restype = _res
@@ -207,6 +211,20 @@ def num_cpus() -> int:
     return lib.orc_num_cpus()
 
 
+def set_fast(on: bool) -> None:
+    """True (the default): the reference's threading and AVX2 lanes; False:
+    every operator serial and scalar.  Outputs are bit-identical."""
+    lib.orc_set_fast(1 if on else 0)
+
+
+def get_fast() -> bool:
+    return bool(lib.orc_get_fast())
+
+
+def have_avx2() -> bool:
+    return bool(lib.orc_have_avx2())
+
+
 class OrcEncConfig(ctypes.Structure):
     _fields_ = [("d_model", ctypes.c_int32), ("n_layers", ctypes.c_int32), ("n_heads", ctypes.c_int32),
                 ("d_ff", ctypes.c_int32), ("feat_in", ctypes.c_int32), ("conv_channels", ctypes.c_int32),
@@ -251,6 +269,13 @@ class StreamingEncoder:
         if lib.orc_enc_last(self._h, which, _p(out), ctypes.byref(c)):
             raise ValueError("no such stage")
         return out[: c.value].copy()
+
+    def phase_times(self) -> dict:
+        """Host seconds spent in encode_new so far, by phase."""
+        out = np.zeros(4, np.float64)
+        lib.orc_enc_phase_times(self._h, _p(out))
+        return {"pre_encode": float(out[0]), "linears": float(out[1]), "attention": float(out[2]),
+                "total": float(out[3])}
 
     def set_gemm_order(self, scalar: bool) -> None:
         """False: the reference's GEMM dispatch (8-lane SIMD order for chunks

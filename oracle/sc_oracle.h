@@ -133,6 +133,19 @@ void orc_gemm_simd_into(size_t m, size_t k, size_t n, const float *a, const floa
 /* Online CPU count used by nthreads <= 0. */
 int orc_num_cpus(void);
 
+/* 1 (default): the reference's threading (rayon over 256-row chunks,
+ * spatial positions and queries) and AVX2 lanes for the f32 GEMM,
+ * score_dot and softmax_v; 0: every operator serial and scalar.  Both give
+ * bit-identical outputs; the switch exists so tests can check that. */
+void orc_set_fast(int on);
+int orc_get_fast(void);
+int orc_have_avx2(void);
+/* Runs fn(ctx, 0 .. nchunks-1) on the oracle's persistent worker pool (all
+ * host threads when fast, else on the caller); chunks are claimed
+ * dynamically, like rayon's par_chunks_mut.  Not reentrant: fn must not
+ * call orc_parallel. */
+void orc_parallel(size_t nchunks, void (*fn)(void *ctx, size_t chunk), void *ctx);
+
 #ifdef __cplusplus
 }
 #endif

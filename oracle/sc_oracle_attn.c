@@ -6,15 +6,62 @@
  */
 #include "sc_oracle.h"
 
+#include <immintrin.h>
 #include <math.h>
 #include <stdlib.h>
 
 #define S_LANES 16 /* simd_kernel.rs:44 `const S: usize = 16` */
 
+/* AVX2 build of score_dot (two 8-lane vectors = the 16 SIMD lanes): the
+ * same two fused multiply-adds per lane and the same ordered lane sum. */
+__attribute__((target("avx2,fma"))) static float score_dot_avx2(const float *qu, const float *uh,
+                                                                 const float *qv, const float *vh,
+                                                                 const float *kk, const float *p,
+                                                                 size_t hd, float scale) {
+    __m256 a0 = _mm256_setzero_ps(), a1 = _mm256_setzero_ps();
+    size_t i = 0;
+    for (; i + S_LANES <= hd; i += S_LANES) {
+        for (int h = 0; h < 2; h++) {
+            const size_t o = i + 8 * (size_t)h;
+            const __m256 quv = _mm256_add_ps(_mm256_loadu_ps(qu + o), _mm256_loadu_ps(uh + o));
+            const __m256 qvv = _mm256_add_ps(_mm256_loadu_ps(qv + o), _mm256_loadu_ps(vh + o));
+            __m256 *acc = h ? &a1 : &a0;
+            const __m256 inner = _mm256_fmadd_ps(qvv, _mm256_loadu_ps(p + o), *acc);
+            *acc = _mm256_fmadd_ps(quv, _mm256_loadu_ps(kk + o), inner);
+        }
+    }
+    float acc[S_LANES];
+    _mm256_storeu_ps(acc, a0);
+    _mm256_storeu_ps(acc + 8, a1);
+    float sum = acc[0];
+    for (int l = 1; l < S_LANES; l++) sum += acc[l];
+    for (; i < hd; i++) sum += (qu[i] + uh[i]) * kk[i] + (qv[i] + vh[i]) * p[i];
+    return sum * scale;
+}
+
+/* the P.V lanes of softmax_v over 16-dim blocks, AVX2 */
+__attribute__((target("avx2,fma"))) static size_t softmax_pv_avx2(const float *e, float inv, size_t k0,
+                                                                   size_t k1, const float *const *vrows,
+                                                                   size_t head_dim, float *out) {
+    size_t j = 0;
+    for (; j + S_LANES <= head_dim; j += S_LANES) {
+        __m256 a0 = _mm256_setzero_ps(), a1 = _mm256_setzero_ps();
+        for (size_t kk = k0, ii = 0; kk < k1; kk++, ii++) {
+            const __m256 w = _mm256_set1_ps(e[ii] * inv);
+            a0 = _mm256_fmadd_ps(w, _mm256_loadu_ps(vrows[kk] + j), a0);
+            a1 = _mm256_fmadd_ps(w, _mm256_loadu_ps(vrows[kk] + j + 8), a1);
+        }
+        _mm256_storeu_ps(out + j, a0);
+        _mm256_storeu_ps(out + j + 8, a1);
+    }
+    return j;
+}
+
 /* simd_kernel.rs:919-983 */
 float orc_score_dot(const float *qu, const float *uh, const float *qv,
                     const float *vh, const float *kk, const float *p,
                     size_t hd, float scale) {
+    if (orc_get_fast() && orc_have_avx2()) return score_dot_avx2(qu, uh, qv, vh, kk, p, hd, scale);
     float acc[S_LANES] = {0};
     size_t i = 0;
     while (i + S_LANES <= hd) {
@@ -50,6 +97,7 @@ void orc_softmax_v(const float *srow, size_t k0, size_t k1, size_t n_heads,
     }
     float inv = 1.0f / sum;
     size_t j = 0;
+    if (orc_get_fast() && orc_have_avx2()) j = softmax_pv_avx2(e, inv, k0, k1, vrows, head_dim, out);
     while (j + S_LANES <= head_dim) {
         float acc[S_LANES] = {0};
         for (size_t kk = k0, ii = 0; kk < k1; kk++, ii++) {

@@ -10,6 +10,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "sc_oracle.h"
 
@@ -166,7 +167,15 @@ struct orc_enc {
     float **last_blk;
     int dump_layer;
     float *dump[8]; /* stages of dump_layer, [c, d] each */
+    double *tm;     /* seconds: [0] pre-encode, [1] Q8 linears, [2] attention, [3] encode_new total,
+                       [4] Q8 linears inside the pre-encode */
 };
+
+static double now_s(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
 
 static const orc_tensor *find(const orc_tensor *t, int n, const char *name) {
     for (int i = 0; i < n; i++)
@@ -240,7 +249,10 @@ static int get_conv(const orc_tensor *t, int n, const char *base, size_t inp,
 /* Lin::forward_t (nemotron/weights.rs:305-337): y_t [out, t] = W x_t [inp, t] + b */
 static void lin_forward_t(const orc_enc *e, const lin_t *l, const float *x_t, size_t t, float *y_t) {
     size_t padded_row = (l->row_len + 31) / 32 * 34;
-    orc_q8_gemm_order(l->rows, l->row_len, t, l->w, padded_row, 34, 2, x_t, y_t, 0, e->scalar_gemm);
+    const double t0 = now_s();
+    orc_q8_gemm_order(l->rows, l->row_len, t, l->w, padded_row, 34, 2, x_t, y_t, orc_get_fast() ? 0 : 1,
+                      e->scalar_gemm);
+    e->tm[1] += now_s() - t0;
     if (l->bias)
         for (size_t j = 0; j < l->rows; j++)
             for (size_t tt = 0; tt < t; tt++) y_t[j * t + tt] += l->bias[j];
@@ -261,6 +273,39 @@ static void lin_tm(const orc_enc *e, const lin_t *l, const float *x, size_t t, f
 /* ------------------------------------------------------------------ */
 static size_t conv_dim(size_t in, size_t pad0, size_t pad1, size_t k, size_t stride) {
     return (in + pad0 + pad1 - k) / stride + 1;
+}
+
+typedef struct {
+    const conv2d_t *cv;
+    const float *x;
+    float *out;
+    size_t t_in, f_in, f_out, pad0, stride;
+} conv_ctx;
+
+/* every output channel of output position sp (the reference's par_chunks
+ * slot): bias, then products summed over (ic, kt, kf) in order */
+static void conv_position(void *vctx, size_t sp) {
+    const conv_ctx *g = (const conv_ctx *)vctx;
+    const conv2d_t *cv = g->cv;
+    const size_t c_out = cv->out, c_in = cv->inp, in_groups = c_in / cv->groups;
+    const size_t ot = sp / g->f_out, of = sp % g->f_out;
+    for (size_t oc = 0; oc < c_out; oc++) {
+        size_t ic0 = (oc % cv->groups) * in_groups;
+        size_t wbase = oc * in_groups * cv->kh * cv->kw;
+        float acc = cv->b[oc];
+        for (size_t ic = 0; ic < in_groups; ic++)
+            for (size_t kt = 0; kt < cv->kh; kt++) {
+                long ti = (long)(ot * g->stride + kt) - (long)g->pad0;
+                if (ti < 0 || ti >= (long)g->t_in) continue;
+                for (size_t kf = 0; kf < cv->kw; kf++) {
+                    long fi = (long)(of * g->stride + kf) - (long)g->pad0;
+                    if (fi < 0 || fi >= (long)g->f_in) continue;
+                    acc += g->x[((size_t)ti * g->f_in + (size_t)fi) * c_in + ic0 + ic] *
+                           cv->w[wbase + (ic * cv->kh + kt) * cv->kw + kf];
+                }
+            }
+        g->out[sp * c_out + oc] = acc;
+    }
 }
 
 static float *conv2d_forward(const conv2d_t *cv, const float *x, size_t t_in, size_t f_in,
@@ -289,26 +334,16 @@ static float *conv2d_forward(const conv2d_t *cv, const float *x, size_t t_in, si
         free(yt);
         free(bt);
     } else {
-        size_t in_groups = c_in / cv->groups;
-        for (size_t ot = 0; ot < t_out; ot++)
-            for (size_t of = 0; of < f_out; of++)
-                for (size_t oc = 0; oc < c_out; oc++) {
-                    size_t ic0 = (oc % cv->groups) * in_groups;
-                    size_t wbase = oc * in_groups * cv->kh * cv->kw;
-                    float acc = cv->b[oc];
-                    for (size_t ic = 0; ic < in_groups; ic++)
-                        for (size_t kt = 0; kt < cv->kh; kt++) {
-                            long ti = (long)(ot * stride + kt) - (long)pad0;
-                            if (ti < 0 || ti >= (long)t_in) continue;
-                            for (size_t kf = 0; kf < cv->kw; kf++) {
-                                long fi = (long)(of * stride + kf) - (long)pad0;
-                                if (fi < 0 || fi >= (long)f_in) continue;
-                                acc += x[((size_t)ti * f_in + (size_t)fi) * c_in + ic0 + ic] *
-                                       cv->w[wbase + (ic * cv->kh + kt) * cv->kw + kf];
-                            }
-                        }
-                    out[(ot * f_out + of) * c_out + oc] = acc;
-                }
+        /* direct conv (weights.rs:444-524): rayon over output positions when
+         * there are at least 8 of them (each position's channels are one
+         * task), serial otherwise; either way every output is the same
+         * ordered sum */
+        conv_ctx g = {cv, x, out, t_in, f_in, f_out, pad0, stride};
+        const size_t spatial = t_out * f_out;
+        if (spatial >= 8)
+            orc_parallel(spatial, conv_position, &g);
+        else
+            for (size_t sp = 0; sp < spatial; sp++) conv_position(&g, sp);
     }
     *t_o = t_out;
     *f_o = f_out;
@@ -382,6 +417,7 @@ orc_enc *orc_enc_create(const orc_enc_config *cfg, const orc_tensor *t, int n, c
                         size_t err_len) {
     orc_enc *e = calloc(1, sizeof *e);
     e->cfg = *cfg;
+    e->tm = calloc(5, sizeof(double));
     size_t d = (size_t)cfg->d_model, dff = (size_t)cfg->d_ff, C = (size_t)cfg->conv_channels;
     e->chunk = (size_t)cfg->att_right + 1;
     e->left_chunks = (size_t)cfg->att_left / e->chunk;
@@ -462,6 +498,7 @@ orc_enc *orc_enc_create(const orc_enc_config *cfg, const orc_tensor *t, int n, c
 
 void orc_enc_destroy(orc_enc *e) {
     if (!e) return;
+    free(e->tm);
     size_t nl = (size_t)e->cfg.n_layers;
     for (size_t i = 0; e->pos_p && i < nl; i++) free(e->pos_p[i]);
     for (size_t i = 0; e->kc && i < nl; i++) {
@@ -491,6 +528,74 @@ static void dump_stage(orc_enc *e, size_t li, int stage, const float *src, size_
     free(e->dump[stage]);
     e->dump[stage] = malloc(c * d * sizeof(float));
     for (size_t j = 0; j < c; j++) memcpy(e->dump[stage] + j * d, src + j * width, d * sizeof(float));
+}
+
+typedef struct {
+    const orc_enc *e;
+    const layer_t *L;
+    size_t li, s, k_lo, k_hi;
+    long pos_lo;
+    size_t band;
+    const float *q_new, *k_new, *v_new;
+    float *scores, *attn;
+    float scale;
+    int exp_cr;
+} attn_ctx;
+
+static void attn_band_of(const attn_ctx *g, size_t qi, size_t *k0, size_t *k1) {
+    const orc_enc *e = g->e;
+    size_t qq = g->s + qi, q_chunk = qq / e->chunk;
+    size_t k_min = (q_chunk > e->left_chunks ? q_chunk - e->left_chunks : 0) * e->chunk;
+    size_t k_max = (q_chunk + 1) * e->chunk < g->k_hi ? (q_chunk + 1) * e->chunk : g->k_hi;
+    *k0 = k_min - g->k_lo;
+    *k1 = k_max - g->k_lo;
+}
+
+/* score row of query qi: every head and band key (streaming.rs:505-523) */
+static void attn_scores_row(void *vctx, size_t qi) {
+    const attn_ctx *g = (const attn_ctx *)vctx;
+    const orc_enc *e = g->e;
+    const size_t d = (size_t)e->cfg.d_model, nh = (size_t)e->cfg.n_heads, hd = e->head_dim;
+    size_t k0, k1;
+    attn_band_of(g, qi, &k0, &k1);
+    float *row = g->scores + qi * g->band * nh;
+    const size_t qq = g->s + qi;
+    for (size_t hh = 0; hh < nh; hh++) {
+        size_t ho = hh * hd;
+        const float *qh = g->q_new + qi * d + ho;
+        for (size_t kk = k0; kk < k1; kk++) {
+            size_t fr = g->k_lo + kk;
+            const float *kd = fr < g->s ? fc_row(&e->kc[g->li], fr) + ho : g->k_new + (fr - g->s) * d + ho;
+            size_t pr = (size_t)((long)qq - (long)fr - g->pos_lo);
+            const float *prow = e->pos_p[g->li] + pr * d + ho;
+            row[kk * nh + hh] =
+                orc_score_dot(qh, g->L->pos_u + ho, qh, g->L->pos_v + ho, kd, prow, hd, g->scale);
+        }
+    }
+}
+
+/* softmax over the band + P.V of query qi, every head (streaming.rs:542-577);
+ * the exp mode is per thread, so the task sets the encoder's */
+static void attn_softmax_row(void *vctx, size_t qi) {
+    const attn_ctx *g = (const attn_ctx *)vctx;
+    const orc_enc *e = g->e;
+    const size_t d = (size_t)e->cfg.d_model, nh = (size_t)e->cfg.n_heads, hd = e->head_dim;
+    const int saved = orc_get_exp_mode();
+    orc_set_exp_mode(g->exp_cr);
+    size_t k0, k1;
+    attn_band_of(g, qi, &k0, &k1);
+    const float **vrows = malloc((g->band ? g->band : 1) * sizeof(float *));
+    const float *row = g->scores + qi * g->band * nh;
+    for (size_t hh = 0; hh < nh; hh++) {
+        size_t ho = hh * hd;
+        for (size_t kk = k0; kk < k1; kk++) {
+            size_t fr = g->k_lo + kk;
+            vrows[kk] = fr < g->s ? fc_row(&e->vc[g->li], fr) + ho : g->v_new + (fr - g->s) * d + ho;
+        }
+        orc_softmax_v(row, k0, k1, nh, hh, vrows, hd, g->attn + qi * d + ho);
+    }
+    free(vrows);
+    orc_set_exp_mode(saved);
 }
 
 static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_t t_new,
@@ -526,33 +631,21 @@ static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_
     dump_stage(e, li, 4, q_new, c, d);
     size_t band = k_hi - k_lo;
     float *scores = calloc(c * band * nh, sizeof(float));
-    const float **vrows = malloc(band * sizeof(float *));
     float *attn = calloc(c * d, sizeof(float));
-    for (size_t qi = 0; qi < c; qi++) {
-        size_t qq = s + qi, q_chunk = qq / e->chunk;
-        size_t k_min = (q_chunk > e->left_chunks ? q_chunk - e->left_chunks : 0) * e->chunk;
-        size_t k_max = (q_chunk + 1) * e->chunk < k_hi ? (q_chunk + 1) * e->chunk : k_hi;
-        size_t k0 = k_min - k_lo, k1 = k_max - k_lo;
-        float *row = scores + qi * band * nh;
-        for (size_t hh = 0; hh < nh; hh++) {
-            size_t ho = hh * hd;
-            const float *qh = q_new + qi * d + ho;
-            for (size_t kk = k0; kk < k1; kk++) {
-                size_t fr = k_lo + kk;
-                const float *kd = fr < s ? fc_row(&e->kc[li], fr) + ho : k_new + (fr - s) * d + ho;
-                size_t pr = (size_t)((long)qq - (long)fr - pos_lo);
-                const float *prow = e->pos_p[li] + pr * d + ho;
-                row[kk * nh + hh] = orc_score_dot(qh, L->pos_u + ho, qh, L->pos_v + ho, kd, prow, hd, scale);
-            }
+    {
+        /* streaming.rs:492-589: the score rows, then softmax + P.V, each
+         * over queries on rayon when c * band * n_heads >= 2048 */
+        const double t0 = now_s();
+        attn_ctx g = {e, L, li, s, k_lo, k_hi, pos_lo, band, q_new, k_new, v_new, scores, attn, scale,
+                      e->exp_cr};
+        if (c * band * nh >= 2048) {
+            orc_parallel(c, attn_scores_row, &g);
+            orc_parallel(c, attn_softmax_row, &g);
+        } else {
+            for (size_t qi = 0; qi < c; qi++) attn_scores_row(&g, qi);
+            for (size_t qi = 0; qi < c; qi++) attn_softmax_row(&g, qi);
         }
-        for (size_t hh = 0; hh < nh; hh++) {
-            size_t ho = hh * hd;
-            for (size_t kk = k0; kk < k1; kk++) {
-                size_t fr = k_lo + kk;
-                vrows[kk] = fr < s ? fc_row(&e->vc[li], fr) + ho : v_new + (fr - s) * d + ho;
-            }
-            orc_softmax_v(row, k0, k1, nh, hh, vrows, hd, attn + qi * d + ho);
-        }
+        e->tm[2] += now_s() - t0;
     }
     dump_stage(e, li, 2, attn, c, d);
     lin_tm(e, &L->out, attn, c, tmp, sa, sb);
@@ -601,7 +694,7 @@ static void block_new(orc_enc *e, size_t li, const float *input, size_t s, size_
     fc_append(&e->glu[li], glu_new, c);
 
     free(sa), free(sb), free(y), free(tmp), free(h), free(f), free(ln_new), free(k_new), free(v_new);
-    free(q_new), free(scores), free(vrows), free(attn), free(lnc), free(h2), free(glu_new), free(glu);
+    free(q_new), free(scores), free(attn), free(lnc), free(h2), free(glu_new), free(glu);
     free(conv), free(o2), free(y2);
 }
 
@@ -615,9 +708,18 @@ int orc_enc_encode_new(orc_enc *e, const float *mel, size_t mel_frames, size_t n
                        size_t t1, int fin) {
     int saved = orc_get_exp_mode();
     orc_set_exp_mode(e->exp_cr);
+    const double ts = now_s();
     int rc = encode_new(e, mel, mel_frames, n_mels, t0, t1, fin);
+    e->tm[3] += now_s() - ts;
     orc_set_exp_mode(saved);
     return rc;
+}
+
+void orc_enc_phase_times(const orc_enc *e, double *out) {
+    out[0] = e->tm[0];
+    out[1] = e->tm[1] - e->tm[4];
+    out[2] = e->tm[2];
+    out[3] = e->tm[3];
 }
 
 static int encode_new(orc_enc *e, const float *mel, size_t mel_frames, size_t n_mels, size_t t0,
@@ -640,7 +742,10 @@ static int encode_new(orc_enc *e, const float *mel, size_t mel_frames, size_t n_
     size_t take = avail < t_mel ? avail : t_mel;
     memcpy(win, mel + win_start * n_mels, take * n_mels * sizeof(float));
     size_t t_pe;
+    const double tp = now_s(), tg = e->tm[1];
     float *pe = pre_encode_forward(e, win, t_mel, n_mels, &t_pe);
+    e->tm[0] += now_s() - tp;
+    e->tm[4] += e->tm[1] - tg;
     free(win);
     if (t_pe < start_rel + c) {
         free(pe);

@@ -78,6 +78,11 @@ int orc_enc_set_prompt(orc_enc *e, int prompt_id);
 void orc_enc_set_dump(orc_enc *e, int layer);
 int orc_enc_dump(const orc_enc *e, int stage, float *out, size_t *c_out);
 
+/* Host seconds this encoder has spent in encode_new since it was created:
+ * out[0] the pre-encode (convs and its linear), out[1] the Q8 linears of the
+ * blocks and the prompt MLP, out[2] the attention (scores, softmax, P.V),
+ * out[3] the whole of encode_new. */
+void orc_enc_phase_times(const orc_enc *e, double *out);
 /* Helper kernels, exposed for unit checks. */
 void orc_ln_forward(const float *x, const float *w, const float *b,
                     float eps, float *out, size_t d);

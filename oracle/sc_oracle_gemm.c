@@ -403,6 +403,29 @@ static void parallel_chunks(int threads, size_t nchunks, chunk_fn fn, void *ctx)
     pthread_mutex_unlock(&call_mu);
 }
 
+/* The reference's threading and SIMD kernels outside the Q8 GEMM (rayon over
+ * spatial positions, queries and 256-row chunks; AVX2 lanes for score_dot,
+ * softmax_v and the f32 GEMM) compute every output in the same order as the
+ * serial scalar restatement, so the switch changes speed only. */
+static atomic_int g_fast = 1;
+
+void orc_set_fast(int on) { atomic_store(&g_fast, on ? 1 : 0); }
+
+int orc_get_fast(void) { return atomic_load(&g_fast); }
+
+int orc_have_avx2(void) {
+    static int have = -1;
+    if (have < 0) {
+        __builtin_cpu_init();
+        have = __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma");
+    }
+    return have;
+}
+
+void orc_parallel(size_t nchunks, void (*fn)(void *ctx, size_t chunk), void *ctx) {
+    parallel_chunks(atomic_load(&g_fast) ? orc_num_cpus() : 1, nchunks, fn, ctx);
+}
+
 typedef struct {
     size_t m, k, n, padded_row, block_bytes, qoff, nblocks, chunk_rows;
     const uint8_t *w;

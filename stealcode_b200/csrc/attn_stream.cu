@@ -481,6 +481,266 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
   }
 }
 
+// ---- lane-major kernel (the encoder's layout) ------------------------------
+// The same arithmetic as the kernels above, laid out for occupancy: four
+// CTAs per SM (at most 128 registers a thread, about 51 KB of shared memory
+// at band 77) and uniform control flow.
+//   A. a warp takes one tile of kLmKT = 4 keys for two groups of 4 queries
+//      (one per half-warp): 16 accumulators per lane, pos rows read through
+//      L1 from one precomputed row offset each.  The 16 lane sums of the
+//      tile's pairs go through the tile's own K rows, dead by then, with a
+//      rotated layout that keeps both the stores and the ordered reads free
+//      of bank conflicts.
+//   C. per query: max and exp over the band on the warp's lanes, then the
+//      warp's two queries' sequential sums on two lanes at once.
+//   D. P.V over the keys any query of the call attends to ([k0 of the
+//      first query, k1 of the last)), 4 keys per step, a uniform tail.
+constexpr int kLmKT = 4;
+
+__host__ __device__ constexpr int lm_wstride(int band) {
+  // a multiple of 4 (16-byte weight loads) with an odd number of 16-byte
+  // units, so that the rows of queries j and j + 4 sit in different banks
+  return ((band + 3) & ~3) | 4;
+}
+
+template <int HD, int CQ>
+__host__ __device__ constexpr size_t attn_lm_smem_floats(int band) {
+  return (size_t)((band + kLmKT - 1) / kLmKT * kLmKT) * HD + 2 * (size_t)CQ * HD + (size_t)CQ * lm_wstride(band) +
+         (kLmKT * HD >= 512 && CQ == 8 ? 0 : (size_t)(HD / 32) * 512);
+}
+
+template <int HD, int CQ>
+__global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
+  constexpr int NW = HD / 32;
+  constexpr int KT = kLmKT;
+  constexpr int NQG = CQ / 4;          // query groups of 4; a warp takes two
+  constexpr int NPV = 4 + KT - 1;      // pos rows of one (group, tile)
+  constexpr int NHALF = HD / 64;       // 16-byte slices of a lane's dims
+  // the tile's K rows hold the lane sums when one warp owns the tile
+  constexpr bool kRedInK = KT * HD >= 512 && NQG == 2;
+  extern __shared__ __align__(16) float sm[];
+  const int band = (int)(p.k_hi - p.k_lo), nt = (band + KT - 1) / KT, bw = lm_wstride(band);
+  float *s_k = sm;                     // [nt*KT][HD] K lane-major, later V natural
+  float *s_qu = s_k + nt * KT * HD;    // [CQ][HD] q + u lane-major
+  float *s_qv = s_qu + CQ * HD;        // [CQ][HD] q + v lane-major
+  float *s_w = s_qv + CQ * HD;         // [CQ][bw] scores, then weights
+  float *s_red = s_w + CQ * bw;        // [NW][512] when the tile's K rows are too small
+  const int h = blockIdx.x;
+  const int64_t z = blockIdx.y;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int hoff = h * HD;
+  const int c = p.c;
+  const int64_t zq = p.zrows > 0 ? p.zrows : c, zn = p.zrows > 0 ? p.zrows : p.rows_new;
+  const int kk_new = (int)(p.new_lo - p.k_lo);
+  const int slot0 = p.cap > 0 ? (int)(p.k_lo % p.cap) : 0;
+  const int cap = (int)p.cap;
+  const int kk_s = (int)(p.s - p.k_lo);
+  auto ring_row = [&](float *ring, int kk) -> float * {
+    int slot = slot0 + kk;
+    slot = slot >= cap ? slot - cap : slot;
+    return ring + (z * cap + slot) * (int64_t)p.d + hoff;
+  };
+  auto key_row = [&](float *ring, const float *nw, int kk) -> const float * {
+    if (kk >= kk_new) return nw + (z * zn + p.r0 + (kk - kk_new)) * p.ld_new + hoff;
+    return ring_row(ring, kk);
+  };
+
+  // ---- stage: K band (a warp per row, 16 bytes a lane), new K rows into the
+  // ring, q + u and q + v ----
+  for (int kk = warp; kk < band; kk += NW) {
+    const float *src = key_row(p.k_ring, p.k_new, kk);
+    for (int e4 = lane; e4 < HD / 4; e4 += 32) cp_async16(s_k + kk * HD + e4 * 4, src + e4 * 4);
+    if (p.k_ring && kk >= kk_s) {
+      float *dst = ring_row(p.k_ring, kk);
+      for (int e4 = lane; e4 < HD / 4; e4 += 32)
+        *reinterpret_cast<float4 *>(dst + e4 * 4) = *reinterpret_cast<const float4 *>(src + e4 * 4);
+    }
+  }
+  {
+    const float uu = p.u[hoff + t], vv = p.v[hoff + t];
+    const float *qrow = p.q + (z * zq + p.r0) * p.ldq + hoff + t;
+#pragma unroll
+    for (int j = 0; j < CQ; j++) {
+      const float qd = j < c ? qrow[(int64_t)j * p.ldq] : 0.0f;
+      s_qu[j * HD + t] = j < c ? __fadd_rn(qd, uu) : 0.0f;
+      s_qv[j * HD + t] = j < c ? __fadd_rn(qd, vv) : 0.0f;
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- A: scores (score_dot order) ----
+  {
+    const int hw = lane >> 4, l = lane & 15;
+    // pos row of (query j, key kk) is prow0 + j - kk
+    const int prow0 = (int)(p.s + p.pos_off - p.k_lo - p.pr_lo);
+    const float *pbase = p.pos_p + p.pr_lo * (int64_t)p.d + hoff + l * 4;
+    const int nunits = nt * (NQG / 2);
+    for (int u = warp; u < nunits; u += NW) {
+      const int tile = u / (NQG / 2), qg = (u % (NQG / 2)) * 2 + hw, kt0 = tile * KT;
+      float acc[4][KT];
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int b = 0; b < KT; b++) acc[j][b] = 0.0f;
+      int poff[NPV];
+#pragma unroll
+      for (int m = 0; m < NPV; m++) {
+        const int pi = prow0 - kt0 + 4 * qg - (KT - 1) + m;  // masked pairs may fall outside
+        poff[m] = (pi < 0 ? 0 : (pi >= p.np ? p.np - 1 : pi)) * p.d;
+      }
+      const float *kb = s_k + kt0 * HD + l * 4;
+      const float *qub = s_qu + 4 * qg * HD + l * 4, *qvb = s_qv + 4 * qg * HD + l * 4;
+#pragma unroll
+      for (int hh = 0; hh < NHALF; hh++) {
+        float4 kv[KT], pv[NPV], qu[4], qv[4];
+#pragma unroll
+        for (int b = 0; b < KT; b++) kv[b] = *reinterpret_cast<const float4 *>(kb + b * HD + hh * 64);
+#pragma unroll
+        for (int m = 0; m < NPV; m++) pv[m] = __ldg(reinterpret_cast<const float4 *>(pbase + poff[m] + hh * 64));
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          qu[j] = *reinterpret_cast<const float4 *>(qub + j * HD + hh * 64);
+          qv[j] = *reinterpret_cast<const float4 *>(qvb + j * HD + hh * 64);
+        }
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++)
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int b = 0; b < KT; b++) {
+              const float inner = __fmaf_rn(f4c(qv[j], cc), f4c(pv[j - b + KT - 1], cc), acc[j][b]);
+              acc[j][b] = __fmaf_rn(f4c(qu[j], cc), f4c(kv[b], cc), inner);
+            }
+      }
+      // the 16 lane sums of each of the half-warp's 16 pairs: pair pr of
+      // half-warp hw, lane x at rbase(hw, pr) + ((x + pr) & 15)
+      float *red = kRedInK ? s_k + kt0 * HD : s_red + warp * 512;
+      __syncwarp();  // both half-warps are done with the tile's K rows
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int b = 0; b < KT; b++) {
+          const int pr = j * KT + b;
+          red[hw * 256 + ((pr + hw) & 15) * 16 + ((l + pr) & 15)] = acc[j][b];
+        }
+      __syncwarp();
+      {
+        const int pr = l;
+        const float *rr = red + hw * 256 + ((pr + hw) & 15) * 16;
+        float sum = rr[pr & 15];
+#pragma unroll
+        for (int x = 1; x < kLanes; x++) sum = __fadd_rn(sum, rr[(x + pr) & 15]);
+        const int j = 4 * qg + pr / KT, kk = kt0 + pr % KT;
+        if (j < c && kk < band) s_w[j * bw + kk] = __fmul_rn(sum, p.scale);
+      }
+      __syncwarp();  // the scratch is read before the warp's next tile
+    }
+  }
+  __syncthreads();
+  // ---- V band into shared memory (natural order), overlapped with C ----
+  for (int kk = warp; kk < band; kk += NW) {
+    const float *src = key_row(p.v_ring, p.v_new, kk);
+    for (int e4 = lane; e4 < HD / 4; e4 += 32) cp_async16(s_k + kk * HD + e4 * 4, src + e4 * 4);
+    if (p.v_ring && kk >= kk_s) {
+      float *dst = ring_row(p.v_ring, kk);
+      for (int e4 = lane; e4 < HD / 4; e4 += 32)
+        *reinterpret_cast<float4 *>(dst + e4 * 4) = *reinterpret_cast<const float4 *>(src + e4 * 4);
+    }
+  }
+  // ---- C: band mask + softmax per query (simd_kernel.rs:1010-1104) ----
+  {
+    constexpr int QPW = (CQ + NW - 1) / NW;  // queries per warp
+    float inv[QPW];
+    int k0s[QPW], k1s[QPW];
+#pragma unroll
+    for (int i = 0; i < QPW; i++) {
+      const int j = warp + i * NW;
+      float *row = s_w + j * bw;
+      k0s[i] = 0;
+      k1s[i] = 0;
+      if (j >= CQ) continue;
+      if (j >= c) {
+        for (int kk = lane; kk < bw; kk += 32) row[kk] = 0.0f;
+        continue;
+      }
+      int64_t kmin, kmax;
+      band_of(p.s + j, p.chunk, p.left_chunks, p.k_hi, kmin, kmax);
+      const int k0 = (int)(kmin - p.k_lo), k1 = (int)(kmax - p.k_lo);
+      k0s[i] = k0;
+      k1s[i] = k1;
+      float mx = -INFINITY;
+      for (int kk = k0 + lane; kk < k1; kk += 32) mx = fmaxf(mx, row[kk]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      for (int kk = lane; kk < bw; kk += 32) row[kk] = (kk >= k0 && kk < k1) ? exp_rn(__fsub_rn(row[kk], mx)) : 0.0f;
+    }
+    __syncwarp();
+    // lane i sums the warp's i-th query over its band in order
+    float mine = 0.0f;
+#pragma unroll
+    for (int i = 0; i < QPW; i++) {
+      const int j = warp + i * NW;
+      if (lane == i && j < c) {
+        const float *row = s_w + j * bw;
+        float sum = 0.0f;
+        for (int kk = k0s[i]; kk < k1s[i]; kk++) sum = __fadd_rn(sum, row[kk]);
+        mine = __fdiv_rn(1.0f, sum);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < QPW; i++) inv[i] = __shfl_sync(0xffffffffu, mine, i);
+#pragma unroll
+    for (int i = 0; i < QPW; i++) {
+      const int j = warp + i * NW;
+      if (j >= c) continue;
+      float *row = s_w + j * bw;
+      for (int kk = lane; kk < bw; kk += 32) row[kk] = __fmul_rn(row[kk], inv[i]);
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  // ---- D: P.V over the keys the call attends to, one thread per head dim ----
+  {
+    int64_t kmin, kmax, kmin2, kmax2;
+    band_of(p.s, p.chunk, p.left_chunks, p.k_hi, kmin, kmax);
+    band_of(p.s + c - 1, p.chunk, p.left_chunks, p.k_hi, kmin2, kmax2);
+    const int ka = (int)(kmin - p.k_lo) & ~3, kb = (int)(kmax2 - p.k_lo);
+    float acc[CQ];
+#pragma unroll
+    for (int j = 0; j < CQ; j++) acc[j] = 0.0f;
+    int kk = ka;
+    for (; kk + 4 <= kb; kk += 4) {
+      float4 w[CQ];
+#pragma unroll
+      for (int j = 0; j < CQ; j++) w[j] = *reinterpret_cast<const float4 *>(s_w + j * bw + kk);
+      float vv[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) vv[e] = s_k[(kk + e) * HD + t];
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+#pragma unroll
+        for (int j = 0; j < CQ; j++) acc[j] = __fmaf_rn(f4c(w[j], e), vv[e], acc[j]);
+    }
+    for (; kk < kb; kk++) {
+      const float vv = s_k[kk * HD + t];
+#pragma unroll
+      for (int j = 0; j < CQ; j++) acc[j] = __fmaf_rn(s_w[j * bw + kk], vv, acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < CQ; j++)
+      if (j < c) {
+        if (p.out) p.out[(z * zq + p.r0 + j) * p.ldo + hoff + t] = acc[j];
+        if (p.qout.xq) {  // the warp's 32 dims are one block of the out-proj input
+          float sblk;
+          const int8_t q = warp_quantize_block(acc[j], true, sblk);
+          p.qout.xq[qout_code_index(p.qout, z * zq + p.r0 + j, hoff + t)] = code_half(q);
+          if (lane == 0) p.qout.dx[qout_dx_index(p.qout, z * zq + p.r0 + j, (hoff + t) >> 5)] = sblk;
+        }
+      }
+  }
+}
+
 // Validates the band and pos rows the chunk touches, fills pr_lo/np.
 int attn_prepare(AttnParams &p, int64_t n_pos) {
   if (p.c <= 0 || p.c > 16 || p.d <= 0 || p.n_heads <= 0 || p.d % p.n_heads != 0) {
@@ -557,14 +817,27 @@ static int launch_stage_lm(const AttnParams &p, int64_t n_streams, cudaStream_t 
 }
 
 template <int HD, int CQ>
-static int launch_stage_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
-  return p.lane_major ? launch_stage_lm<HD, CQ, true>(p, n_streams, st)
-                      : launch_stage_lm<HD, CQ, false>(p, n_streams, st);
+static int launch_lane_major(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
+  const int band = (int)(p.k_hi - p.k_lo);
+  const size_t smem = attn_lm_smem_floats<HD, CQ>(band) * sizeof(float);
+  if (smem > 227 * 1024) {
+    set_error("attn_stream: band %d needs %zu bytes of shared memory", band, smem);
+    return kErrUnsupported;
+  }
+  auto kern = attn_lm_kernel<HD, CQ>;
+  static std::atomic<size_t> smem_limit[64];
+  const int rc = raise_smem_limit((const void *)kern, smem, smem_limit);
+  if (rc) return rc;
+  kern<<<dim3((unsigned)p.n_heads, (unsigned)n_streams), HD, smem, st>>>(p);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
 }
 
 template <int HD, int CQ>
 static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
-  if (stage_fits<HD, CQ>(p)) return launch_stage_t<HD, CQ>(p, n_streams, st);
+  if (p.lane_major && stage_fits<HD, CQ>(p)) return launch_lane_major<HD, CQ>(p, n_streams, st);
+  if (stage_fits<HD, CQ>(p)) return launch_stage_lm<HD, CQ, false>(p, n_streams, st);
   if (p.lane_major || p.qout.xq || p.zrows) {
     set_error("attn_stream: lane-major rows / quantised output / row sub-ranges need the staged kernel (band %lld too large or "
               "rows unaligned)",
