@@ -487,15 +487,30 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
 // at band 77) and uniform control flow.
 //   A. a warp takes one tile of kLmKT = 4 keys for two groups of 4 queries
 //      (one per half-warp): 16 accumulators per lane, pos rows read through
-//      L1 from one precomputed row offset each.  The 16 lane sums of the
-//      tile's pairs go through the tile's own K rows, dead by then, with a
-//      rotated layout that keeps both the stores and the ordered reads free
-//      of bank conflicts.
+//      L1 from one precomputed row offset each.  K tiles sit kLmTile floats
+//      apart (4 rows + 32 spare), and the 16 lane sums of the tile's pairs
+//      go through the tile itself once its K rows are dead: half-warp hw's
+//      pair pr, lane x at hw*272 + pr*17 + x, conflict-free for the stores
+//      (one pair, 16 lanes) and the ordered reads (16 pairs, one lane), and
+//      every address an immediate offset.
 //   C. per query: max and exp over the band on the warp's lanes, then the
 //      warp's two queries' sequential sums on two lanes at once.
 //   D. P.V over the keys any query of the call attends to ([k0 of the
 //      first query, k1 of the last)), 4 keys per step, a uniform tail.
+__device__ __forceinline__ void band_of32(int qq, int chunk, int left_chunks, int k_hi, int &kmin, int &kmax) {
+  const int qc = qq / chunk;
+  kmin = (qc > left_chunks ? qc - left_chunks : 0) * chunk;
+  const int hi = (qc + 1) * chunk;
+  kmax = hi < k_hi ? hi : k_hi;
+}
+
 constexpr int kLmKT = 4;
+constexpr int kLmRed = 2 * 16 * 17;  // lane-sum scratch of one warp's tile
+
+template <int HD>
+__host__ __device__ constexpr int lm_tile_floats() {
+  return kLmKT * HD + 32 > kLmRed ? kLmKT * HD + 32 : kLmRed;
+}
 
 __host__ __device__ constexpr int lm_wstride(int band) {
   // a multiple of 4 (16-byte weight loads) with an odd number of 16-byte
@@ -505,8 +520,8 @@ __host__ __device__ constexpr int lm_wstride(int band) {
 
 template <int HD, int CQ>
 __host__ __device__ constexpr size_t attn_lm_smem_floats(int band) {
-  return (size_t)((band + kLmKT - 1) / kLmKT * kLmKT) * HD + 2 * (size_t)CQ * HD + (size_t)CQ * lm_wstride(band) +
-         (kLmKT * HD >= 512 && CQ == 8 ? 0 : (size_t)(HD / 32) * 512);
+  return (size_t)((band + kLmKT - 1) / kLmKT) * lm_tile_floats<HD>() + 2 * (size_t)CQ * HD +
+         (size_t)CQ * lm_wstride(band) + (CQ == 8 ? 0 : (size_t)(HD / 32) * kLmRed);
 }
 
 template <int HD, int CQ>
@@ -516,46 +531,56 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
   constexpr int NQG = CQ / 4;          // query groups of 4; a warp takes two
   constexpr int NPV = 4 + KT - 1;      // pos rows of one (group, tile)
   constexpr int NHALF = HD / 64;       // 16-byte slices of a lane's dims
-  // the tile's K rows hold the lane sums when one warp owns the tile
-  constexpr bool kRedInK = KT * HD >= 512 && NQG == 2;
+  constexpr int TS = lm_tile_floats<HD>();
+  // the tile holds the lane sums when one warp owns the tile
+  constexpr bool kRedInK = NQG == 2;
   extern __shared__ __align__(16) float sm[];
   const int band = (int)(p.k_hi - p.k_lo), nt = (band + KT - 1) / KT, bw = lm_wstride(band);
-  float *s_k = sm;                     // [nt*KT][HD] K lane-major, later V natural
-  float *s_qu = s_k + nt * KT * HD;    // [CQ][HD] q + u lane-major
+  float *s_k = sm;                     // [nt][TS]: row kk at (kk/4)*TS + (kk%4)*HD; K lane-major, later V natural
+  float *s_qu = s_k + nt * TS;         // [CQ][HD] q + u lane-major
   float *s_qv = s_qu + CQ * HD;        // [CQ][HD] q + v lane-major
   float *s_w = s_qv + CQ * HD;         // [CQ][bw] scores, then weights
-  float *s_red = s_w + CQ * bw;        // [NW][512] when the tile's K rows are too small
+  float *s_red = s_w + CQ * bw;        // [NW][kLmRed] when two warps share a tile
+  auto srow = [&](int kk) { return s_k + (kk >> 2) * TS + (kk & 3) * HD; };
   const int h = blockIdx.x;
   const int64_t z = blockIdx.y;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int hoff = h * HD;
   const int c = p.c;
   const int64_t zq = p.zrows > 0 ? p.zrows : c, zn = p.zrows > 0 ? p.zrows : p.rows_new;
-  const int kk_new = (int)(p.new_lo - p.k_lo);
-  const int slot0 = p.cap > 0 ? (int)(p.k_lo % p.cap) : 0;
-  const int cap = (int)p.cap;
-  const int kk_s = (int)(p.s - p.k_lo);
-  auto ring_row = [&](float *ring, int kk) -> float * {
-    int slot = slot0 + kk;
+  // Frame numbers fit in 32 bits (attn_prepare checks k_hi).  The values
+  // below come straight from the parameters where they are used, so that
+  // none of them stays live through the score tiles.
+#define LM_S32 ((int)p.s)
+#define LM_KLO ((int)p.k_lo)
+  // Band row kk into the tile layout, a warp per row and 16 bytes a lane: the
+  // call's new frames (kk >= kk_new) from the projection output, also
+  // written to the ring (slot = frame % cap), older frames from the ring.
+  auto stage_rows = [&](float *ring, const float *nw) {
+    const int kk_new = (int)p.new_lo - LM_KLO, cap = (int)p.cap;
+    const int slot0 = cap > 0 ? LM_KLO % cap : 0;
+    const int64_t new_row0 = z * zn + p.r0;  // projection row of frame new_lo
+    const bool lane_on = HD / 4 >= 32 || lane < HD / 4;
+    float *rz = ring ? ring + z * cap * (int64_t)p.d + hoff + lane * 4 : nullptr;
+    int slot = slot0 + warp;
     slot = slot >= cap ? slot - cap : slot;
-    return ring + (z * cap + slot) * (int64_t)p.d + hoff;
-  };
-  auto key_row = [&](float *ring, const float *nw, int kk) -> const float * {
-    if (kk >= kk_new) return nw + (z * zn + p.r0 + (kk - kk_new)) * p.ld_new + hoff;
-    return ring_row(ring, kk);
+    for (int kk = warp; kk < band; kk += NW) {
+      if (kk >= kk_new) {
+        const float *src = nw + (new_row0 + (kk - kk_new)) * p.ld_new + hoff + lane * 4;
+        if (lane_on) {
+          cp_async16(srow(kk) + lane * 4, src);
+          if (rz) *reinterpret_cast<float4 *>(rz + slot * p.d) = *reinterpret_cast<const float4 *>(src);
+        }
+      } else if (lane_on) {
+        cp_async16(srow(kk) + lane * 4, rz + slot * p.d);
+      }
+      slot += NW;
+      slot = slot >= cap ? slot - cap : slot;
+    }
   };
 
-  // ---- stage: K band (a warp per row, 16 bytes a lane), new K rows into the
-  // ring, q + u and q + v ----
-  for (int kk = warp; kk < band; kk += NW) {
-    const float *src = key_row(p.k_ring, p.k_new, kk);
-    for (int e4 = lane; e4 < HD / 4; e4 += 32) cp_async16(s_k + kk * HD + e4 * 4, src + e4 * 4);
-    if (p.k_ring && kk >= kk_s) {
-      float *dst = ring_row(p.k_ring, kk);
-      for (int e4 = lane; e4 < HD / 4; e4 += 32)
-        *reinterpret_cast<float4 *>(dst + e4 * 4) = *reinterpret_cast<const float4 *>(src + e4 * 4);
-    }
-  }
+  // ---- stage: K band, new K rows into the ring, q + u and q + v ----
+  stage_rows(p.k_ring, p.k_new);
   {
     const float uu = p.u[hoff + t], vv = p.v[hoff + t];
     const float *qrow = p.q + (z * zq + p.r0) * p.ldq + hoff + t;
@@ -573,7 +598,7 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
   {
     const int hw = lane >> 4, l = lane & 15;
     // pos row of (query j, key kk) is prow0 + j - kk
-    const int prow0 = (int)(p.s + p.pos_off - p.k_lo - p.pr_lo);
+    const int prow0 = LM_S32 + (int)(p.pos_off - p.pr_lo) - LM_KLO;
     const float *pbase = p.pos_p + p.pr_lo * (int64_t)p.d + hoff + l * 4;
     const int nunits = nt * (NQG / 2);
     for (int u = warp; u < nunits; u += NW) {
@@ -589,7 +614,7 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
         const int pi = prow0 - kt0 + 4 * qg - (KT - 1) + m;  // masked pairs may fall outside
         poff[m] = (pi < 0 ? 0 : (pi >= p.np ? p.np - 1 : pi)) * p.d;
       }
-      const float *kb = s_k + kt0 * HD + l * 4;
+      const float *kb = s_k + tile * TS + l * 4;
       const float *qub = s_qu + 4 * qg * HD + l * 4, *qvb = s_qv + 4 * qg * HD + l * 4;
 #pragma unroll
       for (int hh = 0; hh < NHALF; hh++) {
@@ -613,25 +638,20 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
               acc[j][b] = __fmaf_rn(f4c(qu[j], cc), f4c(kv[b], cc), inner);
             }
       }
-      // the 16 lane sums of each of the half-warp's 16 pairs: pair pr of
-      // half-warp hw, lane x at rbase(hw, pr) + ((x + pr) & 15)
-      float *red = kRedInK ? s_k + kt0 * HD : s_red + warp * 512;
+      // the 16 lane sums of each of the half-warp's 16 pairs
+      float *red = (kRedInK ? s_k + tile * TS : s_red + warp * kLmRed) + hw * 272;
       __syncwarp();  // both half-warps are done with the tile's K rows
 #pragma unroll
       for (int j = 0; j < 4; j++)
 #pragma unroll
-        for (int b = 0; b < KT; b++) {
-          const int pr = j * KT + b;
-          red[hw * 256 + ((pr + hw) & 15) * 16 + ((l + pr) & 15)] = acc[j][b];
-        }
+        for (int b = 0; b < KT; b++) red[(j * KT + b) * 17 + l] = acc[j][b];
       __syncwarp();
       {
-        const int pr = l;
-        const float *rr = red + hw * 256 + ((pr + hw) & 15) * 16;
-        float sum = rr[pr & 15];
+        const float *rr = red + l * 17;  // pair pr = l
+        float sum = rr[0];
 #pragma unroll
-        for (int x = 1; x < kLanes; x++) sum = __fadd_rn(sum, rr[(x + pr) & 15]);
-        const int j = 4 * qg + pr / KT, kk = kt0 + pr % KT;
+        for (int x = 1; x < kLanes; x++) sum = __fadd_rn(sum, rr[x]);
+        const int j = 4 * qg + l / KT, kk = kt0 + l % KT;
         if (j < c && kk < band) s_w[j * bw + kk] = __fmul_rn(sum, p.scale);
       }
       __syncwarp();  // the scratch is read before the warp's next tile
@@ -639,36 +659,23 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
   }
   __syncthreads();
   // ---- V band into shared memory (natural order), overlapped with C ----
-  for (int kk = warp; kk < band; kk += NW) {
-    const float *src = key_row(p.v_ring, p.v_new, kk);
-    for (int e4 = lane; e4 < HD / 4; e4 += 32) cp_async16(s_k + kk * HD + e4 * 4, src + e4 * 4);
-    if (p.v_ring && kk >= kk_s) {
-      float *dst = ring_row(p.v_ring, kk);
-      for (int e4 = lane; e4 < HD / 4; e4 += 32)
-        *reinterpret_cast<float4 *>(dst + e4 * 4) = *reinterpret_cast<const float4 *>(src + e4 * 4);
-    }
-  }
+  stage_rows(p.v_ring, p.v_new);
   // ---- C: band mask + softmax per query (simd_kernel.rs:1010-1104) ----
   {
     constexpr int QPW = (CQ + NW - 1) / NW;  // queries per warp
-    float inv[QPW];
-    int k0s[QPW], k1s[QPW];
 #pragma unroll
     for (int i = 0; i < QPW; i++) {
       const int j = warp + i * NW;
-      float *row = s_w + j * bw;
-      k0s[i] = 0;
-      k1s[i] = 0;
       if (j >= CQ) continue;
+      float *row = s_w + j * bw;
       if (j >= c) {
         for (int kk = lane; kk < bw; kk += 32) row[kk] = 0.0f;
         continue;
       }
-      int64_t kmin, kmax;
-      band_of(p.s + j, p.chunk, p.left_chunks, p.k_hi, kmin, kmax);
-      const int k0 = (int)(kmin - p.k_lo), k1 = (int)(kmax - p.k_lo);
-      k0s[i] = k0;
-      k1s[i] = k1;
+      int k0, k1;
+      band_of32(LM_S32 + j, (int)p.chunk, (int)p.left_chunks, (int)p.k_hi, k0, k1);
+      k0 -= LM_KLO;
+      k1 -= LM_KLO;
       float mx = -INFINITY;
       for (int kk = k0 + lane; kk < k1; kk += 32) mx = fmaxf(mx, row[kk]);
 #pragma unroll
@@ -676,36 +683,37 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
       for (int kk = lane; kk < bw; kk += 32) row[kk] = (kk >= k0 && kk < k1) ? exp_rn(__fsub_rn(row[kk], mx)) : 0.0f;
     }
     __syncwarp();
-    // lane i sums the warp's i-th query over its band in order
+    // lane i sums the warp's i-th query over its band in order, the warp's
+    // lanes side by side (rows j and j + NW sit in different banks)
     float mine = 0.0f;
-#pragma unroll
-    for (int i = 0; i < QPW; i++) {
-      const int j = warp + i * NW;
-      if (lane == i && j < c) {
-        const float *row = s_w + j * bw;
+    {
+      const int j = warp + lane * NW;
+      if (lane < QPW && j < c) {
+        int k0, k1;
+        band_of32(LM_S32 + j, (int)p.chunk, (int)p.left_chunks, (int)p.k_hi, k0, k1);
+        const float *row = s_w + j * bw - LM_KLO;
         float sum = 0.0f;
-        for (int kk = k0s[i]; kk < k1s[i]; kk++) sum = __fadd_rn(sum, row[kk]);
+        for (int kk = k0; kk < k1; kk++) sum = __fadd_rn(sum, row[kk]);
         mine = __fdiv_rn(1.0f, sum);
       }
     }
 #pragma unroll
-    for (int i = 0; i < QPW; i++) inv[i] = __shfl_sync(0xffffffffu, mine, i);
-#pragma unroll
     for (int i = 0; i < QPW; i++) {
       const int j = warp + i * NW;
+      const float inv = __shfl_sync(0xffffffffu, mine, i);
       if (j >= c) continue;
       float *row = s_w + j * bw;
-      for (int kk = lane; kk < bw; kk += 32) row[kk] = __fmul_rn(row[kk], inv[i]);
+      for (int kk = lane; kk < bw; kk += 32) row[kk] = __fmul_rn(row[kk], inv);
     }
   }
   cp_async_wait_all();
   __syncthreads();
   // ---- D: P.V over the keys the call attends to, one thread per head dim ----
   {
-    int64_t kmin, kmax, kmin2, kmax2;
-    band_of(p.s, p.chunk, p.left_chunks, p.k_hi, kmin, kmax);
-    band_of(p.s + c - 1, p.chunk, p.left_chunks, p.k_hi, kmin2, kmax2);
-    const int ka = (int)(kmin - p.k_lo) & ~3, kb = (int)(kmax2 - p.k_lo);
+    int kmin, kmax, kmin2, kmax2;
+    band_of32(LM_S32, (int)p.chunk, (int)p.left_chunks, (int)p.k_hi, kmin, kmax);
+    band_of32(LM_S32 + c - 1, (int)p.chunk, (int)p.left_chunks, (int)p.k_hi, kmin2, kmax2);
+    const int ka = (kmin - LM_KLO) & ~3, kb = kmax2 - LM_KLO;
     float acc[CQ];
 #pragma unroll
     for (int j = 0; j < CQ; j++) acc[j] = 0.0f;
@@ -715,15 +723,16 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
 #pragma unroll
       for (int j = 0; j < CQ; j++) w[j] = *reinterpret_cast<const float4 *>(s_w + j * bw + kk);
       float vv[4];
+      const float *vt = s_k + (kk >> 2) * TS + t;
 #pragma unroll
-      for (int e = 0; e < 4; e++) vv[e] = s_k[(kk + e) * HD + t];
+      for (int e = 0; e < 4; e++) vv[e] = vt[e * HD];
 #pragma unroll
       for (int e = 0; e < 4; e++)
 #pragma unroll
         for (int j = 0; j < CQ; j++) acc[j] = __fmaf_rn(f4c(w[j], e), vv[e], acc[j]);
     }
     for (; kk < kb; kk++) {
-      const float vv = s_k[kk * HD + t];
+      const float vv = srow(kk)[t];
 #pragma unroll
       for (int j = 0; j < CQ; j++) acc[j] = __fmaf_rn(s_w[j * bw + kk], vv, acc[j]);
     }
@@ -741,6 +750,9 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
   }
 }
 
+#undef LM_S32
+#undef LM_KLO
+
 // Validates the band and pos rows the chunk touches, fills pr_lo/np.
 int attn_prepare(AttnParams &p, int64_t n_pos) {
   if (p.c <= 0 || p.c > 16 || p.d <= 0 || p.n_heads <= 0 || p.d % p.n_heads != 0) {
@@ -753,7 +765,7 @@ int attn_prepare(AttnParams &p, int64_t n_pos) {
     return kErrUnsupported;
   }
   if (p.chunk <= 0 || p.left_chunks < 0 || p.s < 0 || p.k_lo < 0 || p.k_hi <= p.k_lo ||
-      p.k_hi - p.k_lo > 256) {
+      p.k_hi - p.k_lo > 256 || p.k_hi + p.chunk >= ((int64_t)1 << 30) || p.left_chunks >= ((int64_t)1 << 30)) {
     set_error("attn_stream: bad band [%lld, %lld) chunk %lld (band must be 1..256)",
               (long long)p.k_lo, (long long)p.k_hi, (long long)p.chunk);
     return kErrInvalid;

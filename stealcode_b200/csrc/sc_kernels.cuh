@@ -108,18 +108,22 @@ int gemm_mid(const MidGemmArgs &a, cudaStream_t st);
 // no-swizzle K-major core-matrix layout of ft rows x 16 bytes), and the
 // block scale at dx[((f / ft) * nb + i / 32) * ft + f % ft] (a frame tile's
 // scales for consecutive blocks are contiguous).  xq == nullptr: unused.
+// ft is 64 or 128 (tc_frame_tile), so the indices take shifts, not divisions.
 struct QOut {
   __half *xq;
   float *dx;
   int64_t nb, t_pad;
   int ft;
 };
+__host__ __device__ inline int qout_ft_shift(const QOut &q) { return q.ft == 128 ? 7 : 6; }
 __host__ __device__ inline int64_t qout_dx_index(const QOut &q, int64_t f, int64_t blk) {
-  return ((f / q.ft) * q.nb + blk) * (int64_t)q.ft + f % q.ft;
+  const int sh = qout_ft_shift(q);
+  return (((f >> sh) * q.nb + blk) << sh) + (f & (q.ft - 1));
 }
 __host__ __device__ inline int64_t qout_code_index(const QOut &q, int64_t f, int64_t i) {
-  return ((f / q.ft) * q.nb + i / 32) * (int64_t)q.ft * 32 + ((i & 31) >> 3) * (int64_t)q.ft * 8 +
-         (f % q.ft) * 8 + (i & 7);
+  const int sh = qout_ft_shift(q);
+  return (((f >> sh) * q.nb + (i >> 5)) << (sh + 5)) + (((i & 31) >> 3) << (sh + 3)) + ((f & (q.ft - 1)) << 3) +
+         (i & 7);
 }
 
 struct TcGemmArgs {
