@@ -13,11 +13,14 @@ over ranks of the K steps' CUDA-event time).  The 587 MB of Q8_0 weights a
 step streams are larger than L2 (126 MB).
 
 Also in the line:
-  roofline      the tcgen05 int8 GEMM (the step's dominant kernel) at the
-                step's shapes (the encoder's two halves of the streams, 896
-                frames each at 256 streams, in flight on two CUDA streams),
-                over the 24 layers' own weights, timed with CUDA events
-                (tensor-bound);
+  roofline      the tcgen05 GEMM (the step's dominant kernel: kind::f16
+                on the int8 codes held as f16, exact per-block f32 drain) at
+                the step's shapes (the encoder's two halves of the streams,
+                896 frames each at 256 streams, in flight on two CUDA
+                streams), over the 24 layers' own weights, timed with CUDA
+                events, against the dense f16 tensor peak; drain_issue is the
+                same time against the kernel's own floor, 3 f32 operations
+                per (output, 32-deep block) at 128 per SM per clock;
   gemm_sweep    the Q8_0 GEMM shape sweep of one layer (M = 1, 8, 32, 128;
                 QKV, out-proj, FFN-up, FFN-down; 24 weight copies, 321 MB)
                 as HBM GB/s, and its weight-streaming kernel's roofline;
@@ -42,11 +45,13 @@ Also in the line:
                 joint 640, 1025 classes) straight from the encoder's device
                 output; CUDA-event time per step, the decoder's share, and
                 the tokens emitted per frame;
-  cpu_baseline  the reference CPU path (the oracle's restatement: AVX2 +
-                threads GEMMs, one StreamingEncoder per stream) on a bounded
-                sample of the same workload, and the reference CPU GEMM on
-                one streaming chunk (M 8, K 1024, N 4096) with all host
-                threads and with one.
+  cpu_baseline  the reference CPU path (the oracle's restatement with the
+                reference's threading -- rayon over 256-row GEMM chunks,
+                conv output positions and attention queries -- and AVX2
+                lanes, one StreamingEncoder per stream) on a bounded sample
+                of the same workload with its host seconds by phase, and the
+                reference CPU GEMM on one streaming chunk (M 8, K 1024,
+                N 4096) with all host threads and with one.
 
 Multi-GPU: one process per GPU (torchrun); every rank encodes its own 256
 streams with its own weight copy (streams are independent: no collective on
@@ -194,9 +199,12 @@ def encoder_model():
 
 # ------------------------------------------------------------ CPU paths ---
 def cpu_encoder_sample(m, n_streams, n_steps, budget_s=None):
-    """The reference CPU path (oracle StreamingEncoder per stream, reference
-    GEMM dispatch, all host threads) for n_streams streams x up to n_steps
-    chunks from t = 0.  Returns (audio-s/s, seconds, audio seconds, steps)."""
+    """The reference CPU path for n_streams streams x up to n_steps chunks
+    from t = 0: one oracle StreamingEncoder per stream in its fast mode --
+    the reference's threading (rayon over 256-row chunks, output positions
+    and queries, on all host threads) and AVX2 lanes, bit-identical to the
+    serial restatement -- with the reference's Q8 GEMM dispatch.  Returns
+    (audio-s/s, seconds, audio seconds, steps, host seconds by phase)."""
     import oracle
     from stealcode_b200 import model
 
@@ -213,7 +221,17 @@ def cpu_encoder_sample(m, n_streams, n_steps, budget_s=None):
             break
     dt = time.perf_counter() - t0
     audio = n_streams * done * AUDIO_S_PER_STEP
-    return audio / dt, dt, audio, done
+    return audio / dt, dt, audio, done, phase_sum(encs)
+
+
+def phase_sum(encs):
+    """Host seconds by phase summed over the oracle encoders, with the rest."""
+    tot = {"pre_encode": 0.0, "linears": 0.0, "attention": 0.0, "total": 0.0}
+    for e in encs:
+        for k, v in e.phase_times().items():
+            tot[k] += v
+    tot["rest"] = tot["total"] - tot["pre_encode"] - tot["linears"] - tot["attention"]
+    return tot
 
 
 def cpu_gemm_sample(budget_s=2.0):
@@ -262,21 +280,26 @@ def run_reference(args, rank):
     times = []
     for i in range(total):
         a, b = MEL_PER_STEP * i, MEL_PER_STEP * (i + 1)
+        if i == args.warmup:
+            before = phase_sum(encs)
         t0 = time.perf_counter()
         for z in range(n_streams):
             assert encs[z].encode_new(mel[z, :b], a, b) == 0
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
+    after = phase_sum(encs)
+    phases = {k: after[k] - before[k] for k in after}
     value = n_streams * AUDIO_S_PER_STEP * len(times) / sum(times)
     cores = oracle.num_cpus()
     sample = (f"{n_streams} streams x 1 chunk per step (steps {args.warmup}..{total - 1} of the streams), "
-              "oracle StreamingEncoder with the reference's GEMM dispatch")
+              "oracle StreamingEncoder per stream with the reference's threading, AVX2 lanes and GEMM dispatch")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8+f32",
             "data": "synthetic", "config": {"workload": WORKLOAD, "streams_per_step": n_streams,
                                             "chunk_ms": 560, "layers": N_LAYERS},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+                             "phases_s": phases},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -397,18 +420,30 @@ def tc_roofline(m, streams, dev, stream):
     ops = sum(2.0 * t * rows * k for t in halves for _, rows, k in mats)
     p = peaks()
     bf16 = p.get("bf16_tflops")
-    peak = 2.0 * bf16 if bf16 else 2.0 * 1590.0
+    # the MMAs run kind::f16 on the int8 codes held as f16 (exact), so the
+    # tensor roofline is the dense f16 / bf16 rate
+    peak = bf16 if bf16 else 1590.0
     achieved = ops / (ms_tc * 1e-3) / 1e12
     n = len(mats) * len(halves)
+    # The exact per-block scaling drains every 32-deep block of every output
+    # from TMEM through 3 f32 operations (s = dw*dx, p = s*dot, acc += p):
+    # at 128 f32 operations per SM per clock that is the kernel's issue floor.
+    blocks = sum(t * rows * (k // 32) for t in halves for _, rows, k in mats)
+    clk_ghz = float(p.get("sm_max_mhz") or 1965.0) / 1e3
+    drain_floor_ms = 3.0 * blocks / (148 * 128 * clk_ghz * 1e9) * 1e3
     del mats, bufs
-    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
-            "frac_of_nominal_4500_tops": achieved / 4500.0,
-            "peak_source": ("2 x measured dense bf16 TFLOP/s (B200's dense int8 rate is twice its bf16 rate)"
-                            if bf16 else "2 x fallback bf16"),
-            "kernel": "q8_gemm_tc_kernel (tcgen05 kind::i8)", "traffic": None,
-            "frames": halves, "launches": n, "us_per_launch": 1e3 * ms_tc / n, "ops_per_launch": ops / n,
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "frac_of_nominal_2250": achieved / 2250.0,
+            "peak_source": ("measured dense bf16 TFLOP/s (the kind::f16 rate)" if bf16 else "fallback bf16"),
+            "kernel": "q8_gemm_tc_kernel (tcgen05 kind::f16, int8 codes held as f16, exact per-block f32 drain)",
+            "traffic": None, "frames": halves, "launches": n, "us_per_launch": 1e3 * ms_tc / n,
+            "ops_per_launch": ops / n,
             "note": "the step's sub-batches in flight on two streams: us_per_launch is step GEMM time / launches",
-            "linear_incl_quantize": {"tops": ops / (ms_all * 1e-3) / 1e12, "us_per_launch": 1e3 * ms_all / n}}
+            "drain_issue": {"element_blocks_per_step": blocks, "ops_per_element_block": 3,
+                            "floor_ms_per_step": drain_floor_ms, "measured_ms_per_step": ms_tc,
+                            "frac": drain_floor_ms / ms_tc,
+                            "basis": f"148 SMs x 128 f32 ops per clock at {clk_ghz:.3f} GHz"},
+            "linear_incl_quantize": {"tflops": ops / (ms_all * 1e-3) / 1e12, "us_per_launch": 1e3 * ms_all / n}}
 
 
 def gemm_sweep(args, dev, world, stream):
@@ -681,11 +716,11 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
 
-        v, dt, audio, steps = cpu_encoder_sample(m, 4, 8, budget_s=15.0)
+        v, dt, audio, steps, phases = cpu_encoder_sample(m, 4, 8, budget_s=15.0)
         cpu = {"value": v, "unit": UNIT, "cores": oracle.num_cpus(), "kind": "port",
                "sample": f"4 streams x {steps} chunks from t=0 ({audio:.2f} audio s in {dt:.1f} s), oracle "
-                         "StreamingEncoder with the reference's GEMM dispatch",
-               "gemm": cpu_gemm_sample()}
+                         "StreamingEncoder per stream with the reference's threading, AVX2 lanes and GEMM "
+                         "dispatch", "phases_s": phases, "gemm": cpu_gemm_sample()}
     if rank == 0:
         p = peaks()
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
