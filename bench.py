@@ -109,7 +109,7 @@ def parse():
     ap.add_argument("--box-streams", type=int, default=8192,
                     help="global streams of the box-scale block (sharded over the GPUs); 0 skips it")
     ap.add_argument("--box-steps", type=int, default=3)
-    ap.add_argument("--profile", default=None, choices=["gemm", "attn", "tc", "encoder", "breakdown"],
+    ap.add_argument("--profile", default=None, choices=["gemm", "attn", "tc", "encoder", "breakdown", "batch"],
                     help="small eager case for ncu captures (no timing, no JSON line); breakdown: per-kernel "
                          "device time of 3 steady headline steps (CUPTI through torch.profiler)")
     return ap.parse_args()
@@ -568,7 +568,6 @@ def gemm_sweep(args, dev, world, stream):
     config0 = {"workload": "q8_gemm M=8 K=1024 N=4096 (one streaming chunk), 64 weight copies in a graph",
                "us_per_gemm": 1e3 * ms0 / n0, "bytes_per_gemm": b0, "gbs": b0 * n0 / (ms0 * 1e-3) / 1e9,
                "frac": b0 * n0 / (ms0 * 1e-3) / 1e9 / peak, "peak_source": "measured" if "hbm_gbs" in p else "fallback"}
-    del c0
     # the same sweep per M in batched calls (sc_q8_gemm_batch: every GEMM of
     # the 24 layer copies in one streaming pass, quantisation included)
     from stealcode_b200.ops import q8_gemm_batch
@@ -602,6 +601,28 @@ def gemm_sweep(args, dev, world, stream):
         batched[str(m)] = {"ms_per_sweep": ms_b, "gbs": bb / (ms_b * 1e-3) / 1e9,
                            "frac": bb / (ms_b * 1e-3) / 1e9 / peak, "gemms_per_call": bws_n, "launches": 2}
     del bws
+    # config 0 the batched way: the 64 single-chunk GEMMs (M 8, K 1024,
+    # N 4096, own weights and outputs) as one sc_q8_gemm_batch call
+    h0 = (ctypes.c_void_p * len(c0))(*[mt.handle.value for mt in c0])
+    ws0 = torch.empty(int(lib.sc_q8_gemm_batch_workspace_bytes(h0, len(c0))), dtype=torch.uint8, device=dev)
+    y0s = [torch.empty((8, 4096), dtype=torch.float32, device=dev) for _ in c0]
+
+    def call0b():
+        q8_gemm_batch(c0, [x0] * len(c0), outs=y0s, workspace=ws0)
+
+    s0b = torch.cuda.Stream(device=dev)
+    s0b.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s0b):
+        call0b()
+    torch.cuda.current_stream().wait_stream(s0b)
+    torch.cuda.synchronize()
+    g0b = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g0b):
+        call0b()
+    ms0b = time_graph(g0b, reps)
+    del g0b, c0, ws0, y0s
+    config0["batched"] = {"api": "sc_q8_gemm_batch, the 64 GEMMs in one call", "us_per_gemm": 1e3 * ms0b / n0,
+                          "gbs": b0 * n0 / (ms0b * 1e-3) / 1e9, "frac": b0 * n0 / (ms0b * 1e-3) / 1e9 / peak}
     return {"metric": "Q8_0 GEMM HBM GB/s (FastConformer layer shape sweep)", "value": step_bytes / (ms * 1e-3) / 1e9,
             "unit": "GB/s", "shapes": SHAPES, "m": MS, "weight_copies": SWEEP_LAYERS, "ms_per_sweep": ms,
             "launches_per_sweep": n_launch,
@@ -929,6 +950,19 @@ def run_profile(args):
         for _ in range(3):
             attn_stream_ring(q, kn, vn, rk, rv, pos, u, v, c=c, d=d, n_heads=nh, scale=1 / math.sqrt(128), s=s,
                              k_lo=k_lo, chunk=chunk, left_chunks=lc, pos_off=chunk - 1)
+    elif args.profile == "batch":
+        # one sc_q8_gemm_batch call over the layer sweep's 96 GEMMs (24
+        # weight copies of the four shapes, 321 MB), M = 1 then M = 8
+        from stealcode_b200.ops import q8_gemm_batch
+
+        wh = {name: synth.q8_weights(synth.SEED_BASE + 1 + i, n, k) for i, (name, k, n) in enumerate(SHAPES)}
+        flat = [(Q8Mat(wh[name], n, k), k, n) for _ in range(SWEEP_LAYERS) for name, k, n in SHAPES]
+        for m in (1, 8):
+            xs = {k: torch.from_numpy(synth.normal(synth.SEED_BASE + 100 + m + k, (m, k))).to(dev)
+                  for k in (1024, 4096)}
+            ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _, _, n in flat]
+            for _ in range(3):
+                q8_gemm_batch([mt for mt, _, _ in flat], [xs[k] for _, k, _ in flat], outs=ys)
     elif args.profile == "breakdown":
         import collections
 

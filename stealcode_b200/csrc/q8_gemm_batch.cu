@@ -19,26 +19,47 @@
 //
 // Stream kernel, persistent (one CTA per SM): work unit = (GEMM, 128-row
 // group), all of K; units are dealt round-robin.  Warp 0: one thread streams
-// the units' weight tiles and scales (8 K blocks per bulk copy, no multicast)
-// through a ring of shared-memory stages; warps 1-8 compute:
+// each stage -- 8 K blocks of the unit's weight tiles and scales, and the
+// same 8 blocks' activation codes and scales -- with bulk copies (no
+// multicast) into a ring of shared-memory stages.  The weights never
+// change, so the first stages' weights go out before the quantiser has
+// finished; their activations follow once it has.  Warps 1-8 compute from
+// shared memory only:
 //   * 1-2 frames: lane = weight row, 4 row quarters x 2 block parities, dp4a
-//     from shared memory with the activation codes read through L1;
-//     the two parities' partial sums are added in shared memory at the end;
+//     against broadcast activation codes; the two parities' partial sums
+//     are added in shared memory at the end;
 //   * 4-16 frames: warp w owns 16 of the 128 rows and takes every block: one
 //     int8 tensor-core MMA (mma.sync m16n8k32, s32 accumulator cleared per
 //     block, so every block's dot is exact) per 8 frames, the weight
-//     fragments read straight from the row-group tile layout (conflict-free
+//     fragments read straight from the row-group tile layout and the
+//     activation fragments from the swizzled code rows (both conflict-free
 //     4-byte loads).
+//
+// Activation codes of one GEMM, per group of 8 K blocks (4 KB, one bulk copy
+// per stage): frame j's 256 bytes at j * 256, the block-bb half h (16 bytes)
+// in 16-byte unit (2 bb + h) ^ (j % 8), so that the eight frames of an MMA
+// fragment read eight different bank groups.  Scales: dx[b * 16 + j].
 #include "sc_device.cuh"
 #include "sc_kernels.cuh"
 
 namespace sc {
 
 constexpr int kBatchKb = 8;      // K blocks per stage
-constexpr int kBatchStages = 6;  // 6 x 34 KB in flight per SM
+constexpr int kBatchStages = 5;  // 5 x 39 KB in flight per SM
 constexpr int kBatchComputeWarps = 8;
 constexpr int kBatchThreads = 32 + 32 * kBatchComputeWarps;
-constexpr int kBatchStage = kBatchKb * (SC_TILE_BYTES + SC_GROUP_ROWS * 2);
+constexpr int kBatchActBytes = kBatchFrames * kBatchKb * 32;  // one stage's activation codes
+constexpr int kBatchScOff = kBatchKb * SC_TILE_BYTES;                   // weight scales
+constexpr int kBatchActOff = kBatchScOff + kBatchKb * SC_GROUP_ROWS * 2;  // activation codes
+constexpr int kBatchDxOff = kBatchActOff + kBatchActBytes;               // activation scales
+constexpr int kBatchStage = kBatchDxOff + kBatchKb * kBatchFrames * 4;
+
+// byte offset of activation code (frame j, k index kk) within its GEMM's codes
+__device__ __forceinline__ int64_t batch_code_offset(int j, int64_t kk) {
+  const int64_t b = kk >> 5;
+  const int unit = (int)((b & 7) * 2 + ((kk >> 4) & 1));
+  return (b >> 3) * kBatchActBytes + j * 256 + ((unit ^ (j & 7)) << 4) + (kk & 15);
+}
 
 static __device__ unsigned g_batch_status;
 
@@ -85,7 +106,7 @@ __global__ void batch_quantize_kernel(const __grid_constant__ BatchParams p) {
   const float v = valid ? (it.x_feature_major ? it.x[kk * it.ldx + j] : it.x[(int64_t)j * it.ldx + kk]) : 0.0f;
   float s;
   const int8_t q = warp_quantize_block(v, valid, s);
-  it.xq[(int64_t)j * it.nb * 32 + kk] = q;
+  it.xq[batch_code_offset(j, kk)] = q;
   if (lane == 0) it.dx[(int64_t)b * kBatchFrames + j] = s;
   pdl_launch_dependents();
 }
@@ -118,27 +139,50 @@ __global__ void __launch_bounds__(kBatchThreads, 1) q8_gemm_batch_kernel(const _
     // ---- producer: weights never change, so they stream before the
     // activation codes' kernel has finished ----
     if (lane == 0) {
+      // stage s's activations: codes and scales of blocks b0 .. b0 + nblk
+      auto acts = [&](int s, const BatchItem &it, int b0, int nblk) {
+        unsigned char *st = smem + s * kBatchStage;
+        bulk_g2s(st + kBatchActOff, it.xq + (int64_t)(b0 / kBatchKb) * kBatchActBytes, kBatchActBytes, &full[s]);
+        bulk_g2s(st + kBatchDxOff, it.dx + (int64_t)b0 * kBatchFrames, nblk * kBatchFrames * 4, &full[s]);
+      };
+      // the first ring's worth of stages, whose activations wait for the quantiser
+      int held_item[kBatchStages], held_b0[kBatchStages], held_n[kBatchStages];
+      bool acts_ready = false;
+      auto release_held = [&](int n_held) {
+        pdl_wait();  // the activation codes are written
+        for (int h = 0; h < n_held; h++) acts(h, p.items[held_item[h]], held_b0[h], held_n[h]);
+        acts_ready = true;
+      };
       int gs = 0;
       for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
-        const BatchItem &it = p.items[batch_item(p, u)];
+        const int ii = batch_item(p, u);
+        const BatchItem &it = p.items[ii];
         const int64_t g = u - it.unit0;
         for (int b0 = 0; b0 < it.nb; b0 += kBatchKb, gs++) {
           const int s = gs % kBatchStages, nblk = it.nb - b0 < kBatchKb ? it.nb - b0 : kBatchKb;
+          if (!acts_ready && gs == kBatchStages) release_held(kBatchStages);
           if (!mbar_wait(&empty[s], ((uint32_t)(gs / kBatchStages) & 1u) ^ 1u)) { ok = false; break; }
           unsigned char *st = smem + s * kBatchStage;
-          mbar_arrive_expect_tx(&full[s], nblk * (SC_TILE_BYTES + SC_GROUP_ROWS * 2));
+          mbar_arrive_expect_tx(&full[s],
+                                nblk * (SC_TILE_BYTES + SC_GROUP_ROWS * 2 + kBatchFrames * 4) + kBatchActBytes);
           bulk_g2s(st, it.qs + (g * it.nb + b0) * SC_TILE_BYTES, nblk * SC_TILE_BYTES, &full[s]);
-          bulk_g2s(st + kBatchKb * SC_TILE_BYTES, it.sc + (g * it.nb + b0) * SC_GROUP_ROWS, nblk * SC_GROUP_ROWS * 2,
-                   &full[s]);
+          bulk_g2s(st + kBatchScOff, it.sc + (g * it.nb + b0) * SC_GROUP_ROWS, nblk * SC_GROUP_ROWS * 2, &full[s]);
+          if (acts_ready) {
+            acts(s, it, b0, nblk);
+          } else {
+            held_item[gs] = ii;
+            held_b0[gs] = b0;
+            held_n[gs] = nblk;
+          }
         }
       }
+      if (!acts_ready) release_held(gs < kBatchStages ? gs : kBatchStages);
       // the last copies have landed before the CTA can exit
       for (int q = gs - kBatchStages; q < gs; q++)
         if (q >= 0) mbar_wait(&full[q % kBatchStages], (uint32_t)(q / kBatchStages) & 1u);
     }
     __syncwarp();
   } else if constexpr (MT >= 4) {
-    pdl_wait();  // the activation codes
     // ---- tensor-core path: warp cw owns rows 16 cw .. 16 cw + 15 of the row
     // group; thread (g = lane / 4, q = lane % 4) holds rows 16 cw + g and
     // 16 cw + g + 8 at frames 2 q, 2 q + 1 (+ 8 per further 8-frame tile) ----
@@ -158,18 +202,20 @@ __global__ void __launch_bounds__(kBatchThreads, 1) q8_gemm_batch_kernel(const _
         const int s = gs % kBatchStages, nblk = it.nb - b0 < kBatchKb ? it.nb - b0 : kBatchKb;
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(gs / kBatchStages) & 1u))) { ok = false; break; }
         const unsigned char *st = smem + s * kBatchStage;
-        const __half *scs = (const __half *)(st + kBatchKb * SC_TILE_BYTES);
+        const __half *scs = (const __half *)(st + kBatchScOff);
+        const unsigned char *sa = st + kBatchActOff;
+        const float *sdx = (const float *)(st + kBatchDxOff);
         for (int bb = 0; bb < nblk; bb++) {
-          const int64_t b = b0 + bb;
           uint32_t xb[NT][2];
           float dxv[NT][2];
 #pragma unroll
           for (int nt = 0; nt < NT; nt++) {
-            const int8_t *xr = it.xq + ((int64_t)(8 * nt + g) * it.nb + b) * 32 + 4 * q;
-            xb[nt][0] = __ldg((const uint32_t *)xr);
-            xb[nt][1] = __ldg((const uint32_t *)(xr + 16));
-            dxv[nt][0] = __ldg(it.dx + b * kBatchFrames + 8 * nt + 2 * q);
-            dxv[nt][1] = __ldg(it.dx + b * kBatchFrames + 8 * nt + 2 * q + 1);
+            // frame 8 nt + g (frame % 8 == g): block bb's halves in units (2 bb + h) ^ g
+            const unsigned char *xr = sa + (8 * nt + g) * 256 + 4 * q;
+            xb[nt][0] = *(const uint32_t *)(xr + (((2 * bb) ^ g) << 4));
+            xb[nt][1] = *(const uint32_t *)(xr + (((2 * bb + 1) ^ g) << 4));
+            dxv[nt][0] = sdx[bb * kBatchFrames + 8 * nt + 2 * q];
+            dxv[nt][1] = sdx[bb * kBatchFrames + 8 * nt + 2 * q + 1];
           }
           const unsigned char *tw = st + bb * SC_TILE_BYTES;
           uint32_t a[4];
@@ -205,7 +251,6 @@ __global__ void __launch_bounds__(kBatchThreads, 1) q8_gemm_batch_kernel(const _
         }
     }
   } else {
-    pdl_wait();  // the activation codes
     const int cw = warp - 1, rs = cw & 3, kp = cw >> 2;
     const int r = rs * 32 + lane;
     int gs = 0;
@@ -219,17 +264,19 @@ __global__ void __launch_bounds__(kBatchThreads, 1) q8_gemm_batch_kernel(const _
         const int s = gs % kBatchStages, nblk = it.nb - b0 < kBatchKb ? it.nb - b0 : kBatchKb;
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(gs / kBatchStages) & 1u))) { ok = false; break; }
         const unsigned char *st = smem + s * kBatchStage;
-        const __half *scs = (const __half *)(st + kBatchKb * SC_TILE_BYTES);
+        const __half *scs = (const __half *)(st + kBatchScOff);
+        const unsigned char *sa = st + kBatchActOff;
+        const float *sdx = (const float *)(st + kBatchDxOff);
         for (int bb = kp; bb < nblk; bb += 2) {
           const unsigned char *tw = st + bb * SC_TILE_BYTES + r * 16;
           const int4 w0 = *(const int4 *)tw, w1 = *(const int4 *)(tw + 2048);
           const float dw = __half2float(scs[bb * SC_GROUP_ROWS + r]);
-          const int64_t b = b0 + bb;
 #pragma unroll
           for (int j = 0; j < MT; j++) {
-            const int4 *xp = (const int4 *)(it.xq + ((int64_t)j * it.nb + b) * 32);
-            const int d = bdot32(w0, w1, __ldg(xp), __ldg(xp + 1));
-            acc[j] = fmaf(dw * __ldg(it.dx + b * kBatchFrames + j), (float)d, acc[j]);
+            const unsigned char *xr = sa + j * 256;
+            const int d = bdot32(w0, w1, *(const int4 *)(xr + (((2 * bb) ^ j) << 4)),
+                                 *(const int4 *)(xr + (((2 * bb + 1) ^ j) << 4)));
+            acc[j] = fmaf(dw * sdx[bb * kBatchFrames + j], (float)d, acc[j]);
           }
         }
         __syncwarp();
@@ -301,11 +348,13 @@ static int launch_batch(const BatchParams &p, int sm_count, cudaStream_t st) {
   return kOk;
 }
 
+// per GEMM: its activation codes in whole 8-block groups, then its scales
+static size_t batch_code_bytes(int64_t nb) { return (size_t)ceil_div(nb, kBatchKb) * kBatchActBytes; }
+static size_t batch_dx_bytes(int64_t nb) { return ((size_t)kBatchFrames * nb * 4 + 255) / 256 * 256; }
+
 size_t batch_ws_bytes(const BatchItem *items, int n) {
   size_t bytes = 0;
-  for (int i = 0; i < n; i++)
-    bytes += ((size_t)kBatchFrames * items[i].nb * 32 + 255) / 256 * 256 +
-             ((size_t)kBatchFrames * items[i].nb * 4 + 255) / 256 * 256;
+  for (int i = 0; i < n; i++) bytes += batch_code_bytes(items[i].nb) + batch_dx_bytes(items[i].nb);
   return bytes;
 }
 
@@ -333,9 +382,9 @@ int gemm_batch(BatchItem *items, int n, int t, int y_time_major, void *ws, size_
   for (int i = 0; i < n; i++) {
     BatchItem it = items[i];
     it.xq = (int8_t *)w;
-    w += ((size_t)kBatchFrames * it.nb * 32 + 255) / 256 * 256;
+    w += batch_code_bytes(it.nb);
     it.dx = (float *)w;
-    w += ((size_t)kBatchFrames * it.nb * 4 + 255) / 256 * 256;
+    w += batch_dx_bytes(it.nb);
     it.unit0 = units;
     units += it.groups;
     nb_max = it.nb > nb_max ? it.nb : nb_max;

@@ -75,7 +75,7 @@ struct BatchItem {
   const float *x;
   const float *bias;
   float *y;
-  int8_t *xq;   // [kBatchFrames][nb * 32] activation codes
+  int8_t *xq;   // activation codes, per 8-block group 16 frames x 256 bytes (q8_gemm_batch.cu)
   float *dx;    // [nb][kBatchFrames] their block scales
   int64_t ldx, ldy;
   int32_t nb, rows, groups, unit0, k, x_feature_major;
