@@ -9,8 +9,8 @@ every stream by one 560 ms chunk (56 mel frames -> 7 encoder frames) with
 70 frames of left context; the first 11 steps (untimed priming) bring the
 attention band to its steady 77 frames.  value = audio seconds encoded per
 second of device time over all ranks: n_gpus * streams * 0.56 * K / (max
-over ranks of the K steps' CUDA-event time).  The 587 MB of Q8_0 weights a
-step streams are larger than L2 (126 MB).
+over ranks of the K steps' CUDA-event time).  The f16 weight tiles a step
+streams (1.1 GB; 587 MB as Q8_0) are larger than L2 (126 MB).
 
 Also in the line:
   roofline      the tcgen05 GEMM (the step's dominant kernel: kind::f16
@@ -753,7 +753,7 @@ def run_ours(args, rank, world, local_rank):
                            "frames_per_step": 7, "left_context_frames": 70, "prime_steps": PRIME_STEPS,
                            "frames_per_gemm": step_halves(Z), "sub_batches": len(step_halves(Z)),
                            "parallelism": f"streams sharded, {world} independent ranks",
-                           "l2": "inputs larger than L2: each step streams 587 MB of Q8_0 weights (L2 126 MB)"},
+                           "l2": "inputs larger than L2: each step streams the 24 layers' f16 weight tiles, 1.1 GB (587 MB as Q8_0), L2 126 MB"},
                 "realtime_streams_per_gpu": value / world,
                 "roofline": roof, "gemm_sweep": sweep, "cpu_baseline": cpu, "e2e": e2e, "transcriber": trans, "prefill": prefill, "box_scale": box,
                 "gpu_launches": launches_timed, "launches_per_step": launches / (args.steps + args.warmup),

@@ -92,17 +92,19 @@ __device__ __forceinline__ int batch_item(const BatchParams &p, int u) {
   return lo;
 }
 
-// Activation codes of every item: one warp per (item, frame < 16, block):
-// frames t .. 15 get zero codes, so the stream kernel may read all MT frames.
+// Activation codes of every item: one warp per (item, frame < t, block).
+// Codes and scales of frames t .. 15 are never written: the stream kernel
+// computes those frames' columns from whatever the workspace holds and
+// never stores them (every output column depends on its own frame only).
 __global__ void batch_quantize_kernel(const __grid_constant__ BatchParams p) {
   const int i = blockIdx.y;
   const BatchItem &it = p.items[i];
   const int lane = threadIdx.x & 31;
   const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (wid >= (int64_t)kBatchFrames * it.nb) return;
+  if (wid >= (int64_t)p.t * it.nb) return;
   const int j = (int)(wid / it.nb), b = (int)(wid % it.nb);
   const int64_t kk = (int64_t)b * 32 + lane;
-  const bool valid = j < p.t && kk < it.k;
+  const bool valid = kk < it.k;
   const float v = valid ? (it.x_feature_major ? it.x[kk * it.ldx + j] : it.x[(int64_t)j * it.ldx + kk]) : 0.0f;
   float s;
   const int8_t q = warp_quantize_block(v, valid, s);
@@ -186,7 +188,7 @@ __global__ void __launch_bounds__(kBatchThreads, 1) q8_gemm_batch_kernel(const _
     // ---- tensor-core path: warp cw owns rows 16 cw .. 16 cw + 15 of the row
     // group; thread (g = lane / 4, q = lane % 4) holds rows 16 cw + g and
     // 16 cw + g + 8 at frames 2 q, 2 q + 1 (+ 8 per further 8-frame tile) ----
-    constexpr int NT = MT / 8 > 0 ? MT / 8 : 1;  // 8-frame tiles (MT 4 uses one, frames 4-7 zero codes)
+    constexpr int NT = MT / 8 > 0 ? MT / 8 : 1;  // 8-frame tiles (MT 4 uses one; columns of frames >= t are not stored)
     const int cw = warp - 1, g = lane >> 2, q = lane & 3;
     const int r0 = 16 * cw + g;
     int gs = 0;
@@ -348,6 +350,14 @@ static int launch_batch(const BatchParams &p, int sm_count, cudaStream_t st) {
   return kOk;
 }
 
+int batch_gemm_status(unsigned *out) {
+  unsigned v = 0, zero = 0;
+  SC_CUDA(cudaMemcpyFromSymbol(&v, g_batch_status, sizeof(v)));
+  SC_CUDA(cudaMemcpyToSymbol(g_batch_status, &zero, sizeof(zero)));
+  *out = v;
+  return kOk;
+}
+
 // per GEMM: its activation codes in whole 8-block groups, then its scales
 static size_t batch_code_bytes(int64_t nb) { return (size_t)ceil_div(nb, kBatchKb) * kBatchActBytes; }
 static size_t batch_dx_bytes(int64_t nb) { return ((size_t)kBatchFrames * nb * 4 + 255) / 256 * 256; }
@@ -391,7 +401,7 @@ int gemm_batch(BatchItem *items, int n, int t, int y_time_major, void *ws, size_
     p.items[i] = it;
   }
   p.total_units = units;
-  dim3 qgrid((unsigned)ceil_div((int64_t)kBatchFrames * nb_max * 32, 256), (unsigned)n);
+  dim3 qgrid((unsigned)ceil_div((int64_t)t * nb_max * 32, 256), (unsigned)n);
   batch_quantize_kernel<<<qgrid, 256, 0, st>>>(p);
   note_launch();
   SC_CUDA(cudaGetLastError());

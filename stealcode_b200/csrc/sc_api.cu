@@ -333,11 +333,12 @@ int sc_q8w_device_layout(const sc_q8w *w, const int8_t **quants, const uint16_t 
 
 int sc_device_status(uint32_t *flags) {
   if (!flags) { set_error("device_status: null pointer"); return kErrInvalid; }
-  unsigned v = 0, v2 = 0;
+  unsigned v = 0, v2 = 0, v3 = 0;
   int rc = small_gemm_status(&v);
   if (!rc) rc = tc_gemm_status(&v2);
+  if (!rc) rc = batch_gemm_status(&v3);
   if (rc) return rc;
-  *flags = v | v2;
+  *flags = v | v2 | v3;
   return kOk;
 }
 

@@ -81,6 +81,7 @@ struct BatchItem {
   int32_t nb, rows, groups, unit0, k, x_feature_major;
 };
 size_t batch_ws_bytes(const BatchItem *items, int n);
+int batch_gemm_status(unsigned *out);  // read and clear the batched kernel's status word
 int gemm_batch(BatchItem *items, int n, int t, int y_time_major, void *ws, size_t ws_bytes, int sm_count,
                cudaStream_t st);
 
