@@ -41,14 +41,14 @@ def _err(got, ref):
 TOL = 1e-4  # max |d| / RMS(reference), f32 outputs
 
 
-def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11, simd_too=False, prompts=None):
+def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11, simd_too=False, prompts=None, per=56):
     """Runs the device encoder and per-stream oracles side by side; returns
     (t0, stream, max/RMS, mean/RMS, exact fraction[, oracle scalar-vs-SIMD
     max/RMS, device-vs-SIMD max/RMS]) per step and stream."""
     from stealcode_b200.ops import StreamEncoder
 
     m = model.random_model(cfg, seed=seed)
-    n_mel = 56 * n_steps + tail
+    n_mel = per * n_steps + tail
     mel = model.mel_stream(seed + 1, n_streams, n_mel, cfg.feat_in)
     dev = StreamEncoder(m, n_streams)
     refs = [oracle.StreamingEncoder(m) for _ in range(n_streams)]
@@ -60,9 +60,9 @@ def run_steps(torch, cfg, n_streams, n_steps, tail=0, seed=11, simd_too=False, p
             r.set_prompt(p if p is not None and 0 <= p < cfg.n_prompts else None)
     simd = [oracle.StreamingEncoder(m) for _ in range(n_streams)] if simd_too else []
     stats = []
-    batches = [(56 * i, 56 * (i + 1), False) for i in range(n_steps)]
+    batches = [(per * i, per * (i + 1), False) for i in range(n_steps)]
     if tail:
-        batches.append((56 * n_steps, 56 * n_steps + tail, True))
+        batches.append((per * n_steps, per * n_steps + tail, True))
     for (t0, t1, fin) in batches:
         dev.encode_new(torch.from_numpy(np.ascontiguousarray(mel[:, t0:t1])).cuda(), t0, t1, fin)
         torch.cuda.synchronize()
@@ -137,6 +137,19 @@ def test_encoder_two_layers_matches_oracle(torch):
     cfg = model.EncoderConfig(n_layers=2)
     stats = run_steps(torch, cfg, 3, 13, tail=24)
     _report("encoder 2-layer", stats)
+    assert max(s[2] for s in stats) <= TOL
+
+
+@pytest.mark.parametrize("d,layers", [(512, 2), (1024, 1)])
+def test_encoder_other_attention_geometry_matches_oracle(torch, d, layers):
+    """Attention off the headline's geometry: 14-frame chunks with 28 left
+    frames (att_right 13, att_left 28), fed 28 encoder frames (224 mel) per
+    call, so every attention launch has 14 queries (the 16-query kernel);
+    d 512 with 8 heads gives head_dim 64, d 1024 head_dim 128.  Against the
+    oracle with the device's rounding, 3 streams, 6 calls and a tail."""
+    cfg = model.EncoderConfig(d_model=d, n_layers=layers, d_ff=2 * d, att_left=28, att_right=13, max_frames=32)
+    stats = run_steps(torch, cfg, 3, 6, tail=40, seed=23, per=224)
+    _report(f"encoder d {d}, chunk 14", stats)
     assert max(s[2] for s in stats) <= TOL
 
 
