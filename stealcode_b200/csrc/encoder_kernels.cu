@@ -523,7 +523,7 @@ __global__ void conv02_fused_kernel(const float *__restrict__ win, int t_mel, in
     // conv0 columns 2 f2 - 2, 2 f2 - 1, 2 f2 of the 3 rows; the first is the
     // previous output's last, so each column is computed once
     float vl[3] = {0.0f, 0.0f, 0.0f};
-    for (int f2 = 0; f2 < fb; f2++) {
+    auto column = [&](int f2) {  // any column, every tap checked
       float vm[3], vr[3];
 #pragma unroll
       for (int kt = 0; kt < 3; kt++) {
@@ -541,7 +541,57 @@ __global__ void conv02_fused_kernel(const float *__restrict__ win, int t_mel, in
       o[(size_t)f2 * C] = acc;
 #pragma unroll
       for (int kt = 0; kt < 3; kt++) vl[kt] = vr[kt];
+    };
+    // Interior columns [1, f2b): all 7 mel rows and all 3 conv0 rows exist,
+    // conv0 columns 2 f2 - 2 .. 2 f2 lie in [0, fa) and mel columns
+    // 4 f2 - 4 .. 4 f2 in [0, f_mel), so no tap is skipped: the same sums in
+    // the same order from a 7 x 5 window of mel values held in registers
+    // (mel column 4 f2 - 4 + i at window column i), slid by 4 columns a step.
+    const bool rows_ok = rv[0] && rv[1] && rv[2] && m0 >= 0 && m0 + 6 < t_mel;
+    const int f2b = rows_ok ? min(min((fa - 1) / 2, (f_mel - 1) / 4) + 1, fb) : 1;
+    column(0);
+    if (f2b > 1) {
+      float wv[7][5];
+#pragma unroll
+      for (int rr = 0; rr < 7; rr++)
+#pragma unroll
+        for (int i = 0; i < 5; i++) wv[rr][i] = mel[rr * f_mel + i];
+      for (int f2 = 1; f2 < f2b; f2++) {
+        float vm[3], vr[3];
+#pragma unroll
+        for (int kt = 0; kt < 3; kt++) {
+          float am = bias0, ar = bias0;
+#pragma unroll
+          for (int kt0 = 0; kt0 < 3; kt0++)
+#pragma unroll
+            for (int kf0 = 0; kf0 < 3; kf0++) {
+              am = __fadd_rn(am, __fmul_rn(wv[2 * kt + kt0][kf0], w0r[kt0 * 3 + kf0]));
+              ar = __fadd_rn(ar, __fmul_rn(wv[2 * kt + kt0][2 + kf0], w0r[kt0 * 3 + kf0]));
+            }
+          vm[kt] = fmaxf(am, 0.0f);
+          vr[kt] = fmaxf(ar, 0.0f);
+        }
+        float acc = bias2;
+#pragma unroll
+        for (int kt = 0; kt < 3; kt++) {
+          acc = __fadd_rn(acc, __fmul_rn(vl[kt], w2r[kt * 3 + 0]));
+          acc = __fadd_rn(acc, __fmul_rn(vm[kt], w2r[kt * 3 + 1]));
+          acc = __fadd_rn(acc, __fmul_rn(vr[kt], w2r[kt * 3 + 2]));
+        }
+        o[(size_t)f2 * C] = acc;
+#pragma unroll
+        for (int kt = 0; kt < 3; kt++) vl[kt] = vr[kt];
+        if (f2 + 1 < f2b) {  // the next window: mel columns 4 f2 .. 4 f2 + 4
+#pragma unroll
+          for (int rr = 0; rr < 7; rr++) {
+            wv[rr][0] = wv[rr][4];
+#pragma unroll
+            for (int i = 1; i < 5; i++) wv[rr][i] = mel[rr * f_mel + 4 * f2 + i];
+          }
+        }
+      }
     }
+    for (int f2 = f2b; f2 < fb; f2++) column(f2);
   }
 }
 
