@@ -135,6 +135,17 @@ template <int E, int L>
 __device__ __forceinline__ void ln_lane(float (&v)[E], int lead, const float *w, const float *b, float eps,
                                         int i0) {
   constexpr int d = E * L;
+  // up to 32 features a lane: the weight and bias loaded before the two
+  // ordered sums so that their latency overlaps them (more would spill)
+  constexpr bool kEarly = E <= 32;
+  float4 w4[kEarly ? E / 4 : 1], b4[kEarly ? E / 4 : 1];
+  if constexpr (kEarly) {
+#pragma unroll
+    for (int e4 = 0; e4 < E / 4; e4++) {
+      w4[e4] = __ldg(reinterpret_cast<const float4 *>(w + i0 + 4 * e4));
+      b4[e4] = __ldg(reinterpret_cast<const float4 *>(b + i0 + 4 * e4));
+    }
+  }
   float cs[E / 16];
 #pragma unroll
   for (int c = 0; c < E / 16; c++) {
@@ -157,9 +168,9 @@ __device__ __forceinline__ void ln_lane(float (&v)[E], int lead, const float *w,
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(var, (float)d), eps)));
 #pragma unroll
   for (int e4 = 0; e4 < E / 4; e4++) {
-    const float4 w4 = *reinterpret_cast<const float4 *>(w + i0 + 4 * e4);
-    const float4 b4 = *reinterpret_cast<const float4 *>(b + i0 + 4 * e4);
-    const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+    const float4 wq = kEarly ? w4[kEarly ? e4 : 0] : *reinterpret_cast<const float4 *>(w + i0 + 4 * e4);
+    const float4 bq = kEarly ? b4[kEarly ? e4 : 0] : *reinterpret_cast<const float4 *>(b + i0 + 4 * e4);
+    const float wv[4] = {wq.x, wq.y, wq.z, wq.w}, bv[4] = {bq.x, bq.y, bq.z, bq.w};
 #pragma unroll
     for (int q = 0; q < 4; q++) {
       float &x = v[4 * e4 + q];
