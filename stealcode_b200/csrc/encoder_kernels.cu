@@ -610,10 +610,11 @@ __global__ void conv02_fused_kernel(const float *__restrict__ win, int t_mel, in
 // spatial positions m of all streams (X, Y channels-last).  Each output's
 // k-sum is one fused multiply-add chain from k = 0 upwards, then the bias
 // is added -- the reference's rounding for its pointwise convs.  128 x 128
-// tile per CTA, 8 x 8 outputs per thread, k staged 8 at a time.
-constexpr int kPwBM = 128, kPwBN = 128, kPwBK = 8, kPwThreads = 256;
+// tile per CTA, 8 x 8 outputs per thread, k staged 16 at a time (k is a
+// multiple of 16: 16-byte loads of both operands).
+constexpr int kPwBM = 128, kPwBN = 128, kPwBK = 16, kPwThreads = 256;
 
-__global__ void __launch_bounds__(kPwThreads)
+__global__ void __launch_bounds__(kPwThreads, 2)
     pw_conv_relu_kernel(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
                         float *__restrict__ y, int64_t m_rows, int n, int k) {
   __shared__ __align__(16) float as[2][kPwBK][kPwBM];
@@ -621,16 +622,19 @@ __global__ void __launch_bounds__(kPwThreads)
   const int tid = threadIdx.x;
   const int64_t m0 = (int64_t)blockIdx.x * kPwBM;
   const int n0 = blockIdx.y * kPwBN;
-  // loader: thread -> (row tid / 2, k quad (tid % 2) * 4) of both tiles
-  const int lr = tid >> 1, lk = (tid & 1) * 4;
+  // loader: thread -> (row tid / 2, k quads (tid % 2) * 8 .. + 7) of both tiles
+  const int lr = tid >> 1, lk = (tid & 1) * 8;
   const int64_t am = m0 + lr;
   const int bn = n0 + lr;
-  auto load = [&](int kb, float (&ra)[4], float (&rb)[4]) {
+  auto load = [&](int kb, float (&ra)[8], float (&rb)[8]) {
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int kk = kb + lk + q;
-      ra[q] = (am < m_rows && kk < k) ? x[am * k + kk] : 0.0f;
-      rb[q] = (bn < n && kk < k) ? w[(int64_t)bn * k + kk] : 0.0f;
+    for (int h = 0; h < 2; h++) {
+      const float4 a4 = am < m_rows ? *reinterpret_cast<const float4 *>(x + am * k + kb + lk + 4 * h)
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      const float4 b4 = bn < n ? *reinterpret_cast<const float4 *>(w + (int64_t)bn * k + kb + lk + 4 * h)
+                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      ra[4 * h] = a4.x, ra[4 * h + 1] = a4.y, ra[4 * h + 2] = a4.z, ra[4 * h + 3] = a4.w;
+      rb[4 * h] = b4.x, rb[4 * h + 1] = b4.y, rb[4 * h + 2] = b4.z, rb[4 * h + 3] = b4.w;
     }
   };
   const int ty = tid / 16, tx = tid % 16;
@@ -639,12 +643,12 @@ __global__ void __launch_bounds__(kPwThreads)
   for (int i = 0; i < 8; i++)
 #pragma unroll
     for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
-  float ra[4], rb[4];
+  float ra[8], rb[8];
   load(0, ra, rb);
   int buf = 0;
   for (int kb = 0; kb < k; kb += kPwBK) {
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
+    for (int q = 0; q < 8; q++) {
       as[buf][lk + q][lr] = ra[q];
       bs[buf][lk + q][lr] = rb[q];
     }
@@ -879,6 +883,10 @@ int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y
   if (k % 16 || n % 8 || k > 4096 || sp_base < 0 || sp_base + rows_per_stream > spatial) {
     set_error("pw_conv: c_in %d (multiple of 16, <= 4096), c_out %d (multiple of 8), rows [%lld, %lld) of %lld",
               k, n, (long long)sp_base, (long long)(sp_base + rows_per_stream), (long long)spatial);
+    return kErrUnsupported;
+  }
+  if (((uintptr_t)x | (uintptr_t)w) & 15) {
+    set_error("pw_conv: input and weights must be 16-byte aligned");
     return kErrUnsupported;
   }
   dim3 grid((unsigned)ceil_div(m_rows, kPwBM), (unsigned)ceil_div(n, kPwBN));
