@@ -567,10 +567,7 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
     for (int kk = warp; kk < band; kk += NW) {
       if (kk >= kk_new) {
         const float *src = nw + (new_row0 + (kk - kk_new)) * p.ld_new + hoff + lane * 4;
-        if (lane_on) {
-          cp_async16(srow(kk) + lane * 4, src);
-          if (rz) *reinterpret_cast<float4 *>(rz + slot * p.d) = *reinterpret_cast<const float4 *>(src);
-        }
+        if (lane_on) cp_async16(srow(kk) + lane * 4, src);
       } else if (lane_on) {
         cp_async16(srow(kk) + lane * 4, rz + slot * p.d);
       }
@@ -578,8 +575,21 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
       slot = slot >= cap ? slot - cap : slot;
     }
   };
+  // The call's new rows, landed in shared memory, into the ring (slot =
+  // frame % cap): stores only, so no load latency in the staging loop.
+  auto ring_rows = [&](float *ring) {
+    if (!ring) return;
+    const int kk_new = (int)p.new_lo - LM_KLO, cap = (int)p.cap;
+    float *rz = ring + z * cap * (int64_t)p.d + hoff + lane * 4;
+    for (int kk = kk_new + warp; kk < band; kk += NW) {
+      int slot = LM_KLO % cap + kk;
+      slot = slot >= cap ? slot - cap : slot;
+      if (HD / 4 >= 32 || lane < HD / 4)
+        *reinterpret_cast<float4 *>(rz + slot * p.d) = *reinterpret_cast<const float4 *>(srow(kk) + lane * 4);
+    }
+  };
 
-  // ---- stage: K band, new K rows into the ring, q + u and q + v ----
+  // ---- stage: K band, q + u and q + v; then the new K rows into the ring ----
   stage_rows(p.k_ring, p.k_new);
   {
     const float uu = p.u[hoff + t], vv = p.v[hoff + t];
@@ -593,6 +603,10 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
   }
   cp_async_wait_all();
   __syncthreads();
+  if (p.k_ring) {  // before the score tiles reuse the K rows as scratch
+    ring_rows(p.k_ring);
+    __syncthreads();
+  }
 
   // ---- A: scores (score_dot order) ----
   {
@@ -708,6 +722,7 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
   }
   cp_async_wait_all();
   __syncthreads();
+  ring_rows(p.v_ring);
   // ---- D: P.V over the keys the call attends to, one thread per head dim ----
   {
     int kmin, kmax, kmin2, kmax2;
