@@ -212,7 +212,9 @@ template <int E, int L>
 __global__ void __launch_bounds__(128) ln_quant_kernel(const float *__restrict__ x, int64_t ldx,
                                                        const float *__restrict__ w, const float *__restrict__ b,
                                                        float eps, int64_t rows, QOut qo, float *__restrict__ out,
-                                                       int64_t ldo) {
+                                                       int64_t ldo, const float *__restrict__ w0,
+                                                       const float *__restrict__ b0, float *__restrict__ out0,
+                                                       int64_t ld0) {
   const int lane = threadIdx.x & 31, sub = lane / L, lead = sub * L, l = lane % L;
   const int64_t row = ((int64_t)blockIdx.x * 4 + (threadIdx.x >> 5)) * (32 / L) + sub;
   const bool live = row < rows;
@@ -243,6 +245,14 @@ __global__ void __launch_bounds__(128) ln_quant_kernel(const float *__restrict__
       const float4 t = *reinterpret_cast<const float4 *>(xr + 4 * e4);
       v[4 * e4] = t.x, v[4 * e4 + 1] = t.y, v[4 * e4 + 2] = t.z, v[4 * e4 + 3] = t.w;
     }
+  }
+  if (w0) {  // a first LayerNorm (the previous block's output LN), written to out0
+    ln_lane<E, L>(v, lead, w0, b0, eps, i0);
+    if (live)
+#pragma unroll
+      for (int e4 = 0; e4 < E / 4; e4++)
+        *reinterpret_cast<float4 *>(out0 + row * ld0 + i0 + 4 * e4) =
+            make_float4(v[4 * e4], v[4 * e4 + 1], v[4 * e4 + 2], v[4 * e4 + 3]);
   }
   ln_lane<E, L>(v, lead, w, b, eps, i0);  // all lanes take part in the shuffles
   if (!live) return;
@@ -942,26 +952,41 @@ int launch_prompt_select(float *x, const float *y, int64_t rows, int c, int d, c
 
 template <int E, int L>
 static int launch_ln_quant_t(const float *x, int64_t ldx, const float *w, const float *b, float eps, int64_t rows,
-                             const QOut &qo, float *out, int64_t ldo, cudaStream_t st) {
+                             const QOut &qo, float *out, int64_t ldo, const float *w0, const float *b0, float *out0,
+                             int64_t ld0, cudaStream_t st) {
   const int64_t warps = ceil_div(rows, 32 / L);
-  ln_quant_kernel<E, L><<<(unsigned)ceil_div(warps, 4), 128, 0, st>>>(x, ldx, w, b, eps, rows, qo, out, ldo);
+  ln_quant_kernel<E, L><<<(unsigned)ceil_div(warps, 4), 128, 0, st>>>(x, ldx, w, b, eps, rows, qo, out, ldo, w0, b0,
+                                                                       out0, ld0);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
 }
 
-int launch_ln_quant(const float *x, int64_t ldx, const float *w, const float *b, float eps, int d, int64_t rows,
-                    const QOut &qo, float *out, int64_t ldo, cudaStream_t st) {
+// LayerNorm (w0, b0) of x into out0 (ld0), then LayerNorm (w, b) of that
+// into the codes qo (and out when given): two consecutive per-row LayerNorms
+// in one pass over the rows.  w0 == nullptr: the second one only.
+int launch_ln2_quant(const float *x, int64_t ldx, const float *w0, const float *b0, float *out0, int64_t ld0,
+                     const float *w, const float *b, float eps, int d, int64_t rows, const QOut &qo, float *out,
+                     int64_t ldo, cudaStream_t st) {
+  if (w0 && (!out0 || (((uintptr_t)out0 | ((uintptr_t)ld0 * 4)) & 15))) {
+    set_error("layernorm+quantise: the first LayerNorm's output must be 16-byte aligned");
+    return kErrInvalid;
+  }
   switch (d) {
-    case 256: return launch_ln_quant_t<32, 8>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
-    case 512: return launch_ln_quant_t<32, 16>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
-    case 1024: return launch_ln_quant_t<32, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
-    case 2048: return launch_ln_quant_t<64, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
-    case 4096: return launch_ln_quant_t<128, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, st);
+    case 256: return launch_ln_quant_t<32, 8>(x, ldx, w, b, eps, rows, qo, out, ldo, w0, b0, out0, ld0, st);
+    case 512: return launch_ln_quant_t<32, 16>(x, ldx, w, b, eps, rows, qo, out, ldo, w0, b0, out0, ld0, st);
+    case 1024: return launch_ln_quant_t<32, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, w0, b0, out0, ld0, st);
+    case 2048: return launch_ln_quant_t<64, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, w0, b0, out0, ld0, st);
+    case 4096: return launch_ln_quant_t<128, 32>(x, ldx, w, b, eps, rows, qo, out, ldo, w0, b0, out0, ld0, st);
     default:
       set_error("layernorm+quantise: d=%d must be 256, 512, 1024, 2048 or 4096", d);
       return kErrUnsupported;
   }
+}
+
+int launch_ln_quant(const float *x, int64_t ldx, const float *w, const float *b, float eps, int d, int64_t rows,
+                    const QOut &qo, float *out, int64_t ldo, cudaStream_t st) {
+  return launch_ln2_quant(x, ldx, nullptr, nullptr, nullptr, 0, w, b, eps, d, rows, qo, out, ldo, st);
 }
 
 template <int E, int L>

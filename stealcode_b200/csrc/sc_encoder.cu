@@ -53,6 +53,9 @@ int launch_pw_conv_relu(const float *x, const float *w, const float *b, float *y
                         int rows_per_stream, int64_t sp_base, int64_t spatial, int n, int k, cudaStream_t st);
 int launch_flatten(const float *x, int64_t n_streams, int t, int f, int C, int start_rel, int c, float *out,
                    cudaStream_t st, QOut qo);
+int launch_ln2_quant(const float *x, int64_t ldx, const float *w0, const float *b0, float *out0, int64_t ld0,
+                     const float *w, const float *b, float eps, int d, int64_t rows, const QOut &qo, float *out,
+                     int64_t ldo, cudaStream_t st);
 int launch_ln_quant(const float *x, int64_t ldx, const float *w, const float *b, float eps, int d, int64_t rows,
                     const QOut &qo, float *out, int64_t ldo, cudaStream_t st);
 int launch_dwconv_ln_silu_quant(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s,
@@ -573,7 +576,8 @@ static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *
     const bool dumping = (int)li == e->dump_layer && e->dump;
     const QOut qa = qbuf(0, d), qb_ff = qbuf(1, dff), qb_d = qbuf(1, d);
     // macaron FF1: y = x + 0.5 * FF(LN(x)); the SiLU output goes to ff1_2 as codes
-    TRY(launch_ln_quant(x, d, ly.ln_ff1_w, ly.ln_ff1_b, eps, (int)d, M, qa, nullptr, d, st));
+    if (li == 0)  // later layers get these codes from the previous block's output LayerNorm
+      TRY(launch_ln_quant(x, d, ly.ln_ff1_w, ly.ln_ff1_b, eps, (int)d, M, qa, nullptr, d, st));
     TRY(gemm_q(ly.ff1_1, qa, nullptr, dff, silu, qb_ff));
     TRY(gemm_q(ly.ff1_2, qb_ff, y, d, Epilogue{kEpiResidual, x, 0.5f}, QOut{}));
     TRY(dump(0, y, d));
@@ -639,7 +643,13 @@ static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *
     TRY(launch_ln_quant(y, d, ly.ln_ff2_w, ly.ln_ff2_b, eps, (int)d, M, qa, nullptr, d, st));
     TRY(gemm_q(ly.ff2_1, qa, nullptr, dff, silu, qb_ff));
     TRY(gemm_q(ly.ff2_2, qb_ff, y, d, Epilogue{kEpiResidual, y, 0.5f}, QOut{}));
-    TRY(launch_ln_rows(y, d, ly.ln_out_w, ly.ln_out_b, eps, x, d, M, (int)d, st));
+    if (li + 1 < e->layers.size()) {  // the block's output LN and the next block's FF1 LN in one pass
+      const Layer &nx = e->layers[li + 1];
+      TRY(launch_ln2_quant(y, d, ly.ln_out_w, ly.ln_out_b, x, d, nx.ln_ff1_w, nx.ln_ff1_b, eps, (int)d, M, qa,
+                           nullptr, d, st));
+    } else {
+      TRY(launch_ln_rows(y, d, ly.ln_out_w, ly.ln_out_b, eps, x, d, M, (int)d, st));
+    }
     TRY(dump(7, x, d));
   }
   // ---- prompt MLP on the new frames (streaming.rs:320-342) ----
