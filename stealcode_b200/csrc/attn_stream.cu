@@ -272,11 +272,10 @@ __host__ __device__ constexpr size_t attn_stage_smem_floats(int band, int np) {
          (size_t)(HD / 16) * 4 * kStageKT * kRedStride;
 }
 
-// LM: rows arrive lane-major (the encoder's layout); pos rows are then read
-// straight from global memory (they are shared by every stream, so L1/L2
-// keep them) instead of being staged, which leaves room for 3 CTAs per SM.
-template <int HD, int CQ, bool LM>
-__global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnParams p) {
+// Rows in natural order (the sc_attn_stream* API); the encoder's lane-major
+// rows take attn_lm_kernel below.
+template <int HD, int CQ>
+__global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
   constexpr int NW = HD / 32;
   constexpr int NQG = CQ / 4;        // query groups of 4
   constexpr int KT = kStageKT;
@@ -285,8 +284,8 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
   extern __shared__ __align__(16) float sm[];
   const int band = (int)(p.k_hi - p.k_lo), np = p.np, bp = stage_band_pad(band);
   float *s_k = sm;                   // [band][HD] K lane-major, later V natural
-  float *s_p = s_k + band * HD;      // [np][HD]   pos rows lane-major (natural inputs only)
-  float *s_qu = s_p + (LM ? 0 : np) * HD;  // [CQ][HD]   q + u lane-major
+  float *s_p = s_k + band * HD;      // [np][HD]   pos rows lane-major
+  float *s_qu = s_p + np * HD;       // [CQ][HD]   q + u lane-major
   float *s_qv = s_qu + CQ * HD;      // [CQ][HD]   q + v lane-major
   float *s_w = s_qv + CQ * HD;       // [CQ][bp]   scores, then weights
   float *s_red = s_w + CQ * bp;      // [2*NW][4*KT][kRedStride]
@@ -311,16 +310,9 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
   const int kk_s = (int)(p.s - p.k_lo);
 
   // ---- stage K, pos rows (async copies, all in flight at once), q; the
-  // new K rows also go to the ring.  Rows already in lane-major order are
-  // copied 16 bytes at a time; natural rows element by element into their
-  // lane-major slots. ----
-  if (LM) {
-    constexpr int V4 = HD / 4;  // 16-byte pieces per row
-    for (int x = t; x < band * V4; x += HD) {
-      const int kk = x / V4, e4 = x % V4;
-      cp_async16(s_k + kk * HD + e4 * 4, key_row(p.k_ring, p.k_new, kk) + e4 * 4);
-    }
-  } else {
+  // new K rows also go to the ring.  Natural rows are copied element by
+  // element into their lane-major slots. ----
+  {
     const int dt = lane_major(t);
     for (int kk = 0; kk < band; kk++) cp_async4(s_k + kk * HD + dt, key_row(p.k_ring, p.k_new, kk) + t);
     const float *prow = p.pos_p + p.pr_lo * (int64_t)p.d + hoff + t;
@@ -334,7 +326,7 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
         *reinterpret_cast<float4 *>(dst + e4 * 4) = *reinterpret_cast<const float4 *>(src + e4 * 4);
     }
   {
-    const int dt = LM ? t : lane_major(t);
+    const int dt = lane_major(t);
     for (int j = 0; j < CQ; j++) {
       const float qd = j < c ? p.q[(z * zq + p.r0 + j) * p.ldq + hoff + t] : 0.0f;
       s_qu[j * HD + dt] = j < c ? __fadd_rn(qd, p.u[hoff + t]) : 0.0f;
@@ -372,13 +364,8 @@ __global__ void __launch_bounds__(HD, LM ? 3 : 2) attn_stage_kernel(const AttnPa
           float4 kv[KT], pv[NPV], qu[4], qv[4];
 #pragma unroll
           for (int b = 0; b < KT; b++) kv[b] = *reinterpret_cast<const float4 *>(s_k + koff[b] + hh * 64);
-          const float *pbase = LM ? p.pos_p + p.pr_lo * (int64_t)p.d + hoff : s_p;
-          const int pstride = LM ? p.d : HD;
 #pragma unroll
-          for (int m = 0; m < NPV; m++)
-            pv[m] = LM ? __ldg(reinterpret_cast<const float4 *>(pbase + (poff[m] / HD) * pstride + poff[m] % HD +
-                                                                hh * 64))
-                       : *reinterpret_cast<const float4 *>(s_p + poff[m] + hh * 64);
+          for (int m = 0; m < NPV; m++) pv[m] = *reinterpret_cast<const float4 *>(s_p + poff[m] + hh * 64);
 #pragma unroll
           for (int j = 0; j < 4; j++) {
             qu[j] = *reinterpret_cast<const float4 *>(s_qu + qoff + j * HD + hh * 64);
@@ -826,14 +813,14 @@ static bool stage_fits(const AttnParams &p) {
   auto al = [](const void *q) { return ((uintptr_t)q & 15) == 0; };
   const bool aligned = al(p.q) && al(p.k_new) && al(p.v_new) && al(p.pos_p) && p.d % 4 == 0 && p.ldq % 4 == 0 &&
                        p.ld_new % 4 == 0 && (!p.k_ring || (al(p.k_ring) && al(p.v_ring)));
-  return aligned && attn_stage_smem_floats<HD, CQ>(band, p.lane_major ? 0 : p.np) * sizeof(float) <= 227 * 1024;
+  return aligned && (p.lane_major || attn_stage_smem_floats<HD, CQ>(band, p.np) * sizeof(float) <= 227 * 1024);
 }
 
-template <int HD, int CQ, bool LM>
-static int launch_stage_lm(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
+template <int HD, int CQ>
+static int launch_stage(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
   const int band = (int)(p.k_hi - p.k_lo);
-  const size_t smem = attn_stage_smem_floats<HD, CQ>(band, LM ? 0 : p.np) * sizeof(float);
-  auto kern = attn_stage_kernel<HD, CQ, LM>;
+  const size_t smem = attn_stage_smem_floats<HD, CQ>(band, p.np) * sizeof(float);
+  auto kern = attn_stage_kernel<HD, CQ>;
   static std::atomic<size_t> smem_limit[64];
   const int rc = raise_smem_limit((const void *)kern, smem, smem_limit);
   if (rc) return rc;
@@ -864,7 +851,7 @@ static int launch_lane_major(const AttnParams &p, int64_t n_streams, cudaStream_
 template <int HD, int CQ>
 static int launch_attn_t(const AttnParams &p, int64_t n_streams, cudaStream_t st) {
   if (p.lane_major && stage_fits<HD, CQ>(p)) return launch_lane_major<HD, CQ>(p, n_streams, st);
-  if (stage_fits<HD, CQ>(p)) return launch_stage_lm<HD, CQ, false>(p, n_streams, st);
+  if (!p.lane_major && stage_fits<HD, CQ>(p)) return launch_stage<HD, CQ>(p, n_streams, st);
   if (p.lane_major || p.qout.xq || p.zrows) {
     set_error("attn_stream: lane-major rows / quantised output / row sub-ranges need the staged kernel (band %lld too large or "
               "rows unaligned)",
