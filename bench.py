@@ -106,6 +106,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-decoder", action="store_true", help="skip the transcriber (encoder + decoder) block")
     ap.add_argument("--no-prefill", action="store_true", help="skip the 750-frame prefill block")
+    ap.add_argument("--no-graphs", action="store_true",
+                    help="launch every kernel of a step separately instead of replaying the step's CUDA graph")
     ap.add_argument("--box-streams", type=int, default=8192,
                     help="global streams of the box-scale block (sharded over the GPUs); 0 skips it")
     ap.add_argument("--box-steps", type=int, default=3)
@@ -648,6 +650,8 @@ def run_ours(args, rank, world, local_rank):
     m = encoder_model()
     cfg = m.config
     enc = StreamEncoder(m, Z)
+    if args.no_graphs:
+        enc.set_graphs(False)
     gen = torch.Generator(device=dev)
     gen.manual_seed(MODEL_SEED + 7 + rank)
     pool = [torch.randn((Z, MEL_PER_STEP, cfg.feat_in), device=dev, generator=gen) for _ in range(MEL_POOL)]
@@ -672,6 +676,10 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
     launches_timed = launches * args.steps // (args.steps + args.warmup)
     value = world * Z * AUDIO_S_PER_STEP / (ms_step * 1e-3)
+    g_on, g_cap, g_launch = enc.graph_stats()
+    graphs = {"on": g_on, "captured": g_cap, "graph_launches": g_launch,
+              "note": "steady steps replay a CUDA graph of the whole step (both sub-batches) after a one-thread "
+                      "store of the frame shift; the warm-up captures them"}
 
     # e2e through the C ABI with host buffers: mel in, output frames out
     rows = Z * 7
@@ -752,6 +760,7 @@ def run_ours(args, rank, world, local_rank):
                            "streams_per_gpu": Z, "global_streams": Z * world, "chunk_ms": 560,
                            "frames_per_step": 7, "left_context_frames": 70, "prime_steps": PRIME_STEPS,
                            "frames_per_gemm": step_halves(Z), "sub_batches": len(step_halves(Z)),
+                           "step_graphs": graphs,
                            "parallelism": f"streams sharded, {world} independent ranks",
                            "l2": "inputs larger than L2: each step streams the 24 layers' f16 weight tiles, 1.1 GB (587 MB as Q8_0), L2 126 MB"},
                 "realtime_streams_per_gpu": value / world,

@@ -368,6 +368,23 @@ int sc_stream_encoder_dump(const sc_stream_encoder *e, int32_t stage,
  * one batch.  No counterpart in the reference, which encodes one stream at
  * a time. */
 int sc_stream_encoder_set_concurrency(sc_stream_encoder *e, int32_t n_batches);
+/* Step graphs (on by default), the counterpart of the reference GPU
+ * backend's one submission per step (gpu/batch.rs:50,163,
+ * gpu/streaming.rs:259-298).  A step whose geometry (streams, frames, mel
+ * window, attention bands relative to the step, entry point) repeats the
+ * previous step's is captured into a CUDA graph; later steps with that
+ * geometry replay it as one launch after a one-thread store of their frame
+ * shift, with its copy nodes pointed at the call's own mel and output
+ * buffers.  Steady streaming steps all share one geometry (two graphs: the
+ * mel history alternates between two buffers).  Host buffers of
+ * encode_new_host must be page-locked for a step to use a graph; stage dumps
+ * turn graphs off.  Same bits as separate launches.  enable 0 drops the
+ * graphs (after a device synchronise) and launches every kernel separately. */
+int sc_stream_encoder_set_graphs(sc_stream_encoder *e, int32_t enable);
+/* Step graphs captured and graph launches so far; returns 1 while graphs
+ * are on, 0 when off (set_graphs(0), or a capture that failed, after which
+ * the encoder launches separately), <0 on error. */
+int sc_stream_encoder_graph_stats(const sc_stream_encoder *e, int64_t *captures, int64_t *launches);
 int sc_stream_encoder_destroy(sc_stream_encoder *e);
 
 /* ---- RNN-T greedy decoder --------------------------------------------------

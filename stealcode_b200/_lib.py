@@ -81,6 +81,8 @@ SIGNATURES = {
     "sc_stream_encoder_n_prompts": (c_int64, [_P]),
     "sc_stream_encoder_set_dump": (c_int, [_P, c_int32]),
     "sc_stream_encoder_set_concurrency": (c_int, [_P, c_int32]),
+    "sc_stream_encoder_set_graphs": (c_int, [_P, c_int32]),
+    "sc_stream_encoder_graph_stats": (c_int, [_P, POINTER(c_int64), POINTER(c_int64)]),
     "sc_stream_encoder_encode_new_host": (c_int, [_P, _P, c_int64, c_int64, c_int32, _P, _P, _P]),
     "sc_stream_encoder_dump": (c_int, [_P, c_int32, _P, POINTER(c_int64)]),
     "sc_stream_encoder_destroy": (c_int, [_P]),

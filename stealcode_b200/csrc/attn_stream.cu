@@ -39,6 +39,13 @@ __device__ __forceinline__ void band_of(int64_t qq, int64_t chunk, int64_t left_
   kmax = hi < k_hi ? hi : k_hi;
 }
 
+// Ring slot of band key 0: frame k_lo plus the step graph's frame shift.
+__device__ __forceinline__ int band_slot0(const AttnParams &p) {
+  if (p.cap <= 0) return 0;
+  const int64_t sh = p.frame_shift ? *p.frame_shift : 0;
+  return (int)((p.k_lo + sh) % p.cap);
+}
+
 #ifndef SC_ATTN_PREFETCH
 #define SC_ATTN_PREFETCH 1
 #endif
@@ -79,7 +86,7 @@ __global__ void __launch_bounds__(HD) attn_stream_kernel(const AttnParams p) {
   // kk >= kk_new, else from ring slot (k_lo + kk) % cap (band <= cap, so one
   // wrap at most).  Int32 index math, no 64-bit modulo in the loops.
   const int kk_new = (int)(p.new_lo - p.k_lo);
-  const int slot0 = p.cap > 0 ? (int)(p.k_lo % p.cap) : 0;
+  const int slot0 = band_slot0(p);
   const int cap = (int)p.cap;
   auto ring_row = [&](float *ring, int kk) -> float * {
     int slot = slot0 + kk;
@@ -296,7 +303,7 @@ __global__ void __launch_bounds__(HD, 2) attn_stage_kernel(const AttnParams p) {
   const int c = p.c;
   const int64_t zq = p.zrows > 0 ? p.zrows : c, zn = p.zrows > 0 ? p.zrows : p.rows_new;
   const int kk_new = (int)(p.new_lo - p.k_lo);
-  const int slot0 = p.cap > 0 ? (int)(p.k_lo % p.cap) : 0;
+  const int slot0 = band_slot0(p);
   const int cap = (int)p.cap;
   auto ring_row = [&](float *ring, int kk) -> float * {
     int slot = slot0 + kk;
@@ -545,7 +552,7 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
   // written to the ring (slot = frame % cap), older frames from the ring.
   auto stage_rows = [&](float *ring, const float *nw) {
     const int kk_new = (int)p.new_lo - LM_KLO, cap = (int)p.cap;
-    const int slot0 = cap > 0 ? LM_KLO % cap : 0;
+    const int slot0 = band_slot0(p);
     const int64_t new_row0 = z * zn + p.r0;  // projection row of frame new_lo
     const bool lane_on = HD / 4 >= 32 || lane < HD / 4;
     float *rz = ring ? ring + z * cap * (int64_t)p.d + hoff + lane * 4 : nullptr;
@@ -568,8 +575,9 @@ __global__ void __launch_bounds__(HD, 4) attn_lm_kernel(const AttnParams p) {
     if (!ring) return;
     const int kk_new = (int)p.new_lo - LM_KLO, cap = (int)p.cap;
     float *rz = ring + z * cap * (int64_t)p.d + hoff + lane * 4;
+    const int slot0 = band_slot0(p);
     for (int kk = kk_new + warp; kk < band; kk += NW) {
-      int slot = LM_KLO % cap + kk;
+      int slot = slot0 + kk;
       slot = slot >= cap ? slot - cap : slot;
       if (HD / 4 >= 32 || lane < HD / 4)
         *reinterpret_cast<float4 *>(rz + slot * p.d) = *reinterpret_cast<const float4 *>(srow(kk) + lane * 4);

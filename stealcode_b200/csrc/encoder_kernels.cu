@@ -267,11 +267,13 @@ __global__ void __launch_bounds__(128) ln_quant_kernel(const float *__restrict__
 // Causal depthwise conv over the GLU ring (taps in order, fused multiply-
 // adds as the reference's S-lane loop), the conv module's LayerNorm and
 // SiLU, then codes for pw2.  wt is the depthwise weight transposed to
-// [kh][d].  rows = n_streams * c, frame of row r: s + r % c.
+// [kh][d].  rows = n_streams * c, frame of row r: s + r % c.  Taps before
+// frame 0 are skipped; a tap's ring slot is (frame + shift) % cap (shift:
+// the step graph's device frame shift, nullptr for none).
 template <int E, int L, int KH>
 __global__ void __launch_bounds__(128)
     dwconv_ln_silu_quant_kernel(const float *__restrict__ ring, int cap, int c, int kh_rt, int64_t s,
-                                const float *__restrict__ wt, const float *__restrict__ lnw,
+                                const int64_t *shift, const float *__restrict__ wt, const float *__restrict__ lnw,
                                 const float *__restrict__ lnb, float eps, int64_t rows, QOut qo,
                                 float *__restrict__ out) {
   constexpr int d = E * L;
@@ -281,6 +283,7 @@ __global__ void __launch_bounds__(128)
   const bool live = row < rows;
   const int64_t rr = live ? row : 0;
   const int64_t z = rr / c, fr = s + rr % c;
+  const int64_t sh = shift ? *shift : 0;
   const int i0 = l * E;
   float v[E];
   if constexpr (E == 32 && L == 32) {
@@ -301,7 +304,7 @@ __global__ void __launch_bounds__(128)
       if (KH == 0 && t >= kh) break;
       const int64_t ti = fr - (kh - 1) + t;
       if (ti < 0) continue;
-      const float *rw = ring + (z * cap + ti % cap) * (int64_t)d + 4 * lane;
+      const float *rw = ring + (z * cap + (ti + sh) % cap) * (int64_t)d + 4 * lane;
       const float *ww = wt + (int64_t)t * d + 4 * lane;
 #pragma unroll
       for (int k = 0; k < 8; k++) {
@@ -332,7 +335,7 @@ __global__ void __launch_bounds__(128)
       if (KH == 0 && t >= kh) break;
       const int64_t ti = fr - (kh - 1) + t;
       if (ti < 0) continue;
-      const float *rw = ring + (z * cap + ti % cap) * (int64_t)d + i0;
+      const float *rw = ring + (z * cap + (ti + sh) % cap) * (int64_t)d + i0;
       const float *ww = wt + (int64_t)t * d + i0;
 #pragma unroll
       for (int e4 = 0; e4 < E / 4; e4++) {
@@ -358,11 +361,13 @@ __global__ void __launch_bounds__(128)
 }
 
 // GLU of the new frames (h2 = [M][2d] time-major, gate first, value second)
-// stored into ring slot (s + j) % cap of stream z.
+// stored into ring slot (s + shift + j) % cap of stream z (shift: the step
+// graph's device frame shift, nullptr for none).
 __global__ void glu_ring_kernel(const float *__restrict__ h2, int c, int d, float *__restrict__ ring, int cap,
-                                int64_t s) {
+                                int64_t s, const int64_t *shift) {
   const int64_t row = blockIdx.x;  // z * c + j
   const int64_t z = row / c, j = row % c;
+  if (shift) s += *shift;
   float *dst = ring + (z * cap + (s + j) % cap) * (int64_t)d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
     const float gate = h2[row * 2 * d + i], val = h2[row * 2 * d + d + i];
@@ -799,11 +804,12 @@ __global__ void prompt_select_kernel(float *__restrict__ x, const float *__restr
   for (int i = threadIdx.x; i < d; i += blockDim.x) x[row * d + i] = y[row * d + i];
 }
 
-// Output frames into the per-stream output ring (slot = frame % cap).
+// Output frames into the per-stream output ring (slot = (frame + shift) % cap).
 __global__ void out_ring_kernel(const float *__restrict__ x, int c, int d, float *__restrict__ ring, int cap,
-                                int64_t s) {
+                                int64_t s, const int64_t *shift) {
   const int64_t row = blockIdx.x;
   const int64_t z = row / c, j = row % c;
+  if (shift) s += *shift;
   float *dst = ring + (z * cap + (s + j) % cap) * (int64_t)d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = x[row * d + i];
 }
@@ -821,8 +827,9 @@ int launch_ln_rows(const float *x, int64_t ldx, const float *w, const float *b, 
   return kOk;
 }
 
-int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st) {
-  glu_ring_kernel<<<(unsigned)rows, 256, 0, st>>>(h2, c, d, ring, cap, s);
+int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, int cap, int64_t s,
+                    const int64_t *shift, cudaStream_t st) {
+  glu_ring_kernel<<<(unsigned)rows, 256, 0, st>>>(h2, c, d, ring, cap, s, shift);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;
@@ -990,14 +997,17 @@ int launch_ln_quant(const float *x, int64_t ldx, const float *w, const float *b,
 }
 
 template <int E, int L>
-static int launch_dwq_t(const float *ring, int cap, int64_t rows, int c, int kh, int64_t s, const float *wt,
-                        const float *lnw, const float *lnb, float eps, const QOut &qo, float *out, cudaStream_t st) {
+static int launch_dwq_t(const float *ring, int cap, int64_t rows, int c, int kh, int64_t s, const int64_t *shift,
+                        const float *wt, const float *lnw, const float *lnb, float eps, const QOut &qo, float *out,
+                        cudaStream_t st) {
   const int64_t warps = ceil_div(rows, 32 / L);
   const unsigned grid = (unsigned)ceil_div(warps, 4);
   if (kh == 9)
-    dwconv_ln_silu_quant_kernel<E, L, 9><<<grid, 128, 0, st>>>(ring, cap, c, kh, s, wt, lnw, lnb, eps, rows, qo, out);
+    dwconv_ln_silu_quant_kernel<E, L, 9>
+        <<<grid, 128, 0, st>>>(ring, cap, c, kh, s, shift, wt, lnw, lnb, eps, rows, qo, out);
   else if (kh <= 64)
-    dwconv_ln_silu_quant_kernel<E, L, 0><<<grid, 128, 0, st>>>(ring, cap, c, kh, s, wt, lnw, lnb, eps, rows, qo, out);
+    dwconv_ln_silu_quant_kernel<E, L, 0>
+        <<<grid, 128, 0, st>>>(ring, cap, c, kh, s, shift, wt, lnw, lnb, eps, rows, qo, out);
   else {
     set_error("conv module: kernel %d > 64 unsupported", kh);
     return kErrUnsupported;
@@ -1008,22 +1018,34 @@ static int launch_dwq_t(const float *ring, int cap, int64_t rows, int c, int kh,
 }
 
 int launch_dwconv_ln_silu_quant(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s,
-                                const float *wt, const float *lnw, const float *lnb, float eps, const QOut &qo,
-                                float *out, cudaStream_t st) {
+                                const int64_t *shift, const float *wt, const float *lnw, const float *lnb, float eps,
+                                const QOut &qo, float *out, cudaStream_t st) {
   switch (d) {
-    case 256: return launch_dwq_t<32, 8>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
-    case 512: return launch_dwq_t<32, 16>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
-    case 1024: return launch_dwq_t<32, 32>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
-    case 2048: return launch_dwq_t<64, 32>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
-    case 4096: return launch_dwq_t<128, 32>(ring, cap, rows, c, kh, s, wt, lnw, lnb, eps, qo, out, st);
+    case 256: return launch_dwq_t<32, 8>(ring, cap, rows, c, kh, s, shift, wt, lnw, lnb, eps, qo, out, st);
+    case 512: return launch_dwq_t<32, 16>(ring, cap, rows, c, kh, s, shift, wt, lnw, lnb, eps, qo, out, st);
+    case 1024: return launch_dwq_t<32, 32>(ring, cap, rows, c, kh, s, shift, wt, lnw, lnb, eps, qo, out, st);
+    case 2048: return launch_dwq_t<64, 32>(ring, cap, rows, c, kh, s, shift, wt, lnw, lnb, eps, qo, out, st);
+    case 4096: return launch_dwq_t<128, 32>(ring, cap, rows, c, kh, s, shift, wt, lnw, lnb, eps, qo, out, st);
     default:
       set_error("conv module: d=%d must be 256, 512, 1024, 2048 or 4096", d);
       return kErrUnsupported;
   }
 }
 
-int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st) {
-  out_ring_kernel<<<(unsigned)rows, 256, 0, st>>>(x, c, d, ring, cap, s);
+int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s,
+                    const int64_t *shift, cudaStream_t st) {
+  out_ring_kernel<<<(unsigned)rows, 256, 0, st>>>(x, c, d, ring, cap, s, shift);
+  note_launch();
+  SC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+__global__ void store_i64_kernel(int64_t *dst, int64_t v) { *dst = v; }
+
+// One 64-bit value into device memory, in stream order (the step graph's
+// frame shift, written before each replay).
+int launch_store_i64(int64_t *dst, int64_t v, cudaStream_t st) {
+  store_i64_kernel<<<1, 1, 0, st>>>(dst, v);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;

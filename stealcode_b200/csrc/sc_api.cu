@@ -44,6 +44,7 @@ static DeviceState g_dev[64];
 
 static std::atomic<long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void note_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 // Allocation cap for failure-path tests (sc_debug_set_device_alloc_cap):
 // -1 = none; else the bytes the library may still allocate.

@@ -55,6 +55,9 @@ void set_error(const char *fmt, ...);
 int cuda_fail(cudaError_t e, const char *what);
 // Counts one kernel launch issued by this library (sc_launch_count).
 void note_launch();
+// Adds n (may be negative) to the launch count: a step graph's launches are
+// counted when it replays, not when it is captured.
+void note_launches(long long n);
 // cudaMalloc for every device allocation of this library; fails with
 // cudaErrorMemoryAllocation, without allocating, once the bytes allocated
 // since sc_debug_set_device_alloc_cap would exceed that cap.

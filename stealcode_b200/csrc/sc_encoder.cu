@@ -23,6 +23,7 @@
 #include <new>
 #include <string>
 #include <algorithm>
+#include <functional>
 #include <vector>
 
 #include "sc_kernels.cuh"
@@ -34,7 +35,10 @@ int repack_q8_device(const uint8_t *raw_dev, int64_t rows, int64_t k, int64_t bl
                      Q8Weights *w, cudaStream_t st);
 int launch_ln_rows(const float *x, int64_t ldx, const float *w, const float *b, float eps, float *out, int64_t ldo,
                    int64_t rows, int d, cudaStream_t st);
-int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st);
+// shift (in the ring launchers below): device frame shift of a replayed step
+// graph, added to frame numbers before they become ring slots; nullptr none.
+int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, int cap, int64_t s,
+                    const int64_t *shift, cudaStream_t st);
 int launch_dwconv_ln_silu(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s, const float *w,
                           const float *lnw, const float *lnb, float eps, float *out, cudaStream_t st);
 int launch_mel_window(const float *hist, int hist_cap, int hist_frames, const float *mel_new, int n_new,
@@ -59,9 +63,11 @@ int launch_ln2_quant(const float *x, int64_t ldx, const float *w0, const float *
 int launch_ln_quant(const float *x, int64_t ldx, const float *w, const float *b, float eps, int d, int64_t rows,
                     const QOut &qo, float *out, int64_t ldo, cudaStream_t st);
 int launch_dwconv_ln_silu_quant(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s,
-                                const float *wt, const float *lnw, const float *lnb, float eps, const QOut &qo,
-                                float *out, cudaStream_t st);
-int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s, cudaStream_t st);
+                                const int64_t *shift, const float *wt, const float *lnw, const float *lnb, float eps,
+                                const QOut &qo, float *out, cudaStream_t st);
+int launch_out_ring(const float *x, int64_t rows, int c, int d, float *ring, int cap, int64_t s,
+                    const int64_t *shift, cudaStream_t st);
+int launch_store_i64(int64_t *dst, int64_t v, cudaStream_t st);
 int launch_prompt_cat_quant(const float *x, int64_t rows, int c, int d, int n_prompts, const int32_t *pids,
                             const QOut &qo, cudaStream_t st);
 int launch_prompt_select(float *x, const float *y, int64_t rows, int c, int d, const int32_t *pids,
@@ -96,6 +102,26 @@ struct Conv {
 }  // namespace sc
 
 using namespace sc;
+
+// A copy node of a step graph: the mel of streams [za, za + nz) into the
+// staging buffer (dir 0) or their output frames to the caller (dir 1).
+// Replays point it at the call's own buffers.
+struct StepCopy {
+  cudaGraphNode_t node;
+  int64_t za, nz;
+  int dir;
+};
+
+// One captured encode_new step (both sub-batches, fork and join included).
+struct StepGraph {
+  std::vector<int64_t> key;  // step geometry + mel-history buffer parity
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int64_t s = 0;             // first frame of the captured step
+  long long kernels = 0;     // kernel nodes (launches per replay)
+  std::vector<StepCopy> copies;
+  uint64_t used = 0;         // last use, for eviction
+};
 
 struct sc_stream_encoder {
   sc_encoder_config cfg{};
@@ -142,8 +168,30 @@ struct sc_stream_encoder {
   int dump_layer = -1;
   float *dump = nullptr;  // [kDumpStages][M][2d]
   int64_t dump_rows = 0;
+  // Step graphs: a step whose geometry repeats the previous step's is
+  // captured into a CUDA graph (on cap_stream, which runs nothing); later
+  // steps with the same geometry and history parity replay it as one
+  // submission, after one store of their frame shift (s minus the captured
+  // s) into shift_dev, which the ring kernels add to frame numbers.
+  bool graphs = true;
+  int64_t *shift_dev = nullptr;
+  const int64_t *shift_arg = nullptr;  // what the step's ring kernels get: shift_dev while capturing
+  cudaStream_t cap_stream = nullptr;
+  std::vector<StepGraph> step_graphs;
+  std::vector<int64_t> prev_geom;      // geometry of the previous step (empty: none to compare)
+  int64_t graph_captures = 0, graph_launches = 0;
+  uint64_t graph_clock = 0;
+
+  void drop_graph(StepGraph &g) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (g.graph) cudaGraphDestroy(g.graph);
+    g.exec = nullptr;
+    g.graph = nullptr;
+  }
 
   ~sc_stream_encoder() {
+    for (auto &g : step_graphs) drop_graph(g);
+    if (cap_stream) cudaStreamDestroy(cap_stream);
     for (auto &l : layers)
       for (Lin *q : {&l.ff1_1, &l.ff1_2, &l.qkv, &l.pos, &l.out, &l.pw1, &l.pw2, &l.ff2_1, &l.ff2_2}) {
         cudaFree(q->w.qs);
@@ -443,6 +491,7 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     const int64_t tp = std::max<int64_t>(ceil_div(M, 128) * 128, 64), kp = ceil_div(kmax, 32) * 32;
     e->mel_stage_frames = 8 * (int64_t)c.max_frames;
     e->mel_stage = L.dev_alloc((size_t)(n_streams * e->mel_stage_frames * c.feat_in * 4));
+    e->shift_dev = (int64_t *)L.dev_alloc(sizeof(int64_t));
     e->win_stride = e->t_mel_max * c.feat_in;
     e->conv_stride = tb_max * fb * C;
     e->code_k = kp;
@@ -453,6 +502,7 @@ int sc_stream_encoder_create(const sc_encoder_config *cfg, const sc_tensor *tens
     ok = L.err.empty();
   }
   if (ok && (cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking) != cudaSuccess ||
+             cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking) != cudaSuccess ||
              cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
              cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming) != cudaSuccess)) {
     L.err = "side stream / event creation failed";
@@ -505,6 +555,14 @@ struct StepGeom {
   int64_t s, n_new, t_new, cf, t_mel, start_rel;
   int64_t ta, fa, tb, fb, fc, r3, e3, r5, n5;
 };
+
+// One attention launch of a call's frames from a: frames [a, b) inside one
+// attention chunk, keys from k_lo (left_chunks whole chunks back, clamped at
+// frame 0; streaming.rs:227, 501).
+static void attn_span(const sc_stream_encoder *e, int64_t a, int64_t t_new, int64_t &b, int64_t &k_lo) {
+  b = std::min<int64_t>(t_new, (a / e->chunk + 1) * e->chunk);
+  k_lo = (a / e->chunk > e->left_chunks ? a / e->chunk - e->left_chunks : 0) * e->chunk;
+}
 
 // One step for streams [z0, z0 + nz) on stream st.  Every buffer is indexed
 // by stream (or by row = stream * cf + frame) with per-stream strides that
@@ -591,7 +649,8 @@ static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *
     // the rings before the next one reads them, and every band stays within
     // left context + one chunk however many frames the call brings
     for (int64_t a = s; a < t_new;) {
-      const int64_t b = std::min<int64_t>(t_new, (a / e->chunk + 1) * e->chunk);
+      int64_t b, k_lo;
+      attn_span(e, a, t_new, b, k_lo);
       AttnParams p{};
       p.q = qkv;
       p.ldq = 3 * d;
@@ -614,7 +673,7 @@ static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *
       p.n_heads = c.n_heads;
       p.scale = 1.0f / sqrtf((float)(d / c.n_heads));
       p.s = a;
-      p.k_lo = (a / e->chunk > e->left_chunks ? a / e->chunk - e->left_chunks : 0) * e->chunk;
+      p.k_lo = k_lo;
       p.k_hi = b;
       p.chunk = e->chunk;
       p.left_chunks = e->left_chunks;
@@ -622,6 +681,7 @@ static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *
       p.lane_major = 1;  // q, k, pos rows and biases in lane-major head order
       p.zrows = cf;      // rows of stream z: z * cf + (frame - s)
       p.r0 = a - s;
+      p.frame_shift = e->shift_arg;
       TRY(attn_prepare(p, e->n_pos));
       TRY(launch_attn(p, Z, st));
       a = b;
@@ -632,9 +692,9 @@ static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *
     // conv module: LN, pw1, GLU (ring), causal dw conv + LN + SiLU (codes), pw2
     TRY(launch_ln_quant(y, d, ly.ln_conv_w, ly.ln_conv_b, eps, (int)d, M, qa, nullptr, d, st));
     TRY(gemm_q(ly.pw1, qa, h2, 2 * d, Epilogue{}, QOut{}));
-    TRY(launch_glu_ring(h2, M, (int)cf, (int)d, glu_ring, (int)e->glu_cap, s, st));
-    TRY(launch_dwconv_ln_silu_quant(glu_ring, (int)e->glu_cap, M, (int)cf, (int)d, c.conv_kernel, s, ly.dw_t,
-                                    ly.conv_ln_w, ly.conv_ln_b, eps, qb_d, dumping ? o2 : nullptr, st));
+    TRY(launch_glu_ring(h2, M, (int)cf, (int)d, glu_ring, (int)e->glu_cap, s, e->shift_arg, st));
+    TRY(launch_dwconv_ln_silu_quant(glu_ring, (int)e->glu_cap, M, (int)cf, (int)d, c.conv_kernel, s, e->shift_arg,
+                                    ly.dw_t, ly.conv_ln_w, ly.conv_ln_b, eps, qb_d, dumping ? o2 : nullptr, st));
     TRY(dump(4, qkv, 3 * d));  // q of the new frames
     TRY(dump(5, o2, d));
     TRY(gemm_q(ly.pw2, qb_d, y, d, Epilogue{kEpiResidual, y, 1.0f}, QOut{}));
@@ -660,7 +720,8 @@ static int encode_streams(sc_stream_encoder *e, const StepGeom &g, const float *
     TRY(gemm_q(e->prompt2, qh, y, d, Epilogue{}, QOut{}));
     TRY(launch_prompt_select(x, y, M, (int)cf, (int)d, e->pids + z0, st));
   }
-  TRY(launch_out_ring(x, M, (int)cf, (int)d, e->out_ring + z0 * e->out_cap * d, (int)e->out_cap, s, st));
+  TRY(launch_out_ring(x, M, (int)cf, (int)d, e->out_ring + z0 * e->out_cap * d, (int)e->out_cap, s, e->shift_arg,
+                      st));
   return kOk;
 }
 
@@ -680,6 +741,161 @@ static int64_t split_point(const sc_stream_encoder *e, int64_t cf) {
   const int64_t unit = 128 / gcd;  // streams per 128-frame tile boundary
   const int64_t z0 = (Z / 2) / unit * unit;
   return z0 > 0 && z0 < Z ? z0 : 0;
+}
+
+// ---- step graphs ----------------------------------------------------------
+//
+// The reference's GPU backend records a whole step into one submission
+// (gpu/batch.rs:50,163; gpu/streaming.rs:259-298).  Here a step is captured
+// by stream capture into a CUDA graph and replayed by later steps with the
+// same launches.  Two steps issue the same launches with the same arguments
+// when their geometry below is equal, except for
+//  - frame numbers, which differ by a whole number of attention chunks:
+//    bands, masks, pos rows and the conv taps depend only on frame
+//    differences (and on chunk indices, which shift together), so only ring
+//    slots move, and the ring kernels add the device frame shift;
+//  - the caller's mel and output buffers: the mel always passes through the
+//    staging buffer in a graph step, and replays re-point the copy nodes.
+// The mel-history buffer pair alternates between steps; its parity is part
+// of a graph's key.
+constexpr size_t kMaxStepGraphs = 4;
+
+static std::vector<int64_t> step_geometry(const sc_stream_encoder *e, const StepGeom &g, int64_t z0, bool host_io,
+                                          bool has_out) {
+  std::vector<int64_t> k = {e->n_streams, z0, g.cf, g.n_new, g.t_mel, g.start_rel, e->hist_frames,
+                            g.s % e->chunk,
+                            // depthwise taps before frame 0 are skipped until s >= kernel - 1
+                            std::min<int64_t>(g.s, e->cfg.conv_kernel - 1), host_io, has_out, e->any_prompt};
+  for (int64_t a = g.s; a < g.t_new;) {
+    int64_t b, k_lo;
+    attn_span(e, a, g.t_new, b, k_lo);
+    k.insert(k.end(), {a - g.s, b - g.s, k_lo - g.s});
+    a = b;
+  }
+  return k;
+}
+
+static bool page_locked(const void *p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+static StepGraph *find_step_graph(sc_stream_encoder *e, const std::vector<int64_t> &key) {
+  for (auto &g : e->step_graphs)
+    if (g.exec && g.key == key) return &g;
+  return nullptr;
+}
+
+// Captures the launches issue(stream) makes into a new step graph.  Nothing
+// runs.  On any failure the encoder stops using graphs (its steps run as
+// separate launches, which report errors of their own) and nullptr returns.
+static StepGraph *capture_step(sc_stream_encoder *e, std::vector<int64_t> key, int64_t s, int64_t n_new,
+                               int64_t cf, int64_t z0, const std::function<int(cudaStream_t)> &issue) {
+  const long long n0 = sc_launch_count();
+  e->shift_arg = e->shift_dev;
+  cudaGraph_t graph = nullptr;
+  int rc = kOk;
+  cudaError_t ce = cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal);
+  if (ce == cudaSuccess) {
+    rc = issue(e->cap_stream);
+    ce = cudaStreamEndCapture(e->cap_stream, &graph);
+  }
+  e->shift_arg = nullptr;
+  note_launches(-(sc_launch_count() - n0));  // captured, not run
+  StepGraph sg;
+  sg.key = std::move(key);
+  sg.s = s;
+  sg.graph = graph;
+  bool ok = !rc && ce == cudaSuccess && graph;
+  if (ok) {
+    // kernel nodes, and which copy each copy node is (by its device-side
+    // address: the staging buffer for mel in, the frames for frames out)
+    const int64_t fi = e->cfg.feat_in, d = e->cfg.d_model, Z = e->n_streams;
+    const int64_t halves[2][2] = {{0, z0 ? z0 : Z}, {z0, Z - z0}};
+    size_t n = 0;
+    ok = cudaGraphGetNodes(graph, nullptr, &n) == cudaSuccess;
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (ok && n) ok = cudaGraphGetNodes(graph, nodes.data(), &n) == cudaSuccess;
+    for (size_t i = 0; ok && i < n; i++) {
+      cudaGraphNodeType t;
+      ok = cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess;
+      if (!ok) break;
+      if (t == cudaGraphNodeTypeKernel) {
+        sg.kernels++;
+      } else if (t == cudaGraphNodeTypeMemcpy) {
+        cudaMemcpy3DParms p{};
+        ok = cudaGraphMemcpyNodeGetParams(nodes[i], &p) == cudaSuccess;
+        const char *dst = (const char *)p.dstPtr.ptr + p.dstPos.x, *src = (const char *)p.srcPtr.ptr + p.srcPos.x;
+        bool found = false;
+        for (int h = 0; ok && !found && h < (z0 ? 2 : 1); h++) {
+          const int64_t za = halves[h][0], nz = halves[h][1];
+          if (n_new > 0 && dst == (const char *)(e->mel_stage + za * n_new * fi)) {
+            sg.copies.push_back(StepCopy{nodes[i], za, nz, 0});
+            found = true;
+          } else if (src == (const char *)(e->x + za * cf * d)) {
+            sg.copies.push_back(StepCopy{nodes[i], za, nz, 1});
+            found = true;
+          }
+        }
+        ok = ok && found;
+      }
+    }
+  }
+  if (ok) ok = cudaGraphInstantiate(&sg.exec, graph, 0) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    e->drop_graph(sg);
+    e->graphs = false;
+    return nullptr;
+  }
+  if (e->step_graphs.size() >= kMaxStepGraphs) {
+    // the least recently used one goes; wait until no launch of it is queued
+    size_t lru = 0;
+    for (size_t i = 1; i < e->step_graphs.size(); i++)
+      if (e->step_graphs[i].used < e->step_graphs[lru].used) lru = i;
+    cudaDeviceSynchronize();
+    e->drop_graph(e->step_graphs[lru]);
+    e->step_graphs.erase(e->step_graphs.begin() + (std::ptrdiff_t)lru);
+  }
+  e->graph_captures++;
+  e->step_graphs.push_back(std::move(sg));
+  return &e->step_graphs.back();
+}
+
+// Replays a step graph on st for the step at frame s: copy nodes pointed at
+// this call's buffers, the frame shift stored, one graph launch.  Returns 1
+// (nothing issued) when the graph cannot serve this step.
+static int replay_step(sc_stream_encoder *e, StepGraph &g, int64_t s, const float *mel_new, int64_t n_new,
+                       float *out_host, int64_t cf, bool host_io, cudaStream_t st) {
+  const int64_t fi = e->cfg.feat_in, d = e->cfg.d_model;
+  if (s < g.s || (s - g.s) % e->chunk) return 1;  // the shift must be whole chunks forward
+  for (const StepCopy &c : g.copies) {
+    cudaError_t ce;
+    if (c.dir == 0) {
+      const int64_t off = c.za * n_new * fi;
+      ce = cudaGraphExecMemcpyNodeSetParams1D(g.exec, c.node, e->mel_stage + off, mel_new + off,
+                                              (size_t)(c.nz * n_new * fi) * 4,
+                                              host_io ? cudaMemcpyHostToDevice : cudaMemcpyDefault);
+    } else {
+      const int64_t off = c.za * cf * d;
+      ce = cudaGraphExecMemcpyNodeSetParams1D(g.exec, c.node, out_host + off, e->x + off, (size_t)(c.nz * cf * d) * 4,
+                                              cudaMemcpyDeviceToHost);
+    }
+    if (ce != cudaSuccess) {
+      cudaGetLastError();
+      return 1;
+    }
+  }
+  TRY(launch_store_i64(e->shift_dev, s - g.s, st));
+  SC_CUDA(cudaGraphLaunch(g.exec, st));
+  note_launches(g.kernels);
+  g.used = ++e->graph_clock;
+  e->graph_launches++;
+  return kOk;
 }
 
 // One encode_new step.  host_io: mel_new is host memory, copied per half
@@ -775,11 +991,14 @@ static int encode_call(sc_stream_encoder *e, const float *mel_new, int64_t t0, i
   // under two waves of CTAs, so the other half's kernels fill the SMs their
   // last wave leaves idle) ----
   const int64_t fi = c.feat_in;
-  auto run = [&](int64_t za, int64_t nz, cudaStream_t sa) -> int {
+  // streams [za, za + nz) on sa; stage: the mel goes through the staging
+  // buffer (the host entry point, and every graph step)
+  auto run = [&](int64_t za, int64_t nz, cudaStream_t sa, bool stage) -> int {
     const float *mel = mel_new;
-    if (host_io && n_new > 0) {
+    if (stage && n_new > 0) {
       SC_CUDA(cudaMemcpyAsync(e->mel_stage + za * n_new * fi, mel_new + za * n_new * fi,
-                              (size_t)(nz * n_new * fi) * 4, cudaMemcpyHostToDevice, sa));
+                              (size_t)(nz * n_new * fi) * 4, host_io ? cudaMemcpyHostToDevice : cudaMemcpyDefault,
+                              sa));
       mel = e->mel_stage;
     }
     TRY(encode_streams(e, g, mel, za, nz, sa));
@@ -789,19 +1008,37 @@ static int encode_call(sc_stream_encoder *e, const float *mel_new, int64_t t0, i
     return kOk;
   };
   const int64_t z0 = split_point(e, cf);
-  int rc;
-  if (z0 == 0) {
-    rc = run(0, Z, st);
-  } else {
-    SC_CUDA(cudaEventRecord(e->ev_fork, st));
+  auto run_all = [&](cudaStream_t s0, bool stage) -> int {
+    if (z0 == 0) return run(0, Z, s0, stage);
+    SC_CUDA(cudaEventRecord(e->ev_fork, s0));
     SC_CUDA(cudaStreamWaitEvent(e->side, e->ev_fork, 0));
-    rc = run(0, z0, st);
-    if (!rc) rc = run(z0, Z - z0, e->side);
+    int r = run(0, z0, s0, stage);
+    if (!r) r = run(z0, Z - z0, e->side, stage);
     // join even after an error, so the caller's stream never runs ahead of
     // work left on the side stream
     SC_CUDA(cudaEventRecord(e->ev_join, e->side));
-    SC_CUDA(cudaStreamWaitEvent(st, e->ev_join, 0));
+    SC_CUDA(cudaStreamWaitEvent(s0, e->ev_join, 0));
+    return r;
+  };
+  // a step graph when this step's geometry was seen before (replay) or
+  // repeats the previous step's (capture, then replay); separate launches
+  // otherwise
+  const bool graph_ok = e->graphs && e->dump_layer < 0 && n_new <= e->mel_stage_frames &&
+                        (!host_io || ((n_new == 0 || page_locked(mel_new)) && (!out_host || page_locked(out_host))));
+  std::vector<int64_t> geom;
+  StepGraph *gr = nullptr;
+  if (graph_ok) {
+    geom = step_geometry(e, g, z0, host_io, out_host != nullptr);
+    std::vector<int64_t> key = geom;
+    key.push_back(e->hist_cur);
+    gr = find_step_graph(e, key);
+    if (!gr && geom == e->prev_geom)
+      gr = capture_step(e, std::move(key), s, n_new, cf, z0, [&](cudaStream_t cs) { return run_all(cs, true); });
   }
+  e->prev_geom = std::move(geom);
+  int rc = 1;
+  if (gr) rc = replay_step(e, *gr, s, mel_new, n_new, out_host, cf, host_io, st);
+  if (rc == 1) rc = run_all(st, host_io);
   if (host_io) {
     // even after an error: copies already queued may still be reading the
     // caller's mel buffer or writing its output buffer
@@ -834,6 +1071,31 @@ int sc_stream_encoder_set_concurrency(sc_stream_encoder *e, int32_t n_batches) {
   }
   e->max_batches = n_batches;
   return kOk;
+}
+
+int sc_stream_encoder_set_graphs(sc_stream_encoder *e, int32_t enable) {
+  if (!e || (enable != 0 && enable != 1)) {
+    set_error("stream_encoder_set_graphs: enable must be 0 or 1");
+    return kErrInvalid;
+  }
+  if (!enable && !e->step_graphs.empty()) {
+    SC_CUDA(cudaDeviceSynchronize());  // no replay of them may still be queued
+    for (auto &g : e->step_graphs) e->drop_graph(g);
+    e->step_graphs.clear();
+  }
+  e->graphs = enable != 0;
+  e->prev_geom.clear();
+  return kOk;
+}
+
+int sc_stream_encoder_graph_stats(const sc_stream_encoder *e, int64_t *captures, int64_t *launches) {
+  if (!e || !captures || !launches) {
+    set_error("stream_encoder_graph_stats: invalid argument");
+    return kErrInvalid;
+  }
+  *captures = e->graph_captures;
+  *launches = e->graph_launches;
+  return e->graphs ? 1 : 0;
 }
 
 int sc_stream_encoder_set_prompts(sc_stream_encoder *e, const int32_t *prompt_ids) {

@@ -188,6 +188,12 @@ struct AttnParams {
   // q / out / qout rows of stream z, query j are z*zrows + r0 + j and its new
   // K/V rows z*zrows + r0 + (fr - new_lo); 0 keeps the layouts above.
   int64_t zrows = 0, r0 = 0;
+  // Device frame shift added to every frame number before it becomes a ring
+  // slot (nullptr: none).  A replayed step graph runs its captured launches
+  // at a later step whose frames are these plus a whole number of chunks:
+  // bands, masks and pos rows depend only on frame differences and chunk
+  // indices relative to the band, so only the ring slots move.
+  const int64_t *frame_shift = nullptr;
 };
 int attn_prepare(AttnParams &p, int64_t n_pos);
 int launch_attn(const AttnParams &p, int64_t n_streams, cudaStream_t st);

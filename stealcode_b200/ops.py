@@ -319,6 +319,19 @@ class StreamEncoder:
         """Sub-batches of streams in flight per encode_new (1 or 2; same bits)."""
         check(lib.sc_stream_encoder_set_concurrency(self._h, n_batches))
 
+    def set_graphs(self, enable: bool) -> None:
+        """Step graphs on (the default) or off: steady steps replay one CUDA
+        graph of the whole step, else every kernel launches separately (same
+        bits)."""
+        check(lib.sc_stream_encoder_set_graphs(self._h, 1 if enable else 0))
+
+    def graph_stats(self) -> tuple:
+        """(graphs on, graphs captured, graph launches) so far."""
+        cap, lau = ctypes.c_int64(), ctypes.c_int64()
+        rc = lib.sc_stream_encoder_graph_stats(self._h, ctypes.byref(cap), ctypes.byref(lau))
+        check(min(rc, 0))
+        return bool(rc), int(cap.value), int(lau.value)
+
     def set_dump(self, layer: int) -> None:
         check(lib.sc_stream_encoder_set_dump(self._h, layer))
 
