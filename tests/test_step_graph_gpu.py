@@ -159,3 +159,33 @@ def test_step_graphs_long_calls(torch):
     assert g.graph_stats() == (True, 3, 6)
     g.close()
     e.close()
+
+
+def test_step_graphs_prompt_mlp(torch):
+    """The prompt MLP inside replayed step graphs: 3 streams with prompts
+    (one none), 2 blocks, 128 prompts, 16 steps; at step 14, while graphs
+    replay, the prompts change (the graph reads the per-stream prompt ids
+    from device memory when it runs).  Every step equals the same encoder
+    with graphs off."""
+    from stealcode_b200.ops import StreamEncoder
+
+    cfg = model.EncoderConfig(n_layers=2, n_prompts=128)
+    m = model.random_model(cfg, seed=43)
+    n_steps = 16
+    mel = model.mel_stream(44, 3, 56 * n_steps, cfg.feat_in)
+    g, e = StreamEncoder(m, 3), StreamEncoder(m, 3)
+    e.set_graphs(False)
+    for enc in (g, e):
+        enc.set_prompts([None, 3, 127])
+    for i in range(n_steps):
+        if i == 14:
+            for enc in (g, e):
+                enc.set_prompts([5, None, 2])
+        t0, t1 = 56 * i, 56 * (i + 1)
+        x = torch.from_numpy(np.ascontiguousarray(mel[:, t0:t1])).cuda()
+        g.encode_new(x, t0, t1)
+        e.encode_new(x, t0, t1)
+        assert np.array_equal(_rows(torch, g), _rows(torch, e)), f"step {i}"
+    assert g.graph_stats() == (True, 2, n_steps - 11)
+    g.close()
+    e.close()
