@@ -2,20 +2,27 @@
 // encoder step (everything in block_new and pre_encode_forward except the
 // Q8_0 linears and the attention):
 //   ln_rows_kernel            LayerNorm per frame row   (simd_kernel.rs:734-813)
+//   ln_quant_kernel           LayerNorm (or two in a row) + the next GEMM's
+//                             activation codes
 //   glu_ring_kernel           GLU into the per-stream conv ring
 //                                                       (simd_kernel.rs:868-910)
-//   dwconv_ln_silu_kernel     causal depthwise conv over the ring + LayerNorm
-//                             + SiLU, fused            (streaming.rs:608-638,
+//   dwconv_ln_silu_quant_kernel  causal depthwise conv over the ring +
+//                             LayerNorm + SiLU + codes  (streaming.rs:608-638,
 //                             simd_kernel.rs:1160-1235, 817-839)
-//   mel_window_kernel         pre-encode mel window     (streaming.rs:182-207)
-//   conv2d_3x3s2_kernel       conv0 and the depthwise convs 2/5
-//                                                       (nemotron/weights.rs:418-523)
-//   pw_conv_relu_kernel       pointwise convs 3/6 as an f32 GEMM + bias + ReLU
+//   mel_window_kernel, mel_hist_kernel  pre-encode mel window and the mel
+//                             history kept for the next step
+//                                                       (streaming.rs:182-207)
+//   conv02_fused_kernel       conv0 + ReLU and the depthwise conv2, fused
+//   conv2d_3x3s2_kernel       the depthwise conv5       (nemotron/weights.rs:418-523)
+//   pw_conv_relu_kernel, pw_conv_tail_kernel  pointwise convs 3/6 as an f32
+//                             GEMM + bias + ReLU in the reference GEMM's order
 //                                                       (nemotron/weights.rs:345-417)
 //   flatten_kernel            [t, f, C] -> [t, C*f] of the needed frames
 //                                                       (nemotron/encoder.rs:460-470)
-// Frame rows are time-major [stream][frame][d]; one CTA handles one row for
-// the row-wise kernels (d = 1024: 4 elements per thread).
+//   prompt_cat_quant_kernel, prompt_select_kernel  the prompt MLP's input
+//                             and output                (streaming.rs:320-342)
+//   out_ring_kernel           output frames into the per-stream output ring
+// Frame rows are time-major [stream][frame][d].
 #include "sc_device.cuh"
 #include "sc_kernels.cuh"
 
@@ -373,36 +380,6 @@ __global__ void glu_ring_kernel(const float *__restrict__ h2, int c, int d, floa
     const float gate = h2[row * 2 * d + i], val = h2[row * 2 * d + d + i];
     dst[i] = __fmul_rn(gate, __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-val))));
   }
-}
-
-// Causal depthwise conv (kernel kh, left pad kh - 1) over the GLU ring, then
-// the conv module's LayerNorm and SiLU, for new frame j of stream z.  Taps
-// before frame 0 are the zero padding (as for the first batch of a stream).
-__global__ void __launch_bounds__(kRowThreads)
-    dwconv_ln_silu_kernel(const float *__restrict__ ring, int cap, int c, int d, int kh, int64_t s,
-                          const float *__restrict__ w, const float *__restrict__ lnw,
-                          const float *__restrict__ lnb, float eps, float *__restrict__ out) {
-  __shared__ RowScratch sh;
-  const int64_t row = blockIdx.x;
-  const int64_t z = row / c, fr = s + row % c;
-  const int nv = d / kRowThreads;
-  float v[kMaxRowVals];
-#pragma unroll
-  for (int k = 0; k < kMaxRowVals; k++)
-    if (k < nv) {
-      const int ch = threadIdx.x + k * kRowThreads;
-      float acc = 0.0f;
-      for (int t = 0; t < kh; t++) {
-        const int64_t ti = fr - (kh - 1) + t;
-        if (ti < 0) continue;
-        acc = __fmaf_rn(ring[(z * cap + ti % cap) * (int64_t)d + ch], w[ch * kh + t], acc);
-      }
-      v[k] = acc;
-    }
-  ln_vals(v, d, lnw, lnb, eps, sh);
-#pragma unroll
-  for (int k = 0; k < kMaxRowVals; k++)
-    if (k < nv) out[row * d + threadIdx.x + k * kRowThreads] = silu_ref(v[k]);
 }
 
 // Pre-encode window of stream z: `hist` held frames of history (the last
@@ -830,14 +807,6 @@ int launch_ln_rows(const float *x, int64_t ldx, const float *w, const float *b, 
 int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, int cap, int64_t s,
                     const int64_t *shift, cudaStream_t st) {
   glu_ring_kernel<<<(unsigned)rows, 256, 0, st>>>(h2, c, d, ring, cap, s, shift);
-  note_launch();
-  SC_CUDA(cudaGetLastError());
-  return kOk;
-}
-
-int launch_dwconv_ln_silu(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s, const float *w,
-                          const float *lnw, const float *lnb, float eps, float *out, cudaStream_t st) {
-  dwconv_ln_silu_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(ring, cap, c, d, kh, s, w, lnw, lnb, eps, out);
   note_launch();
   SC_CUDA(cudaGetLastError());
   return kOk;

@@ -39,8 +39,6 @@ int launch_ln_rows(const float *x, int64_t ldx, const float *w, const float *b, 
 // graph, added to frame numbers before they become ring slots; nullptr none.
 int launch_glu_ring(const float *h2, int64_t rows, int c, int d, float *ring, int cap, int64_t s,
                     const int64_t *shift, cudaStream_t st);
-int launch_dwconv_ln_silu(const float *ring, int cap, int64_t rows, int c, int d, int kh, int64_t s, const float *w,
-                          const float *lnw, const float *lnb, float eps, float *out, cudaStream_t st);
 int launch_mel_window(const float *hist, int hist_cap, int hist_frames, const float *mel_new, int n_new,
                       int n_mels, int t_mel, float *win, int64_t n_streams, cudaStream_t st);
 int launch_mel_hist(const float *old_hist, int hist_cap, int hist_frames, const float *mel_new, int n_new,
