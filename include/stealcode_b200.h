@@ -376,7 +376,10 @@ int sc_stream_encoder_set_concurrency(sc_stream_encoder *e, int32_t n_batches);
  * geometry replay it as one launch after a one-thread store of their frame
  * shift, with its copy nodes pointed at the call's own mel and output
  * buffers.  Steady streaming steps all share one geometry (two graphs: the
- * mel history alternates between two buffers).  Host buffers of
+ * mel history alternates between two buffers).  At most four graphs are
+ * kept; capturing a fifth drops the least recently used one after a device
+ * synchronise (a caller that alternates between more than two step
+ * geometries sees that synchronise).  Host buffers of
  * encode_new_host must be page-locked for a step to use a graph; stage dumps
  * turn graphs off.  Same bits as separate launches.  enable 0 drops the
  * graphs (after a device synchronise) and launches every kernel separately. */
